@@ -1,0 +1,310 @@
+/*
+ * tensorium_b200.h -- C ABI of the B200 (sm_100a) backend for Tensorium's darknet-style
+ * convolution-forward inference path.
+ *
+ * This library replaces the CUDA half of the reference's layer dispatch: the TNNCuda<T>
+ * methods in source/nncuda.pas:100-158 that TConvolutionalLayer, TMaxPoolLayer,
+ * TUpSampleLayer, TConcatLayer (route), TAddLayer (shortcut), TYoloLayer and
+ * TXNORConvolutionLayer call from their forwardGPU methods.  The Pascal host keeps its
+ * TSingleTensor / layer API and binds these functions as `external 'tensorium_b200' ... cdecl`.
+ *
+ * Conventions (all entry points):
+ *   - cdecl, plain C types only; every size is int64_t (the reference's SizeInt on x86-64).
+ *   - float pointers are device pointers unless the name ends in _host.
+ *   - tensors are NCHW fp32, as TSingleTensor stores them.
+ *   - every function returns int: TB_OK (0) on success, a negative TB_ERR_* otherwise; the
+ *     message of the last failure on the calling thread is tb_last_error().
+ *     (The reference asserts instead: SAFE_CALL in source/nncuda.pas:237-273.)
+ *   - launches are asynchronous on the context's stream; only tb_sync, tb_memcpy_d2h and the
+ *     functions that say so block.
+ *   - device memory is allocated only by tb_malloc, tb_init, tb_workspace_reserve and
+ *     tb_net_finalize, and by the context's scratch workspace growing on demand inside
+ *     tb_conv2d_fwd (split-K partials), tb_xnor_conv_fwd (packed input bits) and
+ *     tb_yolo_detect (counters). Growth is refused (TB_ERR_STATE) while the stream is being
+ *     captured into a CUDA graph; reserve first with tb_workspace_reserve.
+ */
+#ifndef TENSORIUM_B200_H
+#define TENSORIUM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_VERSION 100
+
+/* ---- status codes ------------------------------------------------------------------ */
+#define TB_OK               0
+#define TB_ERR_INVALID     -1   /* bad argument (null pointer, bad size, unsupported shape) */
+#define TB_ERR_CUDA        -2   /* a CUDA runtime call failed */
+#define TB_ERR_UNSUPPORTED -3   /* valid request that this build does not implement */
+#define TB_ERR_OOM         -4   /* device allocation failed */
+#define TB_ERR_TIMEOUT     -5   /* a bounded wait ran out (collectives) */
+#define TB_ERR_STATE       -6   /* call made in the wrong state (e.g. net not finalized) */
+#define TB_ERR_DEVICE      -7   /* a kernel reported an error through the device status word */
+
+/* ---- activations: same ordinals as TActivationType (source/ntypes.pas:66-71) ----------- */
+#define TB_ACT_LOGISTIC  0
+#define TB_ACT_RELU      1
+#define TB_ACT_RELU6     2
+#define TB_ACT_RELIE     3
+#define TB_ACT_LINEAR    4
+#define TB_ACT_RAMP      5
+#define TB_ACT_TANH      6
+#define TB_ACT_PLSE      7
+#define TB_ACT_REVLEAKY  8
+#define TB_ACT_LEAKY     9
+#define TB_ACT_ELU      10
+#define TB_ACT_LOGGY    11
+#define TB_ACT_HARDTAN  13
+#define TB_ACT_LHTAN    14
+#define TB_ACT_SELU     15
+
+/* ---- math modes of the convolution mainloop ---------------------------------------- */
+#define TB_MATH_FP32  0   /* FP32 CUDA-core FMA mainloop (reference-faithful, default) */
+#define TB_MATH_TF32  1   /* tcgen05 tensor-core mainloop, TF32 operands, FP32 accumulate */
+
+/* ---- context ------------------------------------------------------------------------- */
+typedef struct tb_ctx tb_ctx;
+
+typedef struct tb_options {
+    int64_t math_mode;        /* TB_MATH_* used by tb_conv2d_fwd when a call does not override */
+    int64_t workspace_bytes;  /* initial split-K workspace; 0 = library default (64 MiB) */
+    int64_t flags;            /* reserved, must be 0 */
+} tb_options;
+
+/* Last error message of the calling thread ("" if none). */
+const char* tb_last_error(void);
+int tb_version(void);
+/* Replaces TNNCuda.deviceCount (source/nncuda.pas:100). */
+int tb_device_count(int64_t* count);
+/* Replaces TNNCuda.Create(deviceIndex) (source/nncuda.pas:448-467): selects the device,
+ * creates a stream and the split-K workspace. opts may be NULL. */
+int tb_init(int64_t device, const tb_options* opts, tb_ctx** out);
+/* Replaces TNNCuda.Destroy. */
+int tb_shutdown(tb_ctx* ctx);
+/* Run subsequent launches on an existing cudaStream_t (NULL = the context's own stream). */
+int tb_set_stream(tb_ctx* ctx, void* cuda_stream);
+void* tb_get_stream(tb_ctx* ctx);
+/* Replaces TNNCuda.finish (source/nncuda.pas:1575-1584); also surfaces device status errors. */
+int tb_sync(tb_ctx* ctx);
+/* Replaces createDeviceBuffer / freeDeviceBuffer (source/nncuda.pas:103-104). */
+int tb_malloc(tb_ctx* ctx, int64_t bytes, void** ptr);
+int tb_free(tb_ctx* ctx, void* ptr);
+/* Replaces writeBuffer / readBuffer (source/nncuda.pas:105-106). h2d is asynchronous
+ * (ordered on the stream); d2h blocks until the bytes are on the host. */
+int tb_memcpy_h2d(tb_ctx* ctx, void* dst, const void* src_host, int64_t bytes);
+int tb_memcpy_d2h(tb_ctx* ctx, void* dst_host, const void* src, int64_t bytes);
+/* Grow the split-K workspace to at least `bytes` (allocates; call before graph capture). */
+int tb_workspace_reserve(tb_ctx* ctx, int64_t bytes);
+
+/* ---- elementwise / BLAS-1 helpers used by the layers on the path -------------------- */
+/* TNNCuda.ActivateArray(N, x, offset, activation) (source/nncuda.pas:108). */
+int tb_activate(tb_ctx* ctx, int64_t n, float* x, int64_t offset, int64_t activation);
+/* TNNCuda.forwardBias (source/nncuda.pas:110): dst[b][i][j] += bias[i], i < bias_size,
+ * j < dst_size/(batch*bias_size). */
+int tb_forward_bias(tb_ctx* ctx, int64_t dst_size, float* dst, int64_t offset,
+                    int64_t bias_size, const float* bias, int64_t incb, int64_t batch);
+/* TNNCuda.copy (source/nncuda.pas:123). */
+int tb_copy(tb_ctx* ctx, int64_t n, const float* src, int64_t src_offset, int64_t inca,
+            float* dst, int64_t dst_offset, int64_t incb);
+/* TNNCuda.fill (source/nncuda.pas:122). */
+int tb_fill(tb_ctx* ctx, int64_t n, float* x, int64_t offset, float val, int64_t stride);
+/* TNNCuda.addvv (source/nncuda.pas:116): dst = src1 + src2 elementwise (strided). */
+int tb_addvv(tb_ctx* ctx, int64_t n, const float* src1, int64_t src1_offset, int64_t inca,
+             const float* src2, int64_t src2_offset, int64_t incb,
+             float* dst, int64_t dst_offset, int64_t incc);
+/* TNNCuda.fmavss (source/nncuda.pas:137): dst = src*scalar + bias on n elements at offset. */
+int tb_fmavss(tb_ctx* ctx, int64_t n, float* src, int64_t offset, float scalar, float bias, float* dst);
+
+/* ---- convolution (TConvolutionalLayer.forward / forwardGPU) --------------------------- */
+typedef struct tb_conv_desc {
+    int64_t batch, channels, height, width;        /* input  [batch, channels, height, width] */
+    int64_t filters, kernel_h, kernel_w;           /* weights [filters][channels*kernel_h*kernel_w] */
+    int64_t stride_y, stride_x, pad_y, pad_x;
+    int64_t dilation_y, dilation_x;                /* 0 is read as 1 */
+    int64_t activation;                            /* TB_ACT_* applied after bias / batchnorm */
+    int64_t in_batch_stride;   /* elements between images of x; 0 = channels*height*width */
+    int64_t out_batch_stride;  /* elements between images of y; 0 = filters*out_h*out_w */
+    int64_t res_batch_stride;  /* elements between images of residual; 0 = like y */
+} tb_conv_desc;
+
+/* Output size (h + 2p - dil*(k-1) - 1) div s + 1, as TBaseConvolutionalLayer.outHeight /
+ * outWidth (source/nConvolutionLayer.pas:92-100). */
+int tb_conv_out_shape(const tb_conv_desc* d, int64_t* out_h, int64_t* out_w);
+/* Number of floats of the packed weight buffer tb_conv_pack_weights writes. */
+int tb_conv_packed_weights_count(const tb_conv_desc* d, int64_t* count);
+/* Re-lay the reference weights (row-major [filters][channels][kh][kw], the order of
+ * source/nConvolutionLayer.pas:206 and the darknet .weights file) into the K-major tile layout
+ * the conv kernels read. Device to device, once per weight load (the reference's one-time
+ * weights.pushToDevice, source/nConvolutionLayer.pas:1034-1036). */
+int tb_conv_pack_weights(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed);
+/* Host helper: fold batchnorm into weights and biases in place, the arithmetic of
+ * TBaseConvolutionalLayer.fuseBatchNorm (source/nConvolutionLayer.pas:102-126). */
+int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights_host, float* biases_host,
+                    const float* scales_host, const float* rolling_mean_host,
+                    const float* rolling_variance_host);
+/* Fused conv forward: y = act(conv(x, w) + epilogue) [+ residual].
+ * Replaces, in one launch (two with split-K), the reference sequence
+ *   cuda.im2col per image -> cuda.gemmStridedBatched -> [normalize, forwardScale] ->
+ *   forwardBias -> ActivateArray   (source/nConvolutionLayer.pas:1055-1122)
+ * epilogue: if bn_mean != NULL: v = ((acc - mean)/max(sqrt(var),1e-6))*bn_scale + bias
+ *           (TBaseLayer.batchNorm inference, source/nbaselayer.pas:336-370)
+ *           else v = acc + bias (bias may be NULL = 0; source/ntensors.pas:7709-7727);
+ *           v = act(v); if residual != NULL: v += residual (TAddLayer.forward,
+ *           source/naddlayer.pas:696-699, with a linear shortcut activation).
+ * math_mode: TB_MATH_* or -1 for the context default. */
+int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w,
+                  const float* bias, const float* bn_scale, const float* bn_mean,
+                  const float* bn_variance, const float* residual, float* y, int64_t math_mode);
+
+/* ---- memory-bound layers -------------------------------------------------------------- */
+/* TNNCuda.forwardMaxPool (source/nncuda.pas:132; CPU semantics source/nMaxPoolLayer.pas:
+ * 265-463): out = max over the k x k window at (i*stride_y + n - padding div 2,
+ * j*stride_x + m - padding div 2), out-of-image = -FLT_MAX, strict '>' (first max wins).
+ * out_h = (h + padding - k) div stride_y + 1. indexes (int64, may be NULL) receives the flat
+ * input index of the max (-1 if none). */
+int tb_maxpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int64_t w,
+                   int64_t ksize, int64_t stride_x, int64_t stride_y, int64_t padding,
+                   const float* x, float* y, int64_t* indexes);
+/* TUpSampleLayer.forward (source/nupsamplelayer.pas:83-131): y[c][yy][xx] =
+ * scale * x[c][yy div s][xx div s]. y_batch_stride (0 = dense) lets the result land in a
+ * slice of a route (concat) buffer. */
+int tb_upsample_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int64_t w,
+                    int64_t stride, float scale, const float* x, float* y, int64_t y_batch_stride);
+/* TConcatLayer.forward (source/nconcatlayer.pas:93-119). per_sample != 0: darknet channel
+ * concatenation per image (out[b] = in0[b] | in1[b] | ...). per_sample == 0: the reference's
+ * TTensor.concat (source/ntensors.pas:12045-12061), whole tensors back to back.
+ * sizes[i] = elements per image of input i. */
+int tb_route_fwd(tb_ctx* ctx, int64_t batch, int64_t n_inputs, const float* const* inputs,
+                 const int64_t* sizes, float* y, int64_t per_sample);
+/* TAddLayer.forward single-input branch (source/naddlayer.pas:696-699) + activate():
+ * y = act(a + b) over n elements. */
+int tb_shortcut_fwd(tb_ctx* ctx, int64_t n, const float* a, const float* b, float* y,
+                    int64_t activation);
+/* TYoloLayer.forward (source/nyololayer.pas:786-825): copy x to y, logistic on entries
+ * 0,1 (x,y) and 4..4+classes (objectness, classes) of every anchor, then if scale_xy != 1:
+ * v*scale_xy - 0.5*(scale_xy-1) on entries 0,1. Layout [batch][n][classes+5][h][w]. */
+int tb_yolo_fwd(tb_ctx* ctx, int64_t batch, int64_t n, int64_t classes, int64_t h, int64_t w,
+                const float* x, float* y, float scale_xy);
+
+/* One detection, as TDetection (source/ntypes.pas:278) without the per-class array, which is
+ * written separately (prob[det][classes]). */
+typedef struct tb_detection {
+    float x, y, w, h;        /* TBox after correctBoxes */
+    float objectness;
+    int32_t batch;           /* image */
+    int32_t head;            /* index of the yolo layer in the call */
+    int32_t index;           /* location i = row*w + col */
+    int32_t anchor;          /* _n */
+    int32_t reserved[3];
+} tb_detection;
+
+typedef struct tb_yolo_head {
+    const float* output;     /* activated yolo output [batch][n][classes+5][h][w] */
+    int64_t n, classes, h, w;
+    const int64_t* mask_host;    /* n anchor ids */
+    const float* anchors_host;   /* all anchors (w,h pairs) of the layer, >= 2*max(mask)+2 */
+    int64_t new_coords;
+} tb_yolo_head;
+
+/* TYoloLayer.getDetections + correctBoxes over every head (source/nyololayer.pas:399-498),
+ * for every image, in the reference order (heads in layer order, i-major, anchor-minor,
+ * source/nnet.pas:647-653). Writes at most `capacity` detections per image to
+ * dets[b*capacity + k] and prob[(b*capacity + k)*classes + j]; counts[b] = number found
+ * (may exceed capacity: then only the first `capacity` are written). Blocks until counts are
+ * on the host (counts_host). */
+int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads,
+                   int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
+                   int64_t relative, int64_t letter, int64_t capacity,
+                   tb_detection* dets, float* prob, int64_t* counts_host);
+
+/* ---- XNOR binary convolution (TXNORConvolutionLayer, source/nxnorconvolutionlayer.pas) --- */
+#define TB_XNOR_PAD_BIT0 0   /* padding pixels are bit 0 (= -1), as im2col_cpu_custom_bin :232-316 */
+#define TB_XNOR_PAD_ZERO 1   /* padding pixels contribute 0, as the float fallback :860-868 */
+/* Words (uint32) of the packed weight buffer. */
+int tb_xnor_packed_weights_count(int64_t filters, int64_t channels, int64_t ksize, int64_t* count);
+/* Sign-pack weights (bit = w > 0) and compute mean_f = (sum_i |w_fi|)/size in the reference's
+ * sequential fp32 order (binarize_weights, :95-113). weights and mean are device pointers. */
+int tb_xnor_pack_weights(tb_ctx* ctx, int64_t filters, int64_t channels, int64_t ksize,
+                         const float* weights, uint32_t* packed, float* mean);
+/* out[b][f][p] = (2*matches - K) * mean[f] (gemm_nn_custom_bin_mean_transposed :179-205),
+ * input bit = x > 0 (:793-794); then + bias (may be NULL) and activation. popcount_out
+ * (int32 [batch][filters][oh][ow], may be NULL) receives 2*matches - K. Scratch: the packed
+ * input bits live in the context workspace. */
+int tb_xnor_conv_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int64_t w,
+                     int64_t filters, int64_t ksize, int64_t stride, int64_t pad, int64_t pad_mode,
+                     const float* x, const uint32_t* packed_w, const float* mean,
+                     const float* bias, int64_t activation, int32_t* popcount_out, float* y);
+
+/* ---- layers of the MNIST / CIFAR-shaped configs -------------------------------------- */
+/* TConnectedLayer.forward (source/nconnectedlayer.pas:157-184): y[b][o] = sum_i x[b][i] *
+ * w[o][i] (gemm NoTrans, Trans) + bias[o], then activation. w is the reference layout
+ * [outputs][inputs] packed by tb_conv_pack_weights of a 1x1 conv with channels = inputs. */
+int tb_fc_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t outputs, const float* x,
+              const float* packed_w, const float* bias, int64_t activation, float* y);
+/* TSoftmaxLayer.forward -> softmaxBatch (source/nsoftmaxlayer.pas:83-167). */
+int tb_softmax_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t groups, float temperature,
+                   const float* x, float* y);
+/* TAvgPoolLayer.forward (source/navgpoollayer.pas:60-84): y[b][c] = mean over h*w. */
+int tb_avgpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int64_t w,
+                   const float* x, float* y);
+
+/* ---- whole-network executor (TNNet.forward / predict, source/nnet.pas:275-317,452-472) --- */
+typedef struct tb_net tb_net;
+#define TB_LAYER_CONV      1
+#define TB_LAYER_SHORTCUT  2
+#define TB_LAYER_ROUTE     3
+#define TB_LAYER_UPSAMPLE  4
+#define TB_LAYER_YOLO      5
+#define TB_LAYER_MAXPOOL   6
+#define TB_LAYER_CONNECTED 7
+#define TB_LAYER_SOFTMAX   8
+#define TB_LAYER_AVGPOOL   9
+
+int tb_net_create(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t height, int64_t width,
+                  tb_net** out);
+int tb_net_destroy(tb_net* net);
+/* Each add returns the new layer's index (>= 0) or a negative TB_ERR_*. Weights are host
+ * arrays in the reference layout; they are copied (and uploaded at finalize). BN arrays may be
+ * NULL when batch_normalize == 0. */
+int tb_net_add_conv(tb_net* net, int64_t filters, int64_t ksize, int64_t stride, int64_t pad,
+                    int64_t activation, int64_t batch_normalize, const float* weights_host,
+                    const float* biases_host, const float* scales_host,
+                    const float* rolling_mean_host, const float* rolling_variance_host);
+int tb_net_add_shortcut(tb_net* net, int64_t from, int64_t activation);
+int tb_net_add_route(tb_net* net, int64_t n, const int64_t* layers);
+int tb_net_add_upsample(tb_net* net, int64_t stride, float scale);
+int tb_net_add_yolo(tb_net* net, int64_t classes, int64_t n, const int64_t* mask,
+                    int64_t total_anchors, const float* anchors, float scale_xy);
+int tb_net_add_maxpool(tb_net* net, int64_t ksize, int64_t stride, int64_t padding);
+int tb_net_add_connected(tb_net* net, int64_t outputs, int64_t activation,
+                         const float* weights_host, const float* biases_host);
+int tb_net_add_softmax(tb_net* net, int64_t groups, float temperature);
+int tb_net_add_avgpool(tb_net* net);
+/* Fusion planning switch (default on). With fusion off every layer output is materialised and
+ * every layer runs its own kernel, which lets tests compare each layer with the reference. */
+int tb_net_set_fusion(tb_net* net, int64_t enable);
+/* TNNet.fuseBatchNorm (source/nnet.pas:268-273). */
+int tb_net_fuse_batchnorm(tb_net* net);
+/* Plan fusions (shortcut into conv epilogue, zero-copy route slices, yolo activation into the
+ * head conv), allocate activations and upload packed weights. math_mode: TB_MATH_*. */
+int tb_net_finalize(tb_net* net, int64_t math_mode);
+/* Run the whole network on x (device, [batch][c][h][w]); use_graph != 0 replays a CUDA graph
+ * captured on first use. Asynchronous. */
+int tb_net_forward(tb_net* net, const float* x, int64_t use_graph);
+/* Device pointer / element count of a layer's output (per batch) and its batch stride. */
+int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* count_per_image,
+                        int64_t* batch_stride);
+int tb_net_layer_count(tb_net* net, int64_t* count);
+/* Device launches the last tb_net_forward issued (graph replay counts its kernel nodes). */
+int tb_net_launch_count(tb_net* net, int64_t* count);
+/* Conv FLOPs (2*M*N*K summed over conv / connected layers) of one forward at this batch. */
+int tb_net_flops(tb_net* net, double* flops);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TENSORIUM_B200_H */
