@@ -1,0 +1,338 @@
+// api.cu -- context, memory and the BLAS-1 style helpers of the C ABI (include/tensorium_b200.h).
+#include "common.cuh"
+
+namespace tbi {
+
+static thread_local std::string g_err;
+
+void set_error(const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+}
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+    return e == cudaErrorMemoryAllocation ? TB_ERR_OOM : TB_ERR_CUDA;
+}
+
+int enter(tb_ctx* ctx) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != ctx->device) {
+        e = cudaSetDevice(ctx->device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    }
+    return TB_OK;
+}
+
+int ensure_workspace(tb_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->ws_bytes) return TB_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(ctx->stream, &cs);
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail(TB_ERR_STATE, "workspace of %zu bytes needed during stream capture (have %zu); "
+                    "call tb_workspace_reserve first", bytes, ctx->ws_bytes);
+    // the old buffer may still be read by queued work on this stream
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    if (ctx->ws) cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+    size_t want = round_up((int64_t)bytes, 1 << 20);
+    e = cudaMalloc(&ctx->ws, want);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
+    ctx->ws_bytes = want;
+    return TB_OK;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return TB_OK;
+}
+
+bool act_supported(int64_t a) {
+    switch (a) {
+    case TB_ACT_LOGISTIC: case TB_ACT_RELU: case TB_ACT_RELU6: case TB_ACT_RELIE:
+    case TB_ACT_LINEAR: case TB_ACT_RAMP: case TB_ACT_TANH: case TB_ACT_PLSE:
+    case TB_ACT_REVLEAKY: case TB_ACT_LEAKY: case TB_ACT_ELU: case TB_ACT_LOGGY:
+    case TB_ACT_HARDTAN: case TB_ACT_LHTAN: case TB_ACT_SELU:
+        return true;
+    default:
+        return false;
+    }
+}
+
+}  // namespace tbi
+
+using namespace tbi;
+
+// ---------------------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------------------
+__global__ void k_activate(int64_t n, float* __restrict__ x, int act) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t n4 = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? n / 4 : 0;
+    float4* x4 = reinterpret_cast<float4*>(x);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 v = x4[i];
+        v.x = tb_activate_dev(v.x, act);
+        v.y = tb_activate_dev(v.y, act);
+        v.z = tb_activate_dev(v.z, act);
+        v.w = tb_activate_dev(v.w, act);
+        x4[i] = v;
+    }
+    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        x[i] = tb_activate_dev(x[i], act);
+}
+
+__global__ void k_forward_bias(int64_t total, float* __restrict__ dst, int64_t bias_size,
+                               const float* __restrict__ bias, int64_t incb, int64_t block) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        int64_t f = (i / block) % bias_size;
+        dst[i] = dst[i] + bias[f * incb];
+    }
+}
+
+__global__ void k_copy(int64_t n, const float* __restrict__ src, int64_t inca,
+                       float* __restrict__ dst, int64_t incb) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i * incb] = src[i * inca];
+}
+
+__global__ void k_copy4(int64_t n4, const float4* __restrict__ src, float4* __restrict__ dst) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
+        dst[i] = src[i];
+}
+
+__global__ void k_fill(int64_t n, float* __restrict__ x, float v, int64_t stride_x) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        x[i * stride_x] = v;
+}
+
+__global__ void k_addvv(int64_t n, const float* __restrict__ a, int64_t inca,
+                        const float* __restrict__ b, int64_t incb, float* __restrict__ c,
+                        int64_t incc) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        c[i * incc] = a[i * inca] + b[i * incb];
+}
+
+__global__ void k_fmavss(int64_t n, const float* __restrict__ src, float s, float b,
+                         float* __restrict__ dst) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = __fadd_rn(__fmul_rn(src[i], s), b);
+}
+
+// ---------------------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------------------
+extern "C" {
+
+const char* tb_last_error(void) { return g_err.c_str(); }
+
+int tb_version(void) { return TB_VERSION; }
+
+int tb_device_count(int64_t* count) {
+    if (!count) return fail(TB_ERR_INVALID, "null count");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return cuda_fail(e, "cudaGetDeviceCount");
+    }
+    *count = n;
+    return TB_OK;
+}
+
+int tb_init(int64_t device, const tb_options* opts, tb_ctx** out) {
+    if (!out) return fail(TB_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    int n = 0;
+    TB_CHECK_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n)
+        return fail(TB_ERR_INVALID, "device %lld out of range (have %d)", (long long)device, n);
+    cudaDeviceProp prop;
+    TB_CHECK_CUDA(cudaGetDeviceProperties(&prop, (int)device));
+    if (prop.major != 10)
+        return fail(TB_ERR_UNSUPPORTED, "device %lld is sm_%d%d; this library is built for sm_100a",
+                    (long long)device, prop.major, prop.minor);
+    TB_CHECK_CUDA(cudaSetDevice((int)device));
+    tb_ctx* c = new tb_ctx();
+    c->device = (int)device;
+    c->sm_count = prop.multiProcessorCount;
+    c->max_smem_optin = (int)prop.sharedMemPerBlockOptin;
+    if (opts) {
+        if (opts->flags != 0) { delete c; return fail(TB_ERR_INVALID, "tb_options.flags must be 0"); }
+        c->math_mode = opts->math_mode;
+    }
+    cudaError_t e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) { delete c; return cuda_fail(e, "cudaStreamCreate"); }
+    c->stream = c->own_stream;
+    e = cudaMalloc(&c->d_status, sizeof(int) * 4);
+    if (e != cudaSuccess) { cudaStreamDestroy(c->own_stream); delete c; return cuda_fail(e, "cudaMalloc(status)"); }
+    cudaMemset(c->d_status, 0, sizeof(int) * 4);
+    int64_t ws = (opts && opts->workspace_bytes > 0) ? opts->workspace_bytes : (64ll << 20);
+    int r = ensure_workspace(c, (size_t)ws);
+    if (r != TB_OK) { cudaFree(c->d_status); cudaStreamDestroy(c->own_stream); delete c; return r; }
+    *out = c;
+    return TB_OK;
+}
+
+int tb_shutdown(tb_ctx* ctx) {
+    if (!ctx) return TB_OK;
+    enter(ctx);
+    if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return TB_OK;
+}
+
+int tb_set_stream(tb_ctx* ctx, void* stream) {
+    TB_ENTER(ctx);
+    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    return TB_OK;
+}
+
+void* tb_get_stream(tb_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int tb_sync(tb_ctx* ctx) {
+    TB_ENTER(ctx);
+    TB_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+    int st = 0;
+    TB_CHECK_CUDA(cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != 0) {
+        cudaMemset(ctx->d_status, 0, sizeof(int));
+        return fail(TB_ERR_DEVICE, "a kernel reported device status %d", st);
+    }
+    return TB_OK;
+}
+
+int tb_malloc(tb_ctx* ctx, int64_t bytes, void** ptr) {
+    TB_ENTER(ctx);
+    if (!ptr || bytes < 0) return fail(TB_ERR_INVALID, "bad tb_malloc arguments");
+    *ptr = nullptr;
+    if (bytes == 0) return TB_OK;
+    TB_CHECK_CUDA(cudaMalloc(ptr, (size_t)bytes));
+    return TB_OK;
+}
+
+int tb_free(tb_ctx* ctx, void* ptr) {
+    TB_ENTER(ctx);
+    if (ptr) TB_CHECK_CUDA(cudaFree(ptr));
+    return TB_OK;
+}
+
+int tb_memcpy_h2d(tb_ctx* ctx, void* dst, const void* src, int64_t bytes) {
+    TB_ENTER(ctx);
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(TB_ERR_INVALID, "bad tb_memcpy_h2d arguments");
+    if (bytes == 0) return TB_OK;
+    TB_CHECK_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return TB_OK;
+}
+
+int tb_memcpy_d2h(tb_ctx* ctx, void* dst, const void* src, int64_t bytes) {
+    TB_ENTER(ctx);
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(TB_ERR_INVALID, "bad tb_memcpy_d2h arguments");
+    if (bytes == 0) return TB_OK;
+    TB_CHECK_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+    return TB_OK;
+}
+
+int tb_workspace_reserve(tb_ctx* ctx, int64_t bytes) {
+    TB_ENTER(ctx);
+    if (bytes < 0) return fail(TB_ERR_INVALID, "negative workspace size");
+    return ensure_workspace(ctx, (size_t)bytes);
+}
+
+int tb_activate(tb_ctx* ctx, int64_t n, float* x, int64_t offset, int64_t act) {
+    TB_ENTER(ctx);
+    if (n < 0 || (n > 0 && !x)) return fail(TB_ERR_INVALID, "bad tb_activate arguments");
+    if (!act_supported(act)) return fail(TB_ERR_UNSUPPORTED, "activation %lld not supported", (long long)act);
+    if (n == 0 || act == TB_ACT_LINEAR) return TB_OK;  // ActivateArray skips LINEAR (nncuda.pas:533)
+    k_activate<<<grid_for(n, 256, ctx->sm_count, 4), 256, 0, ctx->stream>>>(n, x + offset, (int)act);
+    return check_launch("k_activate");
+}
+
+int tb_forward_bias(tb_ctx* ctx, int64_t dst_size, float* dst, int64_t offset, int64_t bias_size,
+                    const float* bias, int64_t incb, int64_t batch) {
+    TB_ENTER(ctx);
+    if (dst_size < 0 || bias_size <= 0 || batch <= 0 || !dst || !bias)
+        return fail(TB_ERR_INVALID, "bad tb_forward_bias arguments");
+    int64_t block = dst_size / (batch * bias_size);
+    if (block * batch * bias_size != dst_size)
+        return fail(TB_ERR_INVALID, "forwardBias: sizes do not align");
+    if (dst_size == 0) return TB_OK;
+    k_forward_bias<<<grid_for(dst_size, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        dst_size, dst + offset, bias_size, bias, incb, block);
+    return check_launch("k_forward_bias");
+}
+
+int tb_copy(tb_ctx* ctx, int64_t n, const float* src, int64_t src_offset, int64_t inca, float* dst,
+            int64_t dst_offset, int64_t incb) {
+    TB_ENTER(ctx);
+    if (n < 0 || (n > 0 && (!src || !dst))) return fail(TB_ERR_INVALID, "bad tb_copy arguments");
+    if (n == 0) return TB_OK;
+    const float* s = src + src_offset;
+    float* d = dst + dst_offset;
+    if (inca == 1 && incb == 1 && aligned16(s) && aligned16(d) && (n % 4) == 0) {
+        k_copy4<<<grid_for(n / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+            n / 4, reinterpret_cast<const float4*>(s), reinterpret_cast<float4*>(d));
+    } else {
+        k_copy<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(n, s, inca, d, incb);
+    }
+    return check_launch("k_copy");
+}
+
+int tb_fill(tb_ctx* ctx, int64_t n, float* x, int64_t offset, float val, int64_t stride) {
+    TB_ENTER(ctx);
+    if (n < 0 || (n > 0 && !x)) return fail(TB_ERR_INVALID, "bad tb_fill arguments");
+    if (n == 0) return TB_OK;
+    k_fill<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(n, x + offset, val, stride);
+    return check_launch("k_fill");
+}
+
+int tb_addvv(tb_ctx* ctx, int64_t n, const float* src1, int64_t src1_offset, int64_t inca,
+             const float* src2, int64_t src2_offset, int64_t incb, float* dst, int64_t dst_offset,
+             int64_t incc) {
+    TB_ENTER(ctx);
+    if (n < 0 || (n > 0 && (!src1 || !src2 || !dst))) return fail(TB_ERR_INVALID, "bad tb_addvv arguments");
+    if (n == 0) return TB_OK;
+    k_addvv<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        n, src1 + src1_offset, inca, src2 + src2_offset, incb, dst + dst_offset, incc);
+    return check_launch("k_addvv");
+}
+
+int tb_fmavss(tb_ctx* ctx, int64_t n, float* src, int64_t offset, float scalar, float bias, float* dst) {
+    TB_ENTER(ctx);
+    if (n < 0 || (n > 0 && (!src || !dst))) return fail(TB_ERR_INVALID, "bad tb_fmavss arguments");
+    if (n == 0) return TB_OK;
+    k_fmavss<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(n, src + offset, scalar, bias, dst + offset);
+    return check_launch("k_fmavss");
+}
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+// common.cuh -- shared plumbing of the tensorium_b200 C-ABI library: context, error reporting,
+// launch helpers and the device-side activation functions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+#include <cstdio>
+#include <cstdarg>
+
+#include "../../include/tensorium_b200.h"
+
+struct tb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;      // current launch stream
+    cudaStream_t own_stream = nullptr;  // stream created by tb_init
+    void* ws = nullptr;                 // split-K / scratch workspace
+    size_t ws_bytes = 0;
+    int* d_status = nullptr;            // device status word (kernels report errors here)
+    int64_t math_mode = TB_MATH_FP32;
+    int sm_count = 148;
+    int max_smem_optin = 0;
+};
+
+namespace tbi {
+
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+// Make ctx's device current on this thread; returns TB_OK or an error code.
+int enter(tb_ctx* ctx);
+// Ensure the workspace holds at least `bytes` (may allocate; not capture-safe).
+int ensure_workspace(tb_ctx* ctx, size_t bytes);
+// Check the last launch.
+int check_launch(const char* what);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Grid-stride launch size for n work items of `per_thread` items each.
+inline unsigned grid_for(int64_t n, int threads, int sm_count, int per_thread = 1) {
+    int64_t blocks = ceil_div(ceil_div(n, per_thread), threads);
+    int64_t cap = (int64_t)sm_count * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (unsigned)blocks;
+}
+
+bool act_supported(int64_t act);
+
+}  // namespace tbi
+
+#define TB_CHECK_CUDA(call)                                              \
+    do {                                                                  \
+        cudaError_t _e = (call);                                          \
+        if (_e != cudaSuccess) return tbi::cuda_fail(_e, #call);          \
+    } while (0)
+
+#define TB_ENTER(ctx)                                                    \
+    do {                                                                  \
+        if (!(ctx)) return tbi::fail(TB_ERR_INVALID, "null context");     \
+        int _r = tbi::enter(ctx);                                         \
+        if (_r != TB_OK) return _r;                                       \
+    } while (0)
+
+// ---------------------------------------------------------------------------------------
+// Device activations: the scalar forms of activate_array (source/nactivation.pas:272-401,
+// 508-621).  Untyped Pascal real constants and System.exp are evaluated in double and
+// rounded to single, so the arithmetic here is done in double where the reference does.
+// ---------------------------------------------------------------------------------------
+static __device__ __noinline__ float tb_logistic(float x) {
+    return (float)(1.0 / (1.0 + exp(-(double)x)));
+}
+
+static __device__ __noinline__ float tb_activate_slow(float x, int a);
+
+// Common activations inline, the rest out of line (keeps the unrolled conv epilogues small).
+__device__ __forceinline__ float tb_activate_dev(float x, int a) {
+    if (a == TB_ACT_LEAKY || a == TB_ACT_REVLEAKY) return x < 0.f ? (float)(0.1 * (double)x) : x;
+    if (a == TB_ACT_LINEAR) return x;
+    if (a == TB_ACT_RELU) return x > 0.f ? x : x * 0.0f;
+    return tb_activate_slow(x, a);
+}
+
+// Full activate_array switch; defined in every translation unit that includes this header
+// (static linkage keeps the per-object copies private).
+static __device__ __noinline__ float tb_activate_slow(float x, int a) {
+    switch (a) {
+    case TB_ACT_LOGISTIC: return tb_logistic(x);
+    case TB_ACT_RELU: return x > 0.f ? x : x * 0.0f;
+    case TB_ACT_RELU6: return (x > 0.f && x <= 6.f) ? x : x * 0.0f;
+    case TB_ACT_RELIE: return x > 0.f ? x : (float)(0.01 * (double)x);
+    case TB_ACT_LINEAR: return x;
+    case TB_ACT_RAMP: return (float)((double)(x > 0.f ? x : x * 0.0f) + 0.1 * (double)x);
+    case TB_ACT_TANH: {
+        float px = (float)exp((double)x), nx = (float)exp(-(double)x);
+        return __fdiv_rn(px - nx, px + nx);
+    }
+    case TB_ACT_PLSE:
+        if (x < -4.f) return (float)(0.01 * ((double)x + 4.0));
+        if (x > 4.f) return (float)(0.01 * ((double)x - 4.0) + 1.0);
+        return (float)(0.125 * (double)x + 0.5);
+    case TB_ACT_REVLEAKY:
+    case TB_ACT_LEAKY: return x < 0.f ? (float)(0.1 * (double)x) : x;
+    case TB_ACT_ELU:
+        return (float)((x >= 0.f ? (double)x : 0.0) + (x < 0.f ? exp((double)x) - 1.0 : 0.0));
+    case TB_ACT_LOGGY: return (float)(2.0 / (1.0 + exp(-(double)x)) - 1.0);
+    case TB_ACT_HARDTAN: return x < -1.f ? -1.f : (x > 1.f ? 1.f : x);
+    case TB_ACT_LHTAN:
+        if (x < 0.f) return (float)(0.001 * (double)x);
+        if (x > 1.f) return (float)(0.001 * ((double)x - 1.0) + 1.0);
+        return x;
+    case TB_ACT_SELU:
+        return (float)((x >= 0.f ? 1.0507 * (double)x : 0.0) +
+                       (x < 0.f ? 1.0507 * 1.6732 * (exp((double)x) - 1.0) : 0.0));
+    default: return x;
+    }
+}

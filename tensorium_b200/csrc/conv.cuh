@@ -1,0 +1,91 @@
+// conv.cuh -- shared definitions of the implicit-GEMM convolution kernels.
+//
+// GEMM view of TTensor.Conv2D (source/ntensors.pas:8252-8349), per image:
+//   Y[f][p] = sum_k W[f][k] * im2col(X)[k][p],  M = filters, N = out_h*out_w, K = c*kh*kw.
+// Here the N dimension runs over all images of the batch (n = b*OHW + p), so one launch
+// covers the whole batch; im2col is never materialised (the B tile is gathered from NCHW X).
+//
+// Packed weights (tb_conv_pack_weights): Wp[k][m], row length Mpad = round_up(F, 4), with
+// two K orders:
+//   RSC (channels >= 16): k = (r*kw + s)*Cpad + c, Cpad = round_up(C, 16): a 16-deep k tile
+//        lies inside one kernel tap (r, s), so the im2col validity test is per tile.
+//   CRS (small channel counts): k = (c*kh + r)*kw + s (the reference order), K padded to 16.
+#pragma once
+#include "common.cuh"
+
+namespace tbi {
+
+constexpr int CONV_BK = 16;
+constexpr int CONV_CRS_MAX_K = 1024;  // CRS k-table lives in shared memory
+
+enum ConvMode { MODE_CRS = 0, MODE_RSC = 1, MODE_1X1V = 2 };
+
+struct ConvGeom {
+    int64_t B, C, H, W, F, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW;
+    int64_t x_bs, y_bs, r_bs;
+    bool rsc;
+    int64_t Cpad, Kpad, Mpad;
+};
+
+struct ConvParams {
+    const float* __restrict__ x;
+    const float* __restrict__ w;
+    const float* __restrict__ bias;
+    const float* __restrict__ bn_scale;
+    const float* __restrict__ bn_mean;
+    const float* __restrict__ bn_var;
+    const float* __restrict__ res;
+    float* __restrict__ y;
+    float* __restrict__ ws;
+    int C, H, W, F, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW, OHW;
+    int Cpad, Kpad, Mpad;
+    long long x_bs, y_bs, r_bs, Ntot;
+    int ktiles, kt_per_split, splits;
+    int act, yolo_classes;
+    int vec_out;  // 1: OHW, y_bs, r_bs multiples of 4 and y/res 16-byte aligned
+};
+
+inline bool conv_is_rsc(int64_t C, int64_t KH, int64_t KW) {
+    return !(C < 16 && C * KH * KW <= CONV_CRS_MAX_K);
+}
+
+int conv_geom(const tb_conv_desc* d, ConvGeom* g);
+
+// Launch the conv (FP32 SIMT mainloop) with the given epilogue settings.
+// ws / ws_floats: split-K partial buffer (nullptr = use the context workspace).
+int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
+                     const float* bias, const float* bn_scale, const float* bn_mean,
+                     const float* bn_var, const float* res, float* y, int act, int yolo_classes,
+                     float* ws, int64_t ws_floats, int64_t* launches);
+
+// Floats of split-K workspace the FP32 path needs for this geometry (0 if it does not split).
+int64_t conv_fp32_ws_floats(const tb_ctx* ctx, const ConvGeom& g);
+
+// TBaseLayer.batchNorm inference (source/nbaselayer.pas:336-370):
+// (x - mean)/max(sqrt(var), 1e-6) * scale + bias, one rounding per step as the reference.
+static __device__ __noinline__ float conv_bn(float v, float mean, float var, float scale, float bias) {
+    float d = (float)sqrt((double)var);
+    float sd = fmaxf(d, 0.000001f);
+    float t = __fdiv_rn(__fsub_rn(v, mean), sd);
+    t = __fmul_rn(t, scale);
+    return __fadd_rn(t, bias);
+}
+
+// Epilogue of one output value: bias / unfused batchnorm, activation, fused yolo logistic.
+__device__ __forceinline__ float conv_epilogue(float v, int m, const ConvParams& p) {
+    if (p.bn_mean) {
+        v = conv_bn(v, p.bn_mean[m], p.bn_var[m], p.bn_scale ? p.bn_scale[m] : 1.0f,
+                    p.bias ? p.bias[m] : 0.0f);
+    } else if (p.bias) {
+        v = __fadd_rn(v, p.bias[m]);
+    }
+    if (p.yolo_classes > 0) {
+        int e = m % (p.yolo_classes + 5);
+        if (e != 2 && e != 3) v = tb_logistic(v);  // TYoloLayer.forward entries 0,1,4..
+        return v;
+    }
+    if (p.act != TB_ACT_LINEAR) v = tb_activate_dev(v, p.act);
+    return v;
+}
+
+}  // namespace tbi

@@ -1,0 +1,280 @@
+// conv_fp32.cu -- host side of the FP32 implicit-GEMM convolution: geometry, tile selection,
+// split-K reduction, weight packing and the tb_conv_* entry points.
+#include "conv_fp32_kernel.cuh"
+
+namespace tbi {
+
+// Sum split-K partials in split order (0 + p0 + p1 + ...) and run the epilogue.
+__global__ void conv_splitk_reduce(const ConvParams p) {
+    const long long nq = (p.Ntot + 3) / 4;
+    const long long total = (long long)p.F * nq;
+    const long long plane = (long long)p.F * p.Ntot;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        int m = (int)(idx / nq);
+        long long nb = (idx - (long long)m * nq) * 4;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* src = p.ws + (long long)m * p.Ntot + nb;
+        if ((p.Ntot & 3) == 0) {
+            for (int z = 0; z < p.splits; ++z) {
+                float4 t = *reinterpret_cast<const float4*>(src + z * plane);
+                v[0] = __fadd_rn(v[0], t.x);
+                v[1] = __fadd_rn(v[1], t.y);
+                v[2] = __fadd_rn(v[2], t.z);
+                v[3] = __fadd_rn(v[3], t.w);
+            }
+        } else {
+            for (int z = 0; z < p.splits; ++z)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (nb + q < p.Ntot) v[q] = __fadd_rn(v[q], src[z * plane + q]);
+        }
+        conv_store4(p, m, nb, v);
+    }
+}
+
+__global__ void k_conv_pack(const float* __restrict__ w, float* __restrict__ wp, int F, int C,
+                            int KH, int KW, int Cpad, long long Kpad, int Mpad, int rsc) {
+    const long long total = Kpad * Mpad;
+    const long long fs = (long long)C * KH * KW;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        long long k = idx / Mpad;
+        int m = (int)(idx - k * Mpad);
+        float v = 0.0f;
+        if (m < F) {
+            int c, r, s;
+            if (rsc) {
+                int rs = (int)(k / Cpad);
+                c = (int)(k - (long long)rs * Cpad);
+                r = rs / KW;
+                s = rs - r * KW;
+            } else {
+                int khw = KH * KW;
+                c = (int)(k / khw);
+                int rs = (int)(k - (long long)c * khw);
+                r = rs / KW;
+                s = rs - r * KW;
+            }
+            if (c < C) v = w[(long long)m * fs + ((long long)c * KH + r) * KW + s];
+        }
+        wp[idx] = v;
+    }
+}
+
+int conv_geom(const tb_conv_desc* d, ConvGeom* g) {
+    if (!d) return fail(TB_ERR_INVALID, "null conv descriptor");
+    ConvGeom r;
+    r.B = d->batch; r.C = d->channels; r.H = d->height; r.W = d->width;
+    r.F = d->filters; r.KH = d->kernel_h; r.KW = d->kernel_w;
+    r.SY = d->stride_y; r.SX = d->stride_x; r.PY = d->pad_y; r.PX = d->pad_x;
+    r.DY = d->dilation_y > 0 ? d->dilation_y : 1;
+    r.DX = d->dilation_x > 0 ? d->dilation_x : 1;
+    if (r.B < 0 || r.C <= 0 || r.H <= 0 || r.W <= 0 || r.F <= 0 || r.KH <= 0 || r.KW <= 0 ||
+        r.SY <= 0 || r.SX <= 0 || r.PY < 0 || r.PX < 0)
+        return fail(TB_ERR_INVALID, "conv: bad shape (batch=%lld c=%lld h=%lld w=%lld f=%lld k=%lldx%lld s=%lldx%lld p=%lldx%lld)",
+                    (long long)r.B, (long long)r.C, (long long)r.H, (long long)r.W, (long long)r.F,
+                    (long long)r.KH, (long long)r.KW, (long long)r.SY, (long long)r.SX,
+                    (long long)r.PY, (long long)r.PX);
+    r.OH = (r.H + 2 * r.PY - (r.DY * (r.KH - 1) + 1)) / r.SY + 1;
+    r.OW = (r.W + 2 * r.PX - (r.DX * (r.KW - 1) + 1)) / r.SX + 1;
+    if (r.OH <= 0 || r.OW <= 0) return fail(TB_ERR_INVALID, "conv: empty output (kernel larger than padded input)");
+    r.x_bs = d->in_batch_stride ? d->in_batch_stride : r.C * r.H * r.W;
+    r.y_bs = d->out_batch_stride ? d->out_batch_stride : r.F * r.OH * r.OW;
+    r.r_bs = d->res_batch_stride ? d->res_batch_stride : r.y_bs;
+    if (r.x_bs < r.C * r.H * r.W || r.y_bs < r.F * r.OH * r.OW || r.r_bs < r.F * r.OH * r.OW)
+        return fail(TB_ERR_INVALID, "conv: batch stride smaller than one image");
+    const int64_t lim = (int64_t)1 << 31;
+    if (r.C * r.H * r.W >= lim || r.F * r.OH * r.OW >= lim || r.B * r.OH * r.OW >= ((int64_t)1 << 40))
+        return fail(TB_ERR_INVALID, "conv: tensor too large for this build");
+    r.rsc = conv_is_rsc(r.C, r.KH, r.KW);
+    if (r.rsc) {
+        r.Cpad = round_up(r.C, CONV_BK);
+        r.Kpad = r.KH * r.KW * r.Cpad;
+    } else {
+        r.Cpad = r.C;
+        r.Kpad = round_up(r.C * r.KH * r.KW, CONV_BK);
+    }
+    r.Mpad = round_up(r.F, 4);
+    if (r.Kpad >= lim / 4 || r.Kpad * r.Mpad >= lim * 2)
+        return fail(TB_ERR_INVALID, "conv: weights too large for this build");
+    *g = r;
+    return TB_OK;
+}
+
+struct TileCfg {
+    int BM, BN, threads, splits, kt_per_split;
+    int mode;
+};
+
+static TileCfg choose_tiles(const tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
+    TileCfg t;
+    const int64_t M = g.F, N = g.B * g.OH * g.OW;
+    const int64_t ktiles = g.Kpad / CONV_BK;
+    const int64_t ohw = g.OH * g.OW;
+    if (g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 &&
+        ohw % 4 == 0 && g.x_bs % 4 == 0 && x_aligned16)
+        t.mode = MODE_1X1V;
+    else
+        t.mode = g.rsc ? MODE_RSC : MODE_CRS;
+    if (M <= 32) { t.BM = 32; t.BN = 256; t.threads = 256; }
+    else if (M <= 64) { t.BM = 64; t.BN = 128; t.threads = 128; }
+    else { t.BM = 128; t.BN = 128; t.threads = 256; }
+    const int64_t sms = ctx->sm_count;
+    int64_t tiles = ceil_div(M, t.BM) * ceil_div(N, t.BN);
+    if (tiles < sms && t.BM >= 64) {
+        int64_t t64 = ceil_div(M, 64) * ceil_div(N, 64);
+        if (t64 > tiles) { t.BM = 64; t.BN = 64; t.threads = 64; tiles = t64; }
+    }
+    int64_t splits = 1;
+    const int64_t target = 2 * sms;
+    if (tiles < target && ktiles >= 8) {
+        splits = ceil_div(target, tiles);
+        int64_t maxs = ktiles / 4;
+        if (splits > maxs) splits = maxs;
+        if (splits > 32) splits = 32;
+        if (splits < 1) splits = 1;
+    }
+    int64_t kps = ceil_div(ktiles, splits);
+    splits = ceil_div(ktiles, kps);
+    t.splits = (int)splits;
+    t.kt_per_split = (int)kps;
+    return t;
+}
+
+int64_t conv_fp32_ws_floats(const tb_ctx* ctx, const ConvGeom& g) {
+    TileCfg t = choose_tiles(ctx, g, true);
+    TileCfg t2 = choose_tiles(ctx, g, false);
+    int64_t s = t.splits > t2.splits ? t.splits : t2.splits;
+    if (s <= 1) return 0;
+    return s * g.F * g.B * g.OH * g.OW;
+}
+
+int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
+                     const float* bias, const float* bn_scale, const float* bn_mean,
+                     const float* bn_var, const float* res, float* y, int act, int yolo_classes,
+                     float* ws, int64_t ws_floats, int64_t* launches) {
+    if (g.B == 0) return TB_OK;
+    TileCfg t = choose_tiles(ctx, g, aligned16(x));
+    ConvParams p;
+    p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
+    p.res = res; p.y = y; p.ws = nullptr;
+    p.C = (int)g.C; p.H = (int)g.H; p.W = (int)g.W; p.F = (int)g.F;
+    p.KH = (int)g.KH; p.KW = (int)g.KW; p.SY = (int)g.SY; p.SX = (int)g.SX;
+    p.PY = (int)g.PY; p.PX = (int)g.PX; p.DY = (int)g.DY; p.DX = (int)g.DX;
+    p.OH = (int)g.OH; p.OW = (int)g.OW; p.OHW = (int)(g.OH * g.OW);
+    p.Cpad = (int)g.Cpad; p.Kpad = (int)g.Kpad; p.Mpad = (int)g.Mpad;
+    p.x_bs = g.x_bs; p.y_bs = g.y_bs; p.r_bs = g.r_bs;
+    p.Ntot = g.B * g.OH * g.OW;
+    p.ktiles = (int)(g.Kpad / CONV_BK);
+    p.kt_per_split = t.kt_per_split;
+    p.splits = t.splits;
+    p.act = act;
+    p.yolo_classes = yolo_classes;
+    p.vec_out = (p.OHW % 4 == 0 && g.y_bs % 4 == 0 && aligned16(y) &&
+                 (!res || (g.r_bs % 4 == 0 && aligned16(res)))) ? 1 : 0;
+    if (t.splits > 1) {
+        int64_t need = (int64_t)t.splits * g.F * p.Ntot;
+        if (ws) {
+            if (ws_floats < need) return fail(TB_ERR_INVALID, "conv: scratch of %lld floats too small (need %lld)",
+                                              (long long)ws_floats, (long long)need);
+            p.ws = ws;
+        } else {
+            int r = ensure_workspace(ctx, (size_t)need * sizeof(float));
+            if (r != TB_OK) return r;
+            p.ws = reinterpret_cast<float*>(ctx->ws);
+        }
+    }
+    dim3 grid((unsigned)ceil_div(p.Ntot, t.BN), (unsigned)ceil_div(g.F, t.BM), (unsigned)t.splits);
+    if (grid.y > 65535 || grid.z > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
+    int r;
+    if (t.BM == 128) r = conv_launch_128x128(ctx, p, grid, t.mode);
+    else if (t.BM == 64 && t.BN == 128) r = conv_launch_64x128(ctx, p, grid, t.mode);
+    else if (t.BM == 64) r = conv_launch_64x64(ctx, p, grid, t.mode);
+    else r = conv_launch_32x256(ctx, p, grid, t.mode);
+    if (r != TB_OK) return r;
+    if (launches) ++*launches;
+    if (t.splits > 1) {
+        int64_t work = (int64_t)g.F * ceil_div(p.Ntot, 4);
+        conv_splitk_reduce<<<grid_for(work, 256, ctx->sm_count, 1), 256, 0, ctx->stream>>>(p);
+        r = check_launch("conv_splitk_reduce");
+        if (r != TB_OK) return r;
+        if (launches) ++*launches;
+    }
+    return TB_OK;
+}
+
+}  // namespace tbi
+
+using namespace tbi;
+
+extern "C" {
+
+int tb_conv_out_shape(const tb_conv_desc* d, int64_t* out_h, int64_t* out_w) {
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (out_h) *out_h = g.OH;
+    if (out_w) *out_w = g.OW;
+    return TB_OK;
+}
+
+int tb_conv_packed_weights_count(const tb_conv_desc* d, int64_t* count) {
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!count) return fail(TB_ERR_INVALID, "null count");
+    *count = g.Kpad * g.Mpad;
+    return TB_OK;
+}
+
+int tb_conv_pack_weights(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!weights || !packed) return fail(TB_ERR_INVALID, "conv pack: null pointer");
+    if (!aligned16(packed)) return fail(TB_ERR_INVALID, "conv pack: packed buffer must be 16-byte aligned");
+    int64_t total = g.Kpad * g.Mpad;
+    k_conv_pack<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        weights, packed, (int)g.F, (int)g.C, (int)g.KH, (int)g.KW, (int)g.Cpad, (long long)g.Kpad,
+        (int)g.Mpad, g.rsc ? 1 : 0);
+    return check_launch("k_conv_pack");
+}
+
+int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights, float* biases,
+                    const float* scales, const float* mean, const float* variance) {
+    if (filters <= 0 || filter_size <= 0 || !weights || !biases || !scales || !mean || !variance)
+        return fail(TB_ERR_INVALID, "tb_conv_fold_bn: bad arguments");
+    const float eps = 0.000001f;  // sEPSILON
+    for (int64_t f = 0; f < filters; ++f) {
+        float v = variance[f] > eps ? variance[f] : eps;
+        float pre = (float)((double)scales[f] / sqrt((double)v));
+        biases[f] = biases[f] - mean[f] * pre;
+        float* w = weights + f * filter_size;
+        for (int64_t i = 0; i < filter_size; ++i) w[i] = w[i] * pre;
+    }
+    return TB_OK;
+}
+
+int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w,
+                  const float* bias, const float* bn_scale, const float* bn_mean,
+                  const float* bn_variance, const float* residual, float* y, int64_t math_mode) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (g.B == 0) return TB_OK;
+    if (!x || !packed_w || !y) return fail(TB_ERR_INVALID, "conv: null x, weights or y");
+    if (bn_mean && !bn_variance) return fail(TB_ERR_INVALID, "conv: bn_mean given without bn_variance");
+    if (!aligned16(packed_w)) return fail(TB_ERR_INVALID, "conv: packed weights must be 16-byte aligned");
+    if (!act_supported(d->activation))
+        return fail(TB_ERR_UNSUPPORTED, "conv: activation %lld not supported", (long long)d->activation);
+    if (math_mode < 0) math_mode = ctx->math_mode;
+    if (math_mode != TB_MATH_FP32)
+        return fail(TB_ERR_UNSUPPORTED, "conv: math mode %lld is not available in this build", (long long)math_mode);
+    return conv_fp32_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
+                            (int)d->activation, 0, nullptr, 0, nullptr);
+}
+
+}  // extern "C"

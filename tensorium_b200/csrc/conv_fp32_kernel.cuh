@@ -1,0 +1,287 @@
+// conv_fp32_kernel.cuh -- FP32 CUDA-core implicit-GEMM convolution kernel template.
+//
+// Replaces the reference's GPU conv sequence (source/nConvolutionLayer.pas:1055-1122:
+// per-image cuda.im2col, cublasSgemmStridedBatched, forwardBias / normalize+forwardScale,
+// ActivateArray) and its CPU path (TTensor.Conv2D, source/ntensors.pas:8252-8349) by one
+// kernel per layer:
+//   * CTA tile BM x BN of (filters x pixels-over-the-batch), BK = 16 deep k tiles;
+//   * a STAGES-deep cp.async ring in shared memory: the weight tile arrives as 16-byte
+//     copies of the packed K-major weights, the activation tile is gathered straight from
+//     NCHW X (zero-fill for padding), 16-byte copies for 1x1 stride-1 layers;
+//   * each thread owns a TM x TN register tile (two TM/2 x TN/2 quads, BM/2 and BN/2 apart,
+//     so every shared-memory read is a broadcast or a conflict-free float4);
+//   * epilogue: bias or unfused batchnorm, activation, optional residual (shortcut) add,
+//     optional YOLO logistic, float4 stores into NCHW Y at any batch stride (route slices);
+//   * split-K over blockIdx.z when the tile grid is smaller than the machine; partial sums go
+//     to a workspace and conv_splitk_reduce sums them in split order and runs the epilogue.
+#pragma once
+#include "conv.cuh"
+
+#include <mutex>
+
+namespace tbi {
+
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, bool pred) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    int sz = pred ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
+}
+
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem, bool pred) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    int sz = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Store 4 consecutive outputs (n = nb .. nb+3) of row m after the epilogue.
+__device__ __forceinline__ void conv_store4(const ConvParams& p, int m, long long nb, const float* v) {
+    if (p.vec_out && nb + 3 < p.Ntot) {
+        long long b = nb / p.OHW;
+        int pix = (int)(nb - b * p.OHW);
+        float4 o;
+        o.x = conv_epilogue(v[0], m, p);
+        o.y = conv_epilogue(v[1], m, p);
+        o.z = conv_epilogue(v[2], m, p);
+        o.w = conv_epilogue(v[3], m, p);
+        if (p.res) {
+            float4 r = *reinterpret_cast<const float4*>(p.res + b * p.r_bs + (long long)m * p.OHW + pix);
+            o.x = __fadd_rn(o.x, r.x);
+            o.y = __fadd_rn(o.y, r.y);
+            o.z = __fadd_rn(o.z, r.z);
+            o.w = __fadd_rn(o.w, r.w);
+        }
+        *reinterpret_cast<float4*>(p.y + b * p.y_bs + (long long)m * p.OHW + pix) = o;
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            long long n = nb + q;
+            if (n >= p.Ntot) break;
+            long long b = n / p.OHW;
+            int pix = (int)(n - b * p.OHW);
+            float o = conv_epilogue(v[q], m, p);
+            if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + (long long)m * p.OHW + pix]);
+            p.y[b * p.y_bs + (long long)m * p.OHW + pix] = o;
+        }
+    }
+}
+
+template <int V>
+struct VecT;
+template <>
+struct VecT<2> { typedef float2 T; };
+template <>
+struct VecT<4> { typedef float4 T; };
+
+inline int conv_smem_bytes(int BM, int BN, int STAGES, int mode) {
+    return STAGES * CONV_BK * (BM + BN) * 4 + (mode == MODE_CRS ? CONV_CRS_MAX_K * 16 : 0);
+}
+
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+conv_fp32_kernel(const ConvParams p) {
+    constexpr int BK = CONV_BK;
+    constexpr int NT = (BM / TM) * (BN / TN);
+    constexpr int TX = BN / TN;
+    constexpr int TM2 = TM / 2, TN2 = TN / 2;
+    static_assert(TN == 8, "epilogue stores quads of 4 columns");
+    static_assert(TM == 4 || TM == 8, "TM must be 4 or 8");
+    extern __shared__ __align__(16) float smem[];
+    float* As = smem;                     // [STAGES][BK][BM]
+    float* Bs = smem + STAGES * BK * BM;  // [STAGES][BK][BN]
+    int4* ktab = reinterpret_cast<int4*>(Bs + STAGES * BK * BN);  // CRS k table
+
+    const int tid = threadIdx.x;
+    const int tx = tid % TX, ty = tid / TX;
+    const int m0 = blockIdx.y * BM;
+    const long long n0 = (long long)blockIdx.x * BN;
+    const int kt_begin = blockIdx.z * p.kt_per_split;
+    const int kt_end = min(kt_begin + p.kt_per_split, p.ktiles);
+    const int nkt = kt_end - kt_begin;
+    const long long HW = (long long)p.H * p.W;
+
+    if (MODE == MODE_CRS) {
+        const int khw = p.KH * p.KW;
+        for (int k = tid; k < p.Kpad; k += NT) {
+            int c = k / khw, rs = k - c * khw, r = rs / p.KW, s = rs - r * p.KW;
+            int dr = r * p.DY, ds = s * p.DX;
+            ktab[k] = make_int4(c * (int)HW + dr * p.W + ds, dr, ds, c < p.C ? 1 : 0);
+        }
+        __syncthreads();
+    }
+
+    // ---- per-thread setup of the activation (B) gather ----
+    constexpr int BCOLS = (MODE == MODE_1X1V) ? BN / 4 : BN;
+    static_assert(NT % BCOLS == 0, "threads must cover the B tile columns");
+    constexpr int KSTEP = NT / BCOLS;
+    static_assert(BK % KSTEP == 0, "k rows per thread must be integral");
+    constexpr int BEPT = BK / KSTEP;
+    const int bcol = tid % BCOLS;
+    const int krow0 = tid / BCOLS;
+    const long long ncol = n0 + (MODE == MODE_1X1V ? 4 * bcol : bcol);
+    const bool nvalid = ncol < p.Ntot;
+    long long bimg = 0;
+    int pix = 0, iy0 = 0, ix0 = 0;
+    if (nvalid) {
+        bimg = ncol / p.OHW;
+        pix = (int)(ncol - bimg * p.OHW);
+        int oy = pix / p.OW, ox = pix - oy * p.OW;
+        iy0 = oy * p.SY - p.PY;
+        ix0 = ox * p.SX - p.PX;
+    }
+    const float* xb = p.x + bimg * p.x_bs;
+
+    auto load_tile = [&](int kt, int st) {
+        // weights: BK rows of BM floats, 16-byte copies
+        const float* wsrc = p.w + (long long)kt * BK * p.Mpad;
+        float* as = As + st * BK * BM;
+#pragma unroll
+        for (int idx = tid; idx < BK * BM / 4; idx += NT) {
+            int kl = idx / (BM / 4), mq = idx - kl * (BM / 4);
+            int m = m0 + mq * 4;
+            bool ok = m < p.Mpad;
+            cp_async16(as + kl * BM + mq * 4, ok ? wsrc + (long long)kl * p.Mpad + m : p.w, ok);
+        }
+        float* bs = Bs + st * BK * BN;
+        if (MODE == MODE_CRS) {
+#pragma unroll
+            for (int e = 0; e < BEPT; ++e) {
+                int kl = krow0 + e * KSTEP;
+                int4 t = ktab[kt * BK + kl];
+                int iy = iy0 + t.y, ix = ix0 + t.z;
+                bool ok = nvalid && t.w && (unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W;
+                const float* src = ok ? xb + t.x + (long long)iy0 * p.W + ix0 : p.x;
+                cp_async4(bs + kl * BN + bcol, src, ok);
+            }
+        } else if (MODE == MODE_RSC) {
+            int k0 = kt * BK;
+            int rs = k0 / p.Cpad, c0 = k0 - rs * p.Cpad;
+            int r = rs / p.KW, s = rs - r * p.KW;
+            int iy = iy0 + r * p.DY, ix = ix0 + s * p.DX;
+            bool okp = nvalid && (unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W;
+            const float* base = xb + (okp ? (long long)iy * p.W + ix : 0);
+#pragma unroll
+            for (int e = 0; e < BEPT; ++e) {
+                int kl = krow0 + e * KSTEP;
+                int c = c0 + kl;
+                bool ok = okp && c < p.C;
+                cp_async4(bs + kl * BN + bcol, ok ? base + (long long)c * HW : p.x, ok);
+            }
+        } else {
+            int c0 = kt * BK;
+#pragma unroll
+            for (int e = 0; e < BEPT; ++e) {
+                int kl = krow0 + e * KSTEP;
+                int c = c0 + kl;
+                bool ok = nvalid && c < p.C;
+                cp_async16(bs + kl * BN + 4 * bcol, ok ? xb + pix + (long long)c * HW : p.x, ok);
+            }
+        }
+    };
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nkt) load_tile(kt_begin + s, s);
+        cp_async_commit();
+    }
+
+    typedef typename VecT<TM2>::T AV;
+    for (int t = 0; t < nkt; ++t) {
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        {
+            int tn = t + STAGES - 1;
+            if (tn < nkt) load_tile(kt_begin + tn, tn % STAGES);
+            cp_async_commit();
+        }
+        const float* as = As + (t % STAGES) * BK * BM;
+        const float* bs = Bs + (t % STAGES) * BK * BN;
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[TM], bv[TN];
+            *reinterpret_cast<AV*>(&a[0]) = *reinterpret_cast<const AV*>(as + kk * BM + ty * TM2);
+            *reinterpret_cast<AV*>(&a[TM2]) = *reinterpret_cast<const AV*>(as + kk * BM + BM / 2 + ty * TM2);
+            *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bs + kk * BN + tx * TN2);
+            *reinterpret_cast<float4*>(&bv[TN2]) = *reinterpret_cast<const float4*>(bs + kk * BN + BN / 2 + tx * TN2);
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
+        }
+    }
+    cp_async_wait<0>();
+
+    // ---- epilogue ----
+    const bool split = p.splits > 1;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        int m = m0 + (i < TM2 ? ty * TM2 + i : BM / 2 + ty * TM2 + (i - TM2));
+        if (m >= p.F) continue;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+            long long nb = n0 + g * (BN / 2) + tx * TN2;
+            if (nb >= p.Ntot) continue;
+            const float* v = &acc[i][g * 4];
+            if (split) {
+                float* dst = p.ws + ((long long)blockIdx.z * p.F + m) * p.Ntot + nb;
+                if ((p.Ntot & 3) == 0) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (nb + q < p.Ntot) dst[q] = v[q];
+                }
+            } else {
+                conv_store4(p, m, nb, v);
+            }
+        }
+    }
+}
+
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+int conv_launch_cfg(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
+    constexpr int NT = (BM / TM) * (BN / TN);
+    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE);
+    static std::mutex mu;
+    static bool done[64] = {false};
+    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE>;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (ctx->device < 64 && !done[ctx->device]) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv)");
+            done[ctx->device] = true;
+        }
+    }
+    kern<<<grid, NT, smem, ctx->stream>>>(p);
+    return check_launch("conv_fp32_kernel");
+}
+
+template <int BM, int BN, int TM, int TN, int STAGES>
+int conv_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
+    switch (mode) {
+    case MODE_CRS: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_CRS>(ctx, p, grid);
+    case MODE_RSC: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_RSC>(ctx, p, grid);
+    default: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_1X1V>(ctx, p, grid);
+    }
+}
+
+// one entry per tile configuration, each compiled in its own translation unit
+int conv_launch_128x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
+int conv_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
+int conv_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
+int conv_launch_32x256(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
+
+}  // namespace tbi
