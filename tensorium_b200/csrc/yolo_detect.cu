@@ -1,0 +1,225 @@
+// yolo_detect.cu -- GPU detection extraction: TYoloLayer.getDetections + getBox + correctBoxes
+// (source/nyololayer.pas:105-122, 399-498) for every yolo head and image, compacted on the
+// device in the reference's order (heads in layer order, location i ascending, anchor minor;
+// source/nnet.pas:647-653).  The reference pulls every head to the host and scans it there.
+#include "common.cuh"
+
+#include <cstring>
+#include <vector>
+
+using namespace tbi;
+
+namespace {
+
+constexpr int MAX_HEADS = 8;
+constexpr int MAX_ANCH = 16;
+
+struct HeadDev {
+    const float* out;
+    int n, classes, h, w;
+    float aw[MAX_ANCH], ah[MAX_ANCH];
+    int new_coords;
+};
+
+struct DetectArgs {
+    HeadDev heads[MAX_HEADS];
+    int n_heads;
+    int img_w, img_h, net_w, net_h;
+    int relative, letter;
+    float thresh;
+    long long capacity;
+    float deltaw, deltah, ratiow, ratioh;
+};
+
+__device__ __forceinline__ long long head_outputs(const HeadDev& hd) {
+    return (long long)hd.n * (hd.classes + 5) * hd.h * hd.w;
+}
+
+// counts[b*n_heads + h] = number of candidates with objectness > thresh
+__global__ void k_yolo_count(const DetectArgs a, int* __restrict__ counts) {
+    const int hi = blockIdx.x, b = blockIdx.y;
+    const HeadDev& hd = a.heads[hi];
+    const int hw = hd.h * hd.w, L = hw * hd.n;
+    const float* out = hd.out + b * head_outputs(hd);
+    int c = 0;
+    for (int q = threadIdx.x; q < L; q += blockDim.x) {
+        int i = q / hd.n, an = q - i * hd.n;
+        float obj = out[(long long)an * (hd.classes + 5) * hw + 4LL * hw + i];
+        c += (obj > a.thresh) ? 1 : 0;
+    }
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    __shared__ int ws[32];
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += ws[i];
+        counts[b * a.n_heads + hi] = t;
+    }
+}
+
+// Ordered compaction (block scan per 256-candidate chunk) + box decode + correctBoxes.
+__global__ void __launch_bounds__(256) k_yolo_write(const DetectArgs a, const int* __restrict__ counts,
+                                                   tb_detection* __restrict__ dets, float* __restrict__ prob,
+                                                   int max_classes) {
+    const int hi = blockIdx.x, b = blockIdx.y;
+    const HeadDev& hd = a.heads[hi];
+    const int hw = hd.h * hd.w, L = hw * hd.n;
+    const float* out = hd.out + b * head_outputs(hd);
+    long long base = 0;
+    for (int j = 0; j < hi; ++j) base += counts[b * a.n_heads + j];
+    __shared__ int warp_tot[8];
+    __shared__ long long running;
+    if (threadIdx.x == 0) running = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int q0 = 0; q0 < L; q0 += 256) {
+        int q = q0 + threadIdx.x;
+        int i = 0, an = 0;
+        float obj = 0.f;
+        bool hit = false;
+        if (q < L) {
+            i = q / hd.n;
+            an = q - i * hd.n;
+            obj = out[(long long)an * (hd.classes + 5) * hw + 4LL * hw + i];
+            hit = obj > a.thresh;
+        }
+        unsigned bal = __ballot_sync(0xffffffffu, hit);
+        int before = __popc(bal & ((1u << lane) - 1u));
+        if (lane == 0) warp_tot[wid] = __popc(bal);
+        __syncthreads();
+        int woff = 0, tot = 0;
+        for (int w2 = 0; w2 < 8; ++w2) {
+            if (w2 < wid) woff += warp_tot[w2];
+            tot += warp_tot[w2];
+        }
+        long long pos = base + running + woff + before;
+        if (hit && pos < a.capacity) {
+            const long long st = hw;
+            const float* bx = out + (long long)an * (hd.classes + 5) * hw + i;
+            int row = i / hd.w, col = i - row * hd.w;
+            // getBox (:105-122)
+            float x = (float)(((double)col + (double)bx[0]) / (double)hd.w);
+            float y = (float)(((double)row + (double)bx[st]) / (double)hd.h);
+            float w, h;
+            if (hd.new_coords) {
+                double tw = (double)bx[2 * st], th = (double)bx[3 * st];
+                w = (float)(tw * tw * 4.0 * (double)hd.aw[an] / (double)a.net_w);
+                h = (float)(th * th * 4.0 * (double)hd.ah[an] / (double)a.net_h);
+            } else {
+                w = (float)(exp((double)bx[2 * st]) * (double)hd.aw[an] / (double)a.net_w);
+                h = (float)(exp((double)bx[3 * st]) * (double)hd.ah[an] / (double)a.net_h);
+            }
+            // correctBoxes (:452-498)
+            x = (float)(((double)x - (double)a.deltaw / 2.0 / (double)a.net_w) / (double)a.ratiow);
+            y = (float)(((double)y - (double)a.deltah / 2.0 / (double)a.net_h) / (double)a.ratioh);
+            w = (float)((double)w * (1.0 / (double)a.ratiow));
+            h = (float)((double)h * (1.0 / (double)a.ratioh));
+            if (!a.relative) {
+                x = x * (float)a.img_w;
+                w = w * (float)a.img_w;
+                y = y * (float)a.img_h;
+                h = h * (float)a.img_h;
+            }
+            long long di = (long long)b * a.capacity + pos;
+            tb_detection d;
+            d.x = x; d.y = y; d.w = w; d.h = h;
+            d.objectness = obj;
+            d.batch = b; d.head = hi; d.index = i; d.anchor = an;
+            d.reserved[0] = d.reserved[1] = d.reserved[2] = 0;
+            dets[di] = d;
+            if (prob) {
+                float* pr = prob + di * max_classes;
+                for (int j = 0; j < hd.classes; ++j) {
+                    float p = __fmul_rn(obj, bx[(5LL + j) * st]);
+                    pr[j] = (p > a.thresh) ? p : 0.0f;
+                }
+                for (int j = hd.classes; j < max_classes; ++j) pr[j] = 0.0f;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) running += tot;
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+extern "C" int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads,
+                              int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
+                              int64_t relative, int64_t letter, int64_t capacity, tb_detection* dets,
+                              float* prob, int64_t* counts_host) {
+    TB_ENTER(ctx);
+    if (batch < 0 || n_heads <= 0 || n_heads > MAX_HEADS || !heads || img_w <= 0 || img_h <= 0 ||
+        net_w <= 0 || net_h <= 0 || capacity < 0 || !counts_host || (capacity > 0 && !dets))
+        return fail(TB_ERR_INVALID, "yolo_detect: bad arguments (at most %d heads)", MAX_HEADS);
+    if (batch == 0) return TB_OK;
+    if (batch > 65535) return fail(TB_ERR_INVALID, "yolo_detect: batch too large");
+    DetectArgs a;
+    memset(&a, 0, sizeof(a));
+    int max_classes = 0;
+    for (int64_t h = 0; h < n_heads; ++h) {
+        const tb_yolo_head& s = heads[h];
+        if (!s.output || s.n <= 0 || s.n > MAX_ANCH || s.classes < 0 || s.h <= 0 || s.w <= 0 ||
+            !s.mask_host || !s.anchors_host)
+            return fail(TB_ERR_INVALID, "yolo_detect: bad head %lld", (long long)h);
+        HeadDev& d = a.heads[h];
+        d.out = s.output;
+        d.n = (int)s.n; d.classes = (int)s.classes; d.h = (int)s.h; d.w = (int)s.w;
+        d.new_coords = (int)s.new_coords;
+        for (int64_t k = 0; k < s.n; ++k) {
+            int64_t m = s.mask_host[k];
+            if (m < 0) return fail(TB_ERR_INVALID, "yolo_detect: negative mask");
+            d.aw[k] = s.anchors_host[2 * m];
+            d.ah[k] = s.anchors_host[2 * m + 1];
+        }
+        if (s.classes > max_classes) max_classes = (int)s.classes;
+    }
+    a.n_heads = (int)n_heads;
+    a.img_w = (int)img_w; a.img_h = (int)img_h; a.net_w = (int)net_w; a.net_h = (int)net_h;
+    a.relative = relative ? 1 : 0;
+    a.letter = letter ? 1 : 0;
+    a.thresh = thresh;
+    a.capacity = capacity;
+    int64_t new_w, new_h;
+    if (letter) {
+        if ((double)net_w / (double)img_w < (double)net_h / (double)img_h) {
+            new_w = net_w;
+            new_h = (img_h * net_w) / img_w;
+        } else {
+            new_h = net_h;
+            new_w = (img_w * net_h) / img_h;
+        }
+    } else {
+        new_w = net_w;
+        new_h = net_h;
+    }
+    a.deltaw = (float)(net_w - new_w);
+    a.deltah = (float)(net_h - new_h);
+    a.ratiow = (float)((double)new_w / (double)net_w);
+    a.ratioh = (float)((double)new_h / (double)net_h);
+
+    const int64_t ncounts = batch * n_heads;
+    int r = ensure_workspace(ctx, sizeof(int) * (size_t)ncounts);
+    if (r != TB_OK) return r;
+    int* d_counts = reinterpret_cast<int*>(ctx->ws);
+    dim3 grid((unsigned)n_heads, (unsigned)batch);
+    k_yolo_count<<<grid, 256, 0, ctx->stream>>>(a, d_counts);
+    r = check_launch("k_yolo_count");
+    if (r != TB_OK) return r;
+    if (capacity > 0) {
+        k_yolo_write<<<grid, 256, 0, ctx->stream>>>(a, d_counts, dets, prob, max_classes);
+        r = check_launch("k_yolo_write");
+        if (r != TB_OK) return r;
+    }
+    std::vector<int> hc((size_t)ncounts);
+    TB_CHECK_CUDA(cudaMemcpyAsync(hc.data(), d_counts, sizeof(int) * (size_t)ncounts,
+                                  cudaMemcpyDeviceToHost, ctx->stream));
+    TB_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+    for (int64_t b = 0; b < batch; ++b) {
+        int64_t t = 0;
+        for (int64_t h = 0; h < n_heads; ++h) t += hc[(size_t)(b * n_heads + h)];
+        counts_host[b] = t;
+    }
+    return TB_OK;
+}
