@@ -1,0 +1,702 @@
+// net.cu -- whole-network executor: the device-resident TNNet.forward / predict
+// (source/nnet.pas:275-317, 452-472) for darknet conv networks.
+//
+// The reference runs layer.forwardGPU one after another, each a handful of launches
+// (per-image im2col, GEMM, bias, activation, copies).  This executor:
+//   * folds batchnorm on the host (TNNet.fuseBatchNorm, source/nnet.pas:268-273) when asked;
+//   * fuses a shortcut into the epilogue of the conv before it (residual add) and the yolo
+//     activation into the head conv, when that conv's raw output has no other reader;
+//   * makes multi-input routes zero-copy: producers write straight into their channel slice of
+//     the concat buffer and consumers read it with a batch stride;
+//   * allocates every activation once (HBM is plentiful: YOLOv3-416 at batch 8 needs ~1.3 GB)
+//     and replays the whole forward as one CUDA graph.
+#include "conv.cuh"
+
+#include <algorithm>
+#include <memory>
+#include <vector>
+
+namespace tbi {
+int copy_rows(tb_ctx* ctx, int64_t batch, int64_t n, const float* src, int64_t src_bs, float* dst,
+              int64_t dst_bs);
+}
+using namespace tbi;
+
+namespace {
+
+struct View {
+    float* ptr = nullptr;
+    int64_t bs = 0;  // elements between images
+};
+
+struct Layer {
+    int type = 0;
+    int64_t c = 0, h = 0, w = 0;     // input shape
+    int64_t oc = 0, oh = 0, ow = 0;  // output shape
+    // conv / connected
+    int64_t filters = 0, ksize = 0, stride = 0, pad = 0, act = TB_ACT_LINEAR;
+    bool bn = false;
+    std::vector<float> weights, biases, scales, mean, var;
+    float *d_wp = nullptr, *d_bias = nullptr, *d_scale = nullptr, *d_mean = nullptr, *d_var = nullptr;
+    // shortcut
+    int64_t from = -1;
+    // route
+    std::vector<int64_t> inputs;
+    bool route_zero_copy = false;
+    // upsample
+    float up_scale = 1.0f;
+    // yolo
+    int64_t classes = 0, n = 0;
+    std::vector<int64_t> mask;
+    std::vector<float> anchors;
+    float scale_xy = 1.0f;
+    // softmax
+    int64_t groups = 1;
+    float temperature = 1.0f;
+    // plan
+    bool absorbed = false;      // computed inside the previous conv's epilogue
+    int64_t fuse_res = -1;      // conv: residual layer index
+    int64_t fuse_yolo = 0;      // conv: yolo classes
+    int64_t target = -1;        // conv: layer whose output view it writes (itself or next)
+    View out;
+    float* own = nullptr;       // allocation owned by this layer
+    int64_t own_floats = 0;
+    int64_t per_image() const { return oc * oh * ow; }
+};
+
+}  // namespace
+
+struct tb_net {
+    tb_ctx* ctx = nullptr;
+    int64_t batch = 0, c = 0, h = 0, w = 0;
+    std::vector<std::unique_ptr<Layer>> layers;
+    bool fusion = true;
+    bool finalized = false;
+    int64_t math_mode = TB_MATH_FP32;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const float* graph_x = nullptr;
+    int64_t launches = 0, graph_launches = 0;
+    double flops = 0.0;
+    std::vector<float*> allocs;
+};
+
+namespace {
+
+int add_layer(tb_net* net, std::unique_ptr<Layer> L) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
+    net->layers.push_back(std::move(L));
+    return (int)net->layers.size() - 1;
+}
+
+// output shape of every layer given the shapes of the layers before it
+int infer_shapes(tb_net* net) {
+    for (size_t i = 0; i < net->layers.size(); ++i) {
+        Layer& L = *net->layers[i];
+        if (i == 0) { L.c = net->c; L.h = net->h; L.w = net->w; }
+        else { const Layer& P = *net->layers[i - 1]; L.c = P.oc; L.h = P.oh; L.w = P.ow; }
+        switch (L.type) {
+        case TB_LAYER_CONV: {
+            if (L.weights.size() != (size_t)(L.filters * L.c * L.ksize * L.ksize))
+                return fail(TB_ERR_INVALID, "layer %zu: conv weights hold %zu floats, expected %lld (c=%lld)",
+                            i, L.weights.size(), (long long)(L.filters * L.c * L.ksize * L.ksize), (long long)L.c);
+            L.oc = L.filters;
+            L.oh = (L.h + 2 * L.pad - L.ksize) / L.stride + 1;
+            L.ow = (L.w + 2 * L.pad - L.ksize) / L.stride + 1;
+            if (L.oh <= 0 || L.ow <= 0) return fail(TB_ERR_INVALID, "layer %zu: empty conv output", i);
+            break;
+        }
+        case TB_LAYER_SHORTCUT: {
+            if (L.from < 0 || L.from >= (int64_t)i) return fail(TB_ERR_INVALID, "layer %zu: bad shortcut source", i);
+            const Layer& F = *net->layers[L.from];
+            if (F.oc != L.c || F.oh != L.h || F.ow != L.w)
+                return fail(TB_ERR_UNSUPPORTED, "layer %zu: shortcut between different shapes", i);
+            L.oc = L.c; L.oh = L.h; L.ow = L.w;
+            break;
+        }
+        case TB_LAYER_ROUTE: {
+            int64_t tc = 0, rh = -1, rw = -1;
+            for (int64_t j : L.inputs) {
+                if (j < 0 || j >= (int64_t)i) return fail(TB_ERR_INVALID, "layer %zu: bad route input", i);
+                const Layer& S = *net->layers[j];
+                if (rh < 0) { rh = S.oh; rw = S.ow; }
+                if (S.oh != rh || S.ow != rw) return fail(TB_ERR_INVALID, "layer %zu: route inputs differ in size", i);
+                tc += S.oc;
+            }
+            L.oc = tc; L.oh = rh; L.ow = rw;
+            break;
+        }
+        case TB_LAYER_UPSAMPLE:
+            L.oc = L.c; L.oh = L.h * L.stride; L.ow = L.w * L.stride;
+            break;
+        case TB_LAYER_YOLO:
+            if (L.c != L.n * (L.classes + 5))
+                return fail(TB_ERR_INVALID, "layer %zu: yolo expects %lld channels, got %lld", i,
+                            (long long)(L.n * (L.classes + 5)), (long long)L.c);
+            L.oc = L.c; L.oh = L.h; L.ow = L.w;
+            break;
+        case TB_LAYER_MAXPOOL:
+            L.oc = L.c;
+            L.oh = (L.h + L.pad - L.ksize) / L.stride + 1;
+            L.ow = (L.w + L.pad - L.ksize) / L.stride + 1;
+            break;
+        case TB_LAYER_CONNECTED:
+            if (L.weights.size() != (size_t)(L.filters * L.c * L.h * L.w))
+                return fail(TB_ERR_INVALID, "layer %zu: connected weights hold %zu floats, expected %lld",
+                            i, L.weights.size(), (long long)(L.filters * L.c * L.h * L.w));
+            L.oc = L.filters; L.oh = 1; L.ow = 1;
+            break;
+        case TB_LAYER_SOFTMAX:
+            L.oc = L.c; L.oh = L.h; L.ow = L.w;
+            if ((L.c * L.h * L.w) % L.groups) return fail(TB_ERR_INVALID, "layer %zu: softmax groups", i);
+            break;
+        case TB_LAYER_AVGPOOL:
+            L.oc = L.c; L.oh = 1; L.ow = 1;
+            break;
+        default:
+            return fail(TB_ERR_INVALID, "layer %zu: unknown type", i);
+        }
+    }
+    return TB_OK;
+}
+
+// readers[j] = layers that read layer j's output
+std::vector<std::vector<int64_t>> readers_of(const tb_net* net) {
+    const int64_t n = (int64_t)net->layers.size();
+    std::vector<std::vector<int64_t>> r((size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        const Layer& L = *net->layers[i];
+        if (L.type == TB_LAYER_ROUTE) {
+            for (int64_t j : L.inputs) r[j].push_back(i);
+        } else {
+            if (i > 0) r[i - 1].push_back(i);
+            if (L.type == TB_LAYER_SHORTCUT) r[L.from].push_back(i);
+        }
+    }
+    return r;
+}
+
+float* dev_upload(tb_net* net, const std::vector<float>& v, int* err) {
+    if (v.empty()) return nullptr;
+    float* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, v.size() * sizeof(float));
+    if (e != cudaSuccess) { *err = cuda_fail(e, "cudaMalloc(weights)"); return nullptr; }
+    net->allocs.push_back(p);
+    e = cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { *err = cuda_fail(e, "cudaMemcpy(weights)"); return nullptr; }
+    return p;
+}
+
+void desc_of(const tb_net* net, const Layer& L, tb_conv_desc* d) {
+    *d = tb_conv_desc{};
+    d->batch = net->batch;
+    if (L.type == TB_LAYER_CONV) {
+        d->channels = L.c; d->height = L.h; d->width = L.w;
+        d->kernel_h = L.ksize; d->kernel_w = L.ksize;
+        d->stride_y = L.stride; d->stride_x = L.stride; d->pad_y = L.pad; d->pad_x = L.pad;
+    } else {  // connected: a 1x1 conv over 1x1 images with c*h*w channels
+        d->channels = L.c * L.h * L.w; d->height = 1; d->width = 1;
+        d->kernel_h = d->kernel_w = 1; d->stride_y = d->stride_x = 1;
+    }
+    d->filters = L.filters;
+    d->activation = L.act;
+}
+
+View input_view(tb_net* net, int64_t i, const float* x) {
+    if (i == 0) {
+        View v;
+        v.ptr = const_cast<float*>(x);
+        v.bs = net->c * net->h * net->w;
+        return v;
+    }
+    return net->layers[i - 1]->out;
+}
+
+int run_layer(tb_net* net, int64_t i, const float* x) {
+    tb_ctx* ctx = net->ctx;
+    Layer& L = *net->layers[i];
+    if (L.absorbed) return TB_OK;
+    const int64_t B = net->batch;
+    View in = input_view(net, i, x);
+    int r = TB_OK;
+    switch (L.type) {
+    case TB_LAYER_CONV:
+    case TB_LAYER_CONNECTED: {
+        tb_conv_desc d;
+        desc_of(net, L, &d);
+        const Layer& T = *net->layers[L.target];
+        d.in_batch_stride = in.bs;
+        d.out_batch_stride = T.out.bs;
+        const float* res = nullptr;
+        if (L.fuse_res >= 0) {
+            res = net->layers[L.fuse_res]->out.ptr;
+            d.res_batch_stride = net->layers[L.fuse_res]->out.bs;
+        }
+        ConvGeom g;
+        r = conv_geom(&d, &g);
+        if (r != TB_OK) return r;
+        return conv_fp32_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
+                                L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
+                                (int)L.act, (int)L.fuse_yolo, nullptr, 0, &net->launches);
+    }
+    case TB_LAYER_SHORTCUT: {
+        const Layer& F = *net->layers[L.from];
+        if (in.bs != L.per_image() || F.out.bs != L.per_image() || L.out.bs != L.per_image())
+            return fail(TB_ERR_STATE, "layer %lld: strided shortcut operands", (long long)i);
+        r = tb_shortcut_fwd(ctx, B * L.per_image(), in.ptr, F.out.ptr, L.out.ptr, L.act);
+        net->launches++;
+        return r;
+    }
+    case TB_LAYER_ROUTE: {
+        if (L.route_zero_copy) return TB_OK;
+        int64_t off = 0;
+        for (int64_t j : L.inputs) {
+            const Layer& S = *net->layers[j];
+            r = copy_rows(ctx, B, S.per_image(), S.out.ptr, S.out.bs, L.out.ptr + off, L.out.bs);
+            if (r != TB_OK) return r;
+            net->launches++;
+            off += S.per_image();
+        }
+        return TB_OK;
+    }
+    case TB_LAYER_UPSAMPLE:
+        if (in.bs != L.c * L.h * L.w) return fail(TB_ERR_STATE, "layer %lld: strided upsample input", (long long)i);
+        r = tb_upsample_fwd(ctx, B, L.c, L.h, L.w, L.stride, L.up_scale, in.ptr, L.out.ptr, L.out.bs);
+        net->launches++;
+        return r;
+    case TB_LAYER_YOLO:
+        if (in.bs != L.c * L.h * L.w) return fail(TB_ERR_STATE, "layer %lld: strided yolo input", (long long)i);
+        r = tb_yolo_fwd(ctx, B, L.n, L.classes, L.h, L.w, in.ptr, L.out.ptr, L.scale_xy);
+        net->launches++;
+        return r;
+    case TB_LAYER_MAXPOOL:
+        if (in.bs != L.c * L.h * L.w) return fail(TB_ERR_STATE, "layer %lld: strided maxpool input", (long long)i);
+        r = tb_maxpool_fwd(ctx, B, L.c, L.h, L.w, L.ksize, L.stride, L.stride, L.pad, in.ptr, L.out.ptr, nullptr);
+        net->launches++;
+        return r;
+    case TB_LAYER_SOFTMAX:
+        if (in.bs != L.c * L.h * L.w) return fail(TB_ERR_STATE, "layer %lld: strided softmax input", (long long)i);
+        r = tb_softmax_fwd(ctx, B, L.c * L.h * L.w, L.groups, L.temperature, in.ptr, L.out.ptr);
+        net->launches++;
+        return r;
+    case TB_LAYER_AVGPOOL:
+        if (in.bs != L.c * L.h * L.w) return fail(TB_ERR_STATE, "layer %lld: strided avgpool input", (long long)i);
+        r = tb_avgpool_fwd(ctx, B, L.c, L.h, L.w, in.ptr, L.out.ptr);
+        net->launches++;
+        return r;
+    }
+    return fail(TB_ERR_INVALID, "layer %lld: unknown type", (long long)i);
+}
+
+int run_all(tb_net* net, const float* x) {
+    net->launches = 0;
+    for (int64_t i = 0; i < (int64_t)net->layers.size(); ++i) {
+        int r = run_layer(net, i, x);
+        if (r != TB_OK) return r;
+    }
+    return TB_OK;
+}
+
+void free_graph(tb_net* net) {
+    if (net->exec) cudaGraphExecDestroy(net->exec);
+    if (net->graph) cudaGraphDestroy(net->graph);
+    net->exec = nullptr;
+    net->graph = nullptr;
+    net->graph_x = nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tb_net_create(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t height, int64_t width, tb_net** out) {
+    TB_ENTER(ctx);
+    if (!out || batch <= 0 || channels <= 0 || height <= 0 || width <= 0)
+        return fail(TB_ERR_INVALID, "tb_net_create: bad arguments");
+    tb_net* n = new tb_net();
+    n->ctx = ctx;
+    n->batch = batch; n->c = channels; n->h = height; n->w = width;
+    n->math_mode = ctx->math_mode;
+    *out = n;
+    return TB_OK;
+}
+
+int tb_net_destroy(tb_net* net) {
+    if (!net) return TB_OK;
+    enter(net->ctx);
+    cudaStreamSynchronize(net->ctx->stream);
+    free_graph(net);
+    for (float* p : net->allocs) cudaFree(p);
+    delete net;
+    return TB_OK;
+}
+
+static int prev_channels(tb_net* net, int64_t* out) {
+    if (net->layers.empty()) { *out = net->c; return TB_OK; }
+    int r = infer_shapes(net);
+    if (r != TB_OK) return r;
+    *out = net->layers.back()->oc;
+    return TB_OK;
+}
+
+int tb_net_add_conv(tb_net* net, int64_t filters, int64_t ksize, int64_t stride, int64_t pad,
+                    int64_t activation, int64_t batch_normalize, const float* weights,
+                    const float* biases, const float* scales, const float* mean, const float* var) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (filters <= 0 || ksize <= 0 || stride <= 0 || pad < 0 || !weights)
+        return fail(TB_ERR_INVALID, "conv layer: bad arguments");
+    if (!act_supported(activation)) return fail(TB_ERR_UNSUPPORTED, "conv layer: activation not supported");
+    if (batch_normalize && (!scales || !mean || !var))
+        return fail(TB_ERR_INVALID, "conv layer: batchnorm needs scales, mean and variance");
+    int64_t cin;
+    int r = prev_channels(net, &cin);
+    if (r != TB_OK) return r;
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_CONV;
+    L->filters = filters; L->ksize = ksize; L->stride = stride; L->pad = pad; L->act = activation;
+    L->bn = batch_normalize != 0;
+    L->weights.assign(weights, weights + filters * cin * ksize * ksize);
+    L->biases = biases ? std::vector<float>(biases, biases + filters) : std::vector<float>((size_t)filters, 0.0f);
+    if (L->bn) {
+        L->scales.assign(scales, scales + filters);
+        L->mean.assign(mean, mean + filters);
+        L->var.assign(var, var + filters);
+    }
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_shortcut(tb_net* net, int64_t from, int64_t activation) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (!act_supported(activation)) return fail(TB_ERR_UNSUPPORTED, "shortcut: activation not supported");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_SHORTCUT;
+    int64_t idx = (int64_t)net->layers.size();
+    L->from = from < 0 ? idx + from : from;  // darknet: negative = relative
+    L->act = activation;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_route(tb_net* net, int64_t n, const int64_t* layers) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (n <= 0 || !layers) return fail(TB_ERR_INVALID, "route: bad arguments");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_ROUTE;
+    int64_t idx = (int64_t)net->layers.size();
+    for (int64_t k = 0; k < n; ++k) L->inputs.push_back(layers[k] < 0 ? idx + layers[k] : layers[k]);
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_upsample(tb_net* net, int64_t stride, float scale) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (stride <= 0) return fail(TB_ERR_UNSUPPORTED, "upsample: only forward (positive) strides");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_UPSAMPLE;
+    L->stride = stride;
+    L->up_scale = scale;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_yolo(tb_net* net, int64_t classes, int64_t n, const int64_t* mask,
+                    int64_t total_anchors, const float* anchors, float scale_xy) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (classes < 0 || n <= 0 || !mask || total_anchors <= 0 || !anchors)
+        return fail(TB_ERR_INVALID, "yolo: bad arguments");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_YOLO;
+    L->classes = classes; L->n = n;
+    L->mask.assign(mask, mask + n);
+    for (int64_t m : L->mask)
+        if (m < 0 || m >= total_anchors) return fail(TB_ERR_INVALID, "yolo: mask out of range");
+    L->anchors.assign(anchors, anchors + 2 * total_anchors);
+    L->scale_xy = scale_xy;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_maxpool(tb_net* net, int64_t ksize, int64_t stride, int64_t padding) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (ksize <= 0 || stride <= 0 || padding < 0) return fail(TB_ERR_INVALID, "maxpool: bad arguments");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_MAXPOOL;
+    L->ksize = ksize; L->stride = stride; L->pad = padding;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_connected(tb_net* net, int64_t outputs, int64_t activation, const float* weights,
+                         const float* biases) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (outputs <= 0 || !weights) return fail(TB_ERR_INVALID, "connected: bad arguments");
+    if (!act_supported(activation)) return fail(TB_ERR_UNSUPPORTED, "connected: activation not supported");
+    int64_t inputs;
+    if (net->layers.empty()) inputs = net->c * net->h * net->w;
+    else {
+        int r = infer_shapes(net);
+        if (r != TB_OK) return r;
+        const Layer& P = *net->layers.back();
+        inputs = P.oc * P.oh * P.ow;
+    }
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_CONNECTED;
+    L->filters = outputs; L->act = activation;
+    L->weights.assign(weights, weights + outputs * inputs);
+    L->biases = biases ? std::vector<float>(biases, biases + outputs) : std::vector<float>((size_t)outputs, 0.0f);
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_softmax(tb_net* net, int64_t groups, float temperature) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (groups <= 0) return fail(TB_ERR_INVALID, "softmax: bad groups");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_SOFTMAX;
+    L->groups = groups;
+    L->temperature = temperature;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_add_avgpool(tb_net* net) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    auto L = std::make_unique<Layer>();
+    L->type = TB_LAYER_AVGPOOL;
+    return add_layer(net, std::move(L));
+}
+
+int tb_net_set_fusion(tb_net* net, int64_t enable) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
+    net->fusion = enable != 0;
+    return TB_OK;
+}
+
+int tb_net_fuse_batchnorm(tb_net* net) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
+    int r = infer_shapes(net);
+    if (r != TB_OK) return r;
+    for (auto& Lp : net->layers) {
+        Layer& L = *Lp;
+        if (L.type != TB_LAYER_CONV || !L.bn) continue;
+        r = tb_conv_fold_bn(L.filters, L.c * L.ksize * L.ksize, L.weights.data(), L.biases.data(),
+                            L.scales.data(), L.mean.data(), L.var.data());
+        if (r != TB_OK) return r;
+        L.bn = false;
+    }
+    return TB_OK;
+}
+
+int tb_net_finalize(tb_net* net, int64_t math_mode) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    TB_ENTER(net->ctx);
+    if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
+    if (net->layers.empty()) return fail(TB_ERR_INVALID, "empty net");
+    if (math_mode != TB_MATH_FP32)
+        return fail(TB_ERR_UNSUPPORTED, "net: math mode %lld is not available in this build", (long long)math_mode);
+    net->math_mode = math_mode;
+    int r = infer_shapes(net);
+    if (r != TB_OK) return r;
+    const int64_t n = (int64_t)net->layers.size();
+    const int64_t B = net->batch;
+    auto rd = readers_of(net);
+
+    // 1. fusion decisions: a conv whose only reader is the next layer absorbs a linear
+    //    shortcut (residual epilogue) or a yolo layer (logistic epilogue)
+    for (int64_t i = 0; i < n; ++i) net->layers[i]->target = i;
+    if (net->fusion) {
+        for (int64_t i = 0; i + 1 < n; ++i) {
+            Layer& L = *net->layers[i];
+            Layer& N = *net->layers[i + 1];
+            if (L.type != TB_LAYER_CONV || rd[i].size() != 1 || rd[i][0] != i + 1) continue;
+            if (N.type == TB_LAYER_SHORTCUT && N.act == TB_ACT_LINEAR && N.from != i) {
+                L.fuse_res = N.from;
+                L.target = i + 1;
+                N.absorbed = true;
+            } else if (N.type == TB_LAYER_YOLO && L.act == TB_ACT_LINEAR && N.scale_xy == 1.0f) {
+                L.fuse_yolo = N.classes;
+                L.target = i + 1;
+                N.absorbed = true;
+            }
+        }
+    }
+    // producer[j]: the layer whose kernel writes j's output
+    std::vector<int64_t> producer((size_t)n);
+    for (int64_t i = 0; i < n; ++i) producer[i] = i;
+    for (int64_t i = 0; i < n; ++i)
+        if (net->layers[i]->target != i) producer[net->layers[i]->target] = i;
+    // may j's output live in a route slice (batch stride > one image)? Every reader must take
+    // a batch stride: a conv reading it as input, a conv reading it as residual (through an
+    // absorbed shortcut), or a route copy.
+    auto strided_reader_ok = [&](int64_t j) {
+        for (int64_t k : rd[j]) {
+            const Layer& R = *net->layers[k];
+            if (R.type == TB_LAYER_ROUTE) continue;
+            if (R.type == TB_LAYER_CONV && k == j + 1) continue;
+            if (R.type == TB_LAYER_SHORTCUT && R.absorbed) continue;
+            return false;
+        }
+        return true;
+    };
+    auto strided_writer_ok = [&](int64_t j) {
+        const Layer& P = *net->layers[producer[j]];
+        return P.type == TB_LAYER_CONV || P.type == TB_LAYER_UPSAMPLE;
+    };
+
+    // 2. buffers: multi-input routes first (their inputs may live inside them), then the rest
+    std::vector<bool> placed((size_t)n, false);
+    int err = TB_OK;
+    auto alloc = [&](int64_t floats) -> float* {
+        float* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, (size_t)floats * sizeof(float));
+        if (e != cudaSuccess) { err = cuda_fail(e, "cudaMalloc(activations)"); return nullptr; }
+        net->allocs.push_back(p);
+        return p;
+    };
+    for (int64_t i = 0; i < n; ++i) {
+        Layer& L = *net->layers[i];
+        if (L.type != TB_LAYER_ROUTE || L.inputs.size() == 1) continue;
+        L.own_floats = B * L.per_image();
+        L.own = alloc(L.own_floats);
+        if (!L.own) return err;
+        L.out.ptr = L.own;
+        L.out.bs = L.per_image();
+        placed[i] = true;
+        bool all = net->fusion;
+        for (int64_t j : L.inputs)
+            if (placed[j] || net->layers[j]->type == TB_LAYER_ROUTE || !strided_reader_ok(j) ||
+                !strided_writer_ok(j))
+                all = false;
+        for (size_t a = 0; a < L.inputs.size(); ++a)
+            for (size_t b = a + 1; b < L.inputs.size(); ++b)
+                if (L.inputs[a] == L.inputs[b]) all = false;
+        if (all) {
+            int64_t off = 0;
+            for (int64_t j : L.inputs) {
+                Layer& S = *net->layers[j];
+                S.out.ptr = L.own + off;
+                S.out.bs = L.per_image();
+                placed[j] = true;
+                off += S.per_image();
+            }
+            L.route_zero_copy = true;
+        }
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        Layer& L = *net->layers[i];
+        if (placed[i]) continue;
+        if (L.type == TB_LAYER_ROUTE && L.inputs.size() == 1) {
+            L.out = net->layers[L.inputs[0]]->out;  // alias; the input precedes the route
+            L.route_zero_copy = true;
+            placed[i] = true;
+            continue;
+        }
+        if (L.target != i) {  // conv fused into the next layer: no buffer of its own
+            placed[i] = true;
+            continue;
+        }
+        L.own_floats = B * L.per_image();
+        L.own = alloc(L.own_floats);
+        if (!L.own) return err;
+        L.out.ptr = L.own;
+        L.out.bs = L.per_image();
+        placed[i] = true;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        Layer& L = *net->layers[i];
+        if (L.target != i) L.out = net->layers[L.target]->out;
+    }
+
+    // 3. weights, and the split-K workspace every conv will need
+    int64_t ws_floats = 0;
+    net->flops = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        Layer& L = *net->layers[i];
+        if (L.type != TB_LAYER_CONV && L.type != TB_LAYER_CONNECTED) continue;
+        tb_conv_desc d;
+        desc_of(net, L, &d);
+        ConvGeom g;
+        r = conv_geom(&d, &g);
+        if (r != TB_OK) return r;
+        float* raw = dev_upload(net, L.weights, &err);
+        if (!raw) return err;
+        L.d_wp = alloc(g.Kpad * g.Mpad);
+        if (!L.d_wp) return err;
+        r = tb_conv_pack_weights(net->ctx, &d, raw, L.d_wp);
+        if (r != TB_OK) return r;
+        L.d_bias = dev_upload(net, L.biases, &err);
+        if (err != TB_OK) return err;
+        if (L.bn) {
+            L.d_scale = dev_upload(net, L.scales, &err);
+            L.d_mean = dev_upload(net, L.mean, &err);
+            L.d_var = dev_upload(net, L.var, &err);
+            if (err != TB_OK) return err;
+        }
+        ws_floats = std::max(ws_floats, conv_fp32_ws_floats(net->ctx, g));
+        net->flops += 2.0 * (double)g.F * (double)(g.B * g.OH * g.OW) * (double)(g.C * g.KH * g.KW);
+    }
+    r = ensure_workspace(net->ctx, (size_t)std::max<int64_t>(ws_floats, 1) * sizeof(float));
+    if (r != TB_OK) return r;
+    TB_CHECK_CUDA(cudaStreamSynchronize(net->ctx->stream));
+    net->finalized = true;
+    return TB_OK;
+}
+
+int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    TB_ENTER(net->ctx);
+    if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
+    if (!x) return fail(TB_ERR_INVALID, "null input");
+    cudaStream_t s = net->ctx->stream;
+    if (!use_graph) return run_all(net, x);
+    if (net->exec && net->graph_x == x) {
+        TB_CHECK_CUDA(cudaGraphLaunch(net->exec, s));
+        net->launches = net->graph_launches;
+        return TB_OK;
+    }
+    free_graph(net);
+    TB_CHECK_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int r = run_all(net, x);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (r != TB_OK) { if (g) cudaGraphDestroy(g); return r; }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    net->graph = g;
+    e = cudaGraphInstantiate(&net->exec, g, 0);
+    if (e != cudaSuccess) { free_graph(net); return cuda_fail(e, "cudaGraphInstantiate"); }
+    net->graph_x = x;
+    net->graph_launches = net->launches;
+    TB_CHECK_CUDA(cudaGraphLaunch(net->exec, s));
+    return TB_OK;
+}
+
+int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* count, int64_t* bs) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
+    if (layer < 0 || layer >= (int64_t)net->layers.size()) return fail(TB_ERR_INVALID, "layer out of range");
+    const Layer& L = *net->layers[layer];
+    if (L.target != layer)
+        return fail(TB_ERR_STATE, "layer %lld is fused into layer %lld; its raw output is not materialised",
+                    (long long)layer, (long long)L.target);
+    if (ptr) *ptr = L.out.ptr;
+    if (count) *count = L.per_image();
+    if (bs) *bs = L.out.bs;
+    return TB_OK;
+}
+
+int tb_net_layer_count(tb_net* net, int64_t* count) {
+    if (!net || !count) return fail(TB_ERR_INVALID, "null argument");
+    *count = (int64_t)net->layers.size();
+    return TB_OK;
+}
+
+int tb_net_launch_count(tb_net* net, int64_t* count) {
+    if (!net || !count) return fail(TB_ERR_INVALID, "null argument");
+    *count = net->launches;
+    return TB_OK;
+}
+
+int tb_net_flops(tb_net* net, double* flops) {
+    if (!net || !flops) return fail(TB_ERR_INVALID, "null argument");
+    if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
+    *flops = net->flops;
+    return TB_OK;
+}
+
+}  // extern "C"
