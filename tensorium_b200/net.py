@@ -1,0 +1,160 @@
+"""TNNet for the B200 path: a whole network held by the C++ executor (``tb_net``).
+
+Mirrors TNNet.forward / predict / fuseBatchNorm / Detections (source/nnet.pas:268-317,
+452-472, 584-677): layers are declared from layer specifications (tensorium_b200.synth), weights
+are uploaded once per GPU, and ``forward`` replays the whole network as one CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from ._lib import MATH_FP32, check, lib
+from .context import Context, ptr
+from .layers import TYoloLayer, get_detections
+from .synth import layer_shapes
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, np.float32)
+
+
+class TNNet:
+    def __init__(self, ctx: Context, specs, batch: int, input_shape, fuse_batchnorm: bool = True,
+                 fusion: bool = True, math_mode: int = MATH_FP32):
+        self.ctx = ctx
+        self.specs = specs
+        self.batch = int(batch)
+        self.input_shape = tuple(input_shape)
+        self.shapes = layer_shapes(specs, self.input_shape)
+        self.handle = C.c_void_p()
+        c, h, w = self.input_shape
+        check(lib.tb_net_create(ctx.handle, self.batch, c, h, w, C.byref(self.handle)))
+        self.yolo_layers = []
+        keep = []
+        for i, s in enumerate(specs):
+            self._add(i, s, keep)
+        check(lib.tb_net_set_fusion(self.handle, 1 if fusion else 0))
+        if fuse_batchnorm:
+            check(lib.tb_net_fuse_batchnorm(self.handle))
+        check(lib.tb_net_finalize(self.handle, math_mode))
+
+    def _add(self, i, s, keep):
+        t = s["type"]
+        h = self.handle
+        if t == "conv":
+            arrs = [_f32(s.get(k)) for k in ("weights", "biases", "scales", "mean", "var")]
+            keep += arrs
+            check(lib.tb_net_add_conv(h, s["filters"], s["size"], s["stride"], s["pad"], s["activation"],
+                                      1 if s["batch_normalize"] else 0, *[ptr(a) for a in arrs]))
+        elif t == "shortcut":
+            check(lib.tb_net_add_shortcut(h, s["from"], s.get("activation", 4)))
+        elif t == "route":
+            arr = (C.c_int64 * len(s["layers"]))(*s["layers"])
+            check(lib.tb_net_add_route(h, len(s["layers"]), arr))
+        elif t == "upsample":
+            check(lib.tb_net_add_upsample(h, s["stride"], s.get("scale", 1.0)))
+        elif t == "yolo":
+            mask = np.ascontiguousarray(s["mask"], np.int64)
+            anchors = _f32(s["anchors"])
+            keep += [mask, anchors]
+            check(lib.tb_net_add_yolo(h, s["classes"], len(mask), ptr(mask), len(anchors) // 2, ptr(anchors),
+                                      s.get("scale_xy", 1.0)))
+            self.yolo_layers.append(i)
+        elif t == "maxpool":
+            check(lib.tb_net_add_maxpool(h, s["size"], s["stride"], s.get("padding", 0)))
+        elif t == "connected":
+            w, b = _f32(s["weights"]), _f32(s.get("biases"))
+            keep += [w, b]
+            check(lib.tb_net_add_connected(h, s["outputs"], s["activation"], ptr(w), ptr(b)))
+        elif t == "softmax":
+            check(lib.tb_net_add_softmax(h, s.get("groups", 1), s.get("temperature", 1.0)))
+        elif t == "avgpool":
+            check(lib.tb_net_add_avgpool(h))
+        else:
+            raise ValueError(f"layer {i}: unknown type {t}")
+
+    # -- execution ----------------------------------------------------------------------
+    def forward(self, x: torch.Tensor, use_graph: bool = True) -> None:
+        """TNNet.forward on a device tensor [batch, c, h, w] (asynchronous)."""
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        assert tuple(x.shape) == (self.batch,) + self.input_shape, x.shape
+        check(lib.tb_net_forward(self.handle, ptr(x), 1 if use_graph else 0))
+
+    def output(self, layer: int = -1) -> torch.Tensor:
+        """Device view of a layer's output, [batch, per_image] (strided for route slices)."""
+        if layer < 0:
+            layer += len(self.specs)
+        p = C.c_void_p()
+        n = C.c_int64()
+        bs = C.c_int64()
+        check(lib.tb_net_layer_output(self.handle, layer, C.byref(p), C.byref(n), C.byref(bs)))
+        return _view(p.value, self.batch, n.value, bs.value, self.ctx.torch_device)
+
+    def predict(self, x_host: np.ndarray, layers=None):
+        """TNNet.predict (source/nnet.pas:452-472): host input in, host outputs back
+        (default: the last layer) as numpy arrays [batch, per_image]."""
+        x = self.staging(x_host)
+        self.forward(x)
+        layers = layers if layers is not None else [len(self.specs) - 1]
+        return [self.output(l).cpu().numpy() for l in layers]
+
+    def staging(self, x_host):
+        if getattr(self, "_x", None) is None or tuple(self._x.shape) != tuple(x_host.shape):
+            self._x = torch.empty(x_host.shape, dtype=torch.float32, device=self.ctx.torch_device)
+        self._x.copy_(torch.from_numpy(np.ascontiguousarray(x_host, np.float32)))
+        return self._x
+
+    def yolo_heads(self):
+        heads, outs = [], []
+        for i in self.yolo_layers:
+            s = self.specs[i]
+            c, hh, ww = self.shapes[i]
+            heads.append(TYoloLayer(self.batch, ww, hh, len(s["mask"]), len(s["anchors"]) // 2, s["mask"],
+                                    s["classes"], s["anchors"], s.get("scale_xy", 1.0)))
+            outs.append(self.output(i))
+        return heads, outs
+
+    def detections(self, img_w, img_h, thresh=0.45, relative=True, letter=False, capacity=4096):
+        """TNNet.Detections over every yolo layer, extracted on the GPU."""
+        heads, outs = self.yolo_heads()
+        net_c, net_h, net_w = self.input_shape
+        return get_detections(self.ctx, heads, outs, self.batch, img_w, img_h, net_w, net_h, thresh,
+                              relative, letter, capacity)
+
+    @property
+    def flops(self) -> float:
+        f = C.c_double()
+        check(lib.tb_net_flops(self.handle, C.byref(f)))
+        return f.value
+
+    @property
+    def launch_count(self) -> int:
+        n = C.c_int64()
+        check(lib.tb_net_launch_count(self.handle, C.byref(n)))
+        return n.value
+
+    def close(self):
+        if self.handle:
+            lib.tb_net_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _CAI:
+    def __init__(self, addr, numel):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+def _view(addr, batch, n, bs, device):
+    """A [batch, n] tensor over device memory at `addr` with row stride `bs` (no copy)."""
+    numel = (batch - 1) * bs + n
+    return torch.as_tensor(_CAI(addr, numel), device=device).as_strided((batch, n), (bs, 1))
