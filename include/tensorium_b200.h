@@ -303,6 +303,16 @@ int tb_net_layer_count(tb_net* net, int64_t* count);
 int tb_net_launch_count(tb_net* net, int64_t* count);
 /* Conv FLOPs (2*M*N*K summed over conv / connected layers) of one forward at this batch. */
 int tb_net_flops(tb_net* net, double* flops);
+/* Per-layer timing (replaces the reference's TMetrics / USE_TELEMETRY per-layer clock,
+ * source/nbaselayer.pas:129-178, which synchronises after every op): runs one eager forward
+ * with a CUDA event between layers and writes each layer's device milliseconds to ms_out
+ * (layer_count entries; 0 for layers fused into their neighbour). Blocks. */
+int tb_net_profile(tb_net* net, const float* x, double* ms_out);
+
+/* ---- diagnostics -------------------------------------------------------------------------- */
+/* FP32 FFMA throughput of this GPU (TFLOP/s) from a register-resident FMA loop on every SM;
+ * the roofline denominator of the FP32 CUDA-core conv path (no reference counterpart). Blocks. */
+int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops);
 
 #ifdef __cplusplus
 }

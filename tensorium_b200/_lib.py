@@ -125,6 +125,8 @@ SIGNATURES = {
     "tb_net_layer_count": [P, PI64],
     "tb_net_launch_count": [P, PI64],
     "tb_net_flops": [P, C.POINTER(C.c_double)],
+    "tb_net_profile": [P, P, C.POINTER(C.c_double)],
+    "tb_diag_fp32_fma_tflops": [P, C.POINTER(C.c_double)],
 }
 _RESTYPES = {"tb_get_stream": P}
 

@@ -144,10 +144,50 @@ __global__ void k_fmavss(int64_t n, const float* __restrict__ src, float s, floa
         dst[i] = __fadd_rn(__fmul_rn(src[i], s), b);
 }
 
+// FFMA throughput probe: 8 independent chains per thread, all in registers.
+__global__ void k_fma_probe(float* out, int iters, float a, float b) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = threadIdx.x * 1e-3f + j;
+    for (int i = 0; i < iters; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = fmaf(v[j], a, b);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += v[j];
+    if (s == 12345.678f) out[0] = s;  // keeps the chains live
+}
+
 // ---------------------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------------------
 extern "C" {
+
+int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops) {
+    TB_ENTER(ctx);
+    if (!tflops) return fail(TB_ERR_INVALID, "null output");
+    const int threads = 512, blocks = ctx->sm_count * 4, iters = 4096;
+    cudaEvent_t e0, e1;
+    TB_CHECK_CUDA(cudaEventCreate(&e0));
+    TB_CHECK_CUDA(cudaEventCreate(&e1));
+    float* out = reinterpret_cast<float*>(ctx->ws);
+    k_fma_probe<<<blocks, threads, 0, ctx->stream>>>(out, iters, 0.9999f, 1e-4f);  // warm-up
+    cudaEventRecord(e0, ctx->stream);
+    for (int r = 0; r < 10; ++r) k_fma_probe<<<blocks, threads, 0, ctx->stream>>>(out, iters, 0.9999f, 1e-4f);
+    cudaEventRecord(e1, ctx->stream);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (e == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return cuda_fail(e, "fma probe");
+    int r = check_launch("k_fma_probe");
+    if (r != TB_OK) return r;
+    *tflops = 10.0 * 2.0 * 8.0 * iters * (double)threads * blocks / (ms * 1e-3) / 1e12;
+    return TB_OK;
+}
+
 
 const char* tb_last_error(void) { return g_err.c_str(); }
 

@@ -666,6 +666,34 @@ int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
     return TB_OK;
 }
 
+int tb_net_profile(tb_net* net, const float* x, double* ms_out) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    TB_ENTER(net->ctx);
+    if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
+    if (!x || !ms_out) return fail(TB_ERR_INVALID, "null argument");
+    const int64_t n = (int64_t)net->layers.size();
+    cudaStream_t s = net->ctx->stream;
+    std::vector<cudaEvent_t> ev((size_t)n + 1);
+    for (auto& e : ev) TB_CHECK_CUDA(cudaEventCreate(&e));
+    int r = TB_OK;
+    net->launches = 0;
+    cudaEventRecord(ev[0], s);
+    for (int64_t i = 0; i < n && r == TB_OK; ++i) {
+        r = run_layer(net, i, x);
+        cudaEventRecord(ev[i + 1], s);
+    }
+    cudaError_t e = cudaEventSynchronize(ev[n]);
+    for (int64_t i = 0; i < n; ++i) {
+        float ms = 0.f;
+        if (r == TB_OK && e == cudaSuccess) cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+        ms_out[i] = ms;
+    }
+    for (auto& ee : ev) cudaEventDestroy(ee);
+    if (r != TB_OK) return r;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    return TB_OK;
+}
+
 int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* count, int64_t* bs) {
     if (!net) return fail(TB_ERR_INVALID, "null net");
     if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");

@@ -124,6 +124,12 @@ class TNNet:
         return get_detections(self.ctx, heads, outs, self.batch, img_w, img_h, net_w, net_h, thresh,
                               relative, letter, capacity)
 
+    def profile(self, x: torch.Tensor) -> np.ndarray:
+        """Device milliseconds of every layer in one eager forward (CUDA events)."""
+        ms = (C.c_double * len(self.specs))()
+        check(lib.tb_net_profile(self.handle, ptr(x), ms))
+        return np.array(ms[:])
+
     @property
     def flops(self) -> float:
         f = C.c_double()

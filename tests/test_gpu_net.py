@@ -1,0 +1,97 @@
+"""Whole networks on the GPU executor vs the CPU oracle: YOLOv3-416 (every layer, fused and
+unfused plans, batch 1 and 2), the MNIST- and CIFAR-shaped configs, and CUDA-graph replay."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import FP32_TOL, worst_map_err
+from oracle import oracle as O
+from tensorium_b200 import synth
+from tensorium_b200.net import TNNet
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def yolo_specs():
+    return synth.yolov3_specs()
+
+
+def maps_of(specs, shape, i):
+    return synth.layer_shapes(specs, shape)[i][0]
+
+
+def test_yolov3_every_layer_unfused_plan(ctx, yolo_specs):
+    x = synth.input_images(3, "yolov3", 1, (3, 416, 416))
+    ref = O.run_network(yolo_specs, x)
+    net = TNNet(ctx, yolo_specs, 1, (3, 416, 416), fuse_batchnorm=True, fusion=False)
+    net.forward(torch.from_numpy(x).to(ctx.torch_device), use_graph=False)
+    worst = 0.0
+    for i in range(len(yolo_specs)):
+        got = net.output(i).cpu().numpy()
+        e = worst_map_err(got, ref[i], maps_of(yolo_specs, (3, 416, 416), i))
+        worst = max(worst, e)
+        assert e <= FP32_TOL, (i, yolo_specs[i]["type"], e)
+    print("worst per-map error over 107 layers:", worst)
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_yolov3_fused_heads(ctx, yolo_specs, batch):
+    x = synth.input_images(3, "yolov3", batch, (3, 416, 416))
+    heads = [82, 94, 106]
+    ref = O.run_network(yolo_specs, x, keep=heads)
+    net = TNNet(ctx, yolo_specs, batch, (3, 416, 416))
+    out = net.predict(x, layers=heads)
+    for h, got in zip(heads, out):
+        assert worst_map_err(got, ref[h], batch * 255) <= FP32_TOL
+        # the same top-k boxes by objectness per image (objectness entries of every anchor)
+        g = int(np.sqrt(got.shape[1] // 255))
+        go = got.reshape(batch, 3, 85, g * g)[:, :, 4].reshape(batch, -1)
+        ro = ref[h].reshape(batch, 3, 85, g * g)[:, :, 4].reshape(batch, -1)
+        k = 20
+        for b in range(batch):
+            top = np.argsort(-ro[b], kind="stable")[:k]
+            assert np.max(np.abs(go[b, top] - ro[b, top])) <= 1e-5
+
+
+def test_yolov3_graph_replay_matches_eager(ctx, yolo_specs):
+    x = torch.from_numpy(synth.input_images(4, "yolov3", 2, (3, 416, 416))).to(ctx.torch_device)
+    net = TNNet(ctx, yolo_specs, 2, (3, 416, 416))
+    net.forward(x, use_graph=False)
+    eager = net.output(106).clone()
+    eager_launches = net.launch_count
+    for _ in range(2):
+        net.forward(x, use_graph=True)
+    assert torch.equal(net.output(106), eager)
+    assert net.launch_count == eager_launches
+    assert net.flops == pytest.approx(2 * 65.864075264e9, rel=1e-9)
+
+
+def test_mnist_config(ctx):
+    specs = synth.mnist_specs()
+    x = synth.input_images(1, "mnist", 256, (1, 28, 28))
+    ref = O.run_network(specs, x, keep=[4, 5, 6])
+    net = TNNet(ctx, specs, 256, (1, 28, 28))
+    out = net.predict(x, layers=[4, 5, 6])
+    for got, i in zip(out, (4, 5, 6)):
+        assert worst_map_err(got, ref[i], 256) <= FP32_TOL, i
+    assert np.array_equal(out[2].argmax(1), ref[6].argmax(1))
+
+
+def test_cifar_config(ctx):
+    specs = synth.cifar_specs()
+    x = synth.input_images(2, "cifar", 64, (3, 32, 32))
+    ref = O.run_network(specs, x, keep=[9, 10, 11])
+    net = TNNet(ctx, specs, 64, (3, 32, 32))
+    out = net.predict(x, layers=[9, 10, 11])
+    assert worst_map_err(out[0], ref[9], 64 * 10) <= FP32_TOL
+    assert worst_map_err(out[1], ref[10], 64) <= FP32_TOL
+    assert np.array_equal(out[2].argmax(1), ref[11].argmax(1))
+
+
+def test_unfused_batchnorm_network(ctx):
+    specs = synth.cifar_specs()
+    x = synth.input_images(2, "cifar", 4, (3, 32, 32))
+    ref = O.run_network(specs, x, fuse_batchnorm=False, keep=[7])
+    net = TNNet(ctx, specs, 4, (3, 32, 32), fuse_batchnorm=False)
+    assert worst_map_err(net.predict(x, layers=[7])[0], ref[7], 4 * 512) <= FP32_TOL
