@@ -85,7 +85,8 @@ int tb_device_count(int64_t* count);
 int tb_init(int64_t device, const tb_options* opts, tb_ctx** out);
 /* Replaces TNNCuda.Destroy. */
 int tb_shutdown(tb_ctx* ctx);
-/* Run subsequent launches on an existing cudaStream_t (NULL = the context's own stream). */
+/* Run subsequent launches on an existing cudaStream_t; NULL selects the legacy default stream.
+ * Until this is called the context launches on a stream of its own. */
 int tb_set_stream(tb_ctx* ctx, void* cuda_stream);
 void* tb_get_stream(tb_ctx* ctx);
 /* Replaces TNNCuda.finish (source/nncuda.pas:1575-1584); also surfaces device status errors. */
@@ -293,7 +294,9 @@ int tb_net_fuse_batchnorm(tb_net* net);
  * head conv), allocate activations and upload packed weights. math_mode: TB_MATH_*. */
 int tb_net_finalize(tb_net* net, int64_t math_mode);
 /* Run the whole network on x (device, [batch][c][h][w]); use_graph != 0 replays a CUDA graph
- * captured on first use. Asynchronous. */
+ * captured on first use (per input pointer). The graph runs on the context's own stream, ordered
+ * after prior work on the launch stream and before later work on it (event fork / join), so it
+ * behaves like an eager forward on the launch stream. Asynchronous. */
 int tb_net_forward(tb_net* net, const float* x, int64_t use_graph);
 /* Device pointer / element count of a layer's output (per batch) and its batch stride. */
 int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* count_per_image,

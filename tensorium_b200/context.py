@@ -8,6 +8,7 @@ torch is used only to own device buffers and to share its current stream, never 
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import torch
 
@@ -23,6 +24,7 @@ class Context:
         check(lib.tb_init(self.device, C.byref(opts), C.byref(self.handle)))
         self.torch_device = torch.device("cuda", self.device)
         self.stream = None
+        self._dependents = weakref.WeakSet()  # objects holding library handles tied to this context
         if use_torch_stream:
             self.set_stream(torch.cuda.current_stream(self.device))
 
@@ -41,8 +43,14 @@ class Context:
     def empty(self, shape, dtype=torch.float32) -> torch.Tensor:
         return torch.empty(shape, dtype=dtype, device=self.torch_device)
 
+    def adopt(self, obj) -> None:
+        """Register an object with a close() that must run before this context shuts down."""
+        self._dependents.add(obj)
+
     def close(self) -> None:
         if self.handle:
+            for d in list(self._dependents):
+                d.close()
             lib.tb_shutdown(self.handle)
             self.handle = C.c_void_p()
 

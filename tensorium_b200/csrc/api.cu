@@ -229,6 +229,8 @@ int tb_init(int64_t device, const tb_options* opts, tb_ctx** out) {
     cudaError_t e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) { delete c; return cuda_fail(e, "cudaStreamCreate"); }
     c->stream = c->own_stream;
+    cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
     e = cudaMalloc(&c->d_status, sizeof(int) * 4);
     if (e != cudaSuccess) { cudaStreamDestroy(c->own_stream); delete c; return cuda_fail(e, "cudaMalloc(status)"); }
     cudaMemset(c->d_status, 0, sizeof(int) * 4);
@@ -247,13 +249,15 @@ int tb_shutdown(tb_ctx* ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->fork) cudaEventDestroy(ctx->fork);
+    if (ctx->join) cudaEventDestroy(ctx->join);
     delete ctx;
     return TB_OK;
 }
 
 int tb_set_stream(tb_ctx* ctx, void* stream) {
     TB_ENTER(ctx);
-    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    ctx->stream = (cudaStream_t)stream;  // NULL: legacy default stream
     return TB_OK;
 }
 

@@ -20,6 +20,7 @@ struct tb_ctx {
     int64_t math_mode = TB_MATH_FP32;
     int sm_count = 148;
     int max_smem_optin = 0;
+    cudaEvent_t fork = nullptr, join = nullptr;  // order own_stream work with `stream`
 };
 
 namespace tbi {

@@ -2,6 +2,8 @@
 // split-K reduction, weight packing and the tb_conv_* entry points.
 #include "conv_fp32_kernel.cuh"
 
+#include <cstdlib>
+
 namespace tbi {
 
 // Sum split-K partials in split order (0 + p0 + p1 + ...) and run the epilogue.
@@ -134,6 +136,17 @@ static TileCfg choose_tiles(const tb_ctx* ctx, const ConvGeom& g, bool x_aligned
         if (splits > maxs) splits = maxs;
         if (splits > 32) splits = 32;
         if (splits < 1) splits = 1;
+    }
+    // test hook: TB_CONV_FORCE="BM,BN,splits" pins the tile configuration (parity tests of
+    // every configuration); unset in normal use
+    if (const char* f = getenv("TB_CONV_FORCE")) {
+        int bm = 0, bn = 0, sp = 0;
+        if (sscanf(f, "%d,%d,%d", &bm, &bn, &sp) == 3 &&
+            ((bm == 128 && bn == 128) || (bm == 64 && bn == 128) || (bm == 64 && bn == 64) || (bm == 32 && bn == 256))) {
+            t.BM = bm; t.BN = bn;
+            t.threads = (bm / (bm == 32 ? 4 : 8)) * (bn / 8);
+            splits = sp < 1 ? 1 : (sp > ktiles ? ktiles : sp);
+        }
     }
     int64_t kps = ceil_div(ktiles, splits);
     splits = ceil_div(ktiles, kps);

@@ -643,26 +643,35 @@ int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
     TB_ENTER(net->ctx);
     if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
     if (!x) return fail(TB_ERR_INVALID, "null input");
-    cudaStream_t s = net->ctx->stream;
+    tb_ctx* ctx = net->ctx;
     if (!use_graph) return run_all(net, x);
-    if (net->exec && net->graph_x == x) {
-        TB_CHECK_CUDA(cudaGraphLaunch(net->exec, s));
-        net->launches = net->graph_launches;
-        return TB_OK;
+    if (!(net->exec && net->graph_x == x)) {
+        // capture on the context's own stream (the launch stream may be the legacy default
+        // stream, which cannot be captured)
+        free_graph(net);
+        cudaStream_t saved = ctx->stream;
+        ctx->stream = ctx->own_stream;
+        cudaError_t e = cudaStreamBeginCapture(ctx->own_stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) { ctx->stream = saved; return cuda_fail(e, "cudaStreamBeginCapture"); }
+        int r = run_all(net, x);
+        cudaGraph_t g = nullptr;
+        e = cudaStreamEndCapture(ctx->own_stream, &g);
+        ctx->stream = saved;
+        if (r != TB_OK) { if (g) cudaGraphDestroy(g); return r; }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+        net->graph = g;
+        e = cudaGraphInstantiate(&net->exec, g, 0);
+        if (e != cudaSuccess) { free_graph(net); return cuda_fail(e, "cudaGraphInstantiate"); }
+        net->graph_x = x;
+        net->graph_launches = net->launches;
     }
-    free_graph(net);
-    TB_CHECK_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    int r = run_all(net, x);
-    cudaGraph_t g = nullptr;
-    cudaError_t e = cudaStreamEndCapture(s, &g);
-    if (r != TB_OK) { if (g) cudaGraphDestroy(g); return r; }
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
-    net->graph = g;
-    e = cudaGraphInstantiate(&net->exec, g, 0);
-    if (e != cudaSuccess) { free_graph(net); return cuda_fail(e, "cudaGraphInstantiate"); }
-    net->graph_x = x;
-    net->graph_launches = net->launches;
-    TB_CHECK_CUDA(cudaGraphLaunch(net->exec, s));
+    // fork from the launch stream, replay, join back
+    TB_CHECK_CUDA(cudaEventRecord(ctx->fork, ctx->stream));
+    TB_CHECK_CUDA(cudaStreamWaitEvent(ctx->own_stream, ctx->fork, 0));
+    TB_CHECK_CUDA(cudaGraphLaunch(net->exec, ctx->own_stream));
+    TB_CHECK_CUDA(cudaEventRecord(ctx->join, ctx->own_stream));
+    TB_CHECK_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->join, 0));
+    net->launches = net->graph_launches;
     return TB_OK;
 }
 

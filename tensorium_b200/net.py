@@ -32,6 +32,7 @@ class TNNet:
         self.handle = C.c_void_p()
         c, h, w = self.input_shape
         check(lib.tb_net_create(ctx.handle, self.batch, c, h, w, C.byref(self.handle)))
+        ctx.adopt(self)
         self.yolo_layers = []
         keep = []
         for i, s in enumerate(specs):
@@ -143,7 +144,7 @@ class TNNet:
         return n.value
 
     def close(self):
-        if self.handle:
+        if self.handle and self.ctx.handle:
             lib.tb_net_destroy(self.handle)
             self.handle = C.c_void_p()
 

@@ -98,7 +98,7 @@ def test_softmax_avgpool_connected(ctx):
     b = rng.standard_normal(1024).astype(np.float32) * 0.1
     fc = TConnectedLayer(256, 1, 3136, 1024, "relu", w, b).bind(ctx)
     yf = fc.forward(TNNetState(dev(ctx, xi))).cpu().numpy()
-    assert max_rel_err(yf, O.connected(xi, w, b, 1)) <= FP32_TOL
+    assert worst_map_err(yf, O.connected(xi, w, b, 1), 256) <= FP32_TOL
 
 
 @pytest.mark.parametrize("C,S,B", [(128, 13, 2), (256, 26, 1), (64, 7, 3), (40, 9, 2)])
