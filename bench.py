@@ -282,6 +282,40 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_layer_mode(args):
+    """Time one YOLOv3 conv layer (index args.layer) at batch args.batch through tb_conv2d_fwd:
+    the small, self-contained case used for ncu captures and per-layer tuning."""
+    import torch
+    from tensorium_b200 import Context, synth
+    from tensorium_b200.layers import TConvolutionalLayer, TNNetState
+    specs = synth.yolov3_specs()
+    shapes = synth.layer_shapes(specs, INPUT)
+    i = args.layer
+    s = specs[i]
+    assert s["type"] == "conv", f"layer {i} is a {s['type']}"
+    c, h, w = shapes[i - 1] if i > 0 else INPUT
+    ctx = Context(0)
+    L = TConvolutionalLayer(args.batch, h, w, c, s["filters"], 1, s["size"], s["stride"], s["stride"], 1,
+                            s["pad"], s["activation"], False).bind(ctx)
+    L.weights = s["weights"]
+    x = torch.rand((args.batch, c, h, w), device=ctx.torch_device)
+    st = TNNetState(x)
+    for _ in range(args.warmup):
+        L.forward(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        L.forward(st)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    oc, oh, ow = shapes[i]
+    flops = 2.0 * oc * oh * ow * c * s["size"] ** 2 * args.batch
+    print(json.dumps({"layer": i, "shape": f"{c}x{h}x{w} -> {oc}x{oh}x{ow} k{s['size']} s{s['stride']}",
+                      "batch": args.batch, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -290,8 +324,11 @@ def main():
     ap.add_argument("--batch", type=int, default=8, help="images per GPU per step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.layer is not None:
+        run_layer_mode(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

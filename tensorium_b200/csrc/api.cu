@@ -234,6 +234,10 @@ int tb_init(int64_t device, const tb_options* opts, tb_ctx** out) {
     e = cudaMalloc(&c->d_status, sizeof(int) * 4);
     if (e != cudaSuccess) { cudaStreamDestroy(c->own_stream); delete c; return cuda_fail(e, "cudaMalloc(status)"); }
     cudaMemset(c->d_status, 0, sizeof(int) * 4);
+    c->tile_cnt_len = 1 << 16;
+    e = cudaMalloc(&c->tile_cnt, sizeof(int) * c->tile_cnt_len);
+    if (e != cudaSuccess) { cudaFree(c->d_status); cudaStreamDestroy(c->own_stream); delete c; return cuda_fail(e, "cudaMalloc(tile counters)"); }
+    cudaMemset(c->tile_cnt, 0, sizeof(int) * c->tile_cnt_len);
     int64_t ws = (opts && opts->workspace_bytes > 0) ? opts->workspace_bytes : (64ll << 20);
     int r = ensure_workspace(c, (size_t)ws);
     if (r != TB_OK) { cudaFree(c->d_status); cudaStreamDestroy(c->own_stream); delete c; return r; }
@@ -248,6 +252,7 @@ int tb_shutdown(tb_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->tile_cnt) cudaFree(ctx->tile_cnt);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->fork) cudaEventDestroy(ctx->fork);
     if (ctx->join) cudaEventDestroy(ctx->join);

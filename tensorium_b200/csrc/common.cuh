@@ -21,6 +21,8 @@ struct tb_ctx {
     int sm_count = 148;
     int max_smem_optin = 0;
     cudaEvent_t fork = nullptr, join = nullptr;  // order own_stream work with `stream`
+    int* tile_cnt = nullptr;                      // split-K arrival counters (zeroed, self-resetting)
+    int64_t tile_cnt_len = 0;
 };
 
 namespace tbi {

@@ -37,6 +37,7 @@ struct ConvParams {
     const float* __restrict__ res;
     float* __restrict__ y;
     float* __restrict__ ws;
+    int* __restrict__ tile_cnt;  // split-K arrival counters, one per output tile, left at 0
     int C, H, W, F, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW, OHW;
     int Cpad, Kpad, Mpad;
     long long x_bs, y_bs, r_bs, Ntot;
@@ -59,7 +60,7 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      float* ws, int64_t ws_floats, int64_t* launches);
 
 // Floats of split-K workspace the FP32 path needs for this geometry (0 if it does not split).
-int64_t conv_fp32_ws_floats(const tb_ctx* ctx, const ConvGeom& g);
+int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g);
 
 // TBaseLayer.batchNorm inference (source/nbaselayer.pas:336-370):
 // (x - mean)/max(sqrt(var), 1e-6) * scale + bias, one rounding per step as the reference.

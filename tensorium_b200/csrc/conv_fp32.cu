@@ -6,35 +6,6 @@
 
 namespace tbi {
 
-// Sum split-K partials in split order (0 + p0 + p1 + ...) and run the epilogue.
-__global__ void conv_splitk_reduce(const ConvParams p) {
-    const long long nq = (p.Ntot + 3) / 4;
-    const long long total = (long long)p.F * nq;
-    const long long plane = (long long)p.F * p.Ntot;
-    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (long long)gridDim.x * blockDim.x) {
-        int m = (int)(idx / nq);
-        long long nb = (idx - (long long)m * nq) * 4;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* src = p.ws + (long long)m * p.Ntot + nb;
-        if ((p.Ntot & 3) == 0) {
-            for (int z = 0; z < p.splits; ++z) {
-                float4 t = *reinterpret_cast<const float4*>(src + z * plane);
-                v[0] = __fadd_rn(v[0], t.x);
-                v[1] = __fadd_rn(v[1], t.y);
-                v[2] = __fadd_rn(v[2], t.z);
-                v[3] = __fadd_rn(v[3], t.w);
-            }
-        } else {
-            for (int z = 0; z < p.splits; ++z)
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    if (nb + q < p.Ntot) v[q] = __fadd_rn(v[q], src[z * plane + q]);
-        }
-        conv_store4(p, m, nb, v);
-    }
-}
-
 __global__ void k_conv_pack(const float* __restrict__ w, float* __restrict__ wp, int F, int C,
                             int KH, int KW, int Cpad, long long Kpad, int Mpad, int rsc) {
     const long long total = Kpad * Mpad;
@@ -105,37 +76,66 @@ int conv_geom(const tb_conv_desc* d, ConvGeom* g) {
 }
 
 struct TileCfg {
-    int BM, BN, threads, splits, kt_per_split;
+    int BM, BN, splits, kt_per_split;
     int mode;
 };
 
-static TileCfg choose_tiles(const tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
-    TileCfg t;
+static int conv_mode_of(const ConvGeom& g, bool x_aligned16) {
+    if (g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 &&
+        (g.OH * g.OW) % 4 == 0 && g.x_bs % 4 == 0 && x_aligned16)
+        return MODE_1X1V;
+    return g.rsc ? MODE_RSC : MODE_CRS;
+}
+
+static int ctas_per_sm(tb_ctx* ctx, int BM, int BN, int mode) {
+    ConvParams dummy{};
+    dim3 q(0, 0, 0);
+    if (BM == 128) return conv_launch_128x128(ctx, dummy, q, mode);
+    if (BM == 64 && BN == 128) return conv_launch_64x128(ctx, dummy, q, mode);
+    if (BM == 64) return conv_launch_64x64(ctx, dummy, q, mode);
+    return conv_launch_32x256(ctx, dummy, q, mode);
+}
+
+// Pick the CTA tile and the K split with a wave-quantisation cost model:
+//   waves(s)  = ceil(tiles * s / (SMs * CTAs per SM))
+//   time      = waves * (per-CTA FMAs of one split) * (CTAs per SM) / (SM FMA rate * tile eff.)
+//             + split-K partial traffic (write + read of s partial planes)
+// Larger tiles reuse operands better (efficiency factor); splitting K fills the last wave.
+static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
+    TileCfg best{};
+    best.mode = conv_mode_of(g, x_aligned16);
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int64_t ktiles = g.Kpad / CONV_BK;
-    const int64_t ohw = g.OH * g.OW;
-    if (g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 &&
-        ohw % 4 == 0 && g.x_bs % 4 == 0 && x_aligned16)
-        t.mode = MODE_1X1V;
-    else
-        t.mode = g.rsc ? MODE_RSC : MODE_CRS;
-    if (M <= 32) { t.BM = 32; t.BN = 256; t.threads = 256; }
-    else if (M <= 64) { t.BM = 64; t.BN = 128; t.threads = 128; }
-    else { t.BM = 128; t.BN = 128; t.threads = 256; }
-    const int64_t sms = ctx->sm_count;
-    int64_t tiles = ceil_div(M, t.BM) * ceil_div(N, t.BN);
-    if (tiles < sms && t.BM >= 64) {
-        int64_t t64 = ceil_div(M, 64) * ceil_div(N, 64);
-        if (t64 > tiles) { t.BM = 64; t.BN = 64; t.threads = 64; tiles = t64; }
-    }
-    int64_t splits = 1;
-    const int64_t target = 2 * sms;
-    if (tiles < target && ktiles >= 8) {
-        splits = ceil_div(target, tiles);
-        int64_t maxs = ktiles / 4;
-        if (splits > maxs) splits = maxs;
-        if (splits > 32) splits = 32;
-        if (splits < 1) splits = 1;
+    struct Cand { int BM, BN; double eff; };
+    const Cand cands[] = {{128, 128, 1.00}, {64, 128, 0.90}, {64, 64, 0.78}, {32, 256, 0.85}};
+    double best_cost = 1e300;
+    for (const Cand& c : cands) {
+        if (M <= 32 && c.BM != 32) continue;           // waste more than half the rows
+        if (M > 32 && M <= 64 && c.BM == 128) continue;
+        if (M > 64 && c.BM == 32) continue;
+        const int64_t tiles = ceil_div(M, c.BM) * ceil_div(N, c.BN);
+        const int occ = ctas_per_sm(ctx, c.BM, c.BN, best.mode);
+        const int64_t slots = (int64_t)ctx->sm_count * occ;
+        // useful fraction of the tile (ragged M / N edges)
+        const double fill = (double)M * (double)N / ((double)ceil_div(M, c.BM) * c.BM * (double)ceil_div(N, c.BN) * c.BN);
+        int64_t smax = ktiles / 4;
+        if (smax > 16) smax = 16;
+        if (smax < 1) smax = 1;
+        if (tiles >= 4 * slots) smax = 1;
+        if (tiles * 1 > (ctx->tile_cnt_len)) smax = 1;
+        for (int64_t sp = 1; sp <= smax; ++sp) {
+            const int64_t kps = ceil_div(ktiles, sp);
+            const int64_t s2 = ceil_div(ktiles, kps);
+            if (s2 != sp) continue;
+            const double waves = (double)ceil_div(tiles * sp, slots);
+            const double cta_cycles = (double)c.BM * c.BN * (double)kps * CONV_BK * occ / (128.0 * c.eff * fill);
+            double cost = waves * cta_cycles + 2000.0;  // + launch / prologue latency per wave
+            if (sp > 1) cost += (double)sp * (double)M * (double)N * 8.0 / 3400.0 + 3000.0;
+            if (cost < best_cost * 0.999) {
+                best_cost = cost;
+                best.BM = c.BM; best.BN = c.BN; best.splits = (int)sp; best.kt_per_split = (int)kps;
+            }
+        }
     }
     // test hook: TB_CONV_FORCE="BM,BN,splits" pins the tile configuration (parity tests of
     // every configuration); unset in normal use
@@ -143,19 +143,17 @@ static TileCfg choose_tiles(const tb_ctx* ctx, const ConvGeom& g, bool x_aligned
         int bm = 0, bn = 0, sp = 0;
         if (sscanf(f, "%d,%d,%d", &bm, &bn, &sp) == 3 &&
             ((bm == 128 && bn == 128) || (bm == 64 && bn == 128) || (bm == 64 && bn == 64) || (bm == 32 && bn == 256))) {
-            t.BM = bm; t.BN = bn;
-            t.threads = (bm / (bm == 32 ? 4 : 8)) * (bn / 8);
-            splits = sp < 1 ? 1 : (sp > ktiles ? ktiles : sp);
+            best.BM = bm; best.BN = bn;
+            int64_t spl = sp < 1 ? 1 : (sp > ktiles ? ktiles : sp);
+            int64_t kps = ceil_div(ktiles, spl);
+            best.kt_per_split = (int)kps;
+            best.splits = (int)ceil_div(ktiles, kps);
         }
     }
-    int64_t kps = ceil_div(ktiles, splits);
-    splits = ceil_div(ktiles, kps);
-    t.splits = (int)splits;
-    t.kt_per_split = (int)kps;
-    return t;
+    return best;
 }
 
-int64_t conv_fp32_ws_floats(const tb_ctx* ctx, const ConvGeom& g) {
+int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g) {
     TileCfg t = choose_tiles(ctx, g, true);
     TileCfg t2 = choose_tiles(ctx, g, false);
     int64_t s = t.splits > t2.splits ? t.splits : t2.splits;
@@ -169,9 +167,9 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      float* ws, int64_t ws_floats, int64_t* launches) {
     if (g.B == 0) return TB_OK;
     TileCfg t = choose_tiles(ctx, g, aligned16(x));
-    ConvParams p;
+    ConvParams p{};
     p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
-    p.res = res; p.y = y; p.ws = nullptr;
+    p.res = res; p.y = y; p.ws = nullptr; p.tile_cnt = ctx->tile_cnt;
     p.C = (int)g.C; p.H = (int)g.H; p.W = (int)g.W; p.F = (int)g.F;
     p.KH = (int)g.KH; p.KW = (int)g.KW; p.SY = (int)g.SY; p.SX = (int)g.SX;
     p.PY = (int)g.PY; p.PX = (int)g.PX; p.DY = (int)g.DY; p.DX = (int)g.DX;
@@ -186,7 +184,12 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     p.yolo_classes = yolo_classes;
     p.vec_out = (p.OHW % 4 == 0 && g.y_bs % 4 == 0 && aligned16(y) &&
                  (!res || (g.r_bs % 4 == 0 && aligned16(res)))) ? 1 : 0;
+    dim3 grid((unsigned)ceil_div(p.Ntot, t.BN), (unsigned)ceil_div(g.F, t.BM), (unsigned)t.splits);
+    if (grid.y > 65535 || grid.z > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     if (t.splits > 1) {
+        if ((int64_t)grid.x * grid.y > ctx->tile_cnt_len)
+            return fail(TB_ERR_INVALID, "conv: %lld split-K tiles exceed the counter array",
+                        (long long)grid.x * grid.y);
         int64_t need = (int64_t)t.splits * g.F * p.Ntot;
         if (ws) {
             if (ws_floats < need) return fail(TB_ERR_INVALID, "conv: scratch of %lld floats too small (need %lld)",
@@ -198,8 +201,6 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
             p.ws = reinterpret_cast<float*>(ctx->ws);
         }
     }
-    dim3 grid((unsigned)ceil_div(p.Ntot, t.BN), (unsigned)ceil_div(g.F, t.BM), (unsigned)t.splits);
-    if (grid.y > 65535 || grid.z > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     int r;
     if (t.BM == 128) r = conv_launch_128x128(ctx, p, grid, t.mode);
     else if (t.BM == 64 && t.BN == 128) r = conv_launch_64x128(ctx, p, grid, t.mode);
@@ -207,13 +208,6 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     else r = conv_launch_32x256(ctx, p, grid, t.mode);
     if (r != TB_OK) return r;
     if (launches) ++*launches;
-    if (t.splits > 1) {
-        int64_t work = (int64_t)g.F * ceil_div(p.Ntot, 4);
-        conv_splitk_reduce<<<grid_for(work, 256, ctx->sm_count, 1), 256, 0, ctx->stream>>>(p);
-        r = check_launch("conv_splitk_reduce");
-        if (r != TB_OK) return r;
-        if (launches) ++*launches;
-    }
     return TB_OK;
 }
 

@@ -224,7 +224,70 @@ conv_fp32_kernel(const ConvParams p) {
     cp_async_wait<0>();
 
     // ---- epilogue ----
-    const bool split = p.splits > 1;
+    if (p.splits > 1) {
+        // split-K: publish this split's partial tile, then the last CTA to arrive on the tile
+        // sums all partials in split order 0..S-1 (deterministic, whatever the arrival order)
+        // and runs the epilogue.  No CTA waits for another.
+        const long long plane = (long long)p.F * p.Ntot;
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            int m = m0 + (i < TM2 ? ty * TM2 + i : BM / 2 + ty * TM2 + (i - TM2));
+            if (m >= p.F) continue;
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                long long nb = n0 + g * (BN / 2) + tx * TN2;
+                if (nb >= p.Ntot) continue;
+                const float* v = &acc[i][g * 4];
+                float* dst = p.ws + blockIdx.z * plane + (long long)m * p.Ntot + nb;
+                if ((p.Ntot & 3) == 0) {
+                    __stcg(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (nb + q < p.Ntot) __stcg(dst + q, v[q]);
+                }
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        __shared__ int s_last;
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        if (tid == 0) {
+            int prev = atomicAdd(&p.tile_cnt[tile], 1);
+            s_last = (prev == p.splits - 1);
+            if (s_last) p.tile_cnt[tile] = 0;  // ready for the next launch
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            int m = m0 + (i < TM2 ? ty * TM2 + i : BM / 2 + ty * TM2 + (i - TM2));
+            if (m >= p.F) continue;
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                long long nb = n0 + g * (BN / 2) + tx * TN2;
+                if (nb >= p.Ntot) continue;
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                const float* src = p.ws + (long long)m * p.Ntot + nb;
+                for (int z = 0; z < p.splits; ++z) {
+                    if ((p.Ntot & 3) == 0) {
+                        float4 t = __ldcg(reinterpret_cast<const float4*>(src + z * plane));
+                        v[0] = __fadd_rn(v[0], t.x);
+                        v[1] = __fadd_rn(v[1], t.y);
+                        v[2] = __fadd_rn(v[2], t.z);
+                        v[3] = __fadd_rn(v[3], t.w);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            if (nb + q < p.Ntot) v[q] = __fadd_rn(v[q], __ldcg(src + z * plane + q));
+                    }
+                }
+                conv_store4(p, m, nb, v);
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         int m = m0 + (i < TM2 ? ty * TM2 + i : BM / 2 + ty * TM2 + (i - TM2));
@@ -233,21 +296,24 @@ conv_fp32_kernel(const ConvParams p) {
         for (int g = 0; g < 2; ++g) {
             long long nb = n0 + g * (BN / 2) + tx * TN2;
             if (nb >= p.Ntot) continue;
-            const float* v = &acc[i][g * 4];
-            if (split) {
-                float* dst = p.ws + ((long long)blockIdx.z * p.F + m) * p.Ntot + nb;
-                if ((p.Ntot & 3) == 0) {
-                    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (nb + q < p.Ntot) dst[q] = v[q];
-                }
-            } else {
-                conv_store4(p, m, nb, v);
-            }
+            conv_store4(p, m, nb, &acc[i][g * 4]);
         }
     }
+}
+
+// CTAs of this configuration resident per SM (registers / shared memory), cached per device
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+int conv_ctas_per_sm(tb_ctx* ctx) {
+    static int cache[64] = {0};
+    if (ctx->device < 64 && cache[ctx->device]) return cache[ctx->device];
+    constexpr int NT = (BM / TM) * (BN / TN);
+    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE);
+    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NT, smem) != cudaSuccess || n < 1) n = 1;
+    if (ctx->device < 64) cache[ctx->device] = n;
+    return n;
 }
 
 template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
@@ -270,6 +336,15 @@ int conv_launch_cfg(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
 }
 
 template <int BM, int BN, int TM, int TN, int STAGES>
+int conv_occupancy_modes(tb_ctx* ctx, int mode) {
+    switch (mode) {
+    case MODE_CRS: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_CRS>(ctx);
+    case MODE_RSC: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_RSC>(ctx);
+    default: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_1X1V>(ctx);
+    }
+}
+
+template <int BM, int BN, int TM, int TN, int STAGES>
 int conv_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
     switch (mode) {
     case MODE_CRS: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_CRS>(ctx, p, grid);
@@ -278,7 +353,8 @@ int conv_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
     }
 }
 
-// one entry per tile configuration, each compiled in its own translation unit
+// one entry per tile configuration, each compiled in its own translation unit;
+// launch (grid.x > 0) or, with grid.x == 0, return the resident CTAs per SM
 int conv_launch_128x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
 int conv_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);
 int conv_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode);

@@ -4,6 +4,7 @@
 
 namespace tbi {
 int conv_launch_32x256(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
+    if (grid.x == 0) return conv_occupancy_modes<32, 256, 4, 8, 4>(ctx, mode);
     return conv_launch_modes<32, 256, 4, 8, 4>(ctx, p, grid, mode);
 }
 }  // namespace tbi

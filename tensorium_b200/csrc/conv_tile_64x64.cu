@@ -4,6 +4,7 @@
 
 namespace tbi {
 int conv_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
+    if (grid.x == 0) return conv_occupancy_modes<64, 64, 8, 8, 4>(ctx, mode);
     return conv_launch_modes<64, 64, 8, 8, 4>(ctx, p, grid, mode);
 }
 }  // namespace tbi

@@ -36,6 +36,26 @@ def worst_map_err(a, b, maps):
     return max(max_rel_err(a[i], b[i]) for i in range(maps))
 
 
+def yolo_err(got, ref, raw_ref, n, classes):
+    """Worst error of a yolo output relative to what the FP32 tolerance allows.  Entries 2,3
+    (w, h) are raw conv values: per-map relative error / FP32_TOL.  The other entries are
+    logistic(x): |d logistic| <= |dx|/4, so the allowed error of a map is
+    FP32_TOL * max|raw map| / 4 (plus one ulp of 1).  Returns a ratio; <= 1 passes."""
+    B = got.shape[0]
+    g = got.reshape(B, n, classes + 5, -1).astype(np.float64)
+    r = ref.reshape(B, n, classes + 5, -1).astype(np.float64)
+    x = raw_ref.reshape(B, n, classes + 5, -1).astype(np.float64)
+    worst = 0.0
+    for b in range(B):
+        for a in range(n):
+            for e in range(classes + 5):
+                d = np.max(np.abs(g[b, a, e] - r[b, a, e]))
+                scale = np.max(np.abs(x[b, a, e]))
+                allow = FP32_TOL * scale if e in (2, 3) else FP32_TOL * scale / 4 + 2 ** -23
+                worst = max(worst, d / max(allow, 1e-30))
+    return worst
+
+
 FP32_TOL = 1e-4  # BASELINE north star: max relative error per activation map, FP32 path
 
 

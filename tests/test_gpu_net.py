@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import FP32_TOL, worst_map_err
+from conftest import FP32_TOL, worst_map_err, yolo_err
 from oracle import oracle as O
 from tensorium_b200 import synth
 from tensorium_b200.net import TNNet
@@ -29,29 +29,37 @@ def test_yolov3_every_layer_unfused_plan(ctx, yolo_specs):
     worst = 0.0
     for i in range(len(yolo_specs)):
         got = net.output(i).cpu().numpy()
+        if yolo_specs[i]["type"] == "yolo":
+            assert yolo_err(got, ref[i], ref[i - 1], 3, 80) <= 1.0, i
+            continue
         e = worst_map_err(got, ref[i], maps_of(yolo_specs, (3, 416, 416), i))
         worst = max(worst, e)
         assert e <= FP32_TOL, (i, yolo_specs[i]["type"], e)
-    print("worst per-map error over 107 layers:", worst)
+    print("worst per-map relative error over the non-yolo layers:", worst)
 
 
 @pytest.mark.parametrize("batch", [1, 2])
-def test_yolov3_fused_heads(ctx, yolo_specs, batch):
+def test_yolov3_fused_heads_and_detections(ctx, yolo_specs, batch):
     x = synth.input_images(3, "yolov3", batch, (3, 416, 416))
-    heads = [82, 94, 106]
-    ref = O.run_network(yolo_specs, x, keep=heads)
+    heads, raws = [82, 94, 106], [81, 93, 105]
+    ref = O.run_network(yolo_specs, x, keep=heads + raws)
     net = TNNet(ctx, yolo_specs, batch, (3, 416, 416))
     out = net.predict(x, layers=heads)
-    for h, got in zip(heads, out):
-        assert worst_map_err(got, ref[h], batch * 255) <= FP32_TOL
-        # the same top-k boxes by objectness per image (objectness entries of every anchor)
+    thresh = 0.45
+    logit = np.log(thresh / (1 - thresh))
+    for h, r, got in zip(heads, raws, out):
+        assert yolo_err(got, ref[h], ref[r], 3, 80) <= 1.0, h
+        # the detection index set (objectness > thresh) matches, except candidates whose raw
+        # objectness lies within the FP32 tolerance band around logit(thresh)
         g = int(np.sqrt(got.shape[1] // 255))
-        go = got.reshape(batch, 3, 85, g * g)[:, :, 4].reshape(batch, -1)
-        ro = ref[h].reshape(batch, 3, 85, g * g)[:, :, 4].reshape(batch, -1)
-        k = 20
-        for b in range(batch):
-            top = np.argsort(-ro[b], kind="stable")[:k]
-            assert np.max(np.abs(go[b, top] - ro[b, top])) <= 1e-5
+        go = got.reshape(batch, 3, 85, g * g)[:, :, 4]
+        ro = ref[h].reshape(batch, 3, 85, g * g)[:, :, 4]
+        xo = ref[r].reshape(batch, 3, 85, g * g)
+        band = FP32_TOL * np.abs(xo).max(axis=3)[:, :, 4:5]
+        sure = np.abs(xo[:, :, 4] - logit) > band
+        assert np.array_equal((go > thresh)[sure], (ro > thresh)[sure])
+    recs, probs, counts = net.detections(416, 416, thresh, capacity=16384)
+    assert counts.shape == (batch,) and np.all(counts > 0)
 
 
 def test_yolov3_graph_replay_matches_eager(ctx, yolo_specs):
