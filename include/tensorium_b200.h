@@ -161,6 +161,19 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
                   const float* bias, const float* bn_scale, const float* bn_mean,
                   const float* bn_variance, const float* residual, float* y, int64_t math_mode);
 
+/* tb_conv2d_fwd without any device allocation, for callers that cannot call cudaMalloc
+ * (device memory handed out up front by an arena, an allocator held by another component, or
+ * a loop where an allocation's latency or failure is not acceptable). No counterpart in the
+ * reference. Same arguments and results as tb_conv2d_fwd with the FP32 mainloop; the split-K
+ * scratch is a fixed array inside the library (16 MiB of partial sums + 16384 tile counters,
+ * held on every GPU that loads the library until exit). A layer whose split needs more scratch
+ * than that is rejected with TB_ERR_INVALID. The first call on a device looks up the array's
+ * device address; make that first call before any stream capture. All calls share the one
+ * array: calls that overlap on the GPU (other streams, other contexts on the same device) race. */
+int tb_conv2d_fwd_noalloc(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w,
+                          const float* bias, const float* bn_scale, const float* bn_mean,
+                          const float* bn_variance, const float* residual, float* y);
+
 /* ---- memory-bound layers -------------------------------------------------------------- */
 /* TNNCuda.forwardMaxPool (source/nncuda.pas:132; CPU semantics source/nMaxPoolLayer.pas:
  * 265-463): out = max over the k x k window at (i*stride_y + n - padding div 2,

@@ -93,6 +93,7 @@ SIGNATURES = {
     "tb_conv_pack_weights": [P, C.POINTER(ConvDesc), P, P],
     "tb_conv_fold_bn": [I64, I64, P, P, P, P, P],
     "tb_conv2d_fwd": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P, I64],
+    "tb_conv2d_fwd_noalloc": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P],
     "tb_maxpool_fwd": [P, I64, I64, I64, I64, I64, I64, I64, I64, P, P, P],
     "tb_upsample_fwd": [P, I64, I64, I64, I64, I64, F32, P, P, I64],
     "tb_route_fwd": [P, I64, I64, P, P, P, I64],

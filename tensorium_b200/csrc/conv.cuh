@@ -54,10 +54,14 @@ int conv_geom(const tb_conv_desc* d, ConvGeom* g);
 
 // Launch the conv (FP32 SIMT mainloop) with the given epilogue settings.
 // ws / ws_floats: split-K partial buffer (nullptr = use the context workspace).
+// tile_cnt: split-K arrival counters (nullptr = the context's); tile_cnt_len entries.
 int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
                      const float* bias, const float* bn_scale, const float* bn_mean,
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
-                     float* ws, int64_t ws_floats, int64_t* launches);
+                     float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt = nullptr,
+                     int64_t tile_cnt_len = 0);
+// Split-K partial floats this call would need (0 when it does not split), for a given x.
+int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x);
 
 // Floats of split-K workspace the FP32 path needs for this geometry (0 if it does not split).
 int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g);

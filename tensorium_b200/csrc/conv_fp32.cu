@@ -161,15 +161,23 @@ int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g) {
     return s * g.F * g.B * g.OH * g.OW;
 }
 
+int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x) {
+    TileCfg t = choose_tiles(ctx, g, aligned16(x));
+    return t.splits > 1 ? (int64_t)t.splits * g.F * g.B * g.OH * g.OW : 0;
+}
+
 int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
                      const float* bias, const float* bn_scale, const float* bn_mean,
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
-                     float* ws, int64_t ws_floats, int64_t* launches) {
+                     float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
+                     int64_t tile_cnt_len) {
     if (g.B == 0) return TB_OK;
     TileCfg t = choose_tiles(ctx, g, aligned16(x));
     ConvParams p{};
     p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
-    p.res = res; p.y = y; p.ws = nullptr; p.tile_cnt = ctx->tile_cnt;
+    p.res = res; p.y = y; p.ws = nullptr;
+    p.tile_cnt = tile_cnt ? tile_cnt : ctx->tile_cnt;
+    const int64_t cnt_len = tile_cnt ? tile_cnt_len : ctx->tile_cnt_len;
     p.C = (int)g.C; p.H = (int)g.H; p.W = (int)g.W; p.F = (int)g.F;
     p.KH = (int)g.KH; p.KW = (int)g.KW; p.SY = (int)g.SY; p.SX = (int)g.SX;
     p.PY = (int)g.PY; p.PX = (int)g.PX; p.DY = (int)g.DY; p.DX = (int)g.DX;
@@ -187,7 +195,7 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     dim3 grid((unsigned)ceil_div(p.Ntot, t.BN), (unsigned)ceil_div(g.F, t.BM), (unsigned)t.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     if (t.splits > 1) {
-        if ((int64_t)grid.x * grid.y > ctx->tile_cnt_len)
+        if ((int64_t)grid.x * grid.y > cnt_len)
             return fail(TB_ERR_INVALID, "conv: %lld split-K tiles exceed the counter array",
                         (long long)grid.x * grid.y);
         int64_t need = (int64_t)t.splits * g.F * p.Ntot;
