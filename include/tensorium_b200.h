@@ -147,6 +147,11 @@ int tb_conv_pack_weights(tb_ctx* ctx, const tb_conv_desc* d, const float* weight
 int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights_host, float* biases_host,
                     const float* scales_host, const float* rolling_mean_host,
                     const float* rolling_variance_host);
+/* Time the admissible CTA-tile / split-K choices of this geometry on the given buffers (y is
+ * overwritten) and use the fastest for every later call with the same geometry on this device.
+ * Optional: without it a cost model chooses. Blocks; may grow the workspace. (The reference has
+ * no tuning step; its GPU conv is a fixed cuBLAS call, source/nncuda.pas:846.) */
+int tb_conv_autotune(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y);
 /* Fused conv forward: y = act(conv(x, w) + epilogue) [+ residual].
  * Replaces, in one launch (two with split-K), the reference sequence
  *   cuda.im2col per image -> cuda.gemmStridedBatched -> [normalize, forwardScale] ->

@@ -209,6 +209,42 @@ def xnor_conv(x, w, mean, filters, size, stride, pad, pad_mode=0):
 
 
 # ---- whole network ----------------------------------------------------------------------
+def _src(i, rel):
+    return i + rel if rel < 0 else rel
+
+
+def run_layer(specs, i, prev, get, fuse_batchnorm=True):
+    """Output of layer i (NCHW) given its input `prev` and get(j) = output of layer j."""
+    s = specs[i]
+    t = s["type"]
+    if t == "conv":
+        w, b = s["weights"], s["biases"]
+        bn = None
+        if s["batch_normalize"]:
+            if fuse_batchnorm:
+                w, b = fuse_bn(w, b, s["scales"], s["mean"], s["var"])
+            else:
+                bn = (s["scales"], s["mean"], s["var"])
+        return conv2d(prev, w, b, s["filters"], s["size"], s["stride"], s["pad"], s["activation"], bn)
+    if t == "shortcut":
+        return shortcut(prev, get(_src(i, s["from"])), s.get("activation", 4))
+    if t == "route":
+        return np.concatenate([get(_src(i, l)) for l in s["layers"]], axis=1)
+    if t == "upsample":
+        return upsample(prev, s["stride"], s.get("scale", 1.0))
+    if t == "yolo":
+        return yolo(prev, len(s["mask"]), s["classes"], s.get("scale_xy", 1.0))
+    if t == "maxpool":
+        return maxpool(prev, s["size"], s["stride"], s.get("padding", 0))
+    if t == "connected":
+        return connected(prev, s["weights"], s["biases"], s["activation"])[:, :, None, None]
+    if t == "softmax":
+        return softmax(prev, s.get("groups", 1), s.get("temperature", 1.0)).reshape(prev.shape)
+    if t == "avgpool":
+        return avgpool(prev)[:, :, None, None]
+    raise ValueError(t)
+
+
 def run_network(specs, x, fuse_batchnorm=True, keep=None):
     """{layer: output [B, per_image]} for every layer (or the indices in `keep`)."""
     x = f32(x)
@@ -221,41 +257,12 @@ def run_network(specs, x, fuse_batchnorm=True, keep=None):
     needed = set()
     for i, s in enumerate(specs):
         if s["type"] == "route":
-            needed.update(i + l if l < 0 else l for l in s["layers"])
+            needed.update(_src(i, l) for l in s["layers"])
         if s["type"] == "shortcut":
-            needed.add(i + s["from"] if s["from"] < 0 else s["from"])
+            needed.add(_src(i, s["from"]))
     store = {}
-    for i, s in enumerate(specs):
-        t = s["type"]
-        if t == "conv":
-            w, b = s["weights"], s["biases"]
-            bn = None
-            if s["batch_normalize"]:
-                if fuse_batchnorm:
-                    w, b = fuse_bn(w, b, s["scales"], s["mean"], s["var"])
-                else:
-                    bn = (s["scales"], s["mean"], s["var"])
-            y = conv2d(prev, w, b, s["filters"], s["size"], s["stride"], s["pad"], s["activation"], bn)
-        elif t == "shortcut":
-            j = i + s["from"] if s["from"] < 0 else s["from"]
-            y = shortcut(prev, store[j], s.get("activation", 4))
-        elif t == "route":
-            idx = [i + l if l < 0 else l for l in s["layers"]]
-            y = np.concatenate([store[j] for j in idx], axis=1)
-        elif t == "upsample":
-            y = upsample(prev, s["stride"], s.get("scale", 1.0))
-        elif t == "yolo":
-            y = yolo(prev, len(s["mask"]), s["classes"], s.get("scale_xy", 1.0))
-        elif t == "maxpool":
-            y = maxpool(prev, s["size"], s["stride"], s.get("padding", 0))
-        elif t == "connected":
-            y = connected(prev, s["weights"], s["biases"], s["activation"])[:, :, None, None]
-        elif t == "softmax":
-            y = softmax(prev, s.get("groups", 1), s.get("temperature", 1.0)).reshape(prev.shape)
-        elif t == "avgpool":
-            y = avgpool(prev)[:, :, None, None]
-        else:
-            raise ValueError(t)
+    for i in range(len(specs)):
+        y = run_layer(specs, i, prev, store.__getitem__, fuse_batchnorm)
         if i in needed:
             store[i] = y
         if i in keep_set:

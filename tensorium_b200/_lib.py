@@ -92,6 +92,7 @@ SIGNATURES = {
     "tb_conv_packed_weights_count": [C.POINTER(ConvDesc), PI64],
     "tb_conv_pack_weights": [P, C.POINTER(ConvDesc), P, P],
     "tb_conv_fold_bn": [I64, I64, P, P, P, P, P],
+    "tb_conv_autotune": [P, C.POINTER(ConvDesc), P, P, P],
     "tb_conv2d_fwd": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P, I64],
     "tb_conv2d_fwd_noalloc": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P],
     "tb_maxpool_fwd": [P, I64, I64, I64, I64, I64, I64, I64, I64, P, P, P],

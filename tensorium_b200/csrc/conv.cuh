@@ -60,6 +60,8 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt = nullptr,
                      int64_t tile_cnt_len = 0);
+// Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
+int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // Split-K partial floats this call would need (0 when it does not split), for a given x.
 int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x);
 

@@ -2,7 +2,11 @@
 // split-K reduction, weight packing and the tb_conv_* entry points.
 #include "conv_fp32_kernel.cuh"
 
+#include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <vector>
 
 namespace tbi {
 
@@ -58,7 +62,8 @@ int conv_geom(const tb_conv_desc* d, ConvGeom* g) {
     if (r.x_bs < r.C * r.H * r.W || r.y_bs < r.F * r.OH * r.OW || r.r_bs < r.F * r.OH * r.OW)
         return fail(TB_ERR_INVALID, "conv: batch stride smaller than one image");
     const int64_t lim = (int64_t)1 << 31;
-    if (r.C * r.H * r.W >= lim || r.F * r.OH * r.OW >= lim || r.B * r.OH * r.OW >= ((int64_t)1 << 40))
+    if (r.C * r.H * r.W >= lim || r.F * r.OH * r.OW >= lim || r.B * r.OH * r.OW >= lim ||
+        (r.B - 1) * std::max(r.x_bs, std::max(r.y_bs, r.r_bs)) >= lim * 64)
         return fail(TB_ERR_INVALID, "conv: tensor too large for this build");
     r.rsc = conv_is_rsc(r.C, r.KH, r.KW);
     if (r.rsc) {
@@ -101,9 +106,23 @@ static int ctas_per_sm(tb_ctx* ctx, int BM, int BN, int mode) {
 //   time      = waves * (per-CTA FMAs of one split) * (CTAs per SM) / (SM FMA rate * tile eff.)
 //             + split-K partial traffic (write + read of s partial planes)
 // Larger tiles reuse operands better (efficiency factor); splitting K fills the last wave.
+// Measured choices (conv_fp32_autotune), per device and geometry.
+static std::mutex g_tune_mu;
+static std::map<std::vector<int64_t>, TileCfg> g_tuned;
+
+static std::vector<int64_t> tune_key(const tb_ctx* ctx, const ConvGeom& g, int mode) {
+    return {ctx->device, g.B, g.C, g.H, g.W, g.F, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX,
+            g.x_bs, g.y_bs, mode};
+}
+
 static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
     TileCfg best{};
     best.mode = conv_mode_of(g, x_aligned16);
+    if (!getenv("TB_CONV_FORCE")) {
+        std::lock_guard<std::mutex> lk(g_tune_mu);
+        auto it = g_tuned.find(tune_key(ctx, g, best.mode));
+        if (it != g_tuned.end()) return it->second;
+    }
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int64_t ktiles = g.Kpad / CONV_BK;
     struct Cand { int BM, BN; double eff; };
@@ -166,13 +185,11 @@ int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x) 
     return t.splits > 1 ? (int64_t)t.splits * g.F * g.B * g.OH * g.OW : 0;
 }
 
-int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
-                     const float* bias, const float* bn_scale, const float* bn_mean,
-                     const float* bn_var, const float* res, float* y, int act, int yolo_classes,
-                     float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
-                     int64_t tile_cnt_len) {
-    if (g.B == 0) return TB_OK;
-    TileCfg t = choose_tiles(ctx, g, aligned16(x));
+static int launch_with(tb_ctx* ctx, const ConvGeom& g, const TileCfg& t, const float* x, const float* wp,
+                       const float* bias, const float* bn_scale, const float* bn_mean,
+                       const float* bn_var, const float* res, float* y, int act, int yolo_classes,
+                       float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
+                       int64_t tile_cnt_len) {
     ConvParams p{};
     p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
     p.res = res; p.y = y; p.ws = nullptr;
@@ -216,6 +233,85 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     else r = conv_launch_32x256(ctx, p, grid, t.mode);
     if (r != TB_OK) return r;
     if (launches) ++*launches;
+    return TB_OK;
+}
+
+int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp,
+                     const float* bias, const float* bn_scale, const float* bn_mean,
+                     const float* bn_var, const float* res, float* y, int act, int yolo_classes,
+                     float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
+                     int64_t tile_cnt_len) {
+    if (g.B == 0) return TB_OK;
+    TileCfg t = choose_tiles(ctx, g, aligned16(x));
+    return launch_with(ctx, g, t, x, wp, bias, bn_scale, bn_mean, bn_var, res, y, act, yolo_classes,
+                       ws, ws_floats, launches, tile_cnt, tile_cnt_len);
+}
+
+// Time every admissible (tile, split) of this geometry on the given buffers and remember the
+// fastest; later launches of the same geometry use it.  Blocks; allocates the workspace the
+// candidates need (not during stream capture).
+int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y) {
+    if (g.B == 0) return TB_OK;
+    const int mode = conv_mode_of(g, aligned16(x));
+    const int64_t M = g.F, N = g.B * g.OH * g.OW;
+    const int64_t ktiles = g.Kpad / CONV_BK;
+    const int cfgs[4][2] = {{128, 128}, {64, 128}, {64, 64}, {32, 256}};
+    const int split_list[] = {1, 2, 3, 4, 6, 8, 12, 16};
+    std::vector<TileCfg> cands;
+    for (auto& c : cfgs) {
+        if (M <= 32 && c[0] != 32) continue;
+        if (M > 64 && c[0] == 32) continue;
+        const int64_t tiles = ceil_div(M, c[0]) * ceil_div(N, c[1]);
+        for (int sp : split_list) {
+            if (sp > 1 && (sp > ktiles / 2 || tiles > ctx->tile_cnt_len || tiles * sp > 64 * (int64_t)ctx->sm_count))
+                continue;
+            const int64_t kps = ceil_div(ktiles, sp);
+            if (ceil_div(ktiles, kps) != sp) continue;
+            if ((int64_t)sp * M * N * 4 > ((int64_t)512 << 20)) continue;  // 512 MiB scratch cap
+            TileCfg t;
+            t.BM = c[0]; t.BN = c[1]; t.splits = sp; t.kt_per_split = (int)kps; t.mode = mode;
+            cands.push_back(t);
+        }
+    }
+    if (cands.empty()) return TB_OK;
+    int64_t ws_need = 0;
+    for (auto& t : cands)
+        if (t.splits > 1) ws_need = std::max<int64_t>(ws_need, (int64_t)t.splits * M * N);
+    if (ws_need) {
+        int r = ensure_workspace(ctx, (size_t)ws_need * 4);
+        if (r != TB_OK) return r;
+    }
+    cudaEvent_t e0, e1;
+    TB_CHECK_CUDA(cudaEventCreate(&e0));
+    TB_CHECK_CUDA(cudaEventCreate(&e1));
+    float best_ms = 1e30f;
+    TileCfg best = cands[0];
+    int rc = TB_OK;
+    for (auto& t : cands) {
+        rc = launch_with(ctx, g, t, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR,
+                         0, nullptr, 0, nullptr, nullptr, 0);  // warm-up
+        if (rc != TB_OK) break;
+        cudaEventRecord(e0, ctx->stream);
+        for (int rep = 0; rep < 3 && rc == TB_OK; ++rep)
+            rc = launch_with(ctx, g, t, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR,
+                             0, nullptr, 0, nullptr, nullptr, 0);
+        cudaEventRecord(e1, ctx->stream);
+        cudaError_t e = cudaEventSynchronize(e1);
+        if (rc != TB_OK) break;
+        if (e != cudaSuccess) { rc = cuda_fail(e, "autotune"); break; }
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (getenv("TB_AUTOTUNE_VERBOSE"))
+            fprintf(stderr, "autotune C%lld H%lld F%lld k%lld s%lld B%lld: %dx%d split %d mode %d: %.4f ms\n",
+                    (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
+                    (long long)g.B, t.BM, t.BN, t.splits, t.mode, ms / 3);
+        if (ms < best_ms) { best_ms = ms; best = t; }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc != TB_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_tune_mu);
+    g_tuned[tune_key(ctx, g, mode)] = best;
     return TB_OK;
 }
 
@@ -270,6 +366,15 @@ int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights, float*
         for (int64_t i = 0; i < filter_size; ++i) w[i] = w[i] * pre;
     }
     return TB_OK;
+}
+
+int tb_conv_autotune(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!x || !packed_w || !y) return fail(TB_ERR_INVALID, "conv autotune: null pointer");
+    return conv_fp32_autotune(ctx, g, x, packed_w, y);
 }
 
 int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w,

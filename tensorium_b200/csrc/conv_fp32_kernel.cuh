@@ -40,35 +40,50 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-// Store 4 consecutive outputs (n = nb .. nb+3) of row m after the epilogue.
-__device__ __forceinline__ void conv_store4(const ConvParams& p, int m, long long nb, const float* v) {
-    if (p.vec_out && nb + 3 < p.Ntot) {
-        long long b = nb / p.OHW;
-        int pix = (int)(nb - b * p.OHW);
+// Output column quad n = nb .. nb+3 decoded once per thread: image b and pixel pix of nb.
+struct ColQuad {
+    int b, pix, nvalid;  // nvalid = how many of the 4 columns exist (0..4)
+};
+
+__device__ __forceinline__ ColQuad decode_quad(const ConvParams& p, long long nb) {
+    ColQuad q;
+    long long rem = p.Ntot - nb;
+    q.nvalid = rem <= 0 ? 0 : (rem >= 4 ? 4 : (int)rem);
+    if (q.nvalid == 0) { q.b = 0; q.pix = 0; return q; }
+    unsigned n = (unsigned)nb;  // Ntot < 2^31 (checked on the host)
+    q.b = (int)(n / (unsigned)p.OHW);
+    q.pix = (int)(n - (unsigned)q.b * (unsigned)p.OHW);
+    return q;
+}
+
+// Store the 4 outputs of column quad q in row m after the epilogue.
+__device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const ColQuad& q, const float* v) {
+    if (q.nvalid == 0) return;
+    if (p.vec_out && q.nvalid == 4) {  // OHW % 4 == 0: the quad lies in one image, 16-byte aligned
         float4 o;
         o.x = conv_epilogue(v[0], m, p);
         o.y = conv_epilogue(v[1], m, p);
         o.z = conv_epilogue(v[2], m, p);
         o.w = conv_epilogue(v[3], m, p);
+        const long long off = (long long)m * p.OHW + q.pix;
         if (p.res) {
-            float4 r = *reinterpret_cast<const float4*>(p.res + b * p.r_bs + (long long)m * p.OHW + pix);
+            float4 r = *reinterpret_cast<const float4*>(p.res + q.b * p.r_bs + off);
             o.x = __fadd_rn(o.x, r.x);
             o.y = __fadd_rn(o.y, r.y);
             o.z = __fadd_rn(o.z, r.z);
             o.w = __fadd_rn(o.w, r.w);
         }
-        *reinterpret_cast<float4*>(p.y + b * p.y_bs + (long long)m * p.OHW + pix) = o;
-    } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            long long n = nb + q;
-            if (n >= p.Ntot) break;
-            long long b = n / p.OHW;
-            int pix = (int)(n - b * p.OHW);
-            float o = conv_epilogue(v[q], m, p);
-            if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + (long long)m * p.OHW + pix]);
-            p.y[b * p.y_bs + (long long)m * p.OHW + pix] = o;
-        }
+        *reinterpret_cast<float4*>(p.y + q.b * p.y_bs + off) = o;
+        return;
+    }
+    int b = q.b, pix = q.pix;
+    for (int k = 0; k < q.nvalid; ++k) {
+        while (pix >= p.OHW) { pix -= p.OHW; ++b; }
+        const long long off = (long long)m * p.OHW + pix;
+        float o = conv_epilogue(v[k], m, p);
+        if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + off]);
+        p.y[b * p.y_bs + off] = o;
+        ++pix;
     }
 }
 
@@ -224,6 +239,7 @@ conv_fp32_kernel(const ConvParams p) {
     cp_async_wait<0>();
 
     // ---- epilogue ----
+    const ColQuad cq[2] = {decode_quad(p, n0 + tx * TN2), decode_quad(p, n0 + BN / 2 + tx * TN2)};
     if (p.splits > 1) {
         // split-K: publish this split's partial tile, then the last CTA to arrive on the tile
         // sums all partials in split order 0..S-1 (deterministic, whatever the arrival order)
@@ -283,7 +299,7 @@ conv_fp32_kernel(const ConvParams p) {
                             if (nb + q < p.Ntot) v[q] = __fadd_rn(v[q], __ldcg(src + z * plane + q));
                     }
                 }
-                conv_store4(p, m, nb, v);
+                conv_store4(p, m, cq[g], v);
             }
         }
         return;
@@ -296,7 +312,7 @@ conv_fp32_kernel(const ConvParams p) {
         for (int g = 0; g < 2; ++g) {
             long long nb = n0 + g * (BN / 2) + tx * TN2;
             if (nb >= p.Ntot) continue;
-            conv_store4(p, m, nb, &acc[i][g * 4]);
+            conv_store4(p, m, cq[g], &acc[i][g * 4]);
         }
     }
 }

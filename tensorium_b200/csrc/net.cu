@@ -13,6 +13,7 @@
 #include "conv.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <memory>
 #include <vector>
 
@@ -630,6 +631,37 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         }
         ws_floats = std::max(ws_floats, conv_fp32_ws_floats(net->ctx, g));
         net->flops += 2.0 * (double)g.F * (double)(g.B * g.OH * g.OW) * (double)(g.C * g.KH * g.KW);
+    }
+    // 4. measure the tile / split choices of every conv geometry on the real buffers
+    //    (TB_AUTOTUNE=0 keeps the cost model)
+    const char* at = getenv("TB_AUTOTUNE");
+    if (!(at && at[0] == '0')) {
+        for (int64_t i = 0; i < n; ++i) {
+            Layer& L = *net->layers[i];
+            if (L.type != TB_LAYER_CONV && L.type != TB_LAYER_CONNECTED) continue;
+            tb_conv_desc d;
+            desc_of(net, L, &d);
+            View in;
+            float* tmp = nullptr;
+            if (i == 0) {  // the network input is not known yet: tune on a zeroed stand-in
+                in.bs = net->c * net->h * net->w;
+                TB_CHECK_CUDA(cudaMalloc(&tmp, (size_t)(B * in.bs) * sizeof(float)));
+                cudaMemset(tmp, 0, (size_t)(B * in.bs) * sizeof(float));
+                in.ptr = tmp;
+            } else {
+                in = net->layers[i - 1]->out;
+            }
+            const Layer& T = *net->layers[L.target];
+            d.in_batch_stride = in.bs;
+            d.out_batch_stride = T.out.bs;
+            ConvGeom g;
+            r = conv_geom(&d, &g);
+            if (r != TB_OK) return r;
+            r = conv_fp32_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr);
+            if (r == TB_OK) ws_floats = std::max(ws_floats, conv_fp32_ws_floats_for(net->ctx, g, in.ptr));
+            if (tmp) cudaFree(tmp);
+            if (r != TB_OK) return r;
+        }
     }
     r = ensure_workspace(net->ctx, (size_t)std::max<int64_t>(ws_floats, 1) * sizeof(float));
     if (r != TB_OK) return r;

@@ -36,11 +36,12 @@ def worst_map_err(a, b, maps):
     return max(max_rel_err(a[i], b[i]) for i in range(maps))
 
 
-def yolo_err(got, ref, raw_ref, n, classes):
+def yolo_err(got, ref, raw_ref, n, classes, tol=None):
     """Worst error of a yolo output relative to what the FP32 tolerance allows.  Entries 2,3
     (w, h) are raw conv values: per-map relative error / FP32_TOL.  The other entries are
     logistic(x): |d logistic| <= |dx|/4, so the allowed error of a map is
     FP32_TOL * max|raw map| / 4 (plus one ulp of 1).  Returns a ratio; <= 1 passes."""
+    tol = FP32_TOL if tol is None else tol
     B = got.shape[0]
     g = got.reshape(B, n, classes + 5, -1).astype(np.float64)
     r = ref.reshape(B, n, classes + 5, -1).astype(np.float64)
@@ -51,12 +52,16 @@ def yolo_err(got, ref, raw_ref, n, classes):
             for e in range(classes + 5):
                 d = np.max(np.abs(g[b, a, e] - r[b, a, e]))
                 scale = np.max(np.abs(x[b, a, e]))
-                allow = FP32_TOL * scale if e in (2, 3) else FP32_TOL * scale / 4 + 2 ** -23
+                allow = tol * scale if e in (2, 3) else tol * scale / 4 + 2 ** -23
                 worst = max(worst, d / max(allow, 1e-30))
     return worst
 
 
 FP32_TOL = 1e-4  # max relative error per activation map, FP32 path
+# A whole network run free (each layer fed its own previous output) accumulates the FP32
+# reordering differences of every layer before it; with random He-init weights the YOLOv3
+# activations grow to ~1e5 through 23 residual adds.  End-to-end outputs are held to this bound.
+E2E_TOL = 1e-3
 
 
 @pytest.fixture(scope="session")

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import FP32_TOL, worst_map_err, yolo_err
+from conftest import E2E_TOL, FP32_TOL, worst_map_err, yolo_err
 from oracle import oracle as O
 from tensorium_b200 import synth
 from tensorium_b200.net import TNNet
@@ -21,21 +21,50 @@ def maps_of(specs, shape, i):
     return synth.layer_shapes(specs, shape)[i][0]
 
 
-def test_yolov3_every_layer_unfused_plan(ctx, yolo_specs):
-    x = synth.input_images(3, "yolov3", 1, (3, 416, 416))
+def test_yolov3_every_layer_teacher_forced(ctx, yolo_specs):
+    """Every layer of YOLOv3-416 (unfused plan, batch 1), each checked against the oracle run
+    on the GPU's own inputs to that layer: the per-kernel FP32 bar (1e-4 per activation map)."""
+    shape = (3, 416, 416)
+    shapes = synth.layer_shapes(yolo_specs, shape)
+    x = synth.input_images(3, "yolov3", 1, shape)
+    net = TNNet(ctx, yolo_specs, 1, shape, fuse_batchnorm=True, fusion=False)
+    net.forward(torch.from_numpy(x).to(ctx.torch_device), use_graph=False)
+    outs = {}
+
+    def get(j):
+        if j not in outs:
+            outs[j] = net.output(j).cpu().numpy().reshape((1,) + shapes[j])
+        return outs[j]
+
+    worst = 0.0
+    for i, s in enumerate(yolo_specs):
+        prev = x if i == 0 else get(i - 1)
+        ref = O.run_layer(yolo_specs, i, prev, get)
+        got = get(i)
+        if s["type"] == "yolo":
+            assert yolo_err(got, ref, prev, 3, 80) <= 1.0, i
+            continue
+        e = worst_map_err(got, ref, shapes[i][0])
+        worst = max(worst, e)
+        assert e <= FP32_TOL, (i, s["type"], e)
+    print("worst per-map relative error (teacher forced):", worst)
+
+
+def test_yolov3_end_to_end_drift(ctx, yolo_specs):
+    """Free-running forward vs the free-running oracle: the error accumulated over 75 convs of a
+    random-weight net whose activations grow to ~1e5 (reported; bounded at 1e-3 per map)."""
+    shape = (3, 416, 416)
+    x = synth.input_images(3, "yolov3", 1, shape)
     ref = O.run_network(yolo_specs, x)
-    net = TNNet(ctx, yolo_specs, 1, (3, 416, 416), fuse_batchnorm=True, fusion=False)
+    net = TNNet(ctx, yolo_specs, 1, shape, fuse_batchnorm=True, fusion=False)
     net.forward(torch.from_numpy(x).to(ctx.torch_device), use_graph=False)
     worst = 0.0
-    for i in range(len(yolo_specs)):
-        got = net.output(i).cpu().numpy()
-        if yolo_specs[i]["type"] == "yolo":
-            assert yolo_err(got, ref[i], ref[i - 1], 3, 80) <= 1.0, i
+    for i, s in enumerate(yolo_specs):
+        if s["type"] == "yolo":
             continue
-        e = worst_map_err(got, ref[i], maps_of(yolo_specs, (3, 416, 416), i))
-        worst = max(worst, e)
-        assert e <= FP32_TOL, (i, yolo_specs[i]["type"], e)
-    print("worst per-map relative error over the non-yolo layers:", worst)
+        worst = max(worst, worst_map_err(net.output(i).cpu().numpy(), ref[i], maps_of(yolo_specs, shape, i)))
+    print("worst per-map relative error, free running:", worst)
+    assert worst <= E2E_TOL
 
 
 @pytest.mark.parametrize("batch", [1, 2])
@@ -48,14 +77,14 @@ def test_yolov3_fused_heads_and_detections(ctx, yolo_specs, batch):
     thresh = 0.45
     logit = np.log(thresh / (1 - thresh))
     for h, r, got in zip(heads, raws, out):
-        assert yolo_err(got, ref[h], ref[r], 3, 80) <= 1.0, h
+        assert yolo_err(got, ref[h], ref[r], 3, 80, E2E_TOL) <= 1.0, h
         # the detection index set (objectness > thresh) matches, except candidates whose raw
         # objectness lies within the FP32 tolerance band around logit(thresh)
         g = int(np.sqrt(got.shape[1] // 255))
         go = got.reshape(batch, 3, 85, g * g)[:, :, 4]
         ro = ref[h].reshape(batch, 3, 85, g * g)[:, :, 4]
         xo = ref[r].reshape(batch, 3, 85, g * g)
-        band = FP32_TOL * np.abs(xo).max(axis=3)[:, :, 4:5]
+        band = E2E_TOL * np.abs(xo).max(axis=3)[:, :, 4:5]
         sure = np.abs(xo[:, :, 4] - logit) > band
         assert np.array_equal((go > thresh)[sure], (ro > thresh)[sure])
     recs, probs, counts = net.detections(416, 416, thresh, capacity=16384)
