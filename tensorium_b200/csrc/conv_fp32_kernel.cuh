@@ -77,13 +77,16 @@ __device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const Co
         return;
     }
     int b = q.b, pix = q.pix;
-    for (int k = 0; k < q.nvalid; ++k) {
-        while (pix >= p.OHW) { pix -= p.OHW; ++b; }
-        const long long off = (long long)m * p.OHW + pix;
-        float o = conv_epilogue(v[k], m, p);
-        if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + off]);
-        p.y[b * p.y_bs + off] = o;
-        ++pix;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // constant trip count: v (the accumulators) stays in registers
+        if (k < q.nvalid) {
+            while (pix >= p.OHW) { pix -= p.OHW; ++b; }
+            const long long off = (long long)m * p.OHW + pix;
+            float o = conv_epilogue(v[k], m, p);
+            if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + off]);
+            p.y[b * p.y_bs + off] = o;
+            ++pix;
+        }
     }
 }
 
