@@ -199,11 +199,15 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     with ClockSampler(local) as clk:
+        if args.profile_window:
+            torch.cuda.profiler.start()  # ncu --profile-from-start off captures only this region
         e0.record(stream)
         for _ in range(args.steps):
-            net.forward(x)
+            net.forward(x, use_graph=not args.profile_window)
         e1.record(stream)
         barrier()
+        if args.profile_window:
+            torch.cuda.profiler.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
     clocks = clk.summary()
     value = world * B * args.steps / (ms / 1e3)
@@ -304,11 +308,15 @@ def run_layer_mode(args):
         L.forward(st)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if args.profile_window:
+        torch.cuda.profiler.start()
     e0.record()
     for _ in range(args.steps):
         L.forward(st)
     e1.record()
     torch.cuda.synchronize()
+    if args.profile_window:
+        torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1) / args.steps
     oc, oh, ow = shapes[i]
     flops = 2.0 * oc * oh * ow * c * s["size"] ** 2 * args.batch
@@ -325,6 +333,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
+    ap.add_argument("--profile-window", action="store_true",
+                    help="eager forwards inside cudaProfilerStart/Stop (for ncu --profile-from-start off); "
+                         "the printed numbers are then not bench values")
     args = ap.parse_args()
     if args.layer is not None:
         run_layer_mode(args)
