@@ -167,10 +167,11 @@ def run_ours(args):
     from tensorium_b200 import Context, synth
     from tensorium_b200.net import TNNet
 
+    from tensorium_b200 import dist as tbd
     world, rank, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
+    if world > 1:
+        tbd.init("nccl", timeout_s=300.0, device_id=torch.device("cuda", local))
     B = args.batch
     specs = synth.yolov3_specs()
     ctx = Context(local)
@@ -186,11 +187,7 @@ def run_ours(args):
             dist.barrier()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=ctx.torch_device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return tbd.max_over_ranks(v, device=ctx.torch_device)
 
     # ---- device-resident throughput (graph replay) ----
     for _ in range(max(args.warmup, 1)):
@@ -263,6 +260,12 @@ def run_ours(args):
                 "algorithmic_flops_per_forward": conv_flops, "conv_ms_per_forward": conv_ms,
                 "all_layers_ms_per_forward": total_ms}
 
+    # detections of this rank's images, gathered to rank 0 in global image order (outside the
+    # timed region; NCCL carries only this final gather)
+    net.forward(x)
+    recs, probs, counts = net.detections(416, 416, 0.45, capacity=16384)
+    gathered = tbd.gather_detections(tbd.detections_per_image(recs, probs, counts, 16384))
+
     line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -273,7 +276,10 @@ def run_ours(args):
                        "input": "3x416x416", "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2: each step streams ~1.3 GB of activations per GPU"},
             "e2e": e2e, "roofline": roofline, "clocks": clocks,
-            "gpu_launches": int(launches_per_step * args.steps)}
+            "gpu_launches": int(launches_per_step * args.steps),
+            "detections": {"images_gathered_on_rank0": len(gathered) if gathered is not None else None,
+                           "boxes": int(sum(len(r) for r, _ in gathered)) if gathered is not None else None,
+                           "thresh": 0.45}}
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(specs)
         cb["cpu"] = cpu_model()
@@ -283,6 +289,7 @@ def run_ours(args):
     net.close()
     ctx.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
