@@ -38,6 +38,7 @@ sys.path.insert(0, str(ROOT))
 INPUT = (3, 416, 416)
 HEADS = (82, 94, 106)
 METRIC = "YOLOv3-416 images/sec (FP32 path)"
+MATH_MODES = {"fp32": 0, "tf32": 1}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
 
 
@@ -311,15 +312,16 @@ def run_layer_mode(args):
     L.weights = s["weights"]
     x = torch.rand((args.batch, c, h, w), device=ctx.torch_device)
     st = TNNetState(x)
+    mm = MATH_MODES[args.math]
     for _ in range(args.warmup):
-        L.forward(st)
+        L.forward(st, math_mode=mm)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if args.profile_window:
         torch.cuda.profiler.start()
     e0.record()
     for _ in range(args.steps):
-        L.forward(st)
+        L.forward(st, math_mode=mm)
     e1.record()
     torch.cuda.synchronize()
     if args.profile_window:
@@ -327,7 +329,7 @@ def run_layer_mode(args):
     ms = e0.elapsed_time(e1) / args.steps
     oc, oh, ow = shapes[i]
     flops = 2.0 * oc * oh * ow * c * s["size"] ** 2 * args.batch
-    print(json.dumps({"layer": i, "shape": f"{c}x{h}x{w} -> {oc}x{oh}x{ow} k{s['size']} s{s['stride']}",
+    print(json.dumps({"layer": i, "math": args.math, "shape": f"{c}x{h}x{w} -> {oc}x{oh}x{ow} k{s['size']} s{s['stride']}",
                       "batch": args.batch, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
 
 
@@ -340,6 +342,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
+    ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
+                    help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")
     ap.add_argument("--profile-window", action="store_true",
                     help="eager forwards inside cudaProfilerStart/Stop (for ncu --profile-from-start off); "
                          "the printed numbers are then not bench values")

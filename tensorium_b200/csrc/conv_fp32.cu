@@ -391,8 +391,14 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
     if (!act_supported(d->activation))
         return fail(TB_ERR_UNSUPPORTED, "conv: activation %lld not supported", (long long)d->activation);
     if (math_mode < 0) math_mode = ctx->math_mode;
-    if (math_mode != TB_MATH_FP32)
+    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32)
         return fail(TB_ERR_UNSUPPORTED, "conv: math mode %lld is not available in this build", (long long)math_mode);
+    if (math_mode == TB_MATH_TF32 && conv_tc_supported(g)) {
+        r = ensure_workspace(ctx, (size_t)conv_tc_scratch_floats(g) * sizeof(float));
+        if (r != TB_OK) return r;
+        return conv_tc_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
+                              (int)d->activation, 0, reinterpret_cast<float*>(ctx->ws), nullptr);
+    }
     return conv_fp32_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
                             (int)d->activation, 0, nullptr, 0, nullptr);
 }

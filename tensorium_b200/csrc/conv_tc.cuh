@@ -1,0 +1,135 @@
+// conv_tc.cuh -- tcgen05 (5th-gen tensor core) TF32 implicit-GEMM convolution: device helpers.
+//
+// Shared-memory operand tiles use the one canonical MN-major layout that tcgen05 accepts for
+// 32-bit (TF32) operands, "128-byte swizzle with 32-byte atomicity" (descriptor layout type 1):
+// an atom is 4 K-rows x 128 bytes (32 fp32 along M or N); inside an atom the 32-byte chunk index
+// is XORed with the row index (byte-address bits [5,7) ^= bits [7,9)).  Atoms along MN are
+// 512 bytes apart (the descriptor's leading byte offset), K-groups of 4 rows are (MN/32)*512
+// bytes apart (stride byte offset); one K=8 MMA spans two K-groups.  Tiles start on 1024-byte
+// boundaries.
+#pragma once
+#include "conv.cuh"
+
+namespace tbi {
+namespace tc {
+
+// --- mbarrier ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(a), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(a) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    unsigned ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~2^24 polls (seconds), sets *abort and the device status word.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, volatile int* abort,
+                                                  int* status, int code) {
+    for (unsigned it = 0; it < (1u << 24); ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    *abort = 1;
+    if (status) atomicExch(status, code);
+    return false;
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// --- tcgen05 -----------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(dst_smem);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(a), "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::tf32, one CTA
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// arrive on `bar` once every tcgen05 op issued so far by this thread has completed
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(a)
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// shared-memory matrix descriptor: MN-major, 128-byte swizzle with 32-byte atoms (layout type 1),
+// version 1
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128_32b(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;  // version (Blackwell)
+    d |= (uint64_t)1 << 61;  // SWIZZLE_128B_BASE32B
+    return d;
+}
+
+// instruction descriptor: F32 accumulate, TF32 A and B, both MN-major, shape M x N
+__host__ __device__ constexpr uint32_t idesc_tf32_mn(int M, int N) {
+    return (1u << 4)                       // c_format F32
+           | (2u << 7) | (2u << 10)        // a_format, b_format TF32
+           | (1u << 15) | (1u << 16)       // a_major, b_major = MN
+           | ((uint32_t)(N >> 3) << 17)    // n_dim
+           | ((uint32_t)(M >> 4) << 24);   // m_dim
+}
+
+// byte offset of the 16-byte piece holding elements (mn..mn+3, k), mn % 4 == 0, in an MN-major
+// tile of the 32-byte-atom 128-byte swizzle
+__device__ __forceinline__ uint32_t sw128_32b_chunk(int mn, int k, int mn_tile) {
+    const int krow = k & 3;
+    return (uint32_t)((k >> 2) * (mn_tile / 32) * 512 + (mn >> 5) * 512 + krow * 128 +
+                      ((((mn & 31) >> 3) ^ krow) << 5) + ((mn & 4) << 2));
+}
+
+}  // namespace tc
+}  // namespace tbi

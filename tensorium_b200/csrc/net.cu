@@ -237,6 +237,10 @@ int run_layer(tb_net* net, int64_t i, const float* x) {
         ConvGeom g;
         r = conv_geom(&d, &g);
         if (r != TB_OK) return r;
+        if (net->math_mode == TB_MATH_TF32 && conv_tc_supported(g))
+            return conv_tc_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
+                                  L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
+                                  (int)L.act, (int)L.fuse_yolo, reinterpret_cast<float*>(ctx->ws), &net->launches);
         return conv_fp32_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
                                 L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
                                 (int)L.act, (int)L.fuse_yolo, nullptr, 0, &net->launches);
@@ -489,7 +493,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     TB_ENTER(net->ctx);
     if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
     if (net->layers.empty()) return fail(TB_ERR_INVALID, "empty net");
-    if (math_mode != TB_MATH_FP32)
+    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32)
         return fail(TB_ERR_UNSUPPORTED, "net: math mode %lld is not available in this build", (long long)math_mode);
     net->math_mode = math_mode;
     int r = infer_shapes(net);
@@ -656,7 +660,12 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             d.out_batch_stride = T.out.bs;
             ConvGeom g;
             r = conv_geom(&d, &g);
-            if (r != TB_OK) return r;
+            if (r != TB_OK) { if (tmp) cudaFree(tmp); return r; }
+            if (net->math_mode == TB_MATH_TF32 && conv_tc_supported(g)) {
+                ws_floats = std::max(ws_floats, conv_tc_scratch_floats(g));
+                if (tmp) cudaFree(tmp);
+                continue;
+            }
             r = conv_fp32_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr);
             if (r == TB_OK) ws_floats = std::max(ws_floats, conv_fp32_ws_floats_for(net->ctx, g, in.ptr));
             if (tmp) cudaFree(tmp);

@@ -1,0 +1,88 @@
+"""TF32 tensor-core conv path (tcgen05 / TMEM mainloop) through the C ABI against the CPU oracle.
+
+The reference has no tensor-core path; the bar for it is the one the BASELINE north star states
+for TF32/BF16: relative L2 error <= 1e-2 (here per activation map, stricter than on the final head
+only), and the same top-k boxes on whole networks.  TF32 keeps 10 of fp32's 23 mantissa bits, so a
+map's error is ~1e-3 of its magnitude; an operand-layout error shows up as O(1)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tensorium_b200 import MATH_TF32
+from tensorium_b200.layers import TConvolutionalLayer, TNNetState
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 1e-2  # relative L2 per activation map
+
+
+def rel_l2_maps(a, b, maps):
+    a = np.asarray(a, np.float64).reshape(maps, -1)
+    b = np.asarray(b, np.float64).reshape(maps, -1)
+    assert np.all(np.isfinite(a))
+    num = np.sqrt(((a - b) ** 2).sum(axis=1))
+    den = np.maximum(np.sqrt((b ** 2).sum(axis=1)), 1e-30)
+    return float((num / den).max())
+
+
+def run_layer(ctx, x, w, b, F, k, s, p, act, bn=None, residual=None, math_mode=MATH_TF32):
+    B, C, H, W = x.shape
+    L = TConvolutionalLayer(B, H, W, C, F, 1, k, s, s, 1, p, act, bn is not None).bind(ctx)
+    L.weights, L.biases = w, b
+    if bn is not None:
+        L.scales, L.rolling_mean, L.rolling_variance = bn
+    xd = torch.from_numpy(x).to(ctx.torch_device)
+    rd = None if residual is None else torch.from_numpy(residual).to(ctx.torch_device)
+    y = L.forward(TNNetState(xd), residual=rd, math_mode=math_mode)
+    return y.cpu().numpy()
+
+
+CASES = [  # (B, C, H, F, k)  stride 1, "same" padding, C % 32 == 0: the shapes the tcgen05 path takes
+    (1, 32, 52, 64, 3),      # YOLOv3 stage-1 shape, one k tile per tap
+    (2, 64, 26, 128, 1),     # 1x1, W % 4 == 0: B operand read from x in place
+    (2, 256, 13, 255, 1),    # 1x1 head shape: M = 255, W % 4 != 0 (tap replica), ragged N
+    (3, 128, 13, 256, 3),    # 3x3, odd spatial size, three images per N tile
+    (1, 512, 13, 1024, 3),   # big K (144 k tiles), 8 M tiles
+    (2, 96, 30, 40, 3),      # F < 128 (one partial M tile), W = 30
+]
+
+
+@pytest.mark.parametrize("B,C,H,F,k", CASES)
+def test_tc_conv_matches_oracle(ctx, B, C, H, F, k):
+    rng = np.random.default_rng(B * 1000 + C + F + 7)
+    x = rng.uniform(0, 1, (B, C, H, H)).astype(np.float32)
+    w = (rng.standard_normal((F, C * k * k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    b = rng.standard_normal(F).astype(np.float32) * 0.1
+    p = (k - 1) // 2
+    for act in (9, 4):  # linear, leaky
+        y = run_layer(ctx, x, w, b, F, k, 1, p, act)
+        ref = O.conv2d(x, w, b, F, k, 1, p, act)
+        assert y.shape == ref.shape
+        e = rel_l2_maps(y, ref, B * F)
+        assert e <= TF32_TOL, e
+        assert e > 0.0  # the tensor-core path ran (TF32 rounding is visible)
+
+
+def test_tc_conv_batchnorm_and_residual(ctx):
+    rng = np.random.default_rng(11)
+    x = rng.uniform(0, 1, (2, 64, 26, 26)).astype(np.float32)
+    w = (rng.standard_normal((128, 64 * 9)) * 0.05).astype(np.float32)
+    b = np.zeros(128, np.float32)
+    bn = (np.ones(128, np.float32), (rng.standard_normal(128) * 0.1).astype(np.float32),
+          rng.uniform(0.5, 1.5, 128).astype(np.float32))
+    r = rng.standard_normal((2, 128, 26, 26)).astype(np.float32)
+    y = run_layer(ctx, x, w, b, 128, 3, 1, 1, 9, bn=bn, residual=r)
+    ref = O.shortcut(O.conv2d(x, w, b, 128, 3, 1, 1, 9, bn=bn), r)
+    assert rel_l2_maps(y, ref, 2 * 128) <= TF32_TOL
+
+
+def test_tc_unsupported_shape_uses_fp32_kernel(ctx):
+    """Stride-2 convs are not on the tensor-core path: TF32 mode gives the FP32 kernel's result."""
+    rng = np.random.default_rng(12)
+    x = rng.uniform(0, 1, (1, 32, 26, 26)).astype(np.float32)
+    w = (rng.standard_normal((64, 32 * 9)) * 0.1).astype(np.float32)
+    b = np.zeros(64, np.float32)
+    a = run_layer(ctx, x, w, b, 64, 3, 2, 1, 9)
+    f = run_layer(ctx, x, w, b, 64, 3, 2, 1, 9, math_mode=0)
+    assert np.array_equal(a, f)
