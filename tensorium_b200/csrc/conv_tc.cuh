@@ -1,12 +1,13 @@
 // conv_tc.cuh -- tcgen05 (5th-gen tensor core) TF32 implicit-GEMM convolution: device helpers.
 //
 // Shared-memory operand tiles use the one canonical MN-major layout that tcgen05 accepts for
-// 32-bit (TF32) operands, "128-byte swizzle with 32-byte atomicity" (descriptor layout type 1):
-// an atom is 4 K-rows x 128 bytes (32 fp32 along M or N); inside an atom the 32-byte chunk index
-// is XORed with the row index (byte-address bits [5,7) ^= bits [7,9)).  Atoms along MN are
-// 512 bytes apart (the descriptor's leading byte offset), K-groups of 4 rows are (MN/32)*512
-// bytes apart (stride byte offset); one K=8 MMA spans two K-groups.  Tiles start on 1024-byte
-// boundaries.
+// 32-bit (TF32) operands, "128-byte swizzle with 32-byte atomicity" (descriptor layout type 1,
+// the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): rows of 128 bytes (32 fp32
+// along M or N) hold one K index each; inside a group of 4 rows the 32-byte chunk index is XORed
+// with the row index (byte-address bits [5,7) ^= bits [7,9)).  A TMA box of 32 (M or N) x 32 (K)
+// fills 4 KB: 8 K-groups of 512 bytes (the descriptor's stride byte offset); boxes along M or N
+// are 4 KB apart (leading byte offset).  One K=8 MMA spans two K-groups, so the k-th MMA of a
+// 32-deep stage starts 1024*k bytes into each box.  Tiles start on 1024-byte boundaries.
 #pragma once
 #include "conv.cuh"
 
@@ -22,6 +23,11 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     unsigned a = (unsigned)__cvta_generic_to_shared(bar);
     asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(a) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(a), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
@@ -45,6 +51,30 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
     *abort = 1;
     if (status) atomicExch(status, code);
     return false;
+}
+
+// Wait with a poll limit only (used to drain copies already in flight after an abort).
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, unsigned parity) {
+    for (unsigned it = 0; it < (1u << 22); ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// --- TMA (tensor copies global -> shared, completion counted on an mbarrier; no multicast) ---
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const void* tmap, uint64_t* bar, int x, int y) {
+    unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(b), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(unsigned dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
+    unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(b), "r"(x), "r"(y), "r"(z)
+        : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -121,14 +151,6 @@ __host__ __device__ constexpr uint32_t idesc_tf32_mn(int M, int N) {
            | (1u << 15) | (1u << 16)       // a_major, b_major = MN
            | ((uint32_t)(N >> 3) << 17)    // n_dim
            | ((uint32_t)(M >> 4) << 24);   // m_dim
-}
-
-// byte offset of the 16-byte piece holding elements (mn..mn+3, k), mn % 4 == 0, in an MN-major
-// tile of the 32-byte-atom 128-byte swizzle
-__device__ __forceinline__ uint32_t sw128_32b_chunk(int mn, int k, int mn_tile) {
-    const int krow = k & 3;
-    return (uint32_t)((k >> 2) * (mn_tile / 32) * 512 + (mn >> 5) * 512 + krow * 128 +
-                      ((((mn & 31) >> 3) ^ krow) << 5) + ((mn & 4) << 2));
 }
 
 }  // namespace tc

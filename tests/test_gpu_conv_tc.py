@@ -26,9 +26,9 @@ def rel_l2_maps(a, b, maps):
     return float((num / den).max())
 
 
-def run_layer(ctx, x, w, b, F, k, s, p, act, bn=None, residual=None, math_mode=MATH_TF32):
+def run_layer(ctx, x, w, b, F, k, s, p, act, bn=None, residual=None, math_mode=MATH_TF32, dil=1):
     B, C, H, W = x.shape
-    L = TConvolutionalLayer(B, H, W, C, F, 1, k, s, s, 1, p, act, bn is not None).bind(ctx)
+    L = TConvolutionalLayer(B, H, W, C, F, 1, k, s, s, dil, p, act, bn is not None).bind(ctx)
     L.weights, L.biases = w, b
     if bn is not None:
         L.scales, L.rolling_mean, L.rolling_variance = bn
@@ -38,26 +38,29 @@ def run_layer(ctx, x, w, b, F, k, s, p, act, bn=None, residual=None, math_mode=M
     return y.cpu().numpy()
 
 
-CASES = [  # (B, C, H, F, k)  stride 1, "same" padding, C % 32 == 0: the shapes the tcgen05 path takes
-    (1, 32, 52, 64, 3),      # YOLOv3 stage-1 shape, one k tile per tap
-    (2, 64, 26, 128, 1),     # 1x1, W % 4 == 0: B operand read from x in place
-    (2, 256, 13, 255, 1),    # 1x1 head shape: M = 255, W % 4 != 0 (tap replica), ragged N
-    (3, 128, 13, 256, 3),    # 3x3, odd spatial size, three images per N tile
-    (1, 512, 13, 1024, 3),   # big K (144 k tiles), 8 M tiles
-    (2, 96, 30, 40, 3),      # F < 128 (one partial M tile), W = 30
+CASES = [  # (B, C, H, F, k, s, p, dil): C % 32 == 0, the shapes the tcgen05 path takes
+    (1, 32, 52, 64, 3, 1, 1, 1),      # YOLOv3 stage-1 shape, one k tile per tap
+    (3, 64, 28, 96, 1, 1, 0, 1),      # 1x1, W % 4 == 0: A read from x in place; tiles span images
+    (2, 256, 13, 255, 1, 1, 0, 1),    # 1x1 head shape: F = 255, W % 4 != 0 (replica), ragged tiles
+    (3, 128, 13, 256, 3, 1, 1, 1),    # 3x3, odd spatial size, padded pixel grid
+    (1, 512, 13, 1024, 3, 1, 1, 1),   # big K (144 k tiles), wide filter tiles
+    (2, 96, 30, 40, 3, 1, 1, 1),      # F < 32 multiple (ragged filter tile), W = 30
+    (2, 32, 52, 64, 3, 2, 1, 1),      # stride 2 (YOLOv3 downsampling): two row phases
+    (1, 64, 27, 48, 3, 2, 1, 1),      # stride 2, odd input size
+    (1, 32, 20, 32, 3, 1, 2, 2),      # dilation 2
+    (2, 32, 17, 64, 5, 1, 2, 1),      # 5x5
 ]
 
 
-@pytest.mark.parametrize("B,C,H,F,k", CASES)
-def test_tc_conv_matches_oracle(ctx, B, C, H, F, k):
+@pytest.mark.parametrize("B,C,H,F,k,s,p,dil", CASES)
+def test_tc_conv_matches_oracle(ctx, B, C, H, F, k, s, p, dil):
     rng = np.random.default_rng(B * 1000 + C + F + 7)
     x = rng.uniform(0, 1, (B, C, H, H)).astype(np.float32)
     w = (rng.standard_normal((F, C * k * k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
     b = rng.standard_normal(F).astype(np.float32) * 0.1
-    p = (k - 1) // 2
     for act in (9, 4):  # linear, leaky
-        y = run_layer(ctx, x, w, b, F, k, 1, p, act)
-        ref = O.conv2d(x, w, b, F, k, 1, p, act)
+        y = run_layer(ctx, x, w, b, F, k, s, p, act, dil=dil)
+        ref = O.conv2d(x, w, b, F, k, s, p, act, dilation=dil)
         assert y.shape == ref.shape
         e = rel_l2_maps(y, ref, B * F)
         assert e <= TF32_TOL, e
@@ -78,11 +81,12 @@ def test_tc_conv_batchnorm_and_residual(ctx):
 
 
 def test_tc_unsupported_shape_uses_fp32_kernel(ctx):
-    """Stride-2 convs are not on the tensor-core path: TF32 mode gives the FP32 kernel's result."""
+    """Channel counts that are not a multiple of 32 are not on the tensor-core path: TF32 mode
+    gives the FP32 kernel's result."""
     rng = np.random.default_rng(12)
-    x = rng.uniform(0, 1, (1, 32, 26, 26)).astype(np.float32)
-    w = (rng.standard_normal((64, 32 * 9)) * 0.1).astype(np.float32)
+    x = rng.uniform(0, 1, (1, 20, 26, 26)).astype(np.float32)
+    w = (rng.standard_normal((64, 20 * 9)) * 0.1).astype(np.float32)
     b = np.zeros(64, np.float32)
-    a = run_layer(ctx, x, w, b, 64, 3, 2, 1, 9)
-    f = run_layer(ctx, x, w, b, 64, 3, 2, 1, 9, math_mode=0)
+    a = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9)
+    f = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9, math_mode=0)
     assert np.array_equal(a, f)
