@@ -38,6 +38,7 @@ sys.path.insert(0, str(ROOT))
 INPUT = (3, 416, 416)
 HEADS = (82, 94, 106)
 METRIC = "YOLOv3-416 images/sec (FP32 path)"
+METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
 MATH_MODES = {"fp32": 0, "tf32": 1}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
 
@@ -176,7 +177,7 @@ def run_ours(args):
     B = args.batch
     specs = synth.yolov3_specs()
     ctx = Context(local)
-    net = TNNet(ctx, specs, B, INPUT)
+    net = TNNet(ctx, specs, B, INPUT, math_mode=MATH_MODES[args.math])
     # this rank's images: global images [rank*B, (rank+1)*B) of the seeded stream
     x_host = synth.input_images(3, "yolov3", (rank + 1) * B, INPUT)[rank * B:]
     x = torch.from_numpy(x_host).to(ctx.torch_device)
@@ -247,16 +248,26 @@ def run_ours(args):
     total_ms = float(prof.sum())
     conv_flops = synth.conv_flops(specs, INPUT, B)
     achieved = conv_flops / (conv_ms / 1e3) / 1e12
-    fma = __import__("ctypes").c_double()
-    from tensorium_b200._lib import check, lib
-    check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
     traffic = None
-    if PROFILE_SUMMARY.exists():
+    if PROFILE_SUMMARY.exists() and args.math == "fp32":
         traffic = json.loads(PROFILE_SUMMARY.read_text()).get("dram_bytes_per_forward")
-    roofline = {"bound": "fp32", "kernel": "conv_fp32_kernel (+ split-K reduce), all 75 convs of a forward",
-                "achieved": achieved, "peak": fma.value, "unit": "TFLOP/s", "frac": achieved / fma.value,
-                "peak_source": "FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json "
-                               "holds HBM and bf16 tensor peaks only",
+    if args.math == "fp32":
+        fma = __import__("ctypes").c_double()
+        from tensorium_b200._lib import check, lib
+        check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
+        peak, bound, kernel = fma.value, "fp32", "conv_fp32_kernel (+ split-K fixup), all 75 convs of a forward"
+        peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
+                       "and bf16 tensor peaks only")
+    else:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        peak, bound = bf16 / 2, "tensor"
+        kernel = "k_conv_tc (tcgen05 TF32) + tap-replica repack for 69 convs, conv_fp32_kernel for the rest"
+        peak_source = (f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)"
+                       if "bf16_tflops" in peaks else "TF32 dense = half the fallback bf16 1590 TFLOP/s")
+    roofline = {"bound": bound, "kernel": kernel,
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": peak_source,
                 "traffic": traffic, "traffic_unit": "bytes per forward (ncu, summed over conv launches)",
                 "algorithmic_flops_per_forward": conv_flops, "conv_ms_per_forward": conv_ms,
                 "all_layers_ms_per_forward": total_ms}
@@ -267,9 +278,9 @@ def run_ours(args):
     recs, probs, counts = net.detections(416, 416, 0.45, capacity=16384)
     gathered = tbd.gather_detections(tbd.detections_per_image(recs, probs, counts, 16384))
 
-    line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+    line = {"metric": METRIC if args.math == "fp32" else METRIC_TF32, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.math == "fp32" else "tf32 (fp32 accumulate)",
             "data": "synthetic (seeded uniform images, random He-init weights, BN stats as config 0; "
                     "no dataset or .weights in the container)",
             "config": {"workload": "YOLOv3-416 forward (BASELINE config 3), batch 8 per GPU",

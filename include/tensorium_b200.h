@@ -142,6 +142,15 @@ int tb_conv_packed_weights_count(const tb_conv_desc* d, int64_t* count);
  * the conv kernels read. Device to device, once per weight load (the reference's one-time
  * weights.pushToDevice, source/nConvolutionLayer.pas:1034-1036). */
 int tb_conv_pack_weights(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed);
+/* tb_conv_pack_weights followed by rounding every packed weight to TF32 (nearest, ties away):
+ * the weights for TB_MATH_TF32 calls. The tensor core would otherwise truncate them, a bias
+ * toward zero that adds up over a deep network. Same layout and count. (The reference has no
+ * tensor-core path; this replaces the same weights.pushToDevice step.) */
+int tb_conv_pack_weights_tf32(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed);
+/* *yes = 1 when tb_conv2d_fwd with this descriptor and math mode runs the tensor-core mainloop
+ * (TB_MATH_TF32 and channels % 32 == 0), 0 when it runs the FP32 kernel: which packing the
+ * caller should hand it (no reference counterpart). */
+int tb_conv_uses_tensor_cores(const tb_conv_desc* d, int64_t math_mode, int64_t* yes);
 /* Host helper: fold batchnorm into weights and biases in place, the arithmetic of
  * TBaseConvolutionalLayer.fuseBatchNorm (source/nConvolutionLayer.pas:102-126). */
 int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights_host, float* biases_host,
@@ -334,6 +343,14 @@ int tb_net_profile(tb_net* net, const float* x, double* ms_out);
 /* FP32 FFMA throughput of this GPU (TFLOP/s) from a register-resident FMA loop on every SM;
  * the roofline denominator of the FP32 CUDA-core conv path (no reference counterpart). Blocks. */
 int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops);
+/* One launch of the TF32 tensor-core conv on this geometry (bias, batchnorm and residual off)
+ * with per-CTA cycle counters; out12 = averages over CTAs of: producer total cycles, producer
+ * cycles waiting for a free stage, MMA-issuer total, MMA waiting for loaded stages, MMA waiting
+ * for a free accumulator, epilogue total, epilogue waiting for a finished accumulator, tiles
+ * per CTA, epilogue cycles in TMEM loads, epilogue cycles in the per-value work and stores,
+ * 0, 0 (no reference counterpart). Blocks. */
+int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y,
+                           double* out12);
 
 #ifdef __cplusplus
 }

@@ -91,6 +91,8 @@ SIGNATURES = {
     "tb_conv_out_shape": [C.POINTER(ConvDesc), PI64, PI64],
     "tb_conv_packed_weights_count": [C.POINTER(ConvDesc), PI64],
     "tb_conv_pack_weights": [P, C.POINTER(ConvDesc), P, P],
+    "tb_conv_uses_tensor_cores": [C.POINTER(ConvDesc), I64, PI64],
+    "tb_conv_pack_weights_tf32": [P, C.POINTER(ConvDesc), P, P],
     "tb_conv_fold_bn": [I64, I64, P, P, P, P, P],
     "tb_conv_autotune": [P, C.POINTER(ConvDesc), P, P, P],
     "tb_conv2d_fwd": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P, I64],
@@ -129,6 +131,7 @@ SIGNATURES = {
     "tb_net_flops": [P, C.POINTER(C.c_double)],
     "tb_net_profile": [P, P, C.POINTER(C.c_double)],
     "tb_diag_fp32_fma_tflops": [P, C.POINTER(C.c_double)],
+    "tb_diag_conv_tc_phases": [P, P, P, P, P, C.POINTER(C.c_double)],
 }
 _RESTYPES = {"tb_get_stream": P}
 

@@ -19,6 +19,7 @@ class Context:
     def __init__(self, device: int = 0, math_mode: int = MATH_FP32, workspace_bytes: int = 0,
                  use_torch_stream: bool = True):
         self.device = int(device)
+        self.math_mode = int(math_mode)
         self.handle = C.c_void_p()
         opts = Options(math_mode, workspace_bytes, 0)
         check(lib.tb_init(self.device, C.byref(opts), C.byref(self.handle)))

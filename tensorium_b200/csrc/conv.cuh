@@ -60,12 +60,15 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt = nullptr,
                      int64_t tile_cnt_len = 0);
-// TF32 tensor-core path (conv_tc.cu): stride-1 "same" convolutions with channels % 32 == 0.
+// TF32 tensor-core path (conv_tc.cu): convolutions with channels % 32 == 0 (any stride, dilation).
 bool conv_tc_supported(const ConvGeom& g);
 int64_t conv_tc_scratch_floats(const ConvGeom& g);
 int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
                    const float* bn_scale, const float* bn_mean, const float* bn_var, const float* res,
-                   float* y, int act, int yolo_classes, float* scratch, int64_t* launches);
+                   float* y, int act, int yolo_classes, float* scratch, int64_t* launches,
+                   unsigned long long* phases = nullptr);
+// Round packed weights to TF32 (nearest, ties away) in place.
+int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // Split-K partial floats this call would need (0 when it does not split), for a given x.

@@ -353,6 +353,23 @@ int tb_conv_pack_weights(tb_ctx* ctx, const tb_conv_desc* d, const float* weight
     return check_launch("k_conv_pack");
 }
 
+int tb_conv_uses_tensor_cores(const tb_conv_desc* d, int64_t math_mode, int64_t* yes) {
+    if (!yes) return fail(TB_ERR_INVALID, "tb_conv_uses_tensor_cores: null result pointer");
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    *yes = (math_mode == TB_MATH_TF32 && conv_tc_supported(g)) ? 1 : 0;
+    return TB_OK;
+}
+
+int tb_conv_pack_weights_tf32(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed) {
+    int r = tb_conv_pack_weights(ctx, d, weights, packed);
+    if (r != TB_OK) return r;
+    ConvGeom g;
+    conv_geom(d, &g);
+    return conv_tc_round_weights(ctx, packed, g.Kpad * g.Mpad);
+}
+
 int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights, float* biases,
                     const float* scales, const float* mean, const float* variance) {
     if (filters <= 0 || filter_size <= 0 || !weights || !biases || !scales || !mean || !variance)
@@ -401,6 +418,39 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
     }
     return conv_fp32_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
                             (int)d->activation, 0, nullptr, 0, nullptr);
+}
+
+int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y,
+                           double* out12) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!x || !packed_w || !y || !out12) return fail(TB_ERR_INVALID, "conv tc phases: null pointer");
+    if (!conv_tc_supported(g)) return fail(TB_ERR_UNSUPPORTED, "conv tc phases: geometry not on the tensor-core path");
+    r = ensure_workspace(ctx, (size_t)conv_tc_scratch_floats(g) * sizeof(float));
+    if (r != TB_OK) return r;
+    const int n = ctx->sm_count * 12;
+    unsigned long long* dph = nullptr;
+    TB_CHECK_CUDA(cudaMalloc(&dph, n * sizeof(unsigned long long)));
+    cudaMemsetAsync(dph, 0, n * sizeof(unsigned long long), ctx->stream);
+    r = conv_tc_launch(ctx, g, x, packed_w, nullptr, nullptr, nullptr, nullptr, nullptr, y, (int)d->activation, 0,
+                       reinterpret_cast<float*>(ctx->ws), nullptr, dph);
+    std::vector<unsigned long long> h(n);
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), dph, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(dph);
+    if (r != TB_OK) return r;
+    if (e != cudaSuccess) return cuda_fail(e, "conv tc phases");
+    int ctas = 0;
+    for (int i = 0; i < 12; ++i) out12[i] = 0;
+    for (int c = 0; c < ctx->sm_count; ++c) {
+        if (h[c * 12 + 0] == 0) continue;
+        ++ctas;
+        for (int i = 0; i < 12; ++i) out12[i] += (double)h[c * 12 + i];
+    }
+    for (int i = 0; i < 12 && ctas; ++i) out12[i] /= ctas;
+    return TB_OK;
 }
 
 }  // extern "C"

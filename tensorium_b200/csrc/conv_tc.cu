@@ -46,17 +46,31 @@ struct TcParams {
     const float* __restrict__ res;
     float* __restrict__ y;
     int* status;
-    int B, F, KW, OH, OW, Wp, NPH, Lp, OHWp, OHW;
+    unsigned long long* phases;  // diagnostics: per-CTA cycle counters (null in normal launches)
+    int B, C, F, KW, OH, OW, Wp, NPH, Lp, OHWp, OHW;
+    int b_grouped;  // weights read as one 3-D box per stage (Mpad % 32 == 0)
     int tiles_n, csteps, ktiles;
     int tiles_total;
     long long y_bs, r_bs;
     int act, yolo_classes;
-    int rowoff[TC_MAX_KH], phase[TC_MAX_KH];
+    int phase[TC_MAX_KH];
+};
+
+// Tensor maps of one launch.  A (pixels x channels) is viewed 4-D as (32 pixels, channel,
+// 32-pixel group, plane index) so that one copy brings a whole 128-pixel tile; one map per kernel
+// row r has its base moved rowoff(r) replica rows down.  a4 maps copy 4 groups (a tile inside
+// one image), a1 maps one group (tiles that straddle two images).  b views the packed weights as
+// (32 filters, k, 32-filter group) with a box of BN/32 groups (bw: 2-D boxes of 32 x 32, for a
+// filter count Mpad that is not a multiple of 32).
+struct TcMaps {
+    CUtensorMap a4[TC_MAX_KH];
+    CUtensorMap a1[TC_MAX_KH];
+    CUtensorMap b;
 };
 
 // Replica layout plan of one geometry.
 struct TcPlan {
-    int64_t Wp, NPH, pad_top, Hrep, Lp;
+    int64_t Wp, NPH, pad_top, Hrep, Lp, PS;  // PS: replica plane stride (elements)
     bool inplace;
     int rowoff[TC_MAX_KH], phase[TC_MAX_KH];
 };
@@ -77,13 +91,18 @@ static void tc_plan(const ConvGeom& g, TcPlan* pl) {
     for (int r = 0; r < g.KH; ++r) pl->rowoff[r] += (int)pl->pad_top;
     pl->Hrep = g.OH + pl->pad_top + mx;
     pl->Lp = round_up(g.OH * pl->Wp, 32);
-    pl->inplace = g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 && g.W % 4 == 0 &&
-                  g.x_bs % 4 == 0;
+    // a 32-pixel group read at a row offset never runs past its own plane
+    pl->PS = round_up(pl->Hrep * pl->Wp, 32) + 32;
+    pl->inplace = g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 &&
+                  (g.H * g.W) % 32 == 0 && g.x_bs % 4 == 0;
 }
 
-// P[s][ph][b][c][Hrep][Wp]; each thread writes 4 consecutive columns (one 16-byte store).
+// P[s][ph][b][c][Hrep][Wp] with planes PS elements apart (the tail of a plane is never
+// written: it is read only for pixels that are dropped); each thread writes 4 consecutive
+// columns (one 16-byte store).
 __global__ void k_tc_repack(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C, int H,
-                            int W, int SY, int SX, int DX, int PX, int NPH, int pad_top, int Hrep, int Wp, int OW) {
+                            int W, int SY, int SX, int DX, int PX, int NPH, int pad_top, int Hrep, int Wp, int OW,
+                            int PS) {
     const int plane = Hrep * Wp;
     const int i4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i4 >= plane) return;
@@ -98,16 +117,21 @@ __global__ void k_tc_repack(const float* __restrict__ x, long long x_bs, float* 
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int xx = x0 + j, ix = SX * xx + s * DX - PX;
-            if (xx < OW && (unsigned)ix < (unsigned)W) v[j] = __ldg(src + ix);
+            if (xx < OW && (unsigned)ix < (unsigned)W) v[j] = tc::to_tf32_rna(__ldg(src + ix));
         }
     }
-    float4* dst = reinterpret_cast<float4*>(P + ((long long)zb * C + c) * plane + i4);
+    float4* dst = reinterpret_cast<float4*>(P + ((long long)zb * C + c) * PS + i4);
     *dst = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+__global__ void k_round_tf32(float* __restrict__ p, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        p[i] = tc::to_tf32_rna(p[i]);
 }
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    k_conv_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+    k_conv_tc(const __grid_constant__ TcMaps maps, const TcParams p) {
     constexpr int A_BYTES = TC_BM * TC_BK * 4;
     constexpr int B_BYTES = BN * TC_BK * 4;
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -133,8 +157,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
     }
     if (warp == 1) tc::tmem_alloc(&tmem_base, 2 * BN);
     tc::tc_fence_before();
@@ -147,34 +170,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // ---------------- TMA producer ----------------
             int it = 0;
             bool ok = true;
+            const long long c_start = clock64();
+            long long c_wait = 0;
             for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
                 const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
-                const int n0 = mt * TC_BM, f0 = nt * BN;
-                int bq[4], qq[4];
+                const int n0 = mt * TC_BM;
+                int bq[4], gq[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int n = n0 + 32 * j;
                     bq[j] = n / p.Lp;
-                    qq[j] = n - bq[j] * p.Lp;
+                    gq[j] = (n - bq[j] * p.Lp) >> 5;
                 }
+                const bool straddle = bq[0] != bq[3];
+                int r = 0, s = 0, c0 = 0;  // kernel tap and first channel of k tile kt
                 for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
+                    const long long c0w = clock64();
                     if (use > 0 && !tc::mbar_wait_bounded(&empty_bar[st], (use - 1) & 1, &abort_flag, p.status, 911)) {
                         ok = false;
                         break;
                     }
+                    c_wait += clock64() - c0w;
                     tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES);
-                    const int rs = kt / p.csteps, c0 = (kt - rs * p.csteps) * TC_BK;
-                    const int r = rs / p.KW, s = rs - r * p.KW;
-                    const int xoff = p.rowoff[r] * p.Wp, z0 = (s * p.NPH + p.phase[r]) * p.B;
+                    const int z0 = (s * p.NPH + p.phase[r]) * p.B;
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + A_BYTES;
+                    if (!straddle) {
+                        tc::tma_load_4d(sa, &maps.a4[r], &full_bar[st], 0, c0, gq[0], z0 + bq[0]);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        tc::tma_load_3d(sa + j * TC_BOX_BYTES, &tmA, &full_bar[st], qq[j] + xoff, c0, z0 + bq[j]);
+                        for (int j = 0; j < 4; ++j)
+                            tc::tma_load_4d(sa + j * TC_BOX_BYTES, &maps.a1[r], &full_bar[st], 0, c0, gq[j], z0 + bq[j]);
+                    }
+                    if (p.b_grouped) {
+                        tc::tma_load_3d(sb, &maps.b, &full_bar[st], 0, kt * TC_BK, nt * (BN / 32));
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < NCHUNK; ++j)
-                        tc::tma_load_2d(sb + j * TC_BOX_BYTES, &tmB, &full_bar[st], f0 + 32 * j, kt * TC_BK);
+                        for (int j = 0; j < NCHUNK; ++j)
+                            tc::tma_load_2d(sb + j * TC_BOX_BYTES, &maps.b, &full_bar[st], nt * BN + 32 * j, kt * TC_BK);
+                    }
+                    c0 += TC_BK;
+                    if (c0 == p.C) {
+                        c0 = 0;
+                        if (++s == p.KW) s = 0, ++r;
+                    }
                 }
+            }
+            if (p.phases) {
+                p.phases[blockIdx.x * 12 + 0] = clock64() - c_start;
+                p.phases[blockIdx.x * 12 + 1] = c_wait;
             }
             if (!ok) {  // an abort: let the copies already issued land before the CTA exits
                 for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
@@ -187,17 +231,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             constexpr uint32_t idesc = tc::idesc_tf32_mn(TC_BM, BN);
             int it = 0, tl = 0;
             bool ok = true, issued = false;
+            const long long c_start = clock64();
+            long long c_wf = 0, c_we = 0;
             for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x, ++tl) {
                 const int buf = tl & 1, u = tl >> 1;
+                long long c0w = clock64();
                 if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 912)) break;
+                c_we += clock64() - c0w;
                 tc::tc_fence_after();
                 const uint32_t d = tmem0 + buf * BN;
                 for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
+                    c0w = clock64();
                     if (!tc::mbar_wait_bounded(&full_bar[st], use & 1, &abort_flag, p.status, 913)) {
                         ok = false;
                         break;
                     }
+                    c_wf += clock64() - c0w;
                     tc::tc_fence_after();
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
@@ -210,6 +260,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     tc::mma_commit(&empty_bar[st]);
                 }
                 if (ok) tc::mma_commit(&tfull_bar[buf]);
+            }
+            if (p.phases) {
+                p.phases[blockIdx.x * 12 + 2] = clock64() - c_start;
+                p.phases[blockIdx.x * 12 + 3] = c_wf;
+                p.phases[blockIdx.x * 12 + 4] = c_we;
             }
             if (issued) {  // every MMA has finished before TMEM is freed
                 tc::mma_commit(&drain_bar);
@@ -227,10 +282,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ep.bn_var = p.bn_var;
         ep.act = p.act;
         ep.yolo_classes = p.yolo_classes;
+        // the common epilogue (folded batchnorm: bias, then leaky or linear) has its own loop
+        const bool fast = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
+        const bool leaky = p.act == TB_ACT_LEAKY;
         int tl = 0;
+        const long long c_start = clock64();
+        long long c_wt = 0, c_ld = 0, c_st = 0;
         for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
+            const long long c0w = clock64();
             const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 914);
+            c_wt += clock64() - c0w;
             if (!__all_sync(0xffffffffu, ok)) break;  // tcgen05.ld is warp-collective: all lanes or none
             tc::tc_fence_after();
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
@@ -245,23 +307,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll 1
             for (int c = half; c < NCHUNK; c += 2) {
                 float v[32];
+                const long long c0l = clock64();
                 tc::tmem_ld32(taddr + c * 32, v);
+                const long long c1l = clock64();
+                c_ld += c1l - c0l;
                 const int fb = nt * BN + c * 32;
                 if (valid) {
+                    if (fast) {
+                        // bias (+ leaky) (+ residual): every load is issued before the first store
+                        float bv[32], rv[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {  // fully unrolled: v stays in registers
-                        const int f = fb + i;
-                        if (f < p.F) {
-                            float o = conv_epilogue(v[i], f, ep);
-                            const long long off = (long long)f * p.OHW;
-                            if (rb) o = __fadd_rn(o, rb[off]);
-                            yb[off] = o;
+                        for (int i = 0; i < 32; ++i) {
+                            const int f = min(fb + i, p.F - 1);
+                            bv[i] = p.bias ? __ldg(p.bias + f) : 0.f;
+                            rv[i] = rb ? __ldg(rb + (long long)f * p.OHW) : 0.f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float o = p.bias ? __fadd_rn(v[i], bv[i]) : v[i];
+                            if (leaky && o < 0.f) o = (float)(0.1 * (double)o);
+                            if (rb) o = __fadd_rn(o, rv[i]);
+                            if (fb + i < p.F) __stcs(yb + (long long)(fb + i) * p.OHW, o);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int f = fb + i;
+                            if (f < p.F) {
+                                float o = conv_epilogue(v[i], f, ep);
+                                const long long off = (long long)f * p.OHW;
+                                if (rb) o = __fadd_rn(o, rb[off]);
+                                yb[off] = o;
+                            }
                         }
                     }
                 }
+                c_st += clock64() - c1l;
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&tempty_bar[buf]);
+        }
+        if (p.phases && warp == 2 && lane == 0) {
+            p.phases[blockIdx.x * 12 + 5] = clock64() - c_start;
+            p.phases[blockIdx.x * 12 + 6] = c_wt;
+            p.phases[blockIdx.x * 12 + 7] = tl;
+            p.phases[blockIdx.x * 12 + 8] = c_ld;
+            p.phases[blockIdx.x * 12 + 9] = c_st;
         }
     }
     tc::tc_fence_before();
@@ -288,15 +379,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// fp32 tensor map with boxes of 32 x 32 (x 1), 128-byte swizzle with 32-byte atoms, zero fill
-static int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes) {
+// fp32 tensor map, 128-byte swizzle with 32-byte atoms, zero fill out of bounds
+static int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                      const uint32_t* box) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(TB_ERR_CUDA, "tensor-core conv: cuTensorMapEncodeTiled is not available");
-    cuuint64_t d[3], s[2];
-    cuuint32_t box[3] = {32, 32, 1}, es[3] = {1, 1, 1};
-    for (int i = 0; i < rank; ++i) d[i] = dims[i];
+    cuuint64_t d[4], s[3];
+    cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
+    for (int i = 0; i < rank; ++i) d[i] = dims[i], bx[i] = box[i];
     for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, s, box, es,
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, s, bx, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "tensor-core conv: cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -311,11 +403,11 @@ bool conv_tc_supported(const ConvGeom& g) {
 int64_t conv_tc_scratch_floats(const ConvGeom& g) {
     TcPlan pl;  // in-place layers still get a replica when x is not 16-byte aligned
     tc_plan(g, &pl);
-    return g.KW * pl.NPH * g.B * g.C * pl.Hrep * pl.Wp;
+    return g.KW * pl.NPH * g.B * g.C * pl.PS;
 }
 
 template <int BN, int STAGES>
-static int launch_bn(tb_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const TcParams& p) {
+static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
     constexpr int smem = STAGES * (TC_BM * TC_BK * 4 + BN * TC_BK * 4) + 1024;
     static std::mutex mu;
     static bool done[64] = {false};
@@ -328,7 +420,7 @@ static int launch_bn(tb_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, co
         }
     }
     const int grid = (int)std::min<int64_t>(p.tiles_total, ctx->sm_count);
-    k_conv_tc<BN, STAGES><<<grid, TC_THREADS, smem, ctx->stream>>>(a, b, p);
+    k_conv_tc<BN, STAGES><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch("k_conv_tc");
 }
 
@@ -347,78 +439,100 @@ static int choose_bn(const ConvGeom& g, int64_t tiles_m, int sms) {
 
 int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
                    const float* bn_scale, const float* bn_mean, const float* bn_var, const float* res, float* y,
-                   int act, int yolo_classes, float* scratch, int64_t* launches) {
+                   int act, int yolo_classes, float* scratch, int64_t* launches, unsigned long long* phases) {
     if (!conv_tc_supported(g)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: unsupported geometry");
     if (g.B == 0) return TB_OK;
     TcPlan pl;
     tc_plan(g, &pl);
     const bool inplace = pl.inplace && aligned16(x);
-    const float* src = x;
-    uint64_t dims[3], strides[2];
+    TcMaps maps;
+    int r;
+    int64_t Wp, NPH;
     if (inplace) {
-        dims[0] = (uint64_t)(g.H * g.W);
-        dims[1] = (uint64_t)g.C;
-        dims[2] = (uint64_t)g.B;
-        strides[0] = (uint64_t)(g.H * g.W) * 4;
-        strides[1] = (uint64_t)g.x_bs * 4;
+        // x itself: (32 pixels, channel, group, image); H*W % 32 == 0
+        Wp = g.W;
+        NPH = 1;
+        const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)(g.H * g.W / 32), (uint64_t)g.B};
+        const uint64_t st[3] = {(uint64_t)(g.H * g.W) * 4, 128, (uint64_t)g.x_bs * 4};
+        const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
+        r = encode_map(&maps.a4[0], x, 4, dims, st, b4);
+        if (r == TB_OK) r = encode_map(&maps.a1[0], x, 4, dims, st, b1);
+        if (r != TB_OK) return r;
     } else {
         if (!scratch || !aligned16(scratch))
             return fail(TB_ERR_INVALID, "tensor-core conv: this geometry needs a 16-byte-aligned replica buffer");
+        Wp = pl.Wp;
+        NPH = pl.NPH;
         const int64_t plane = pl.Hrep * pl.Wp;
         dim3 rg((unsigned)ceil_div(plane, 4 * 256), (unsigned)g.C, (unsigned)(g.KW * pl.NPH * g.B));
         if (rg.y > 65535 || rg.z > 65535) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: replica grid too large");
         k_tc_repack<<<rg, 256, 0, ctx->stream>>>(x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W,
                                                  (int)g.SY, (int)g.SX, (int)g.DX, (int)g.PX, (int)pl.NPH,
-                                                 (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW);
-        int r = check_launch("k_tc_repack");
+                                                 (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
+        r = check_launch("k_tc_repack");
         if (r != TB_OK) return r;
         if (launches) ++*launches;
-        src = scratch;
-        dims[0] = (uint64_t)plane;
-        dims[1] = (uint64_t)g.C;
-        dims[2] = (uint64_t)(g.KW * pl.NPH * g.B);
-        strides[0] = (uint64_t)plane * 4;
-        strides[1] = (uint64_t)(g.C * plane) * 4;
+        // one view per kernel row: the base moves rowoff(r) replica rows down; a 32-pixel group
+        // at a valid pixel then stays inside its plane (PS has 32 elements of slack)
+        const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)((pl.PS - 32) / 32), (uint64_t)(g.KW * pl.NPH * g.B)};
+        const uint64_t st[3] = {(uint64_t)pl.PS * 4, 128, (uint64_t)(g.C * pl.PS) * 4};
+        const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
+        for (int k = 0; k < g.KH; ++k) {
+            const float* base = scratch + (int64_t)pl.rowoff[k] * pl.Wp;
+            r = encode_map(&maps.a4[k], base, 4, dims, st, b4);
+            if (r == TB_OK) r = encode_map(&maps.a1[k], base, 4, dims, st, b1);
+            if (r != TB_OK) return r;
+        }
     }
-    CUtensorMap ta, tb;
-    int r = encode_map(&ta, src, 3, dims, strides);
-    if (r != TB_OK) return r;
-    const uint64_t wd[2] = {(uint64_t)g.Mpad, (uint64_t)g.Kpad}, ws[1] = {(uint64_t)g.Mpad * 4};
-    r = encode_map(&tb, wp, 2, wd, ws);
-    if (r != TB_OK) return r;
 
     TcParams p{};
     p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
-    p.res = res; p.y = y; p.status = ctx->d_status;
-    p.B = (int)g.B; p.F = (int)g.F; p.KW = (int)g.KW; p.OH = (int)g.OH; p.OW = (int)g.OW;
-    p.Wp = inplace ? (int)g.W : (int)pl.Wp;
-    p.NPH = inplace ? 1 : (int)pl.NPH;
-    p.Lp = (int)round_up(g.OH * p.Wp, 32);
-    p.OHWp = (int)(g.OH * p.Wp);
+    p.res = res; p.y = y; p.status = ctx->d_status; p.phases = phases;
+    p.B = (int)g.B; p.C = (int)g.C; p.F = (int)g.F; p.KW = (int)g.KW; p.OH = (int)g.OH; p.OW = (int)g.OW;
+    p.Wp = (int)Wp;
+    p.NPH = (int)NPH;
+    p.Lp = (int)round_up(g.OH * Wp, 32);
+    p.OHWp = (int)(g.OH * Wp);
     p.OHW = (int)(g.OH * g.OW);
     p.csteps = (int)(g.C / TC_BK);
     p.ktiles = (int)(g.KH * g.KW * p.csteps);
     p.y_bs = g.y_bs; p.r_bs = g.r_bs;
     p.act = act; p.yolo_classes = yolo_classes;
-    for (int i = 0; i < TC_MAX_KH; ++i) {
-        p.rowoff[i] = i < g.KH && !inplace ? pl.rowoff[i] : 0;
-        p.phase[i] = i < g.KH && !inplace ? pl.phase[i] : 0;
-    }
+    for (int i = 0; i < TC_MAX_KH; ++i) p.phase[i] = i < g.KH && !inplace ? pl.phase[i] : 0;
     const int64_t tiles_m = ceil_div(g.B * p.Lp, TC_BM);
     const int bn = choose_bn(g, tiles_m, ctx->sm_count);
     p.tiles_n = (int)ceil_div(g.F, bn);
     const int64_t tiles = tiles_m * p.tiles_n;
     if (tiles >= ((int64_t)1 << 31)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: too many tiles");
     p.tiles_total = (int)tiles;
+    p.b_grouped = g.Mpad % 32 == 0;
+    if (p.b_grouped) {  // (32 filters, k, filter group), one box of bn/32 groups per stage
+        const uint64_t dims[3] = {32, (uint64_t)g.Kpad, (uint64_t)(g.Mpad / 32)};
+        const uint64_t st[2] = {(uint64_t)g.Mpad * 4, 128};
+        const uint32_t box[3] = {32, 32, (uint32_t)(bn / 32)};
+        r = encode_map(&maps.b, wp, 3, dims, st, box);
+    } else {
+        const uint64_t dims[2] = {(uint64_t)g.Mpad, (uint64_t)g.Kpad};
+        const uint64_t st[1] = {(uint64_t)g.Mpad * 4};
+        const uint32_t box[2] = {32, 32};
+        r = encode_map(&maps.b, wp, 2, dims, st, box);
+    }
+    if (r != TB_OK) return r;
     switch (bn) {
-    case 32: r = launch_bn<32, 8>(ctx, ta, tb, p); break;
-    case 64: r = launch_bn<64, 8>(ctx, ta, tb, p); break;
-    case 128: r = launch_bn<128, 6>(ctx, ta, tb, p); break;
-    default: r = launch_bn<256, 4>(ctx, ta, tb, p); break;
+    case 32: r = launch_bn<32, 8>(ctx, maps, p); break;
+    case 64: r = launch_bn<64, 8>(ctx, maps, p); break;
+    case 128: r = launch_bn<128, 6>(ctx, maps, p); break;
+    default: r = launch_bn<256, 4>(ctx, maps, p); break;
     }
     if (r != TB_OK) return r;
     if (launches) ++*launches;
     return TB_OK;
+}
+
+int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n) {
+    if (n <= 0) return TB_OK;
+    k_round_tf32<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(packed, n);
+    return check_launch("k_round_tf32");
 }
 
 }  // namespace tbi

@@ -77,8 +77,26 @@ __device__ __forceinline__ void tma_load_3d(unsigned dst, const void* tmap, uint
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(unsigned dst, const void* tmap, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+    unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(b), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// fp32 -> tf32 (10-bit mantissa), round to nearest with ties away from zero; the low 13 bits
+// of the result are zero.  The tensor core itself drops those bits (truncation), which biases
+// every product toward zero; operands rounded here carry an unbiased error instead.
+__device__ __forceinline__ float to_tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
 }
 
 // --- tcgen05 -----------------------------------------------------------------------------

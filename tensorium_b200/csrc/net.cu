@@ -624,6 +624,8 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         L.d_wp = alloc(g.Kpad * g.Mpad);
         if (!L.d_wp) return err;
         r = tb_conv_pack_weights(net->ctx, &d, raw, L.d_wp);
+        if (r == TB_OK && net->math_mode == TB_MATH_TF32 && conv_tc_supported(g))
+            r = conv_tc_round_weights(net->ctx, L.d_wp, g.Kpad * g.Mpad);
         if (r != TB_OK) return r;
         L.d_bias = dev_upload(net, L.biases, &err);
         if (err != TB_OK) return err;

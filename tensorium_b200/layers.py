@@ -130,7 +130,17 @@ class TConvolutionalLayer(TBaseLayer):
         y = out if out is not None else self.ctx.empty((batch, self.filters, self.outHeight(), self.outWidth()))
         dv = self._dev
         bn = self.isBatchNormalized
-        check(lib.tb_conv2d_fwd(self.ctx.handle, C.byref(d), ptr(x), ptr(dv["w"]), ptr(dv["b"]),
+        w = dv["w"]
+        tc = C.c_int64(0)
+        check(lib.tb_conv_uses_tensor_cores(C.byref(d), math_mode if math_mode >= 0 else self.ctx.math_mode,
+                                            C.byref(tc)))
+        if tc.value:
+            if "w_tf32" not in dv:  # weights rounded to TF32 for the tensor-core mainloop
+                dv["w_tf32"] = torch.empty_like(w)
+                check(lib.tb_conv_pack_weights_tf32(self.ctx.handle, C.byref(self.desc()), ptr(dv["raw"]),
+                                                    ptr(dv["w_tf32"])))
+            w = dv["w_tf32"]
+        check(lib.tb_conv2d_fwd(self.ctx.handle, C.byref(d), ptr(x), ptr(w), ptr(dv["b"]),
                                 ptr(dv["scales"] if bn else None), ptr(dv["mean"] if bn else None),
                                 ptr(dv["var"] if bn else None), ptr(residual), ptr(y), math_mode))
         self.output = y

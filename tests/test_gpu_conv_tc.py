@@ -90,3 +90,33 @@ def test_tc_unsupported_shape_uses_fp32_kernel(ctx):
     a = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9)
     f = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9, math_mode=0)
     assert np.array_equal(a, f)
+
+
+def test_yolov3_tf32_heads_and_boxes(ctx):
+    """Whole YOLOv3-416 on the TF32 path (69 of 75 convs on tensor cores), batch 2, against the
+    FP32 oracle: relative L2 <= 1e-2 on each head conv (per image), and the same detection index
+    set (objectness > 0.45) apart from candidates whose logit lies inside the tolerance band."""
+    from tensorium_b200 import synth
+    from tensorium_b200.net import TNNet
+    specs = synth.yolov3_specs()
+    shape = (3, 416, 416)
+    x = synth.input_images(3, "yolov3", 2, shape)
+    heads, raws = [82, 94, 106], [81, 93, 105]
+    ref = O.run_network(specs, x, keep=heads + raws)
+    net = TNNet(ctx, specs, 2, shape, fusion=False, math_mode=MATH_TF32)
+    net.forward(torch.from_numpy(x).to(ctx.torch_device), use_graph=False)
+    thresh = 0.45
+    logit = np.log(thresh / (1 - thresh))
+    for h, r in zip(heads, raws):
+        raw = net.output(r).cpu().numpy().reshape(2, -1)
+        e = rel_l2_maps(raw, ref[r].reshape(2, -1), 2)
+        print(f"head conv {r}: relative L2 {e:.2e}")
+        assert e <= TF32_TOL, (r, e)
+        got = net.output(h).cpu().numpy().reshape(2, 3, 85, -1)
+        g = got.shape[-1]
+        go, ro = got[:, :, 4], ref[h].reshape(2, 3, 85, g)[:, :, 4]
+        xo = ref[r].reshape(2, 3, 85, g)[:, :, 4]
+        band = TF32_TOL * np.sqrt((ref[r].reshape(2, 3, 85, g)[:, :, 4] ** 2).mean(axis=2, keepdims=True))
+        sure = np.abs(xo - logit) > 4 * band
+        assert np.array_equal((go > thresh)[sure], (ro > thresh)[sure]), h
+    net.close()
