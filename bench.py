@@ -292,6 +292,8 @@ def run_ours(args):
             "detections": {"images_gathered_on_rank0": len(gathered) if gathered is not None else None,
                            "boxes": int(sum(len(r) for r, _ in gathered)) if gathered is not None else None,
                            "thresh": 0.45}}
+    if args.math == "fp32" and not args.no_tf32_block:
+        line["tf32_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream)
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(specs)
         cb["cpu"] = cpu_model()
@@ -303,6 +305,54 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, stream):
+    """The same forward on the TF32 tensor-core path (BASELINE config 3's optional path), timed the
+    same way, with its head error against the FP32 path on the same images."""
+    import torch
+    from tensorium_b200 import synth
+    from tensorium_b200.net import TNNet
+    B = args.batch
+    net = TNNet(ctx, specs, B, INPUT, math_mode=MATH_MODES["tf32"])
+    for _ in range(max(args.warmup, 1)):
+        net.forward(x)
+    launches = net.launch_count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        net.forward(x)
+    e1.record(stream)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    prof = np.zeros(len(specs))
+    for _ in range(3):
+        prof += net.profile(x)
+    prof /= 3
+    conv_ms = float(sum(prof[i] + (prof[i + 1] if i + 1 < len(specs) and specs[i + 1]["type"] in ("shortcut", "yolo") else 0.0)
+                        for i, s in enumerate(specs) if s["type"] == "conv"))
+    flops = synth.conv_flops(specs, INPUT, B)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    achieved = flops / (conv_ms / 1e3) / 1e12
+    # head error of the TF32 path against the FP32 path (relative L2 over the batch)
+    net.forward(x)
+    net32.forward(x)
+    errs = []
+    for h in HEADS:  # yolo outputs (the head convs are fused into them)
+        a, b = net.output(h).double(), net32.output(h).double()
+        errs.append(float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b)))
+    out = {"metric": METRIC_TF32, "value": world * B * args.steps / (ms / 1e3), "unit": "images/s",
+           "ms_per_step": ms / args.steps, "dtype": "tf32 operands rounded to nearest, fp32 accumulate",
+           "gpu_launches": int(launches * args.steps),
+           "roofline": {"bound": "tensor", "kernel": "k_conv_tc (tcgen05 TF32) + tap-replica repack; layer 0 on conv_fp32_kernel",
+                        "achieved": achieved, "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
+                        "peak_source": f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)",
+                        "conv_ms_per_forward": conv_ms},
+           "head_rel_l2_vs_fp32_path": errs, "heads": list(HEADS)}
+    net.close()
+    return out
 
 
 def run_layer_mode(args):
@@ -352,6 +402,7 @@ def main():
     ap.add_argument("--batch", type=int, default=8, help="images per GPU per step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tf32-block", action="store_true", help="skip the TF32-path measurement of the default run")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
     ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
                     help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")

@@ -21,8 +21,10 @@
 // TMEM allocation; one thread issues tcgen05.mma (M = 128, N = BN, K = 8, TF32 in, FP32
 // accumulate) into one of two TMEM accumulators and commits each stage back to the producer.
 // Warps 2-9: the epilogue, overlapped with the next tile's mainloop: tcgen05.ld of 32 filters of
-// one pixel per thread, bias / batchnorm / activation / residual / yolo logistic, NCHW stores
-// in which a warp writes 32 consecutive pixels of one filter.  Every wait is bounded: on timeout
+// one pixel per thread, bias / batchnorm / activation / yolo logistic, then a transpose through
+// a per-warp shared slab so that residual loads and NCHW stores are 16-byte vectors of 4
+// consecutive pixels of one filter.  Outputs are rounded to TF32 (nearest), so a following 1x1
+// layer that reads them in place sees exact TF32 operands.  Every wait is bounded: on timeout
 // the kernel sets the context status word, drains the copies and MMAs in flight, frees its TMEM
 // and returns.
 #include "conv_tc.cuh"
@@ -31,11 +33,14 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace tbi {
 
 constexpr int TC_BM = 128, TC_BK = 32, TC_THREADS = 320, TC_MAX_KH = 8;
+constexpr int TC_STG_LD = 36;                                // slab row stride (floats)
+constexpr int TC_STG_BYTES = 8 * 16 * TC_STG_LD * 4;         // 8 epilogue warps x 16 x 36 floats
 constexpr int TC_BOX_BYTES = 32 * 32 * 4;
 
 struct TcParams {
@@ -49,6 +54,9 @@ struct TcParams {
     unsigned long long* phases;  // diagnostics: per-CTA cycle counters (null in normal launches)
     int B, C, F, KW, OH, OW, Wp, NPH, Lp, OHWp, OHW;
     int b_grouped;  // weights read as one 3-D box per stage (Mpad % 32 == 0)
+    int vec_out;    // y (and res) take 16-byte stores of pixel quads: OW, OHW, batch strides % 4 == 0
+    int g_full;     // 32-pixel groups per image that lie wholly inside it (a1/a4 maps); later
+                    // groups are read through the bounds-checked tail map
     int tiles_n, csteps, ktiles;
     int tiles_total;
     long long y_bs, r_bs;
@@ -65,18 +73,49 @@ struct TcParams {
 struct TcMaps {
     CUtensorMap a4[TC_MAX_KH];
     CUtensorMap a1[TC_MAX_KH];
+    CUtensorMap tail;  // in-place x: (pixel, channel, image), bounds-checked, for a partial last group
     CUtensorMap b;
 };
 
-// Replica layout plan of one geometry.
+// How the A operand is laid out for one geometry.
+enum TcMode {
+    TC_TAPS = 0,     // tap replicas P[s][ph][b][c][Hrep][Wp] (channels % 32 == 0)
+    TC_INPLACE = 1,  // 1x1 stride-1 unpadded, H*W % 4 == 0: x itself on a flat pixel grid
+    TC_IM2COL = 2,   // any other channel count: P[b][k][OH][Wp], one row per packed weight row
+};
+
 struct TcPlan {
+    int mode;
     int64_t Wp, NPH, pad_top, Hrep, Lp, PS;  // PS: replica plane stride (elements)
-    bool inplace;
+    int64_t Cr;                              // channels of the GEMM view (k rows per tap)
     int rowoff[TC_MAX_KH], phase[TC_MAX_KH];
 };
 
 static void tc_plan(const ConvGeom& g, TcPlan* pl) {
+    for (int r = 0; r < TC_MAX_KH; ++r) pl->rowoff[r] = pl->phase[r] = 0;
+    pl->NPH = 1;
+    pl->pad_top = 0;
+    if (g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 && (g.H * g.W) % 4 == 0 &&
+        g.x_bs % 4 == 0 && g.rsc && g.C % 32 == 0) {
+        pl->mode = TC_INPLACE;
+        pl->Wp = g.H * g.W;  // one flat row: pixel q of the image is output pixel q
+        pl->Hrep = 1;
+        pl->Lp = round_up(pl->Wp, 32);
+        pl->PS = 0;
+        pl->Cr = g.C;
+        return;
+    }
     pl->Wp = round_up(g.OW, 4);
+    pl->Lp = round_up(g.OH * pl->Wp, 32);
+    if (!(g.rsc && g.C % 32 == 0)) {
+        pl->mode = TC_IM2COL;
+        pl->Hrep = g.OH;
+        pl->Cr = round_up(g.Kpad, 32);
+        pl->PS = round_up(g.OH * pl->Wp, 32) + 32;
+        return;
+    }
+    pl->mode = TC_TAPS;
+    pl->Cr = g.C;
     pl->NPH = g.SY;
     int64_t mn = 0, mx = 0;
     for (int r = 0; r < g.KH; ++r) {
@@ -90,43 +129,93 @@ static void tc_plan(const ConvGeom& g, TcPlan* pl) {
     pl->pad_top = -mn;
     for (int r = 0; r < g.KH; ++r) pl->rowoff[r] += (int)pl->pad_top;
     pl->Hrep = g.OH + pl->pad_top + mx;
-    pl->Lp = round_up(g.OH * pl->Wp, 32);
     // a 32-pixel group read at a row offset never runs past its own plane
     pl->PS = round_up(pl->Hrep * pl->Wp, 32) + 32;
-    pl->inplace = g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 &&
-                  (g.H * g.W) % 32 == 0 && g.x_bs % 4 == 0;
 }
 
-// P[s][ph][b][c][Hrep][Wp] with planes PS elements apart (the tail of a plane is never
-// written: it is read only for pixels that are dropped); each thread writes 4 consecutive
-// columns (one 16-byte store).
-__global__ void k_tc_repack(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C, int H,
-                            int W, int SY, int SX, int DX, int PX, int NPH, int pad_top, int Hrep, int Wp, int OW,
-                            int PS) {
-    const int plane = Hrep * Wp;
-    const int i4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (i4 >= plane) return;
-    const int c = blockIdx.y;
-    const int zb = blockIdx.z;  // (s * NPH + ph) * B + b
-    const int b = zb % B, sp = zb / B, ph = sp % NPH, s = sp / NPH;
-    const int row = i4 / Wp, x0 = i4 - row * Wp;
-    const int iy = SY * (row - pad_top) + ph;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if ((unsigned)iy < (unsigned)H) {
-        const float* src = x + (long long)b * x_bs + ((long long)c * H + iy) * W;
+// Tap replicas P[s][ph][b][c][Hrep][Wp], planes PS elements apart (the tail of a plane is never
+// written: it is read only for pixels that are dropped).  One thread makes 4 consecutive
+// columns of one (ph, b, c) row for every kernel column s: one 16-byte store per s, values
+// rounded to TF32.
+__global__ void k_tc_repack_taps(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C,
+                                 int H, int W, int KW, int SY, int SX, int DX, int PX, int NPH, int pad_top, int Hrep,
+                                 int Wp, int OW, int PS) {
+    const int q4 = Wp >> 2, per_plane = Hrep * q4;
+    const long long total = (long long)NPH * B * C * per_plane;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int pc = (int)(i / per_plane);  // (ph * B + b) * C + c
+        const int j = (int)(i - (long long)pc * per_plane);
+        const int row = j / q4, x0 = (j - row * q4) * 4;
+        const int c = pc % C, pb = pc / C, b = pb % B, ph = pb / B;
+        const int iy = SY * (row - pad_top) + ph;
+        const bool rok = (unsigned)iy < (unsigned)H;
+        const float* src = x + (long long)b * x_bs + ((long long)c * H + (rok ? iy : 0)) * W;
+        for (int s = 0; s < KW; ++s) {
+            float v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int xx = x0 + j, ix = SX * xx + s * DX - PX;
-            if (xx < OW && (unsigned)ix < (unsigned)W) v[j] = tc::to_tf32_rna(__ldg(src + ix));
+            for (int k = 0; k < 4; ++k) {
+                const int xx = x0 + k, ix = SX * xx + s * DX - PX;
+                v[k] = (rok && xx < OW && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+            }
+            const long long z = ((long long)s * NPH + ph) * B + b;
+            *reinterpret_cast<float4*>(P + (z * C + c) * PS + row * Wp + x0) = make_float4(v[0], v[1], v[2], v[3]);
         }
     }
-    float4* dst = reinterpret_cast<float4*>(P + ((long long)zb * C + c) * PS + i4);
-    *dst = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// im2col rows P[b][k][OH][Wp] in the k order of the packed weights (RSC with Cpad channels per
+// tap, or CRS), rows past the real K zero; values rounded to TF32.
+__global__ void k_tc_repack_im2col(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C,
+                                   int H, int W, int KH, int KW, int SY, int SX, int DY, int DX, int PY, int PX,
+                                   int rsc, int Cpad, int Kreal, int Cr, int OH, int OW, int Wp, int PS) {
+    const int q4 = Wp >> 2, per_plane = OH * q4;
+    const long long total = (long long)B * Cr * per_plane;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int pk = (int)(i / per_plane);  // b * Cr + k
+        const int j = (int)(i - (long long)pk * per_plane);
+        const int oy = j / q4, x0 = (j - oy * q4) * 4;
+        const int k = pk % Cr, b = pk / Cr;
+        int c, r, s;
+        if (rsc) {
+            const int rs = k / Cpad;
+            c = k - rs * Cpad;
+            r = rs / KW;
+            s = rs - r * KW;
+        } else {
+            c = k / (KH * KW);
+            const int rs = k - c * KH * KW;
+            r = rs / KW;
+            s = rs - r * KW;
+        }
+        const bool kok = k < Kreal && c < C && r < KH;
+        const int iy = oy * SY + r * DY - PY;
+        const bool rok = kok && (unsigned)iy < (unsigned)H;
+        const float* src = x + (long long)b * x_bs + ((long long)(rok ? c : 0) * H + (rok ? iy : 0)) * W;
+        float v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int xx = x0 + t, ix = xx * SX + s * DX - PX;
+            v[t] = (rok && xx < OW && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+        }
+        *reinterpret_cast<float4*>(P + (long long)pk * PS + oy * Wp + x0) = make_float4(v[0], v[1], v[2], v[3]);
+    }
 }
 
 __global__ void k_round_tf32(float* __restrict__ p, long long n) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         p[i] = tc::to_tf32_rna(p[i]);
+}
+
+// The epilogue of a pixel quad of one filter for the less common cases (unfused batchnorm,
+// yolo logistic, activations other than leaky / linear); out of line to keep the kernel small.
+static __device__ __noinline__ float4 tc_epilogue4(float4 o, int f, const ConvParams ep) {
+    o.x = conv_epilogue(o.x, f, ep);
+    o.y = conv_epilogue(o.y, f, ep);
+    o.z = conv_epilogue(o.z, f, ep);
+    o.w = conv_epilogue(o.w, f, ep);
+    return o;
 }
 
 template <int BN, int STAGES>
@@ -182,7 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     bq[j] = n / p.Lp;
                     gq[j] = (n - bq[j] * p.Lp) >> 5;
                 }
-                const bool straddle = bq[0] != bq[3];
+                const bool split = bq[0] != bq[3] || gq[3] >= p.g_full;
                 int r = 0, s = 0, c0 = 0;  // kernel tap and first channel of k tile kt
                 for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
@@ -195,12 +284,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES);
                     const int z0 = (s * p.NPH + p.phase[r]) * p.B;
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + A_BYTES;
-                    if (!straddle) {
+                    if (!split) {
                         tc::tma_load_4d(sa, &maps.a4[r], &full_bar[st], 0, c0, gq[0], z0 + bq[0]);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            tc::tma_load_4d(sa + j * TC_BOX_BYTES, &maps.a1[r], &full_bar[st], 0, c0, gq[j], z0 + bq[j]);
+                        for (int j = 0; j < 4; ++j) {
+                            if (gq[j] < p.g_full)
+                                tc::tma_load_4d(sa + j * TC_BOX_BYTES, &maps.a1[r], &full_bar[st], 0, c0, gq[j], z0 + bq[j]);
+                            else
+                                tc::tma_load_3d(sa + j * TC_BOX_BYTES, &maps.tail, &full_bar[st], gq[j] * 32, c0, z0 + bq[j]);
+                        }
                     }
                     if (p.b_grouped) {
                         tc::tma_load_3d(sb, &maps.b, &full_bar[st], 0, kt * TC_BK, nt * (BN / 32));
@@ -273,8 +366,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ---------------- epilogue (warps 2-9) ----------------
+        // TMEM lane = pixel, column = filter.  Per 16-filter slab a warp moves its 32 pixels x 16
+        // filters through a per-warp shared tile (filter-major); then each lane takes a quad of 4
+        // consecutive pixels of one filter: bias / activation / residual / TF32 rounding on a
+        // float4 and one 16-byte store.  The two warps of a TMEM lane window split the slabs.
         const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31 (a warp's lane window)
-        const int half = (warp - 2) >> 2;  // column chunks half, half+2, ...
+        const int half = (warp - 2) >> 2;  // slabs half, half+2, ...
+        float* stg = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES) + (warp - 2) * (16 * TC_STG_LD);
         ConvParams ep;
         ep.bias = p.bias;
         ep.bn_scale = p.bn_scale;
@@ -282,9 +380,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ep.bn_var = p.bn_var;
         ep.act = p.act;
         ep.yolo_classes = p.yolo_classes;
-        // the common epilogue (folded batchnorm: bias, then leaky or linear) has its own loop
+        // the common epilogue (folded batchnorm: bias, then leaky or linear) is inline
         const bool fast = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
         const bool leaky = p.act == TB_ACT_LEAKY;
+        const int qd = lane & 7, frow = lane >> 3;  // this lane's pixel quad and first slab row
         int tl = 0;
         const long long c_start = clock64();
         long long c_wt = 0, c_ld = 0, c_st = 0;
@@ -296,52 +395,77 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!__all_sync(0xffffffffu, ok)) break;  // tcgen05.ld is warp-collective: all lanes or none
             tc::tc_fence_after();
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
-            const int n = mt * TC_BM + quarter * 32 + lane;
+            // this lane's quad: pixels n .. n+3 of the padded grid (one row, one image)
+            const int n = mt * TC_BM + quarter * 32 + qd * 4;
             const int b = n / p.Lp, q = n - b * p.Lp;
             const int oy = q / p.Wp, ox = q - oy * p.Wp;
-            const bool valid = b < p.B && q < p.OHWp && ox < p.OW;
+            const int nvalid = (b < p.B && q < p.OHWp) ? max(0, min(4, p.OW - ox)) : 0;
             const long long pix = (long long)oy * p.OW + ox;
-            float* yb = p.y + (valid ? b * p.y_bs + pix : 0);
-            const float* rb = p.res ? p.res + (valid ? b * p.r_bs + pix : 0) : nullptr;
+            float* yq = p.y + (nvalid ? b * p.y_bs + pix : 0);
+            const float* rq = p.res ? p.res + (nvalid ? b * p.r_bs + pix : 0) : nullptr;
+            const bool vec = nvalid == 4 && p.vec_out;
             const uint32_t taddr = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-            for (int c = half; c < NCHUNK; c += 2) {
-                float v[32];
+            for (int sl = half; sl < BN / 16; sl += 2) {
+                float v[16];
                 const long long c0l = clock64();
-                tc::tmem_ld32(taddr + c * 32, v);
+                tc::tmem_ld16(taddr + sl * 16, v);
                 const long long c1l = clock64();
                 c_ld += c1l - c0l;
-                const int fb = nt * BN + c * 32;
-                if (valid) {
-                    if (fast) {
-                        // bias (+ leaky) (+ residual): every load is issued before the first store
-                        float bv[32], rv[32];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int f = min(fb + i, p.F - 1);
-                            bv[i] = p.bias ? __ldg(p.bias + f) : 0.f;
-                            rv[i] = rb ? __ldg(rb + (long long)f * p.OHW) : 0.f;
+                for (int i = 0; i < 16; ++i) stg[i * TC_STG_LD + lane] = v[i];
+                __syncwarp();
+                const int fb = nt * BN + sl * 16;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int f = fb + frow + 4 * j;
+                    float4 o = *reinterpret_cast<const float4*>(stg + (frow + 4 * j) * TC_STG_LD + qd * 4);
+                    if (f < p.F && nvalid) {
+                        if (fast) {
+                            if (p.bias) {
+                                const float bf = __ldg(p.bias + f);
+                                o.x = __fadd_rn(o.x, bf);
+                                o.y = __fadd_rn(o.y, bf);
+                                o.z = __fadd_rn(o.z, bf);
+                                o.w = __fadd_rn(o.w, bf);
+                            }
+                            if (leaky) {
+                                o.x = o.x < 0.f ? (float)(0.1 * (double)o.x) : o.x;
+                                o.y = o.y < 0.f ? (float)(0.1 * (double)o.y) : o.y;
+                                o.z = o.z < 0.f ? (float)(0.1 * (double)o.z) : o.z;
+                                o.w = o.w < 0.f ? (float)(0.1 * (double)o.w) : o.w;
+                            }
+                        } else {
+                            o = tc_epilogue4(o, f, ep);
                         }
+                        const long long off = (long long)f * p.OHW;
+                        if (vec) {
+                            if (rq) {
+                                const float4 r4 = __ldg(reinterpret_cast<const float4*>(rq + off));
+                                o.x = __fadd_rn(o.x, r4.x);
+                                o.y = __fadd_rn(o.y, r4.y);
+                                o.z = __fadd_rn(o.z, r4.z);
+                                o.w = __fadd_rn(o.w, r4.w);
+                            }
+                            o.x = tc::to_tf32_rna(o.x);
+                            o.y = tc::to_tf32_rna(o.y);
+                            o.z = tc::to_tf32_rna(o.z);
+                            o.w = tc::to_tf32_rna(o.w);
+                            __stcs(reinterpret_cast<float4*>(yq + off), o);
+                        } else {
+                            const float ov[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            float o = p.bias ? __fadd_rn(v[i], bv[i]) : v[i];
-                            if (leaky && o < 0.f) o = (float)(0.1 * (double)o);
-                            if (rb) o = __fadd_rn(o, rv[i]);
-                            if (fb + i < p.F) __stcs(yb + (long long)(fb + i) * p.OHW, o);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int f = fb + i;
-                            if (f < p.F) {
-                                float o = conv_epilogue(v[i], f, ep);
-                                const long long off = (long long)f * p.OHW;
-                                if (rb) o = __fadd_rn(o, rb[off]);
-                                yb[off] = o;
+                            for (int e = 0; e < 4; ++e) {
+                                if (e < nvalid) {
+                                    float w = ov[e];
+                                    if (rq) w = __fadd_rn(w, __ldg(rq + off + e));
+                                    yq[off + e] = tc::to_tf32_rna(w);
+                                }
                             }
                         }
                     }
                 }
+                __syncwarp();
                 c_st += clock64() - c1l;
             }
             tc::tc_fence_before();
@@ -396,19 +520,29 @@ static int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_
 }
 
 bool conv_tc_supported(const ConvGeom& g) {
-    return g.rsc && g.C % TC_BK == 0 && g.Cpad == g.C && g.KH <= TC_MAX_KH && g.SY <= 4 &&
-           g.B * round_up(g.OH * round_up(g.OW, 4), 32) < ((int64_t)1 << 31) - TC_BM;
+    // one output pixel per image (a connected layer) would fill one row of a 32-pixel group
+    if (g.KH > TC_MAX_KH || g.SY > 4 || g.OH * g.OW == 1) return false;
+    TcPlan pl;
+    tc_plan(g, &pl);
+    return pl.Cr <= 4096 && g.B * pl.Lp < ((int64_t)1 << 31) - TC_BM &&
+           g.KW * pl.NPH * g.B <= 65535 && g.B * pl.Cr * pl.PS < ((int64_t)1 << 40);
 }
 
 int64_t conv_tc_scratch_floats(const ConvGeom& g) {
-    TcPlan pl;  // in-place layers still get a replica when x is not 16-byte aligned
+    TcPlan pl;
     tc_plan(g, &pl);
+    if (pl.mode == TC_INPLACE) {
+        // x that is not 16-byte aligned is copied into a tap replica instead
+        const int64_t Wp = round_up(g.OW, 4);
+        return g.B * g.C * (round_up(g.OH * Wp, 32) + 32);
+    }
+    if (pl.mode == TC_IM2COL) return g.B * pl.Cr * pl.PS;
     return g.KW * pl.NPH * g.B * g.C * pl.PS;
 }
 
 template <int BN, int STAGES>
 static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
-    constexpr int smem = STAGES * (TC_BM * TC_BK * 4 + BN * TC_BK * 4) + 1024;
+    constexpr int smem = STAGES * (TC_BM * TC_BK * 4 + BN * TC_BK * 4) + TC_STG_BYTES + 1024;
     static std::mutex mu;
     static bool done[64] = {false};
     {
@@ -444,40 +578,59 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     if (g.B == 0) return TB_OK;
     TcPlan pl;
     tc_plan(g, &pl);
-    const bool inplace = pl.inplace && aligned16(x);
+    if (pl.mode == TC_INPLACE && !aligned16(x)) {  // same result through a (1-tap) replica
+        ConvGeom g2 = g;
+        g2.x_bs = g.x_bs + 1;  // any stride that is not a multiple of 4 selects the replica plan
+        tc_plan(g2, &pl);
+    }
     TcMaps maps;
+    memset(&maps, 0, sizeof(maps));
     int r;
-    int64_t Wp, NPH;
-    if (inplace) {
-        // x itself: (32 pixels, channel, group, image); H*W % 32 == 0
-        Wp = g.W;
-        NPH = 1;
-        const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)(g.H * g.W / 32), (uint64_t)g.B};
-        const uint64_t st[3] = {(uint64_t)(g.H * g.W) * 4, 128, (uint64_t)g.x_bs * 4};
-        const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
+    int kmaps = 1;  // A maps in use (one per distinct kernel row for tap replicas)
+    const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
+    int g_full = 1 << 30;
+    if (pl.mode == TC_INPLACE) {
+        // x itself: (32 pixels, channel, 32-pixel group, image); a partial last group of an
+        // image goes through the bounds-checked (pixel, channel, image) tail map
+        const int64_t HW = g.H * g.W;
+        g_full = (int)(HW / 32);
+        const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)std::max<int64_t>(g_full, 1), (uint64_t)g.B};
+        const uint64_t st[3] = {(uint64_t)HW * 4, 128, (uint64_t)g.x_bs * 4};
         r = encode_map(&maps.a4[0], x, 4, dims, st, b4);
         if (r == TB_OK) r = encode_map(&maps.a1[0], x, 4, dims, st, b1);
+        const uint64_t td[3] = {(uint64_t)HW, (uint64_t)g.C, (uint64_t)g.B};
+        const uint64_t ts[2] = {(uint64_t)HW * 4, (uint64_t)g.x_bs * 4};
+        const uint32_t tb[3] = {32, 32, 1};
+        if (r == TB_OK) r = encode_map(&maps.tail, x, 3, td, ts, tb);
         if (r != TB_OK) return r;
     } else {
         if (!scratch || !aligned16(scratch))
             return fail(TB_ERR_INVALID, "tensor-core conv: this geometry needs a 16-byte-aligned replica buffer");
-        Wp = pl.Wp;
-        NPH = pl.NPH;
-        const int64_t plane = pl.Hrep * pl.Wp;
-        dim3 rg((unsigned)ceil_div(plane, 4 * 256), (unsigned)g.C, (unsigned)(g.KW * pl.NPH * g.B));
-        if (rg.y > 65535 || rg.z > 65535) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: replica grid too large");
-        k_tc_repack<<<rg, 256, 0, ctx->stream>>>(x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W,
-                                                 (int)g.SY, (int)g.SX, (int)g.DX, (int)g.PX, (int)pl.NPH,
-                                                 (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
+        int64_t Z;
+        if (pl.mode == TC_IM2COL) {
+            Z = g.B;
+            const int64_t total = g.B * pl.Cr * g.OH * (pl.Wp / 4);
+            k_tc_repack_im2col<<<grid_for(total, 256, ctx->sm_count, 4), 256, 0, ctx->stream>>>(
+                x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KH, (int)g.KW, (int)g.SY,
+                (int)g.SX, (int)g.DY, (int)g.DX, (int)g.PY, (int)g.PX, g.rsc ? 1 : 0, (int)g.Cpad,
+                (int)(g.rsc ? g.KH * g.KW * g.Cpad : g.C * g.KH * g.KW), (int)pl.Cr, (int)g.OH, (int)g.OW,
+                (int)pl.Wp, (int)pl.PS);
+        } else {
+            Z = g.KW * pl.NPH * g.B;
+            const int64_t total = pl.NPH * g.B * g.C * pl.Hrep * (pl.Wp / 4);
+            k_tc_repack_taps<<<grid_for(total, 256, ctx->sm_count, 2), 256, 0, ctx->stream>>>(
+                x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KW, (int)g.SY, (int)g.SX,
+                (int)g.DX, (int)g.PX, (int)pl.NPH, (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
+            kmaps = (int)g.KH;
+        }
         r = check_launch("k_tc_repack");
         if (r != TB_OK) return r;
         if (launches) ++*launches;
         // one view per kernel row: the base moves rowoff(r) replica rows down; a 32-pixel group
         // at a valid pixel then stays inside its plane (PS has 32 elements of slack)
-        const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)((pl.PS - 32) / 32), (uint64_t)(g.KW * pl.NPH * g.B)};
-        const uint64_t st[3] = {(uint64_t)pl.PS * 4, 128, (uint64_t)(g.C * pl.PS) * 4};
-        const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
-        for (int k = 0; k < g.KH; ++k) {
+        const uint64_t dims[4] = {32, (uint64_t)pl.Cr, (uint64_t)((pl.PS - 32) / 32), (uint64_t)Z};
+        const uint64_t st[3] = {(uint64_t)pl.PS * 4, 128, (uint64_t)(pl.Cr * pl.PS) * 4};
+        for (int k = 0; k < kmaps; ++k) {
             const float* base = scratch + (int64_t)pl.rowoff[k] * pl.Wp;
             r = encode_map(&maps.a4[k], base, 4, dims, st, b4);
             if (r == TB_OK) r = encode_map(&maps.a1[k], base, 4, dims, st, b1);
@@ -488,17 +641,26 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     TcParams p{};
     p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
     p.res = res; p.y = y; p.status = ctx->d_status; p.phases = phases;
-    p.B = (int)g.B; p.C = (int)g.C; p.F = (int)g.F; p.KW = (int)g.KW; p.OH = (int)g.OH; p.OW = (int)g.OW;
-    p.Wp = (int)Wp;
-    p.NPH = (int)NPH;
-    p.Lp = (int)round_up(g.OH * Wp, 32);
-    p.OHWp = (int)(g.OH * Wp);
+    p.B = (int)g.B; p.C = (int)pl.Cr; p.F = (int)g.F; p.OW = (int)(pl.mode == TC_INPLACE ? pl.Wp : g.OW);
+    p.OH = (int)g.OH;
+    p.Wp = (int)pl.Wp;
+    p.NPH = (int)pl.NPH;
+    p.Lp = (int)pl.Lp;
+    p.OHWp = (int)(pl.mode == TC_INPLACE ? pl.Wp : g.OH * pl.Wp);
     p.OHW = (int)(g.OH * g.OW);
-    p.csteps = (int)(g.C / TC_BK);
-    p.ktiles = (int)(g.KH * g.KW * p.csteps);
+    p.g_full = g_full;
+    {
+        const bool ow4 = pl.mode == TC_INPLACE || g.OW % 4 == 0;
+        p.vec_out = ow4 && (g.OH * g.OW) % 4 == 0 && g.y_bs % 4 == 0 && aligned16(y) &&
+                    (!res || (g.r_bs % 4 == 0 && aligned16(res)));
+    }
+    p.csteps = (int)(pl.Cr / TC_BK);
+    const int taps = pl.mode == TC_TAPS ? (int)(g.KH * g.KW) : 1;
+    p.KW = pl.mode == TC_TAPS ? (int)g.KW : 1;
+    p.ktiles = taps * p.csteps;
     p.y_bs = g.y_bs; p.r_bs = g.r_bs;
     p.act = act; p.yolo_classes = yolo_classes;
-    for (int i = 0; i < TC_MAX_KH; ++i) p.phase[i] = i < g.KH && !inplace ? pl.phase[i] : 0;
+    for (int i = 0; i < TC_MAX_KH; ++i) p.phase[i] = pl.phase[i];
     const int64_t tiles_m = ceil_div(g.B * p.Lp, TC_BM);
     const int bn = choose_bn(g, tiles_m, ctx->sm_count);
     p.tiles_n = (int)ceil_div(g.F, bn);

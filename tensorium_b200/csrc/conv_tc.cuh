@@ -30,23 +30,28 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(a), "r"(bytes) : "memory");
 }
 
+// Waits for the phase with this parity, the thread suspended in hardware for up to ~1 us per try.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
     unsigned a = (unsigned)__cvta_generic_to_shared(bar);
     unsigned ok;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(1000u)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait: gives up after ~2^24 polls (seconds), sets *abort and the device status word.
+// Bounded wait: gives up after ~2^32 SM clock cycles (about 2 s), or at once when another role
+// has aborted; on timeout sets *abort and the device status word.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, volatile int* abort,
                                                   int* status, int code) {
-    for (unsigned it = 0; it < (1u << 24); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
+        if (clock64() - t0 > (1ll << 32)) break;
     }
     *abort = 1;
     if (status) atomicExch(status, code);
@@ -55,7 +60,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
 
 // Wait with a poll limit only (used to drain copies already in flight after an abort).
 __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, unsigned parity) {
-    for (unsigned it = 0; it < (1u << 22); ++it)
+    const long long t0 = clock64();
+    while (clock64() - t0 < (1ll << 31))
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
@@ -90,13 +96,15 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
-// fp32 -> tf32 (10-bit mantissa), round to nearest with ties away from zero; the low 13 bits
-// of the result are zero.  The tensor core itself drops those bits (truncation), which biases
-// every product toward zero; operands rounded here carry an unbiased error instead.
+// fp32 -> tf32 (10-bit mantissa), round to nearest with ties away from zero: add half of the
+// tf32 unit in the last place (bit 12) to the magnitude bits and clear the 13 low bits (a carry
+// into the exponent is the correct rounding up, to infinity past the largest finite value);
+// infinities and NaNs pass unchanged.  The tensor core itself drops those bits (truncation),
+// which biases every product toward zero; operands rounded here carry an unbiased error.
 __device__ __forceinline__ float to_tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+    return __uint_as_float(u);
 }
 
 // --- tcgen05 -----------------------------------------------------------------------------
@@ -148,6 +156,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // shared-memory matrix descriptor: MN-major, 128-byte swizzle with 32-byte atoms (layout type 1),

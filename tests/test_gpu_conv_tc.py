@@ -49,6 +49,11 @@ CASES = [  # (B, C, H, F, k, s, p, dil): C % 32 == 0, the shapes the tcgen05 pat
     (1, 64, 27, 48, 3, 2, 1, 1),      # stride 2, odd input size
     (1, 32, 20, 32, 3, 1, 2, 2),      # dilation 2
     (2, 32, 17, 64, 5, 1, 2, 1),      # 5x5
+    (2, 3, 64, 32, 3, 1, 1, 1),       # YOLOv3 layer-0 shape (3 channels): im2col rows, K = 27 -> 32
+    (4, 1, 28, 32, 5, 1, 2, 1),       # MNIST conv1 (1 channel, 5x5)
+    (1, 20, 17, 40, 3, 1, 2, 2),      # 20 channels (RSC packing, Cpad 32), dilation 2: im2col rows
+    (2, 64, 13, 96, 1, 1, 0, 1),      # 1x1 with H*W % 4 != 0: one-tap replica
+    (2, 64, 26, 48, 1, 1, 0, 1),      # 1x1 in place, H*W % 32 != 0: bounds-checked last group
 ]
 
 
@@ -81,14 +86,14 @@ def test_tc_conv_batchnorm_and_residual(ctx):
 
 
 def test_tc_unsupported_shape_uses_fp32_kernel(ctx):
-    """Channel counts that are not a multiple of 32 are not on the tensor-core path: TF32 mode
-    gives the FP32 kernel's result."""
+    """A conv with one output pixel per image (a connected layer) is not on the tensor-core path:
+    TF32 mode gives the FP32 kernel's result."""
     rng = np.random.default_rng(12)
-    x = rng.uniform(0, 1, (1, 20, 26, 26)).astype(np.float32)
-    w = (rng.standard_normal((64, 20 * 9)) * 0.1).astype(np.float32)
-    b = np.zeros(64, np.float32)
-    a = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9)
-    f = run_layer(ctx, x, w, b, 64, 3, 1, 1, 9, math_mode=0)
+    x = rng.uniform(0, 1, (16, 64, 1, 1)).astype(np.float32)
+    w = (rng.standard_normal((32, 64)) * 0.1).astype(np.float32)
+    b = np.zeros(32, np.float32)
+    a = run_layer(ctx, x, w, b, 32, 1, 1, 0, 9)
+    f = run_layer(ctx, x, w, b, 32, 1, 1, 0, 9, math_mode=0)
     assert np.array_equal(a, f)
 
 
