@@ -294,6 +294,11 @@ def run_ours(args):
                            "thresh": 0.45}}
     if args.math == "fp32" and not args.no_tf32_block:
         line["tf32_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream)
+    if world == 1 and not args.no_kernel_suite:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        mem, xnor = kernel_suite(ctx, peaks.get("hbm_gbs", 6650.0))
+        line["memory_bound_kernels"] = mem
+        line["xnor_conv"] = xnor
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(specs)
         cb["cpu"] = cpu_model()
@@ -355,6 +360,123 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
     return out
 
 
+def kernel_suite(ctx, hbm_gbs):
+    """Each memory-bound layer kernel on its own, at a BASELINE shape scaled past the 126 MB L2
+    (so every launch streams from HBM), and the XNOR conv over BASELINE config 4.  Bytes are the
+    compulsory reads + writes of the kernel's logical inputs and outputs."""
+    import ctypes as C
+    import torch
+    from tensorium_b200._lib import XNOR_PAD_BIT0, check, lib
+    from tensorium_b200.context import ptr
+    from tensorium_b200.layers import TXNORConvolutionLayer, TNNetState
+    dev = ctx.torch_device
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timeit(fn, reps=20, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = []
+
+    def add(name, shape, nbytes, fn, ref):
+        ms = timeit(fn)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out.append({"kernel": name, "replaces": ref, "shape": shape, "bytes": int(nbytes), "ms": ms,
+                    "gb_s": gbs, "frac_of_measured_hbm": gbs / hbm_gbs})
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    # maxpool 2x2/2, config 2 stage-1 shape [1024,128,32,32]
+    x = torch.rand((1024, 128, 32, 32), device=dev, generator=g)
+    y = torch.empty((1024, 128, 16, 16), device=dev)
+    idx = torch.empty((1024, 128, 16, 16), dtype=torch.int64, device=dev)
+    add("k_maxpool2x2", "1024x128x32x32 -> 16x16", x.numel() * 4 + y.numel() * 4,
+        lambda: check(lib.tb_maxpool_fwd(ctx.handle, 1024, 128, 32, 32, 2, 2, 2, 0, ptr(x), ptr(y), None)),
+        "TMaxPoolLayer.forwardMaxPool (source/nMaxPoolLayer.pas:363-463)")
+    add("k_maxpool2x2 +argmax", "1024x128x32x32 -> 16x16, int64 indexes", x.numel() * 4 + y.numel() * 12,
+        lambda: check(lib.tb_maxpool_fwd(ctx.handle, 1024, 128, 32, 32, 2, 2, 2, 0, ptr(x), ptr(y), ptr(idx))),
+        "same, with indexes")
+    del x, y, idx
+    # upsample x2, YOLOv3 route-97 input [B,128,26,26] at B = 256
+    x = torch.rand((256, 128, 26, 26), device=dev, generator=g)
+    y = torch.empty((256, 128, 52, 52), device=dev)
+    add("k_upsample2", "256x128x26x26 -> 52x52", x.numel() * 4 + y.numel() * 4,
+        lambda: check(lib.tb_upsample_fwd(ctx.handle, 256, 128, 26, 26, 2, 1.0, ptr(x), ptr(y), 0)),
+        "upsample (source/nupsamplelayer.pas:83-113)")
+    del x, y
+    # shortcut (unfused), 52x52x256 at B = 64
+    a = torch.rand((64, 256, 52, 52), device=dev, generator=g)
+    b = torch.rand_like(a)
+    y = torch.empty_like(a)
+    add("k_shortcut4", "64x256x52x52", a.numel() * 12,
+        lambda: check(lib.tb_shortcut_fwd(ctx.handle, a.numel(), ptr(a), ptr(b), ptr(y), 9)),
+        "TAddLayer.forward addvv + activate (source/naddlayer.pas:667-725)")
+    # route (per-image concat, when not zero-copy): [64,256,26,26] + [64,512,26,26]
+    r1 = a.view(-1)[: 64 * 256 * 676].view(64, 256 * 676)
+    r2 = b.view(-1)[: 64 * 512 * 676].view(64, 512 * 676)
+    yr = torch.empty((64, 768 * 676), device=dev)
+    arr = (C.c_void_p * 2)(r1.data_ptr(), r2.data_ptr())
+    sizes = (C.c_int64 * 2)(256 * 676, 512 * 676)
+    add("k_copy_rows4 (route)", "64x(256+512)x26x26", yr.numel() * 8,
+        lambda: check(lib.tb_route_fwd(ctx.handle, 64, 2, arr, sizes, ptr(yr), 1)),
+        "TConcatLayer.forward / TTensor.concat (source/ntensors.pas:12045-12061)")
+    # leaky activation in place
+    add("k_activate (leaky)", "64x256x52x52", a.numel() * 8,
+        lambda: check(lib.tb_activate(ctx.handle, a.numel(), ptr(a), 0, 9)),
+        "activate_array (source/nactivation.pas:508-621)")
+    del a, b, y, yr
+    # yolo forward (unfused), [64, 3*85, 52, 52]
+    x = torch.rand((64, 255, 52, 52), device=dev, generator=g)
+    y = torch.empty_like(x)
+    add("k_yolo", "64x255x52x52", x.numel() * 8,
+        lambda: check(lib.tb_yolo_fwd(ctx.handle, 64, 3, 80, 52, 52, ptr(x), ptr(y), 1.0)),
+        "TYoloLayer.forward (source/nyololayer.pas:786-825)")
+    del x, y
+    torch.cuda.empty_cache()
+
+    # XNOR conv, BASELINE config 4: C_in = C_out in {128..1024}, 3x3 s1 p1, batch 64; its
+    # roofline is the measured xor+popcount+add rate of this GPU
+    popc = C.c_double()
+    check(lib.tb_diag_popc_tbitmac(ctx.handle, C.byref(popc)))
+    xnor = [{"popc_peak_tbitmac_s": popc.value,
+             "peak_source": "tb_diag_popc_tbitmac: register-resident xor+popcount+add on every SM, this run"}]
+    rng = np.random.default_rng(4)
+    for S in (52, 26, 13):
+        for Cn in (128, 256, 512, 1024):
+            L = TXNORConvolutionLayer(64, S, S, Cn, Cn, 3, 1, 1, "linear", XNOR_PAD_BIT0)
+            L.upload(ctx, rng.standard_normal((Cn, Cn * 9)).astype(np.float32))
+            xx = torch.randn((64, Cn, S, S), device=dev, generator=g)
+            st = TNNetState(xx)
+            ms = timeit(lambda: L.forward(st), reps=5, warm=2)
+            bitmacs = Cn * (64 * S * S) * (Cn * 9)
+            out_bytes = 64 * Cn * S * S * 4 * 2  # fp32 input read + output written
+            xnor.append({"shape": f"{Cn}->{Cn} 3x3 at {S}x{S}, batch 64", "ms": ms,
+                         "tbitmac_s": bitmacs / (ms / 1e3) / 1e12,
+                         "frac_of_measured_popc_rate": bitmacs / (ms / 1e3) / 1e12 / popc.value,
+                         "io_gb_s": out_bytes / (ms / 1e3) / 1e9})
+            del L, xx, st
+            torch.cuda.empty_cache()
+    return out, xnor
+
+
+def run_kernel_suite(args):
+    from tensorium_b200 import Context
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    ctx = Context(0)
+    mem, xnor = kernel_suite(ctx, peaks.get("hbm_gbs", 6650.0))
+    print(json.dumps({"memory_bound_kernels": mem, "xnor_conv": xnor,
+                      "hbm_peak_gb_s": peaks.get("hbm_gbs", 6650.0),
+                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s"}))
+    ctx.close()
+
+
 def run_layer_mode(args):
     """Time one YOLOv3 conv layer (index args.layer) at batch args.batch through tb_conv2d_fwd:
     the small, self-contained case used for ncu captures and per-layer tuning."""
@@ -403,6 +525,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tf32-block", action="store_true", help="skip the TF32-path measurement of the default run")
+    ap.add_argument("--no-kernel-suite", action="store_true", help="skip the memory-bound / XNOR kernel suite")
+    ap.add_argument("--suite", choices=["kernels"], default=None, help="run only the kernel suite")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
     ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
                     help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")
@@ -410,7 +534,9 @@ def main():
                     help="eager forwards inside cudaProfilerStart/Stop (for ncu --profile-from-start off); "
                          "the printed numbers are then not bench values")
     args = ap.parse_args()
-    if args.layer is not None:
+    if args.suite == "kernels":
+        run_kernel_suite(args)
+    elif args.layer is not None:
         run_layer_mode(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -343,6 +343,10 @@ int tb_net_profile(tb_net* net, const float* x, double* ms_out);
 /* FP32 FFMA throughput of this GPU (TFLOP/s) from a register-resident FMA loop on every SM;
  * the roofline denominator of the FP32 CUDA-core conv path (no reference counterpart). Blocks. */
 int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops);
+/* Integer-pipe rate of the XNOR conv's inner step (xor + popcount + add of 32-bit words, in
+ * registers, on every SM) in Tbit-MAC/s (32 per popcount): the roofline denominator of
+ * tb_xnor_conv_fwd (no reference counterpart). Blocks. */
+int tb_diag_popc_tbitmac(tb_ctx* ctx, double* tbitmac);
 /* One launch of the TF32 tensor-core conv on this geometry (bias, batchnorm and residual off)
  * with per-CTA cycle counters; out12 = averages over CTAs of: producer total cycles, producer
  * cycles waiting for a free stage, MMA-issuer total, MMA waiting for loaded stages, MMA waiting

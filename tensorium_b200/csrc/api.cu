@@ -85,20 +85,31 @@ using namespace tbi;
 // ---------------------------------------------------------------------------------------
 // kernels
 // ---------------------------------------------------------------------------------------
+// Four float4 per thread, all loads issued before any arithmetic (keeps enough bytes in flight
+// per SM to stream at HBM speed); the ragged tail is scalar.
 __global__ void k_activate(int64_t n, float* __restrict__ x, int act) {
-    int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    int64_t n4 = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? n / 4 : 0;
+    const int64_t n4 = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? n / 4 : 0;
     float4* x4 = reinterpret_cast<float4*>(x);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-        float4 v = x4[i];
-        v.x = tb_activate_dev(v.x, act);
-        v.y = tb_activate_dev(v.y, act);
-        v.z = tb_activate_dev(v.z, act);
-        v.w = tb_activate_dev(v.w, act);
-        x4[i] = v;
+    const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x) * 4 + threadIdx.x;
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int64_t i = i0 + (int64_t)k * blockDim.x;
+        if (i < n4) v[k] = x4[i];
     }
-    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-        x[i] = tb_activate_dev(x[i], act);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int64_t i = i0 + (int64_t)k * blockDim.x;
+        if (i < n4) {
+            v[k].x = tb_activate_dev(v[k].x, act);
+            v[k].y = tb_activate_dev(v[k].y, act);
+            v[k].z = tb_activate_dev(v[k].z, act);
+            v[k].w = tb_activate_dev(v[k].w, act);
+            x4[i] = v[k];
+        }
+    }
+    if (blockIdx.x == 0)
+        for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) x[i] = tb_activate_dev(x[i], act);
 }
 
 __global__ void k_forward_bias(int64_t total, float* __restrict__ dst, int64_t bias_size,
@@ -159,10 +170,54 @@ __global__ void k_fma_probe(float* out, int iters, float a, float b) {
     if (s == 12345.678f) out[0] = s;  // keeps the chains live
 }
 
+// XNOR inner-loop probe: per step one xor + popcount + add on 8 independent words per thread
+// (the k_xnor_conv inner loop without memory), the operand changing every step.
+__global__ void k_popc_probe(int* out, int iters) {
+    uint32_t x[8];
+    int acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = threadIdx.x * 2654435761u + j * 40503u, acc[j] = 0;
+    uint32_t k = blockIdx.x;
+    for (int i = 0; i < iters; ++i) {
+        k = k * 1664525u + 1013904223u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __popc(x[j] ^ k);
+    }
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += acc[j];
+    if (s == 123456789) out[0] = s;  // keeps the chains live
+}
+
 // ---------------------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------------------
 extern "C" {
+
+int tb_diag_popc_tbitmac(tb_ctx* ctx, double* tbitmac) {
+    TB_ENTER(ctx);
+    if (!tbitmac) return fail(TB_ERR_INVALID, "null output");
+    const int threads = 512, blocks = ctx->sm_count * 4, iters = 4096;
+    cudaEvent_t e0, e1;
+    TB_CHECK_CUDA(cudaEventCreate(&e0));
+    TB_CHECK_CUDA(cudaEventCreate(&e1));
+    int* out = reinterpret_cast<int*>(ctx->ws);
+    k_popc_probe<<<blocks, threads, 0, ctx->stream>>>(out, iters);  // warm-up
+    cudaEventRecord(e0, ctx->stream);
+    for (int r = 0; r < 10; ++r) k_popc_probe<<<blocks, threads, 0, ctx->stream>>>(out, iters);
+    cudaEventRecord(e1, ctx->stream);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (e == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return cuda_fail(e, "popc probe");
+    int r = check_launch("k_popc_probe");
+    if (r != TB_OK) return r;
+    // 32 bit-MACs (xnor + count of one 32-bit word pair) per popcount
+    *tbitmac = 10.0 * 32.0 * 8.0 * iters * (double)threads * blocks / (ms * 1e-3) / 1e12;
+    return TB_OK;
+}
 
 int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops) {
     TB_ENTER(ctx);
@@ -323,7 +378,12 @@ int tb_activate(tb_ctx* ctx, int64_t n, float* x, int64_t offset, int64_t act) {
     if (n < 0 || (n > 0 && !x)) return fail(TB_ERR_INVALID, "bad tb_activate arguments");
     if (!act_supported(act)) return fail(TB_ERR_UNSUPPORTED, "activation %lld not supported", (long long)act);
     if (n == 0 || act == TB_ACT_LINEAR) return TB_OK;  // ActivateArray skips LINEAR (nncuda.pas:533)
-    k_activate<<<grid_for(n, 256, ctx->sm_count, 4), 256, 0, ctx->stream>>>(n, x + offset, (int)act);
+    {
+        const int64_t n4 = ((reinterpret_cast<uintptr_t>(x + offset) & 15u) == 0) ? n / 4 : 0;
+        const int64_t blocks = std::max<int64_t>(1, ceil_div(n4, 256 * 4));
+        if (blocks > 2147483647) return fail(TB_ERR_UNSUPPORTED, "tb_activate: tensor too large");
+        k_activate<<<(unsigned)blocks, 256, 0, ctx->stream>>>(n, x + offset, (int)act);
+    }
     return check_launch("k_activate");
 }
 

@@ -152,15 +152,32 @@ __global__ void k_shortcut(int64_t n, const float* __restrict__ a, const float* 
 }
 
 // ---- yolo: TYoloLayer.forward (source/nyololayer.pas:786-825) ----
-__global__ void k_yolo(int64_t total, int entries, int hw, const float* __restrict__ x,
-                       float* __restrict__ y, float scale_xy, float bias_xy) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        int e = (int)((i / hw) % entries);
-        float v = x[i];
-        if (e != 2 && e != 3) v = tb_logistic(v);
-        if (e < 2 && scale_xy != 1.0f) v = __fadd_rn(__fmul_rn(v, scale_xy), bias_xy);
-        y[i] = v;
+// One (image, anchor, entry) plane of hw values per blockIdx.y, so the entry (and whether the
+// logistic applies) is uniform in a block; float4 accesses when every plane is 16-byte aligned.
+__global__ void k_yolo(int entries, int hw, int vec4, const float* __restrict__ x, float* __restrict__ y,
+                       float scale_xy, float bias_xy) {
+    const int e = blockIdx.y % entries;
+    const bool logi = e != 2 && e != 3, sxy = e < 2 && scale_xy != 1.0f;
+    const int64_t base = (int64_t)blockIdx.y * hw;
+    auto f = [&](float v) {
+        if (logi) v = tb_logistic(v);
+        if (sxy) v = __fadd_rn(__fmul_rn(v, scale_xy), bias_xy);
+        return v;
+    };
+    if (vec4) {
+        const float4* x4 = reinterpret_cast<const float4*>(x + base);
+        float4* y4 = reinterpret_cast<float4*>(y + base);
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hw / 4; i += gridDim.x * blockDim.x) {
+            float4 v = __ldg(x4 + i);
+            v.x = f(v.x);
+            v.y = f(v.y);
+            v.z = f(v.z);
+            v.w = f(v.w);
+            y4[i] = v;
+        }
+    } else {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hw; i += gridDim.x * blockDim.x)
+            y[base + i] = f(__ldg(x + base + i));
     }
 }
 
@@ -309,10 +326,16 @@ int tb_yolo_fwd(tb_ctx* ctx, int64_t batch, int64_t n, int64_t classes, int64_t 
     if (batch < 0 || n <= 0 || classes < 0 || h <= 0 || w <= 0) return fail(TB_ERR_INVALID, "yolo: bad shape");
     if (batch == 0) return TB_OK;
     if (!x || !y) return fail(TB_ERR_INVALID, "yolo: null pointer");
-    const int64_t total = batch * n * (classes + 5) * h * w;
+    const int64_t planes = batch * n * (classes + 5), hw = h * w;
+    if (planes > 2147483647 || hw > 2147483647) return fail(TB_ERR_UNSUPPORTED, "yolo: tensor too large");
     float bias_xy = (float)(0.5 * (1.0 - (double)scale_xy));
-    k_yolo<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        total, (int)(classes + 5), (int)(h * w), x, y, scale_xy, bias_xy);
+    const int vec4 = hw % 4 == 0 && aligned16(x) && aligned16(y);
+    const int64_t per = vec4 ? hw / 4 : hw;
+    dim3 grid((unsigned)std::min<int64_t>(ceil_div(per, 256), 64), (unsigned)planes);
+    if (grid.y > 65535) {  // fall back to fewer, longer planes per block is not needed at darknet sizes
+        return fail(TB_ERR_UNSUPPORTED, "yolo: more than 65535 (image, anchor, entry) planes");
+    }
+    k_yolo<<<grid, 256, 0, ctx->stream>>>((int)(classes + 5), (int)hw, vec4, x, y, scale_xy, bias_xy);
     return check_launch("k_yolo");
 }
 
