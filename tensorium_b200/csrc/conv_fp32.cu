@@ -254,19 +254,19 @@ int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
     if (g.B == 0) return TB_OK;
     const int mode = conv_mode_of(g, aligned16(x));
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
-    const int64_t ktiles = g.Kpad / CONV_BK;
     const int cfgs[4][2] = {{128, 128}, {64, 128}, {64, 64}, {32, 256}};
     const int split_list[] = {1, 2, 3, 4, 6, 8, 12, 16};
     std::vector<TileCfg> cands;
     for (auto& c : cfgs) {
         if (M <= 32 && c[0] != 32) continue;
         if (M > 64 && c[0] == 32) continue;
+        const int64_t kt = g.Kpad / CONV_BK;
         const int64_t tiles = ceil_div(M, c[0]) * ceil_div(N, c[1]);
         for (int sp : split_list) {
-            if (sp > 1 && (sp > ktiles / 2 || tiles > ctx->tile_cnt_len || tiles * sp > 64 * (int64_t)ctx->sm_count))
+            if (sp > 1 && (sp > kt / 2 || tiles > ctx->tile_cnt_len || tiles * sp > 64 * (int64_t)ctx->sm_count))
                 continue;
-            const int64_t kps = ceil_div(ktiles, sp);
-            if (ceil_div(ktiles, kps) != sp) continue;
+            const int64_t kps = ceil_div(kt, sp);
+            if (ceil_div(kt, kps) != sp) continue;
             if ((int64_t)sp * M * N * 4 > ((int64_t)512 << 20)) continue;  // 512 MiB scratch cap
             TileCfg t;
             t.BM = c[0]; t.BN = c[1]; t.splits = sp; t.kt_per_split = (int)kps; t.mode = mode;

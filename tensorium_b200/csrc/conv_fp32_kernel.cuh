@@ -97,14 +97,13 @@ struct VecT<2> { typedef float2 T; };
 template <>
 struct VecT<4> { typedef float4 T; };
 
-inline int conv_smem_bytes(int BM, int BN, int STAGES, int mode) {
-    return STAGES * CONV_BK * (BM + BN) * 4 + (mode == MODE_CRS ? CONV_CRS_MAX_K * 16 : 0);
+inline int conv_smem_bytes(int BM, int BN, int STAGES, int mode, int BK = CONV_BK) {
+    return STAGES * BK * (BM + BN) * 4 + (mode == MODE_CRS ? CONV_CRS_MAX_K * 16 : 0);
 }
 
-template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE, int BK = CONV_BK>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
 conv_fp32_kernel(const ConvParams p) {
-    constexpr int BK = CONV_BK;
     constexpr int NT = (BM / TM) * (BN / TN);
     constexpr int TX = BN / TN;
     constexpr int TM2 = TM / 2, TN2 = TN / 2;
@@ -155,17 +154,45 @@ conv_fp32_kernel(const ConvParams p) {
     }
     const float* xb = p.x + bimg * p.x_bs;
 
+    // Loader state: k tiles are loaded in increasing order from kt_begin, so the weight pointer,
+    // the tap (r, s) and the channel offset advance incrementally (no divisions per tile).
+    constexpr int AITER = (BK * BM / 4 + NT - 1) / NT;
+    static_assert(NT % (BM / 4) == 0, "a weight row of the tile is whole 16-byte copies");
+    constexpr int AKSTEP = NT / (BM / 4);  // weight rows between a thread's copies
+    const int a_kl0 = tid / (BM / 4), a_mq = tid - a_kl0 * (BM / 4);
+    const bool a_ok = m0 + a_mq * 4 < p.Mpad;
+    const int a_off = a_kl0 * p.Mpad + m0 + a_mq * 4;
+    const float* wnext = p.w + (long long)kt_begin * BK * p.Mpad;
+    int ld_c0 = 0, ld_s = 0, ld_iy = 0, ld_ix = 0;  // channel, kernel column, input row / column
+    bool ld_okp = false;
+    const float* ld_base = p.x;  // x at (ld_iy, ld_ix), channel krow0
+    auto ld_tap = [&]() {
+        ld_okp = nvalid && (unsigned)ld_iy < (unsigned)p.H && (unsigned)ld_ix < (unsigned)p.W;
+        ld_base = xb + (ld_okp ? (long long)ld_iy * p.W + ld_ix : 0) + (long long)krow0 * HW;
+    };
+    if (MODE == MODE_RSC) {
+        const int k0 = kt_begin * BK;
+        const int rs = k0 / p.Cpad;
+        ld_c0 = k0 - rs * p.Cpad;
+        const int r = rs / p.KW;
+        ld_s = rs - r * p.KW;
+        ld_iy = iy0 + r * p.DY;
+        ld_ix = ix0 + ld_s * p.DX;
+        ld_tap();
+    } else if (MODE == MODE_1X1V) {
+        ld_c0 = kt_begin * BK;
+    }
+
     auto load_tile = [&](int kt, int st) {
         // weights: BK rows of BM floats, 16-byte copies
-        const float* wsrc = p.w + (long long)kt * BK * p.Mpad;
         float* as = As + st * BK * BM;
 #pragma unroll
-        for (int idx = tid; idx < BK * BM / 4; idx += NT) {
-            int kl = idx / (BM / 4), mq = idx - kl * (BM / 4);
-            int m = m0 + mq * 4;
-            bool ok = m < p.Mpad;
-            cp_async16(as + kl * BM + mq * 4, ok ? wsrc + (long long)kl * p.Mpad + m : p.w, ok);
+        for (int i = 0; i < AITER; ++i) {
+            const int kl = a_kl0 + i * AKSTEP;
+            if (kl < BK)
+                cp_async16(as + kl * BM + a_mq * 4, a_ok ? wnext + a_off + i * AKSTEP * p.Mpad : p.w, a_ok);
         }
+        wnext += BK * p.Mpad;
         float* bs = Bs + st * BK * BN;
         if (MODE == MODE_CRS) {
 #pragma unroll
@@ -178,28 +205,29 @@ conv_fp32_kernel(const ConvParams p) {
                 cp_async4(bs + kl * BN + bcol, src, ok);
             }
         } else if (MODE == MODE_RSC) {
-            int k0 = kt * BK;
-            int rs = k0 / p.Cpad, c0 = k0 - rs * p.Cpad;
-            int r = rs / p.KW, s = rs - r * p.KW;
-            int iy = iy0 + r * p.DY, ix = ix0 + s * p.DX;
-            bool okp = nvalid && (unsigned)iy < (unsigned)p.H && (unsigned)ix < (unsigned)p.W;
-            const float* base = xb + (okp ? (long long)iy * p.W + ix : 0);
+            const float* cb = ld_base + (long long)ld_c0 * HW;
 #pragma unroll
             for (int e = 0; e < BEPT; ++e) {
-                int kl = krow0 + e * KSTEP;
-                int c = c0 + kl;
-                bool ok = okp && c < p.C;
-                cp_async4(bs + kl * BN + bcol, ok ? base + (long long)c * HW : p.x, ok);
+                const int kl = krow0 + e * KSTEP;
+                const bool ok = ld_okp && ld_c0 + kl < p.C;
+                cp_async4(bs + kl * BN + bcol, ok ? cb + (long long)e * KSTEP * HW : p.x, ok);
+            }
+            ld_c0 += BK;
+            if (ld_c0 == p.Cpad) {
+                ld_c0 = 0;
+                ld_ix += p.DX;
+                if (++ld_s == p.KW) ld_s = 0, ld_ix = ix0, ld_iy += p.DY;
+                ld_tap();
             }
         } else {
-            int c0 = kt * BK;
+            const float* cb = xb + pix + (long long)(ld_c0 + krow0) * HW;
 #pragma unroll
             for (int e = 0; e < BEPT; ++e) {
-                int kl = krow0 + e * KSTEP;
-                int c = c0 + kl;
-                bool ok = nvalid && c < p.C;
-                cp_async16(bs + kl * BN + 4 * bcol, ok ? xb + pix + (long long)c * HW : p.x, ok);
+                const int kl = krow0 + e * KSTEP;
+                const bool ok = nvalid && ld_c0 + kl < p.C;
+                cp_async16(bs + kl * BN + 4 * bcol, ok ? cb + (long long)e * KSTEP * HW : p.x, ok);
             }
+            ld_c0 += BK;
         }
     };
 
@@ -321,13 +349,13 @@ conv_fp32_kernel(const ConvParams p) {
 }
 
 // CTAs of this configuration resident per SM (registers / shared memory), cached per device
-template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE, int BK = CONV_BK>
 int conv_ctas_per_sm(tb_ctx* ctx) {
     static int cache[64] = {0};
     if (ctx->device < 64 && cache[ctx->device]) return cache[ctx->device];
     constexpr int NT = (BM / TM) * (BN / TN);
-    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE);
-    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE>;
+    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE, BK);
+    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE, BK>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     int n = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NT, smem) != cudaSuccess || n < 1) n = 1;
@@ -335,13 +363,13 @@ int conv_ctas_per_sm(tb_ctx* ctx) {
     return n;
 }
 
-template <int BM, int BN, int TM, int TN, int STAGES, int MODE>
+template <int BM, int BN, int TM, int TN, int STAGES, int MODE, int BK = CONV_BK>
 int conv_launch_cfg(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
     constexpr int NT = (BM / TM) * (BN / TN);
-    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE);
+    const int smem = conv_smem_bytes(BM, BN, STAGES, MODE, BK);
     static std::mutex mu;
     static bool done[64] = {false};
-    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE>;
+    auto kern = conv_fp32_kernel<BM, BN, TM, TN, STAGES, MODE, BK>;
     {
         std::lock_guard<std::mutex> lk(mu);
         if (ctx->device < 64 && !done[ctx->device]) {
@@ -354,21 +382,22 @@ int conv_launch_cfg(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
     return check_launch("conv_fp32_kernel");
 }
 
-template <int BM, int BN, int TM, int TN, int STAGES>
+template <int BM, int BN, int TM, int TN, int STAGES, int BK = CONV_BK>
 int conv_occupancy_modes(tb_ctx* ctx, int mode) {
     switch (mode) {
-    case MODE_CRS: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_CRS>(ctx);
-    case MODE_RSC: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_RSC>(ctx);
-    default: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_1X1V>(ctx);
+    case MODE_CRS: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_CRS, CONV_BK>(ctx);
+    case MODE_RSC: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_RSC, BK>(ctx);
+    default: return conv_ctas_per_sm<BM, BN, TM, TN, STAGES, MODE_1X1V, BK>(ctx);
     }
 }
 
-template <int BM, int BN, int TM, int TN, int STAGES>
+// MODE_CRS (the small-channel first layer) always runs 16-deep k tiles: its K is padded to 16.
+template <int BM, int BN, int TM, int TN, int STAGES, int BK = CONV_BK>
 int conv_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode) {
     switch (mode) {
-    case MODE_CRS: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_CRS>(ctx, p, grid);
-    case MODE_RSC: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_RSC>(ctx, p, grid);
-    default: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_1X1V>(ctx, p, grid);
+    case MODE_CRS: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_CRS, CONV_BK>(ctx, p, grid);
+    case MODE_RSC: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_RSC, BK>(ctx, p, grid);
+    default: return conv_launch_cfg<BM, BN, TM, TN, STAGES, MODE_1X1V, BK>(ctx, p, grid);
     }
 }
 

@@ -88,11 +88,12 @@ def test_all_activations(ctx):
                                  "64,64,2", "32,256,4"])
 def test_every_tile_and_split_configuration(ctx, cfg, monkeypatch):
     """Each CTA tile and split-K count (pinned through the TB_CONV_FORCE test hook), on a
-    strided RSC layer, a CRS layer and a vectorised 1x1 layer; each twice, so the split-K
-    arrival counters are seen to reset."""
+    strided RSC layer, a stride-1 RSC layer, a CRS layer and a vectorised 1x1 layer; each twice,
+    so the split-K arrival counters are seen to reset."""
     monkeypatch.setenv("TB_CONV_FORCE", cfg)
     rng = np.random.default_rng(11)
-    for (B, C, H, F, k, s, p) in [(2, 32, 26, 64, 3, 2, 1), (1, 3, 21, 16, 3, 1, 1), (2, 64, 12, 96, 1, 1, 0)]:
+    for (B, C, H, F, k, s, p) in [(2, 32, 26, 64, 3, 2, 1), (1, 64, 20, 128, 3, 1, 1), (1, 3, 21, 16, 3, 1, 1),
+                                  (2, 64, 12, 96, 1, 1, 0)]:
         x = rng.uniform(0, 1, (B, C, H, H)).astype(np.float32)
         w = (rng.standard_normal((F, C * k * k)) * 0.1).astype(np.float32)
         b = rng.standard_normal(F).astype(np.float32) * 0.1
