@@ -347,6 +347,11 @@ int tb_diag_fp32_fma_tflops(tb_ctx* ctx, double* tflops);
  * registers, on every SM) in Tbit-MAC/s (32 per popcount): the roofline denominator of
  * tb_xnor_conv_fwd (no reference counterpart). Blocks. */
 int tb_diag_popc_tbitmac(tb_ctx* ctx, double* tbitmac);
+/* tcgen05.mma kind::tf32 issue rate with operands resident in shared memory (M 128, N 256,
+ * K 8, one CTA per SM): cycles per MMA and the implied TFLOP/s at 1965 MHz, for MN-major
+ * (kmajor = 0, the conv kernel's layout) or K-major (kmajor = 1) operands (no reference
+ * counterpart). Blocks. */
+int tb_diag_tc_mma_rate(tb_ctx* ctx, int64_t kmajor, double* tflops, double* cycles_per_mma);
 /* One launch of the TF32 tensor-core conv on this geometry (bias, batchnorm and residual off)
  * with per-CTA cycle counters; out12 = averages over CTAs of: producer total cycles, producer
  * cycles waiting for a free stage, MMA-issuer total, MMA waiting for loaded stages, MMA waiting

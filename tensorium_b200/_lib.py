@@ -132,6 +132,7 @@ SIGNATURES = {
     "tb_net_profile": [P, P, C.POINTER(C.c_double)],
     "tb_diag_fp32_fma_tflops": [P, C.POINTER(C.c_double)],
     "tb_diag_popc_tbitmac": [P, C.POINTER(C.c_double)],
+    "tb_diag_tc_mma_rate": [P, I64, C.POINTER(C.c_double), C.POINTER(C.c_double)],
     "tb_diag_conv_tc_phases": [P, P, P, P, P, C.POINTER(C.c_double)],
 }
 _RESTYPES = {"tb_get_stream": P}

@@ -420,6 +420,12 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
                             (int)d->activation, 0, nullptr, 0, nullptr);
 }
 
+int tb_diag_tc_mma_rate(tb_ctx* ctx, int64_t kmajor, double* tflops, double* cycles_per_mma) {
+    TB_ENTER(ctx);
+    if (!tflops || !cycles_per_mma) return fail(TB_ERR_INVALID, "null output");
+    return conv_tc_mma_rate(ctx, (int)kmajor, tflops, cycles_per_mma);
+}
+
 int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y,
                            double* out12) {
     TB_ENTER(ctx);

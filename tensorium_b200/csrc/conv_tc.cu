@@ -33,14 +33,18 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace tbi {
 
 constexpr int TC_BM = 128, TC_BK = 32, TC_THREADS = 320, TC_MAX_KH = 8;
 constexpr int TC_STG_LD = 36;                                // slab row stride (floats)
 constexpr int TC_STG_BYTES = 8 * 16 * TC_STG_LD * 4;         // 8 epilogue warps x 16 x 36 floats
+constexpr int TC_BIAS_BYTES = 8 * 256 * 4;                   // 8 epilogue warps x one tile's bias
 constexpr int TC_BOX_BYTES = 32 * 32 * 4;
 
 struct TcParams {
@@ -218,13 +222,18 @@ static __device__ __noinline__ float4 tc_epilogue4(float4 o, int f, const ConvPa
     return o;
 }
 
-template <int BN, int STAGES>
+// CTAS = 2: a cluster of two CTAs on two SMs computes a 256-pixel x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA loads its own 128 pixels of A and BN/2 filters of
+// B, so each SM receives half the B bytes per FLOP of a single-CTA tile; the even CTA's thread
+// issues the MMAs, each CTA's TMEM holds the accumulator rows of its own pixels.
+template <int BN, int STAGES, int CTAS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_conv_tc(const __grid_constant__ TcMaps maps, const TcParams p) {
     constexpr int A_BYTES = TC_BM * TC_BK * 4;
-    constexpr int B_BYTES = BN * TC_BK * 4;
+    constexpr int BNC = BN / CTAS;  // filters of B held by this CTA
+    constexpr int B_BYTES = BNC * TC_BK * 4;
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr int NCHUNK = BN / 32;  // 32-filter column chunks of an accumulator
+    constexpr int NBOX_B = BNC / 32;  // 32-filter boxes of this CTA's B tile
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024 - ((unsigned)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
@@ -233,6 +242,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const unsigned sbase = (unsigned)__cvta_generic_to_shared(smem);
+    const int rank = CTAS == 2 ? (int)tc::cluster_rank() : 0;
+    const int t_first = blockIdx.x / CTAS, t_step = gridDim.x / CTAS;
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -241,16 +252,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull_bar[b], 1);
-            tc::mbar_init(&tempty_bar[b], 256);
+            tc::mbar_init(&tempty_bar[b], 8 * CTAS);  // one arrival per epilogue warp of the pair
         }
         tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
     }
-    if (warp == 1) tc::tmem_alloc(&tmem_base, 2 * BN);
+    if (warp == 1) tc::tmem_alloc_g<CTAS>(&tmem_base, 2 * BN);
     tc::tc_fence_before();
     __syncthreads();
+    if (CTAS == 2) tc::cluster_sync();  // the peer's barriers exist before anything signals them
     tc::tc_fence_after();
     const uint32_t tmem0 = tmem_base;
 
@@ -261,9 +273,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool ok = true;
             const long long c_start = clock64();
             long long c_wait = 0;
-            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+            for (int t = t_first; ok && t < p.tiles_total; t += t_step) {
                 const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
-                const int n0 = mt * TC_BM;
+                const int n0 = mt * (TC_BM * CTAS) + rank * TC_BM;
                 int bq[4], gq[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -281,26 +293,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         break;
                     }
                     c_wait += clock64() - c0w;
-                    tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES);
+                    if (rank == 0) tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES * CTAS);
                     const int z0 = (s * p.NPH + p.phase[r]) * p.B;
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + A_BYTES;
                     if (!split) {
-                        tc::tma_load_4d(sa, &maps.a4[r], &full_bar[st], 0, c0, gq[0], z0 + bq[0]);
+                        tc::tma_load_4d_g<CTAS>(sa, &maps.a4[r], &full_bar[st], 0, c0, gq[0], z0 + bq[0]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             if (gq[j] < p.g_full)
-                                tc::tma_load_4d(sa + j * TC_BOX_BYTES, &maps.a1[r], &full_bar[st], 0, c0, gq[j], z0 + bq[j]);
+                                tc::tma_load_4d_g<CTAS>(sa + j * TC_BOX_BYTES, &maps.a1[r], &full_bar[st], 0, c0, gq[j], z0 + bq[j]);
                             else
-                                tc::tma_load_3d(sa + j * TC_BOX_BYTES, &maps.tail, &full_bar[st], gq[j] * 32, c0, z0 + bq[j]);
+                                tc::tma_load_3d_g<CTAS>(sa + j * TC_BOX_BYTES, &maps.tail, &full_bar[st], gq[j] * 32, c0, z0 + bq[j]);
                         }
                     }
                     if (p.b_grouped) {
-                        tc::tma_load_3d(sb, &maps.b, &full_bar[st], 0, kt * TC_BK, nt * (BN / 32));
+                        tc::tma_load_3d_g<CTAS>(sb, &maps.b, &full_bar[st], 0, kt * TC_BK, nt * (BN / 32) + rank * NBOX_B);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < NCHUNK; ++j)
-                            tc::tma_load_2d(sb + j * TC_BOX_BYTES, &maps.b, &full_bar[st], nt * BN + 32 * j, kt * TC_BK);
+                        for (int j = 0; j < NBOX_B; ++j)
+                            tc::tma_load_2d_g<CTAS>(sb + j * TC_BOX_BYTES, &maps.b, &full_bar[st],
+                                                    nt * BN + rank * BNC + 32 * j, kt * TC_BK);
                     }
                     c0 += TC_BK;
                     if (c0 == p.C) {
@@ -313,20 +326,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 p.phases[blockIdx.x * 12 + 0] = clock64() - c_start;
                 p.phases[blockIdx.x * 12 + 1] = c_wait;
             }
-            if (!ok) {  // an abort: let the copies already issued land before the CTA exits
+            // an abort: let the copies already issued land before the CTA exits (a pair's odd CTA
+            // cannot see its copies complete: they are counted on the even CTA's barriers)
+            if (!ok && rank == 0) {
                 for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
                     tc::mbar_wait_limit(&full_bar[j % STAGES], (j / STAGES) & 1);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = tc::idesc_tf32_mn(TC_BM, BN);
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (the pair's even CTA) ----------------
+            constexpr uint32_t idesc = tc::idesc_tf32_mn(TC_BM * CTAS, BN);
             int it = 0, tl = 0;
             bool ok = true, issued = false;
             const long long c_start = clock64();
             long long c_wf = 0, c_we = 0;
-            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x, ++tl) {
+            for (int t = t_first; ok && t < p.tiles_total; t += t_step, ++tl) {
                 const int buf = tl & 1, u = tl >> 1;
                 long long c0w = clock64();
                 if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 912)) break;
@@ -347,12 +362,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int kk = 0; kk < TC_BK / 8; ++kk) {
                         const uint64_t da = tc::smem_desc_mn_sw128_32b(sa + kk * 1024, TC_BOX_BYTES, 512);
                         const uint64_t db = tc::smem_desc_mn_sw128_32b(sb + kk * 1024, TC_BOX_BYTES, 512);
-                        tc::mma_tf32(d, da, db, idesc, (kt | kk) ? 1u : 0u);
+                        tc::mma_tf32_g<CTAS>(d, da, db, idesc, (kt | kk) ? 1u : 0u);
                     }
                     issued = true;
-                    tc::mma_commit(&empty_bar[st]);
+                    tc::mma_commit_g<CTAS>(&empty_bar[st]);
                 }
-                if (ok) tc::mma_commit(&tfull_bar[buf]);
+                if (ok) tc::mma_commit_g<CTAS>(&tfull_bar[buf]);
             }
             if (p.phases) {
                 p.phases[blockIdx.x * 12 + 2] = clock64() - c_start;
@@ -360,7 +375,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 p.phases[blockIdx.x * 12 + 4] = c_we;
             }
             if (issued) {  // every MMA has finished before TMEM is freed
-                tc::mma_commit(&drain_bar);
+                tc::mma_commit_g<CTAS>(&drain_bar);
                 tc::mbar_wait_limit(&drain_bar, 0);
             }
         }
@@ -373,6 +388,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31 (a warp's lane window)
         const int half = (warp - 2) >> 2;  // slabs half, half+2, ...
         float* stg = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES) + (warp - 2) * (16 * TC_STG_LD);
+        float* bsm = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + TC_STG_BYTES) + (warp - 2) * 256;
         ConvParams ep;
         ep.bias = p.bias;
         ep.bn_scale = p.bn_scale;
@@ -387,7 +403,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int tl = 0;
         const long long c_start = clock64();
         long long c_wt = 0, c_ld = 0, c_st = 0;
-        for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++tl) {
+        for (int t = t_first; t < p.tiles_total; t += t_step, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
             const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 914);
@@ -396,7 +412,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc::tc_fence_after();
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
             // this lane's quad: pixels n .. n+3 of the padded grid (one row, one image)
-            const int n = mt * TC_BM + quarter * 32 + qd * 4;
+            const int n = mt * (TC_BM * CTAS) + rank * TC_BM + quarter * 32 + qd * 4;
             const int b = n / p.Lp, q = n - b * p.Lp;
             const int oy = q / p.Wp, ox = q - oy * p.Wp;
             const int nvalid = (b < p.B && q < p.OHWp) ? max(0, min(4, p.OW - ox)) : 0;
@@ -405,35 +421,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const float* rq = p.res ? p.res + (nvalid ? b * p.r_bs + pix : 0) : nullptr;
             const bool vec = nvalid == 4 && p.vec_out;
             const uint32_t taddr = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
+            // this tile's bias values in the warp's own shared row (one latency per tile)
+            const bool sbias = fast && p.bias;
+            if (sbias) {
+                for (int i = lane; i < BN; i += 32) {
+                    const int f = nt * BN + i;
+                    bsm[i] = f < p.F ? __ldg(p.bias + f) : 0.f;
+                }
+            }
+            uint32_t vr[16];
+            const long long c0l = clock64();
+            if (half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
 #pragma unroll 1
             for (int sl = half; sl < BN / 16; sl += 2) {
-                float v[16];
-                const long long c0l = clock64();
-                tc::tmem_ld16(taddr + sl * 16, v);
-                const long long c1l = clock64();
-                c_ld += c1l - c0l;
+                tc::tmem_wait16(vr);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) stg[i * TC_STG_LD + lane] = v[i];
+                for (int i = 0; i < 16; ++i) stg[i * TC_STG_LD + lane] = __uint_as_float(vr[i]);
+                // the next slab's TMEM load runs while this slab is finished
+                if (sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
                 __syncwarp();
                 const int fb = nt * BN + sl * 16;
+                float4 r4[4];
+                if (rq && vec) {  // all residual loads of the slab before any arithmetic
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int f = min(fb + frow + 4 * j, p.F - 1);
+                        r4[j] = __ldg(reinterpret_cast<const float4*>(rq + (long long)f * p.OHW));
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int f = fb + frow + 4 * j;
                     float4 o = *reinterpret_cast<const float4*>(stg + (frow + 4 * j) * TC_STG_LD + qd * 4);
                     if (f < p.F && nvalid) {
                         if (fast) {
-                            if (p.bias) {
-                                const float bf = __ldg(p.bias + f);
+                            if (sbias) {
+                                const float bf = bsm[sl * 16 + frow + 4 * j];
                                 o.x = __fadd_rn(o.x, bf);
                                 o.y = __fadd_rn(o.y, bf);
                                 o.z = __fadd_rn(o.z, bf);
                                 o.w = __fadd_rn(o.w, bf);
                             }
-                            if (leaky) {
-                                o.x = o.x < 0.f ? (float)(0.1 * (double)o.x) : o.x;
-                                o.y = o.y < 0.f ? (float)(0.1 * (double)o.y) : o.y;
-                                o.z = o.z < 0.f ? (float)(0.1 * (double)o.z) : o.z;
-                                o.w = o.w < 0.f ? (float)(0.1 * (double)o.w) : o.w;
+                            if (leaky) {  // the result is rounded to TF32: a float product suffices
+                                o.x = o.x < 0.f ? __fmul_rn(o.x, 0.1f) : o.x;
+                                o.y = o.y < 0.f ? __fmul_rn(o.y, 0.1f) : o.y;
+                                o.z = o.z < 0.f ? __fmul_rn(o.z, 0.1f) : o.z;
+                                o.w = o.w < 0.f ? __fmul_rn(o.w, 0.1f) : o.w;
                             }
                         } else {
                             o = tc_epilogue4(o, f, ep);
@@ -441,11 +474,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const long long off = (long long)f * p.OHW;
                         if (vec) {
                             if (rq) {
-                                const float4 r4 = __ldg(reinterpret_cast<const float4*>(rq + off));
-                                o.x = __fadd_rn(o.x, r4.x);
-                                o.y = __fadd_rn(o.y, r4.y);
-                                o.z = __fadd_rn(o.z, r4.z);
-                                o.w = __fadd_rn(o.w, r4.w);
+                                o.x = __fadd_rn(o.x, r4[j].x);
+                                o.y = __fadd_rn(o.y, r4[j].y);
+                                o.z = __fadd_rn(o.z, r4[j].z);
+                                o.w = __fadd_rn(o.w, r4[j].w);
                             }
                             o.x = tc::to_tf32_rna(o.x);
                             o.y = tc::to_tf32_rna(o.y);
@@ -466,10 +498,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 __syncwarp();
-                c_st += clock64() - c1l;
             }
+            c_st += clock64() - c0l;
             tc::tc_fence_before();
-            tc::mbar_arrive(&tempty_bar[buf]);
+            __syncwarp();
+            if (lane == 0) {  // this warp's TMEM reads are done: the accumulator may be reused
+                if (CTAS == 1) tc::mbar_arrive(&tempty_bar[buf]);
+                else tc::mbar_arrive_cluster(&tempty_bar[buf], 0);
+            }
         }
         if (p.phases && warp == 2 && lane == 0) {
             p.phases[blockIdx.x * 12 + 5] = clock64() - c_start;
@@ -481,9 +517,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     tc::tc_fence_before();
     __syncthreads();
+    // neither CTA of a pair leaves while the other may still read its shared memory (MMA
+    // operands) or signal its barriers
+    if (CTAS == 2) tc::cluster_sync();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem0, 2 * BN);
+        tc::tmem_dealloc_g<CTAS>(tmem0, 2 * BN);
     }
 }
 
@@ -540,33 +579,69 @@ int64_t conv_tc_scratch_floats(const ConvGeom& g) {
     return g.KW * pl.NPH * g.B * g.C * pl.PS;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CTAS>
 static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
-    constexpr int smem = STAGES * (TC_BM * TC_BK * 4 + BN * TC_BK * 4) + TC_STG_BYTES + 1024;
+    constexpr int smem = STAGES * (TC_BM * TC_BK * 4 + (BN / CTAS) * TC_BK * 4) + TC_STG_BYTES + TC_BIAS_BYTES + 1024;
     static std::mutex mu;
     static bool done[64] = {false};
     {
         std::lock_guard<std::mutex> lk(mu);
         if (ctx->device < 64 && !done[ctx->device]) {
-            cudaError_t e = cudaFuncSetAttribute(k_conv_tc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaError_t e = cudaFuncSetAttribute(k_conv_tc<BN, STAGES, CTAS>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv_tc)");
             done[ctx->device] = true;
         }
     }
-    const int grid = (int)std::min<int64_t>(p.tiles_total, ctx->sm_count);
-    k_conv_tc<BN, STAGES><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    const int slots = CTAS == 1 ? ctx->sm_count : (ctx->sm_count & ~1);
+    const int grid = (int)std::min<int64_t>((int64_t)p.tiles_total * CTAS, slots);
+    if constexpr (CTAS == 1) {
+        k_conv_tc<BN, STAGES, 1><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_tc<BN, STAGES, CTAS>, maps, p);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(conv_tc pair)");
+    }
     return check_launch("k_conv_tc");
 }
 
-// Filter-tile width: the smallest modelled time (waves of one CTA per SM x per-tile cost).
-static int choose_bn(const ConvGeom& g, int64_t tiles_m, int sms) {
-    int best = 32;
+// Tile shape (filters per tile, CTAs per tile) with the smallest modelled time: waves of tiles
+// over the SMs (or SM pairs) x per-tile cycles, a k tile costing the larger of its MMA time
+// (2*BN cycles per SM) and its operand delivery (A 16 KB + this CTA's part of B at ~64 B/cycle).
+struct TcShape { int bn, ctas; };
+
+static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms) {
+    TcShape best{32, 1};
     double best_cost = 1e300;
-    for (int bn : {32, 64, 128, 256}) {
-        if (bn > round_up(g.F, 32) && bn != 32) break;
-        const int64_t tiles = tiles_m * ceil_div(g.F, bn);
-        const double cost = (double)ceil_div(tiles, sms) * (bn + 48);
-        if (cost < best_cost) best = bn, best_cost = cost;
+    if (const char* f = getenv("TB_TC_FORCE")) {  // test hook "BN,CTAS"
+        int bn = 0, ct = 0;
+        if (sscanf(f, "%d,%d", &bn, &ct) == 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) &&
+            (ct == 1 || (ct == 2 && bn >= 64)))
+            return TcShape{bn, ct};
+    }
+    // CTA pairs (cta_group::2) are built and tested but not picked: at the batch sizes of the
+    // bench a pair tile leaves fewer tiles per SM, and its tail epilogue is not hidden
+    for (int ct : {1}) {
+        for (int bn : {32, 64, 128, 256}) {
+            if (bn > round_up(g.F, 32) && bn != 32) break;
+            if (ct == 2 && bn < 64) continue;
+            const int64_t tiles = ceil_div(npix, (int64_t)TC_BM * ct) * ceil_div(g.F, bn);
+            const int64_t slots = ct == 1 ? sms : sms / 2;
+            const double kc = std::max(2.0 * bn, (16384.0 + bn * 128.0 / ct) / 64.0);
+            const double cost = (double)ceil_div(tiles, slots) * (ktiles * kc + 2500.0);
+            if (cost < best_cost * 0.999) best = TcShape{bn, ct}, best_cost = cost;
+        }
     }
     return best;
 }
@@ -661,17 +736,18 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     p.y_bs = g.y_bs; p.r_bs = g.r_bs;
     p.act = act; p.yolo_classes = yolo_classes;
     for (int i = 0; i < TC_MAX_KH; ++i) p.phase[i] = pl.phase[i];
-    const int64_t tiles_m = ceil_div(g.B * p.Lp, TC_BM);
-    const int bn = choose_bn(g, tiles_m, ctx->sm_count);
+    const TcShape sh = choose_shape(g, g.B * p.Lp, p.ktiles, ctx->sm_count);
+    const int bn = sh.bn;
+    const int64_t tiles_m = ceil_div(g.B * p.Lp, (int64_t)TC_BM * sh.ctas);
     p.tiles_n = (int)ceil_div(g.F, bn);
     const int64_t tiles = tiles_m * p.tiles_n;
-    if (tiles >= ((int64_t)1 << 31)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: too many tiles");
+    if (tiles >= ((int64_t)1 << 30)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: too many tiles");
     p.tiles_total = (int)tiles;
     p.b_grouped = g.Mpad % 32 == 0;
     if (p.b_grouped) {  // (32 filters, k, filter group), one box of bn/32 groups per stage
         const uint64_t dims[3] = {32, (uint64_t)g.Kpad, (uint64_t)(g.Mpad / 32)};
         const uint64_t st[2] = {(uint64_t)g.Mpad * 4, 128};
-        const uint32_t box[3] = {32, 32, (uint32_t)(bn / 32)};
+        const uint32_t box[3] = {32, 32, (uint32_t)(bn / 32 / sh.ctas)};  // this CTA's filters
         r = encode_map(&maps.b, wp, 3, dims, st, box);
     } else {
         const uint64_t dims[2] = {(uint64_t)g.Mpad, (uint64_t)g.Kpad};
@@ -680,14 +756,99 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
         r = encode_map(&maps.b, wp, 2, dims, st, box);
     }
     if (r != TB_OK) return r;
-    switch (bn) {
-    case 32: r = launch_bn<32, 8>(ctx, maps, p); break;
-    case 64: r = launch_bn<64, 8>(ctx, maps, p); break;
-    case 128: r = launch_bn<128, 6>(ctx, maps, p); break;
-    default: r = launch_bn<256, 4>(ctx, maps, p); break;
+    if (sh.ctas == 1) {
+        switch (bn) {
+        case 32: r = launch_bn<32, 8, 1>(ctx, maps, p); break;
+        case 64: r = launch_bn<64, 8, 1>(ctx, maps, p); break;
+        case 128: r = launch_bn<128, 6, 1>(ctx, maps, p); break;
+        default: r = launch_bn<256, 4, 1>(ctx, maps, p); break;
+        }
+    } else {
+        switch (bn) {
+        case 64: r = launch_bn<64, 8, 2>(ctx, maps, p); break;
+        case 128: r = launch_bn<128, 8, 2>(ctx, maps, p); break;
+        default: r = launch_bn<256, 6, 2>(ctx, maps, p); break;
+        }
     }
     if (r != TB_OK) return r;
     if (launches) ++*launches;
+    return TB_OK;
+}
+
+
+// ---------------------------------------------------------------------------------------
+// Diagnostic: tcgen05.mma kind::tf32 issue rate on shared-memory operands already in place
+// (no loads), M = 128, N = 256, K = 8, in the two operand layouts: both MN-major with the
+// 32-byte-atom 128-byte swizzle (what k_conv_tc uses), or both K-major with the 128-byte
+// swizzle.  One CTA per SM; batches of 64 MMAs committed to an mbarrier; cycles of the batches
+// after the first.
+__global__ void __launch_bounds__(128, 1) k_mma_rate(int kmajor, int batches, unsigned long long* cycles) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024 - ((unsigned)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < (128 + 256) * 32; i += blockDim.x) reinterpret_cast<float*>(smem)[i] = 0.f;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    if (warp == 0) tc::tmem_alloc(&tmem_base, 256);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (threadIdx.x == 0) {
+        const unsigned sa = (unsigned)__cvta_generic_to_shared(smem), sb = sa + 128 * 32 * 4;
+        uint32_t idesc = tc::idesc_tf32_mn(128, 256);
+        if (kmajor) idesc &= ~((1u << 15) | (1u << 16));
+        long long t0 = 0;
+        for (int b = 0; b < batches; ++b) {
+            if (b == 1) t0 = clock64();
+            for (int i = 0; i < 64; ++i) {
+                const int kk = i & 3;
+                uint64_t da, db;
+                if (kmajor) {  // K-major SW128: rows of 32 fp32 along K, 8-row groups 1024 B apart
+                    da = tc::smem_desc_mn_sw128_32b(sa + kk * 32, 16, 1024);
+                    db = tc::smem_desc_mn_sw128_32b(sb + kk * 32, 16, 1024);
+                    da = (da & ~(7ull << 61)) | (2ull << 61);
+                    db = (db & ~(7ull << 61)) | (2ull << 61);
+                } else {
+                    da = tc::smem_desc_mn_sw128_32b(sa + kk * 1024, 4096, 512);
+                    db = tc::smem_desc_mn_sw128_32b(sb + kk * 1024, 4096, 512);
+                }
+                tc::mma_tf32(tmem_base, da, db, idesc, i ? 1u : 0u);
+            }
+            tc::mma_commit(&bar);
+            tc::mbar_wait_limit(&bar, b & 1);
+        }
+        cycles[blockIdx.x] = clock64() - t0;
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, 256);
+    }
+}
+
+int conv_tc_mma_rate(tb_ctx* ctx, int kmajor, double* tflops_at_clock, double* cycles_per_mma) {
+    const int batches = 65, smem = (128 + 256) * 32 * 4 + 1024;
+    unsigned long long* d = nullptr;
+    TB_CHECK_CUDA(cudaMalloc(&d, ctx->sm_count * sizeof(unsigned long long)));
+    cudaFuncSetAttribute(k_mma_rate, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k_mma_rate<<<ctx->sm_count, 128, smem, ctx->stream>>>(kmajor, batches, d);
+    std::vector<unsigned long long> h(ctx->sm_count);
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, h.size() * 8, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_fail(e, "mma rate probe");
+    double c = 0;
+    for (auto v : h) c += (double)v;
+    c /= h.size();
+    *cycles_per_mma = c / ((batches - 1) * 64.0);
+    // 2*128*256*8 FLOPs per MMA, per SM, at 1.965 GHz on every SM
+    *tflops_at_clock = 2.0 * 128 * 256 * 8 / *cycles_per_mma * 1.965e9 * ctx->sm_count / 1e12;
     return TB_OK;
 }
 

@@ -171,6 +171,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tmem_ld16 split in two: the load is issued, and the registers are valid only after
+// tmem_wait16 on the same array (the wait takes them as operands, so no use can move above it)
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait16(uint32_t* r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
 // shared-memory matrix descriptor: MN-major, 128-byte swizzle with 32-byte atoms (layout type 1),
 // version 1
 __device__ __forceinline__ uint64_t smem_desc_mn_sw128_32b(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -190,6 +208,121 @@ __host__ __device__ constexpr uint32_t idesc_tf32_mn(int M, int N) {
            | (1u << 15) | (1u << 16)       // a_major, b_major = MN
            | ((uint32_t)(N >> 3) << 17)    // n_dim
            | ((uint32_t)(M >> 4) << 24);   // m_dim
+}
+
+
+// --- CTA pairs (cta_group::2): a cluster of 2 CTAs on two SMs computes one M = 256 tile -----
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// arrive on the mbarrier at the same shared offset in CTA `rank` of the cluster
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, unsigned rank) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(ra) : "memory");
+}
+
+template <int CTAS>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t* dst_smem, uint32_t ncols) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(dst_smem);
+    if constexpr (CTAS == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(a), "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    } else {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(a), "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
+    }
+}
+
+template <int CTAS>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+    if constexpr (CTAS == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+    else
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+
+// D (+)= A * B; with CTAS == 2, issued by the pair's even CTA: A rows and B columns are read
+// half from each CTA's shared memory at the same offsets, D rows half into each CTA's TMEM.
+template <int CTAS>
+__device__ __forceinline__ void mma_tf32_g(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                           uint32_t accumulate) {
+    if constexpr (CTAS == 1)
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+            "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+    else
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+            "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// arrive on `bar` (in both CTAs of the pair when CTAS == 2) once every tcgen05 op issued so far
+// by this thread has completed
+template <int CTAS>
+__device__ __forceinline__ void mma_commit_g(uint64_t* bar) {
+    unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    if constexpr (CTAS == 1) {
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(a)
+                     : "memory");
+    } else {
+        const unsigned short mask = 3;
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(a),
+            "h"(mask)
+            : "memory");
+    }
+}
+
+// TMA loads into this CTA's shared memory; with CTAS == 2 the completed bytes are counted on the
+// mbarrier of the pair's even CTA (the one whose MMA thread waits for both halves)
+template <int CTAS>
+__device__ __forceinline__ unsigned tma_bar(uint64_t* bar) {
+    unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    return CTAS == 1 ? b : (b & 0xFEFFFFFFu);
+}
+
+template <int CTAS>
+__device__ __forceinline__ void tma_load_2d_g(unsigned dst, const void* tmap, uint64_t* bar, int x, int y) {
+    if constexpr (CTAS == 1)
+        tma_load_2d(dst, tmap, bar, x, y);
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(tmap)), "r"(tma_bar<2>(bar)), "r"(x), "r"(y)
+            : "memory");
+}
+
+template <int CTAS>
+__device__ __forceinline__ void tma_load_3d_g(unsigned dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
+    if constexpr (CTAS == 1)
+        tma_load_3d(dst, tmap, bar, x, y, z);
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(tmap)), "r"(tma_bar<2>(bar)), "r"(x), "r"(y), "r"(z)
+            : "memory");
+}
+
+template <int CTAS>
+__device__ __forceinline__ void tma_load_4d_g(unsigned dst, const void* tmap, uint64_t* bar, int x, int y, int z,
+                                              int w) {
+    if constexpr (CTAS == 1)
+        tma_load_4d(dst, tmap, bar, x, y, z, w);
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(tmap)), "r"(tma_bar<2>(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+            : "memory");
 }
 
 }  // namespace tc

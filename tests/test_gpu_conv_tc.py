@@ -125,3 +125,30 @@ def test_yolov3_tf32_heads_and_boxes(ctx):
         sure = np.abs(xo - logit) > 4 * band
         assert np.array_equal((go > thresh)[sure], (ro > thresh)[sure]), h
     net.close()
+
+
+PAIR_CASES = [  # (B, C, H, F, k, s, p) under a forced tile shape
+    (1, 32, 52, 64, 3, 1, 1),      # 3x3 replica
+    (3, 64, 28, 96, 1, 1, 0),      # in place, pair tiles straddling images
+    (2, 256, 13, 255, 1, 1, 0),    # ragged filters (255) and pixels
+    (2, 32, 52, 64, 3, 2, 1),      # stride 2
+    (2, 3, 40, 32, 3, 1, 1),       # im2col rows
+]
+
+
+@pytest.mark.parametrize("shape", ["64,2", "128,2", "256,2", "256,1", "32,1"])
+def test_tc_conv_every_tile_shape(ctx, shape, monkeypatch):
+    """Each (filters per tile, CTAs per tile) shape of the tensor-core kernel, pinned through the
+    TB_TC_FORCE test hook: 2 = a CTA pair on two SMs (cta_group::2, M = 256)."""
+    monkeypatch.setenv("TB_TC_FORCE", shape)
+    rng = np.random.default_rng(21)
+    for (B, C, H, F, k, s, p) in PAIR_CASES:
+        x = rng.uniform(0, 1, (B, C, H, H)).astype(np.float32)
+        w = (rng.standard_normal((F, C * k * k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+        b = rng.standard_normal(F).astype(np.float32) * 0.1
+        y1 = run_layer(ctx, x, w, b, F, k, s, p, 4)
+        y2 = run_layer(ctx, x, w, b, F, k, s, p, 4)
+        assert np.array_equal(y1, y2), (shape, C)
+        ref = O.conv2d(x, w, b, F, k, s, p, 4)
+        e = rel_l2_maps(y1, ref, B * F)
+        assert 0.0 < e <= TF32_TOL, (shape, C, e)
