@@ -69,6 +69,8 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
                    unsigned long long* phases = nullptr);
 // Diagnostic: MMA issue rate (see conv_tc.cu).
 int conv_tc_mma_rate(tb_ctx* ctx, int kmajor, double* tflops_at_clock, double* cycles_per_mma);
+// Measure the tensor-core tile shapes of this geometry on x / y and keep the fastest.
+int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // Round packed weights to TF32 (nearest, ties away) in place.
 int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.

@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <map>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -212,13 +213,14 @@ __global__ void k_round_tf32(float* __restrict__ p, long long n) {
         p[i] = tc::to_tf32_rna(p[i]);
 }
 
-// The epilogue of a pixel quad of one filter for the less common cases (unfused batchnorm,
+// The epilogue of one pixel for 4 consecutive filters, for the less common cases (unfused batchnorm,
 // yolo logistic, activations other than leaky / linear); out of line to keep the kernel small.
-static __device__ __noinline__ float4 tc_epilogue4(float4 o, int f, const ConvParams ep) {
-    o.x = conv_epilogue(o.x, f, ep);
-    o.y = conv_epilogue(o.y, f, ep);
-    o.z = conv_epilogue(o.z, f, ep);
-    o.w = conv_epilogue(o.w, f, ep);
+static __device__ __noinline__ float4 tc_epilogue4_f(float4 o, int f0, int F, const ConvParams ep) {
+    // filters f0 .. f0+3, clamped to F-1 (values past the last filter are never stored)
+    o.x = conv_epilogue(o.x, min(f0, F - 1), ep);
+    o.y = conv_epilogue(o.y, min(f0 + 1, F - 1), ep);
+    o.z = conv_epilogue(o.z, min(f0 + 2, F - 1), ep);
+    o.w = conv_epilogue(o.w, min(f0 + 3, F - 1), ep);
     return o;
 }
 
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int qd = lane & 7, frow = lane >> 3;  // this lane's pixel quad and first slab row
         int tl = 0;
         const long long c_start = clock64();
-        long long c_wt = 0, c_ld = 0, c_st = 0;
+        long long c_wt = 0, c_ld = 0, c_st = 0, c_sts = 0;
         for (int t = t_first; t < p.tiles_total; t += t_step, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
@@ -434,13 +436,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
 #pragma unroll 1
             for (int sl = half; sl < BN / 16; sl += 2) {
+                const long long cw0 = clock64();
                 tc::tmem_wait16(vr);
+                const long long cw1 = clock64();
+                c_ld += cw1 - cw0;
+                const int fb = nt * BN + sl * 16;
+                // 1. this lane's pixel, 16 independent filters: bias, activation (and, without a
+                //    residual, the TF32 rounding), into the filter-major slab
+                if (fast) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) stg[i * TC_STG_LD + lane] = __uint_as_float(vr[i]);
-                // the next slab's TMEM load runs while this slab is finished
+                    for (int i = 0; i < 16; ++i) {
+                        float o = __uint_as_float(vr[i]);
+                        if (sbias) o = __fadd_rn(o, bsm[sl * 16 + i]);
+                        if (leaky && o < 0.f) o = __fmul_rn(o, 0.1f);  // rounded to TF32 below
+                        stg[i * TC_STG_LD + lane] = rq ? o : tc::to_tf32_rna(o);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        float4 o = make_float4(__uint_as_float(vr[i]), __uint_as_float(vr[i + 1]),
+                                               __uint_as_float(vr[i + 2]), __uint_as_float(vr[i + 3]));
+                        o = tc_epilogue4_f(o, fb + i, p.F, ep);
+                        stg[i * TC_STG_LD + lane] = rq ? o.x : tc::to_tf32_rna(o.x);
+                        stg[(i + 1) * TC_STG_LD + lane] = rq ? o.y : tc::to_tf32_rna(o.y);
+                        stg[(i + 2) * TC_STG_LD + lane] = rq ? o.z : tc::to_tf32_rna(o.z);
+                        stg[(i + 3) * TC_STG_LD + lane] = rq ? o.w : tc::to_tf32_rna(o.w);
+                    }
+                }
+                // the next slab's TMEM load runs while this slab is stored
                 if (sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
                 __syncwarp();
-                const int fb = nt * BN + sl * 16;
+                c_sts += clock64() - cw1;
+                // 2. 16 filters x 8 pixel quads: lane -> quad qd of filter rows frow, frow+4, ...
                 float4 r4[4];
                 if (rq && vec) {  // all residual loads of the slab before any arithmetic
 #pragma unroll
@@ -454,35 +481,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int f = fb + frow + 4 * j;
                     float4 o = *reinterpret_cast<const float4*>(stg + (frow + 4 * j) * TC_STG_LD + qd * 4);
                     if (f < p.F && nvalid) {
-                        if (fast) {
-                            if (sbias) {
-                                const float bf = bsm[sl * 16 + frow + 4 * j];
-                                o.x = __fadd_rn(o.x, bf);
-                                o.y = __fadd_rn(o.y, bf);
-                                o.z = __fadd_rn(o.z, bf);
-                                o.w = __fadd_rn(o.w, bf);
-                            }
-                            if (leaky) {  // the result is rounded to TF32: a float product suffices
-                                o.x = o.x < 0.f ? __fmul_rn(o.x, 0.1f) : o.x;
-                                o.y = o.y < 0.f ? __fmul_rn(o.y, 0.1f) : o.y;
-                                o.z = o.z < 0.f ? __fmul_rn(o.z, 0.1f) : o.z;
-                                o.w = o.w < 0.f ? __fmul_rn(o.w, 0.1f) : o.w;
-                            }
-                        } else {
-                            o = tc_epilogue4(o, f, ep);
-                        }
                         const long long off = (long long)f * p.OHW;
                         if (vec) {
                             if (rq) {
-                                o.x = __fadd_rn(o.x, r4[j].x);
-                                o.y = __fadd_rn(o.y, r4[j].y);
-                                o.z = __fadd_rn(o.z, r4[j].z);
-                                o.w = __fadd_rn(o.w, r4[j].w);
+                                o.x = tc::to_tf32_rna(__fadd_rn(o.x, r4[j].x));
+                                o.y = tc::to_tf32_rna(__fadd_rn(o.y, r4[j].y));
+                                o.z = tc::to_tf32_rna(__fadd_rn(o.z, r4[j].z));
+                                o.w = tc::to_tf32_rna(__fadd_rn(o.w, r4[j].w));
                             }
-                            o.x = tc::to_tf32_rna(o.x);
-                            o.y = tc::to_tf32_rna(o.y);
-                            o.z = tc::to_tf32_rna(o.z);
-                            o.w = tc::to_tf32_rna(o.w);
                             __stcs(reinterpret_cast<float4*>(yq + off), o);
                         } else {
                             const float ov[4] = {o.x, o.y, o.z, o.w};
@@ -490,8 +496,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             for (int e = 0; e < 4; ++e) {
                                 if (e < nvalid) {
                                     float w = ov[e];
-                                    if (rq) w = __fadd_rn(w, __ldg(rq + off + e));
-                                    yq[off + e] = tc::to_tf32_rna(w);
+                                    if (rq) w = tc::to_tf32_rna(__fadd_rn(w, __ldg(rq + off + e)));
+                                    yq[off + e] = w;
                                 }
                             }
                         }
@@ -513,6 +519,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             p.phases[blockIdx.x * 12 + 7] = tl;
             p.phases[blockIdx.x * 12 + 8] = c_ld;
             p.phases[blockIdx.x * 12 + 9] = c_st;
+            p.phases[blockIdx.x * 12 + 10] = c_sts;
         }
     }
     tc::tc_fence_before();
@@ -621,14 +628,30 @@ static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
 // (2*BN cycles per SM) and its operand delivery (A 16 KB + this CTA's part of B at ~64 B/cycle).
 struct TcShape { int bn, ctas; };
 
-static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms) {
+// Shapes measured by conv_tc_autotune, per device and geometry; a shape pinned for one launch
+// by the autotuner itself.
+static std::mutex g_tc_mu;
+static std::map<std::vector<int64_t>, TcShape> g_tc_tuned;
+static thread_local const TcShape* t_tc_pin = nullptr;
+
+static std::vector<int64_t> tc_key(int device, const ConvGeom& g, bool xa) {
+    return {device, g.B, g.C, g.H, g.W, g.F, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX, g.x_bs, g.y_bs, xa};
+}
+
+static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms, int device, bool xa) {
     TcShape best{32, 1};
     double best_cost = 1e300;
+    if (t_tc_pin) return *t_tc_pin;
     if (const char* f = getenv("TB_TC_FORCE")) {  // test hook "BN,CTAS"
         int bn = 0, ct = 0;
         if (sscanf(f, "%d,%d", &bn, &ct) == 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) &&
             (ct == 1 || (ct == 2 && bn >= 64)))
             return TcShape{bn, ct};
+    }
+    {
+        std::lock_guard<std::mutex> lk(g_tc_mu);
+        auto it = g_tc_tuned.find(tc_key(device, g, xa));
+        if (it != g_tc_tuned.end()) return it->second;
     }
     // CTA pairs (cta_group::2) are built and tested but not picked: at the batch sizes of the
     // bench a pair tile leaves fewer tiles per SM, and its tail epilogue is not hidden
@@ -736,7 +759,7 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     p.y_bs = g.y_bs; p.r_bs = g.r_bs;
     p.act = act; p.yolo_classes = yolo_classes;
     for (int i = 0; i < TC_MAX_KH; ++i) p.phase[i] = pl.phase[i];
-    const TcShape sh = choose_shape(g, g.B * p.Lp, p.ktiles, ctx->sm_count);
+    const TcShape sh = choose_shape(g, g.B * p.Lp, p.ktiles, ctx->sm_count, ctx->device, aligned16(x));
     const int bn = sh.bn;
     const int64_t tiles_m = ceil_div(g.B * p.Lp, (int64_t)TC_BM * sh.ctas);
     p.tiles_n = (int)ceil_div(g.F, bn);
@@ -849,6 +872,54 @@ int conv_tc_mma_rate(tb_ctx* ctx, int kmajor, double* tflops_at_clock, double* c
     *cycles_per_mma = c / ((batches - 1) * 64.0);
     // 2*128*256*8 FLOPs per MMA, per SM, at 1.965 GHz on every SM
     *tflops_at_clock = 2.0 * 128 * 256 * 8 / *cycles_per_mma * 1.965e9 * ctx->sm_count / 1e12;
+    return TB_OK;
+}
+
+// Time every tile shape (filters per tile, CTAs per tile) of this geometry on the given buffers
+// (bias, batchnorm, residual off) and keep the fastest for later launches.  Blocks; grows the
+// workspace for the replica (not during stream capture).
+int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y) {
+    if (g.B == 0 || !conv_tc_supported(g)) return TB_OK;
+    int r = ensure_workspace(ctx, (size_t)conv_tc_scratch_floats(g) * sizeof(float));
+    if (r != TB_OK) return r;
+    std::vector<TcShape> cands;
+    for (int ct : {1, 2})
+        for (int bn : {32, 64, 128, 256}) {
+            if (ct == 2 && bn < 64) continue;
+            if (bn > round_up(g.F, 32) && bn != 32) continue;
+            cands.push_back(TcShape{bn, ct});
+        }
+    cudaEvent_t e0, e1;
+    TB_CHECK_CUDA(cudaEventCreate(&e0));
+    TB_CHECK_CUDA(cudaEventCreate(&e1));
+    float best_ms = 1e30f;
+    TcShape best = cands[0];
+    for (const TcShape& c : cands) {
+        t_tc_pin = &c;
+        float* ws = reinterpret_cast<float*>(ctx->ws);
+        r = conv_tc_launch(ctx, g, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR, 0, ws, nullptr);
+        cudaEventRecord(e0, ctx->stream);
+        for (int rep = 0; rep < 3 && r == TB_OK; ++rep)
+            r = conv_tc_launch(ctx, g, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR, 0, ws,
+                               nullptr);
+        cudaEventRecord(e1, ctx->stream);
+        t_tc_pin = nullptr;
+        cudaError_t e = cudaEventSynchronize(e1);
+        if (r != TB_OK) break;
+        if (e != cudaSuccess) { r = cuda_fail(e, "tensor-core autotune"); break; }
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (getenv("TB_AUTOTUNE_VERBOSE"))
+            fprintf(stderr, "tc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d ctas %d: %.4f ms\n",
+                    (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
+                    (long long)g.B, c.bn, c.ctas, ms / 3);
+        if (ms < best_ms) best_ms = ms, best = c;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (r != TB_OK) return r;
+    std::lock_guard<std::mutex> lk(g_tc_mu);
+    g_tc_tuned[tc_key(ctx->device, g, aligned16(x))] = best;
     return TB_OK;
 }
 

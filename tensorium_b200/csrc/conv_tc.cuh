@@ -66,7 +66,7 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, unsigned parity) 
     return false;
 }
 
-// --- TMA (tensor copies global -> shared, completion counted on an mbarrier; no multicast) ---
+// --- TMA (tensor copies global -> shared of this CTA only, completion counted on an mbarrier) ---
 __device__ __forceinline__ void tma_load_2d(unsigned dst, const void* tmap, uint64_t* bar, int x, int y) {
     unsigned b = (unsigned)__cvta_generic_to_shared(bar);
     asm volatile(
@@ -266,7 +266,8 @@ __device__ __forceinline__ void mma_tf32_g(uint32_t tmem_d, uint64_t desc_a, uin
             "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
-// arrive on `bar` (in both CTAs of the pair when CTAS == 2) once every tcgen05 op issued so far
+// arrive on `bar` (in both CTAs of the pair when CTAS == 2: one commit to each CTA's barrier,
+// the peer's addressed through its shared::cluster window) once every tcgen05 op issued so far
 // by this thread has completed
 template <int CTAS>
 __device__ __forceinline__ void mma_commit_g(uint64_t* bar) {
@@ -275,11 +276,12 @@ __device__ __forceinline__ void mma_commit_g(uint64_t* bar) {
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(a)
                      : "memory");
     } else {
-        const unsigned short mask = 3;
-        asm volatile(
-            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(a),
-            "h"(mask)
-            : "memory");
+        unsigned peer;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, 1;\n" : "=r"(peer) : "r"(a));
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(a)
+                     : "memory");
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(peer)
+                     : "memory");
     }
 }
 

@@ -665,7 +665,9 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             if (r != TB_OK) { if (tmp) cudaFree(tmp); return r; }
             if (net->math_mode == TB_MATH_TF32 && conv_tc_supported(g)) {
                 ws_floats = std::max(ws_floats, conv_tc_scratch_floats(g));
+                r = conv_tc_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr);
                 if (tmp) cudaFree(tmp);
+                if (r != TB_OK) return r;
                 continue;
             }
             r = conv_fp32_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr);
