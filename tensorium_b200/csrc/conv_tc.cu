@@ -139,33 +139,52 @@ static void tc_plan(const ConvGeom& g, TcPlan* pl) {
 }
 
 // Tap replicas P[s][ph][b][c][Hrep][Wp], planes PS elements apart (the tail of a plane is never
-// written: it is read only for pixels that are dropped).  One thread makes 4 consecutive
-// columns of one (ph, b, c) row for every kernel column s: one 16-byte store per s, values
-// rounded to TF32.
+// written: it is read only for pixels that are dropped).  blockIdx.y = (ph * B + b) * C + c;
+// one thread makes 4 consecutive columns of one row for every kernel column s: it reads the
+// input window those need once (SX*3 + (KW-1)*DX + 1 <= 32 values) and writes one 16-byte quad
+// per s, values rounded to TF32.
+// SXC, DXC: compile-time column stride and dilation (0 = taken from SX, DX at run time)
+template <int SXC, int DXC>
 __global__ void k_tc_repack_taps(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C,
-                                 int H, int W, int KW, int SY, int SX, int DX, int PX, int NPH, int pad_top, int Hrep,
-                                 int Wp, int OW, int PS) {
-    const int q4 = Wp >> 2, per_plane = Hrep * q4;
-    const long long total = (long long)NPH * B * C * per_plane;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int pc = (int)(i / per_plane);  // (ph * B + b) * C + c
-        const int j = (int)(i - (long long)pc * per_plane);
-        const int row = j / q4, x0 = (j - row * q4) * 4;
-        const int c = pc % C, pb = pc / C, b = pb % B, ph = pb / B;
-        const int iy = SY * (row - pad_top) + ph;
-        const bool rok = (unsigned)iy < (unsigned)H;
-        const float* src = x + (long long)b * x_bs + ((long long)c * H + (rok ? iy : 0)) * W;
-        for (int s = 0; s < KW; ++s) {
-            float v[4];
+                                 int H, int W, int KW, int SY, int SX_, int DX_, int PX, int NPH, int pad_top,
+                                 int Hrep, int Wp, int OW, int PS) {
+    const int SX = SXC ? SXC : SX_, DX = DXC ? DXC : DX_;
+    const int q4 = Wp >> 2;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= Hrep * q4) return;
+    const int pc = blockIdx.y;
+    const int c = pc % C, pb = pc / C, b = pb % B, ph = pb / B;
+    const int row = j / q4, x0 = (j - row * q4) * 4;
+    const int iy = SY * (row - pad_top) + ph;
+    const bool rok = (unsigned)iy < (unsigned)H;
+    const float* src = x + (long long)b * x_bs + ((long long)c * H + (rok ? iy : 0)) * W;
+    const int ix0 = SX * x0 - PX;                  // input column of output column x0, tap 0
+    const int span = SX * 3 + (KW - 1) * DX + 1;  // input columns the 4 outputs x KW taps read
+    float win[32];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int xx = x0 + k, ix = SX * xx + s * DX - PX;
-                v[k] = (rok && xx < OW && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+    for (int t = 0; t < 32; ++t) {
+        const int ix = ix0 + t;
+        win[t] = (t < span && rok && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+    }
+    const long long plane_z = (long long)ph * B + b;  // z of kernel column s is s*NPH*B + plane_z
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        if (s >= KW) break;
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float w = 0.f;
+            if (SXC && DXC) {
+                w = win[(SXC * k + s * DXC) & 31];  // compile-time index (< span <= 32)
+            } else {
+                const int t = SX * k + s * DX;  // < span
+#pragma unroll
+                for (int u = 0; u < 32; ++u) w = (u == t) ? win[u] : w;  // register select, no local memory
             }
-            const long long z = ((long long)s * NPH + ph) * B + b;
-            *reinterpret_cast<float4*>(P + (z * C + c) * PS + row * Wp + x0) = make_float4(v[0], v[1], v[2], v[3]);
+            v[k] = (x0 + k < OW) ? w : 0.f;
         }
+        const long long z = (long long)s * NPH * B + plane_z;
+        *reinterpret_cast<float4*>(P + (z * C + c) * PS + row * Wp + x0) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
@@ -570,6 +589,8 @@ bool conv_tc_supported(const ConvGeom& g) {
     if (g.KH > TC_MAX_KH || g.SY > 4 || g.OH * g.OW == 1) return false;
     TcPlan pl;
     tc_plan(g, &pl);
+    if (pl.mode == TC_TAPS && (g.KW > 8 || g.SX * 3 + (g.KW - 1) * g.DX + 1 > 32 || pl.NPH * g.B * g.C > 65535))
+        return false;
     return pl.Cr <= 4096 && g.B * pl.Lp < ((int64_t)1 << 31) - TC_BM &&
            g.KW * pl.NPH * g.B <= 65535 && g.B * pl.Cr * pl.PS < ((int64_t)1 << 40);
 }
@@ -715,10 +736,14 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
                 (int)pl.Wp, (int)pl.PS);
         } else {
             Z = g.KW * pl.NPH * g.B;
-            const int64_t total = pl.NPH * g.B * g.C * pl.Hrep * (pl.Wp / 4);
-            k_tc_repack_taps<<<grid_for(total, 256, ctx->sm_count, 2), 256, 0, ctx->stream>>>(
-                x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KW, (int)g.SY, (int)g.SX,
-                (int)g.DX, (int)g.PX, (int)pl.NPH, (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
+            const int64_t rows4 = pl.Hrep * (pl.Wp / 4);
+            dim3 rg((unsigned)ceil_div(rows4, 256), (unsigned)(pl.NPH * g.B * g.C));
+            auto kern = (g.SX == 1 && g.DX == 1)   ? k_tc_repack_taps<1, 1>
+                        : (g.SX == 2 && g.DX == 1) ? k_tc_repack_taps<2, 1>
+                                                   : k_tc_repack_taps<0, 0>;
+            kern<<<rg, 256, 0, ctx->stream>>>(x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KW,
+                                              (int)g.SY, (int)g.SX, (int)g.DX, (int)g.PX, (int)pl.NPH,
+                                              (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
             kmaps = (int)g.KH;
         }
         r = check_launch("k_tc_repack");
