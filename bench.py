@@ -41,6 +41,7 @@ METRIC = "YOLOv3-416 images/sec (FP32 path)"
 METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
 MATH_MODES = {"fp32": 0, "tf32": 1}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
+PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "conv_tc_yolov3_b8.json"
 
 
 def dist_env():
@@ -354,7 +355,10 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
            "roofline": {"bound": "tensor", "kernel": "k_conv_tc (tcgen05 TF32) + tap-replica repack; layer 0 on conv_fp32_kernel",
                         "achieved": achieved, "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
                         "peak_source": f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)",
-                        "conv_ms_per_forward": conv_ms},
+                        "conv_ms_per_forward": conv_ms,
+                        "traffic": (json.loads(PROFILE_SUMMARY_TF32.read_text()).get("dram_bytes_per_forward")
+                                    if PROFILE_SUMMARY_TF32.exists() else None),
+                        "traffic_unit": "bytes per forward (ncu, summed over conv and repack launches)"},
            "head_rel_l2_vs_fp32_path": errs, "heads": list(HEADS)}
     net.close()
     return out
