@@ -64,6 +64,9 @@ struct TcParams {
                     // groups are read through the bounds-checked tail map
     int tiles_n, csteps, ktiles;
     int tiles_total;
+    int splits, kt_per_split, units;  // split-K: units = tiles_total * splits, unit w = tile w/splits
+    float* part;                      // split-K partial tiles [unit][128 pixels][BN] (splits > 1)
+    int* tile_cnt;                    // split-K arrival counters, one per tile, left at 0
     long long y_bs, r_bs;
     int act, yolo_classes;
     int phase[TC_MAX_KH];
@@ -260,6 +263,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
+    __shared__ volatile int last_unit;  // split-K: this CTA's unit is the last of its tile
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const unsigned sbase = (unsigned)__cvta_generic_to_shared(smem);
@@ -294,7 +298,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool ok = true;
             const long long c_start = clock64();
             long long c_wait = 0;
-            for (int t = t_first; ok && t < p.tiles_total; t += t_step) {
+            for (int w = t_first; ok && w < p.units; w += t_step) {
+                const int t = w / p.splits, z = w - t * p.splits;
+                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
                 const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
                 const int n0 = mt * (TC_BM * CTAS) + rank * TC_BM;
                 int bq[4], gq[4];
@@ -305,8 +311,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     gq[j] = (n - bq[j] * p.Lp) >> 5;
                 }
                 const bool split = bq[0] != bq[3] || gq[3] >= p.g_full;
-                int r = 0, s = 0, c0 = 0;  // kernel tap and first channel of k tile kt
-                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                // kernel tap (r, s) and first channel c0 of k tile kt
+                const int rs0 = kb / p.csteps;
+                int r = rs0 / p.KW, s = rs0 - r * p.KW, c0 = (kb - rs0 * p.csteps) * TC_BK;
+                for (int kt = kb; kt < ke; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
                     const long long c0w = clock64();
                     if (use > 0 && !tc::mbar_wait_bounded(&empty_bar[st], (use - 1) & 1, &abort_flag, p.status, 911)) {
@@ -362,14 +370,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool ok = true, issued = false;
             const long long c_start = clock64();
             long long c_wf = 0, c_we = 0;
-            for (int t = t_first; ok && t < p.tiles_total; t += t_step, ++tl) {
+            for (int w = t_first; ok && w < p.units; w += t_step, ++tl) {
+                const int z = w % p.splits;
+                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
                 const int buf = tl & 1, u = tl >> 1;
                 long long c0w = clock64();
                 if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 912)) break;
                 c_we += clock64() - c0w;
                 tc::tc_fence_after();
                 const uint32_t d = tmem0 + buf * BN;
-                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                for (int kt = kb; kt < ke; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
                     c0w = clock64();
                     if (!tc::mbar_wait_bounded(&full_bar[st], use & 1, &abort_flag, p.status, 913)) {
@@ -383,7 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int kk = 0; kk < TC_BK / 8; ++kk) {
                         const uint64_t da = tc::smem_desc_mn_sw128_32b(sa + kk * 1024, TC_BOX_BYTES, 512);
                         const uint64_t db = tc::smem_desc_mn_sw128_32b(sb + kk * 1024, TC_BOX_BYTES, 512);
-                        tc::mma_tf32_g<CTAS>(d, da, db, idesc, (kt | kk) ? 1u : 0u);
+                        tc::mma_tf32_g<CTAS>(d, da, db, idesc, (kt != kb || kk) ? 1u : 0u);
                     }
                     issued = true;
                     tc::mma_commit_g<CTAS>(&empty_bar[st]);
@@ -424,13 +434,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int tl = 0;
         const long long c_start = clock64();
         long long c_wt = 0, c_ld = 0, c_st = 0, c_sts = 0;
-        for (int t = t_first; t < p.tiles_total; t += t_step, ++tl) {
+        for (int w = t_first; w < p.units; w += t_step, ++tl) {
+            const int t = w / p.splits;
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
             const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 914);
             c_wt += clock64() - c0w;
-            if (!__all_sync(0xffffffffu, ok)) break;  // tcgen05.ld is warp-collective: all lanes or none
+            // all 8 epilogue warps leave together (tcgen05.ld is warp-collective, and the split-K
+            // path below meets at a named barrier)
+            if (tc::epi_any(!ok)) break;
             tc::tc_fence_after();
+            const bool from_tmem = p.splits == 1;
+            if (!from_tmem) {
+                // split-K: this unit's raw accumulator rows -> partial tile, then free TMEM
+                float* prow = p.part + ((size_t)w * TC_BM + quarter * 32 + lane) * BN;
+#pragma unroll 1
+                for (int sl = half; sl < BN / 16; sl += 2) {
+                    uint32_t pr[16];
+                    tc::tmem_ld16_issue(tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16) + sl * 16, pr);
+                    tc::tmem_wait16(pr);
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4)
+                        __stcg(reinterpret_cast<float4*>(prow + sl * 16 + i),
+                               make_float4(__uint_as_float(pr[i]), __uint_as_float(pr[i + 1]),
+                                           __uint_as_float(pr[i + 2]), __uint_as_float(pr[i + 3])));
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);
+                // the last unit of the tile to arrive sums the partials in split order
+                __threadfence();
+                tc::epi_sync();
+                if (warp == 2 && lane == 0) {
+                    const int prev = atomicAdd(&p.tile_cnt[t], 1);
+                    last_unit = prev == p.splits - 1;
+                    if (last_unit) p.tile_cnt[t] = 0;  // ready for the next launch
+                }
+                tc::epi_sync();
+                if (!last_unit) continue;
+                __threadfence();
+            }
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
             // this lane's quad: pixels n .. n+3 of the padded grid (one row, one image)
             const int n = mt * (TC_BM * CTAS) + rank * TC_BM + quarter * 32 + qd * 4;
@@ -452,11 +495,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             uint32_t vr[16];
             const long long c0l = clock64();
-            if (half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
+            if (from_tmem && half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
 #pragma unroll 1
             for (int sl = half; sl < BN / 16; sl += 2) {
                 const long long cw0 = clock64();
-                tc::tmem_wait16(vr);
+                if (from_tmem) {
+                    tc::tmem_wait16(vr);
+                } else {  // sum of the tile's partials, split 0 first
+                    float acc[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+                    const float* pb = p.part + ((size_t)t * p.splits * TC_BM + quarter * 32 + lane) * BN + sl * 16;
+                    for (int zz = 0; zz < p.splits; ++zz) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 q4 = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)zz * TC_BM * BN + i));
+                            acc[i] = __fadd_rn(acc[i], q4.x);
+                            acc[i + 1] = __fadd_rn(acc[i + 1], q4.y);
+                            acc[i + 2] = __fadd_rn(acc[i + 2], q4.z);
+                            acc[i + 3] = __fadd_rn(acc[i + 3], q4.w);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) vr[i] = __float_as_uint(acc[i]);
+                }
                 const long long cw1 = clock64();
                 c_ld += cw1 - cw0;
                 const int fb = nt * BN + sl * 16;
@@ -483,7 +545,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 // the next slab's TMEM load runs while this slab is stored
-                if (sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
+                if (from_tmem && sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
                 __syncwarp();
                 c_sts += clock64() - cw1;
                 // 2. 16 filters x 8 pixel quads: lane -> quad qd of filter rows frow, frow+4, ...
@@ -525,6 +587,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 __syncwarp();
             }
             c_st += clock64() - c0l;
+            if (!from_tmem) continue;  // the accumulator was released after the partial was written
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) {  // this warp's TMEM reads are done: the accumulator may be reused
@@ -595,16 +658,28 @@ bool conv_tc_supported(const ConvGeom& g) {
            g.KW * pl.NPH * g.B <= 65535 && g.B * pl.Cr * pl.PS < ((int64_t)1 << 40);
 }
 
-int64_t conv_tc_scratch_floats(const ConvGeom& g) {
-    TcPlan pl;
-    tc_plan(g, &pl);
+// Replica floats of a plan (rounded to 64 floats, so the split-K partials after it stay aligned).
+static int64_t replica_floats(const ConvGeom& g, const TcPlan& pl) {
+    int64_t n;
     if (pl.mode == TC_INPLACE) {
         // x that is not 16-byte aligned is copied into a tap replica instead
         const int64_t Wp = round_up(g.OW, 4);
-        return g.B * g.C * (round_up(g.OH * Wp, 32) + 32);
+        n = g.B * g.C * (round_up(g.OH * Wp, 32) + 32);
+    } else if (pl.mode == TC_IM2COL) {
+        n = g.B * pl.Cr * pl.PS;
+    } else {
+        n = g.KW * pl.NPH * g.B * g.C * pl.PS;
     }
-    if (pl.mode == TC_IM2COL) return g.B * pl.Cr * pl.PS;
-    return g.KW * pl.NPH * g.B * g.C * pl.PS;
+    return round_up(n, 64);
+}
+
+// split-K partial tiles live after the replica, up to this many floats (128 MB)
+constexpr int64_t TC_PART_CAP = (int64_t)1 << 25;
+
+int64_t conv_tc_scratch_floats(const ConvGeom& g) {
+    TcPlan pl;
+    tc_plan(g, &pl);
+    return replica_floats(g, pl) + TC_PART_CAP;
 }
 
 template <int BN, int STAGES, int CTAS>
@@ -622,7 +697,7 @@ static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
         }
     }
     const int slots = CTAS == 1 ? ctx->sm_count : (ctx->sm_count & ~1);
-    const int grid = (int)std::min<int64_t>((int64_t)p.tiles_total * CTAS, slots);
+    const int grid = (int)std::min<int64_t>((int64_t)p.units * CTAS, slots);
     if constexpr (CTAS == 1) {
         k_conv_tc<BN, STAGES, 1><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     } else {
@@ -647,7 +722,7 @@ static int launch_bn(tb_ctx* ctx, const TcMaps& maps, const TcParams& p) {
 // Tile shape (filters per tile, CTAs per tile) with the smallest modelled time: waves of tiles
 // over the SMs (or SM pairs) x per-tile cycles, a k tile costing the larger of its MMA time
 // (2*BN cycles per SM) and its operand delivery (A 16 KB + this CTA's part of B at ~64 B/cycle).
-struct TcShape { int bn, ctas; };
+struct TcShape { int bn, ctas, splits; };
 
 // Shapes measured by conv_tc_autotune, per device and geometry; a shape pinned for one launch
 // by the autotuner itself.
@@ -660,14 +735,14 @@ static std::vector<int64_t> tc_key(int device, const ConvGeom& g, bool xa) {
 }
 
 static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms, int device, bool xa) {
-    TcShape best{32, 1};
+    TcShape best{32, 1, 1};
     double best_cost = 1e300;
     if (t_tc_pin) return *t_tc_pin;
-    if (const char* f = getenv("TB_TC_FORCE")) {  // test hook "BN,CTAS"
-        int bn = 0, ct = 0;
-        if (sscanf(f, "%d,%d", &bn, &ct) == 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) &&
-            (ct == 1 || (ct == 2 && bn >= 64)))
-            return TcShape{bn, ct};
+    if (const char* f = getenv("TB_TC_FORCE")) {  // test hook "BN,CTAS[,SPLITS]"
+        int bn = 0, ct = 0, sp = 1;
+        if (sscanf(f, "%d,%d,%d", &bn, &ct, &sp) >= 2 && (bn == 32 || bn == 64 || bn == 128 || bn == 256) &&
+            (ct == 1 || (ct == 2 && bn >= 64)) && sp >= 1 && sp <= 8)
+            return TcShape{bn, ct, ct == 1 ? sp : 1};
     }
     {
         std::lock_guard<std::mutex> lk(g_tc_mu);
@@ -684,7 +759,7 @@ static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms
             const int64_t slots = ct == 1 ? sms : sms / 2;
             const double kc = std::max(2.0 * bn, (16384.0 + bn * 128.0 / ct) / 64.0);
             const double cost = (double)ceil_div(tiles, slots) * (ktiles * kc + 2500.0);
-            if (cost < best_cost * 0.999) best = TcShape{bn, ct}, best_cost = cost;
+            if (cost < best_cost * 0.999) best = TcShape{bn, ct, 1}, best_cost = cost;
         }
     }
     return best;
@@ -791,6 +866,17 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     const int64_t tiles = tiles_m * p.tiles_n;
     if (tiles >= ((int64_t)1 << 30)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: too many tiles");
     p.tiles_total = (int)tiles;
+    // split-K over units of kt_per_split k tiles (one CTA per tile; the counters and the partial
+    // buffer bound it)
+    int splits = std::min(sh.splits, p.ktiles);
+    if (sh.ctas != 1 || !scratch || tiles > ctx->tile_cnt_len ||
+        tiles * splits * TC_BM * bn > TC_PART_CAP)
+        splits = 1;
+    p.kt_per_split = (int)ceil_div(p.ktiles, splits);
+    p.splits = (int)ceil_div(p.ktiles, p.kt_per_split);
+    p.units = p.tiles_total * p.splits;
+    p.part = p.splits > 1 ? scratch + replica_floats(g, pl) : nullptr;
+    p.tile_cnt = ctx->tile_cnt;
     p.b_grouped = g.Mpad % 32 == 0;
     if (p.b_grouped) {  // (32 filters, k, filter group), one box of bn/32 groups per stage
         const uint64_t dims[3] = {32, (uint64_t)g.Kpad, (uint64_t)(g.Mpad / 32)};
@@ -908,11 +994,15 @@ int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     int r = ensure_workspace(ctx, (size_t)conv_tc_scratch_floats(g) * sizeof(float));
     if (r != TB_OK) return r;
     std::vector<TcShape> cands;
+    const int64_t ktiles = (g.rsc && g.C % 32 == 0) ? g.KH * g.KW * (g.C / 32) : round_up(g.Kpad, 32) / 32;
     for (int ct : {1, 2})
         for (int bn : {32, 64, 128, 256}) {
             if (ct == 2 && bn < 64) continue;
             if (bn > round_up(g.F, 32) && bn != 32) continue;
-            cands.push_back(TcShape{bn, ct});
+            for (int sp : {1, 2, 3, 4}) {
+                if (sp > 1 && (ct != 1 || ktiles < 4 * sp)) continue;
+                cands.push_back(TcShape{bn, ct, sp});
+            }
         }
     cudaEvent_t e0, e1;
     TB_CHECK_CUDA(cudaEventCreate(&e0));
@@ -935,9 +1025,9 @@ int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
         float ms = 0.f;
         cudaEventElapsedTime(&ms, e0, e1);
         if (getenv("TB_AUTOTUNE_VERBOSE"))
-            fprintf(stderr, "tc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d ctas %d: %.4f ms\n",
+            fprintf(stderr, "tc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d ctas %d splits %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
-                    (long long)g.B, c.bn, c.ctas, ms / 3);
+                    (long long)g.B, c.bn, c.ctas, c.splits, ms / 3);
         if (ms < best_ms) best_ms = ms, best = c;
     }
     cudaEventDestroy(e0);

@@ -211,6 +211,20 @@ __host__ __device__ constexpr uint32_t idesc_tf32_mn(int M, int N) {
 }
 
 
+// --- the 8 epilogue warps (256 threads) of the conv kernel: named barrier 1 ---------------
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
+
+// barrier of the epilogue warps that also tells every thread whether any thread passed `v`
+__device__ __forceinline__ bool epi_any(bool v) {
+    unsigned r;
+    asm volatile(
+        "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, 1, 256, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((unsigned)v)
+        : "memory");
+    return r != 0;
+}
+
 // --- CTA pairs (cta_group::2): a cluster of 2 CTAs on two SMs computes one M = 256 tile -----
 __device__ __forceinline__ unsigned cluster_rank() {
     unsigned r;

@@ -133,13 +133,16 @@ PAIR_CASES = [  # (B, C, H, F, k, s, p) under a forced tile shape
     (2, 256, 13, 255, 1, 1, 0),    # ragged filters (255) and pixels
     (2, 32, 52, 64, 3, 2, 1),      # stride 2
     (2, 3, 40, 32, 3, 1, 1),       # im2col rows
+    (1, 256, 13, 160, 3, 1, 1),    # 72 k tiles: split-K units of uneven tiles
 ]
 
 
-@pytest.mark.parametrize("shape", ["64,2", "128,2", "256,2", "256,1", "32,1"])
+@pytest.mark.parametrize("shape", ["64,2", "128,2", "256,2", "256,1", "32,1", "128,1,2", "256,1,3", "64,1,4"])
 def test_tc_conv_every_tile_shape(ctx, shape, monkeypatch):
-    """Each (filters per tile, CTAs per tile) shape of the tensor-core kernel, pinned through the
-    TB_TC_FORCE test hook: 2 = a CTA pair on two SMs (cta_group::2, M = 256)."""
+    """Each (filters per tile, CTAs per tile[, K splits]) shape of the tensor-core kernel, pinned
+    through the TB_TC_FORCE test hook: 2 CTAs = a pair on two SMs (cta_group::2, M = 256); splits =
+    split-K units whose partial tiles the last arriving unit sums in split order.  Each case runs
+    twice: identical results (deterministic split-K, counters reset)."""
     monkeypatch.setenv("TB_TC_FORCE", shape)
     rng = np.random.default_rng(21)
     for (B, C, H, F, k, s, p) in PAIR_CASES:
