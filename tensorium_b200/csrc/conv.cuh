@@ -59,7 +59,7 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      const float* bias, const float* bn_scale, const float* bn_mean,
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt = nullptr,
-                     int64_t tile_cnt_len = 0);
+                     int64_t tile_cnt_len = 0, bool allow_tma = true);
 // TF32 tensor-core path (conv_tc.cu): convolutions with channels % 32 == 0 (any stride, dilation).
 bool conv_tc_supported(const ConvGeom& g);
 int64_t conv_tc_scratch_floats(const ConvGeom& g);
@@ -69,6 +69,11 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
                    unsigned long long* phases = nullptr);
 // Diagnostic: MMA issue rate (see conv_tc.cu).
 int conv_tc_mma_rate(tb_ctx* ctx, int kmajor, double* tflops_at_clock, double* cycles_per_mma);
+// FP32 conv fed by TMA (conv_fp32_tma.cu): RSC layers with more than one output pixel.
+bool conv_fp32_tma_supported(const ConvGeom& g);
+int64_t conv_fp32_tma_ws_floats(const ConvGeom& g, int splits);
+int conv_fp32_tma_run(tb_ctx* ctx, const ConvGeom& g, ConvParams p, float* ws, int64_t ws_floats,
+                      int64_t tile_cnt_len, int64_t* launches);
 // Measure the tensor-core tile shapes of this geometry on x / y and keep the fastest.
 int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // Round packed weights to TF32 (nearest, ties away) in place.
@@ -76,7 +81,8 @@ int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // Split-K partial floats this call would need (0 when it does not split), for a given x.
-int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x);
+// allow_tma = false: only the gather kernels (callers whose scratch cannot hold a replica)
+int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x, bool allow_tma = true);
 
 // Floats of split-K workspace the FP32 path needs for this geometry (0 if it does not split).
 int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g);

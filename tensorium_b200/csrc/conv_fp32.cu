@@ -83,6 +83,7 @@ int conv_geom(const tb_conv_desc* d, ConvGeom* g) {
 struct TileCfg {
     int BM, BN, splits, kt_per_split;
     int mode;
+    int tma;  // 1: the TMA-fed kernel (conv_fp32_tma.cu, 128 x 128 tile); chosen only by measurement
 };
 
 static int conv_mode_of(const ConvGeom& g, bool x_aligned16) {
@@ -115,13 +116,13 @@ static std::vector<int64_t> tune_key(const tb_ctx* ctx, const ConvGeom& g, int m
             g.x_bs, g.y_bs, mode};
 }
 
-static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
+static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16, bool allow_tma = true) {
     TileCfg best{};
     best.mode = conv_mode_of(g, x_aligned16);
     if (!getenv("TB_CONV_FORCE")) {
         std::lock_guard<std::mutex> lk(g_tune_mu);
         auto it = g_tuned.find(tune_key(ctx, g, best.mode));
-        if (it != g_tuned.end()) return it->second;
+        if (it != g_tuned.end() && (allow_tma || !it->second.tma)) return it->second;
     }
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int64_t ktiles = g.Kpad / CONV_BK;
@@ -159,10 +160,11 @@ static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
     // test hook: TB_CONV_FORCE="BM,BN,splits" pins the tile configuration (parity tests of
     // every configuration); unset in normal use
     if (const char* f = getenv("TB_CONV_FORCE")) {
-        int bm = 0, bn = 0, sp = 0;
-        if (sscanf(f, "%d,%d,%d", &bm, &bn, &sp) == 3 &&
+        int bm = 0, bn = 0, sp = 0, tma = 0;
+        if (sscanf(f, "%d,%d,%d,%d", &bm, &bn, &sp, &tma) >= 3 &&
             ((bm == 128 && bn == 128) || (bm == 64 && bn == 128) || (bm == 64 && bn == 64) || (bm == 32 && bn == 256))) {
             best.BM = bm; best.BN = bn;
+            best.tma = (tma == 1 && bm == 128 && bn == 128 && allow_tma && conv_fp32_tma_supported(g)) ? 1 : 0;
             int64_t spl = sp < 1 ? 1 : (sp > ktiles ? ktiles : sp);
             int64_t kps = ceil_div(ktiles, spl);
             best.kt_per_split = (int)kps;
@@ -172,17 +174,17 @@ static TileCfg choose_tiles(tb_ctx* ctx, const ConvGeom& g, bool x_aligned16) {
     return best;
 }
 
-int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g) {
-    TileCfg t = choose_tiles(ctx, g, true);
-    TileCfg t2 = choose_tiles(ctx, g, false);
-    int64_t s = t.splits > t2.splits ? t.splits : t2.splits;
-    if (s <= 1) return 0;
-    return s * g.F * g.B * g.OH * g.OW;
+static int64_t ws_floats_of(const ConvGeom& g, const TileCfg& t) {
+    if (t.tma) return conv_fp32_tma_ws_floats(g, t.splits);
+    return t.splits > 1 ? (int64_t)t.splits * g.F * g.B * g.OH * g.OW : 0;
 }
 
-int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x) {
-    TileCfg t = choose_tiles(ctx, g, aligned16(x));
-    return t.splits > 1 ? (int64_t)t.splits * g.F * g.B * g.OH * g.OW : 0;
+int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g) {
+    return std::max(ws_floats_of(g, choose_tiles(ctx, g, true)), ws_floats_of(g, choose_tiles(ctx, g, false)));
+}
+
+int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x, bool allow_tma) {
+    return ws_floats_of(g, choose_tiles(ctx, g, aligned16(x), allow_tma));
 }
 
 static int launch_with(tb_ctx* ctx, const ConvGeom& g, const TileCfg& t, const float* x, const float* wp,
@@ -209,6 +211,18 @@ static int launch_with(tb_ctx* ctx, const ConvGeom& g, const TileCfg& t, const f
     p.yolo_classes = yolo_classes;
     p.vec_out = (p.OHW % 4 == 0 && g.y_bs % 4 == 0 && aligned16(y) &&
                  (!res || (g.r_bs % 4 == 0 && aligned16(res)))) ? 1 : 0;
+    if (t.tma) {  // replica + split-K partials in the given scratch or the context workspace
+        const int64_t need = conv_fp32_tma_ws_floats(g, t.splits);
+        float* wsp = ws;
+        int64_t wsf = ws_floats;
+        if (!wsp) {
+            int r = ensure_workspace(ctx, (size_t)need * sizeof(float));
+            if (r != TB_OK) return r;
+            wsp = reinterpret_cast<float*>(ctx->ws);
+            wsf = need;
+        }
+        return conv_fp32_tma_run(ctx, g, p, wsp, wsf, cnt_len, launches);
+    }
     dim3 grid((unsigned)ceil_div(p.Ntot, t.BN), (unsigned)ceil_div(g.F, t.BM), (unsigned)t.splits);
     if (grid.y > 65535 || grid.z > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     if (t.splits > 1) {
@@ -240,9 +254,9 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      const float* bias, const float* bn_scale, const float* bn_mean,
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
-                     int64_t tile_cnt_len) {
+                     int64_t tile_cnt_len, bool allow_tma) {
     if (g.B == 0) return TB_OK;
-    TileCfg t = choose_tiles(ctx, g, aligned16(x));
+    TileCfg t = choose_tiles(ctx, g, aligned16(x), allow_tma);
     return launch_with(ctx, g, t, x, wp, bias, bn_scale, bn_mean, bn_var, res, y, act, yolo_classes,
                        ws, ws_floats, launches, tile_cnt, tile_cnt_len);
 }
@@ -268,15 +282,18 @@ int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
             const int64_t kps = ceil_div(kt, sp);
             if (ceil_div(kt, kps) != sp) continue;
             if ((int64_t)sp * M * N * 4 > ((int64_t)512 << 20)) continue;  // 512 MiB scratch cap
-            TileCfg t;
+            TileCfg t{};
             t.BM = c[0]; t.BN = c[1]; t.splits = sp; t.kt_per_split = (int)kps; t.mode = mode;
             cands.push_back(t);
+            if (c[0] == 128 && conv_fp32_tma_supported(g)) {  // the TMA-fed kernel, same split
+                t.tma = 1;
+                cands.push_back(t);
+            }
         }
     }
     if (cands.empty()) return TB_OK;
     int64_t ws_need = 0;
-    for (auto& t : cands)
-        if (t.splits > 1) ws_need = std::max<int64_t>(ws_need, (int64_t)t.splits * M * N);
+    for (auto& t : cands) ws_need = std::max<int64_t>(ws_need, ws_floats_of(g, t));
     if (ws_need) {
         int r = ensure_workspace(ctx, (size_t)ws_need * 4);
         if (r != TB_OK) return r;
@@ -290,7 +307,13 @@ int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
     for (auto& t : cands) {
         rc = launch_with(ctx, g, t, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR,
                          0, nullptr, 0, nullptr, nullptr, 0);  // warm-up
-        if (rc != TB_OK) break;
+        if (rc != TB_OK) {
+            if (t.tma) {  // a geometry the TMA maps cannot describe: keep the gather kernels
+                rc = TB_OK;
+                continue;
+            }
+            break;
+        }
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && rc == TB_OK; ++rep)
             rc = launch_with(ctx, g, t, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR,
@@ -302,9 +325,9 @@ int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
         float ms = 0.f;
         cudaEventElapsedTime(&ms, e0, e1);
         if (getenv("TB_AUTOTUNE_VERBOSE"))
-            fprintf(stderr, "autotune C%lld H%lld F%lld k%lld s%lld B%lld: %dx%d split %d mode %d: %.4f ms\n",
+            fprintf(stderr, "autotune C%lld H%lld F%lld k%lld s%lld B%lld: %dx%d split %d mode %d tma %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
-                    (long long)g.B, t.BM, t.BN, t.splits, t.mode, ms / 3);
+                    (long long)g.B, t.BM, t.BN, t.splits, t.mode, t.tma, ms / 3);
         if (ms < best_ms) { best_ms = ms; best = t; }
     }
     cudaEventDestroy(e0);

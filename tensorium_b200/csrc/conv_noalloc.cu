@@ -57,7 +57,7 @@ extern "C" int tb_conv2d_fwd_noalloc(tb_ctx* ctx, const tb_conv_desc* d, const f
     if (!aligned16(packed_w)) return fail(TB_ERR_INVALID, "noalloc conv: packed weights must be 16-byte aligned");
     if (!act_supported(d->activation))
         return fail(TB_ERR_UNSUPPORTED, "noalloc conv: activation %lld not supported", (long long)d->activation);
-    const int64_t need = conv_fp32_ws_floats_for(ctx, g, x);
+    const int64_t need = conv_fp32_ws_floats_for(ctx, g, x, false);
     if (need > NOALLOC_PARTIAL_FLOATS)
         return fail(TB_ERR_INVALID,
                     "noalloc conv: this layer needs %lld bytes of split-K scratch; the static scratch holds "
@@ -74,5 +74,5 @@ extern "C" int tb_conv2d_fwd_noalloc(tb_ctx* ctx, const tb_conv_desc* d, const f
     }
     return conv_fp32_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
                             (int)d->activation, 0, partials, NOALLOC_PARTIAL_FLOATS, nullptr, counters,
-                            NOALLOC_COUNTERS);
+                            NOALLOC_COUNTERS, false);
 }

@@ -42,7 +42,7 @@
 
 namespace tbi {
 
-constexpr int TC_BM = 128, TC_BK = 32, TC_THREADS = 320, TC_MAX_KH = 8;
+constexpr int TC_BM = 128, TC_BK = 32, TC_THREADS = 320;
 constexpr int TC_STG_LD = 36;                                // slab row stride (floats)
 constexpr int TC_STG_BYTES = 8 * 16 * TC_STG_LD * 4;         // 8 epilogue warps x 16 x 36 floats
 constexpr int TC_BIAS_BYTES = 8 * 256 * 4;                   // 8 epilogue warps x one tile's bias
@@ -85,26 +85,14 @@ struct TcMaps {
     CUtensorMap b;
 };
 
-// How the A operand is laid out for one geometry.
-enum TcMode {
-    TC_TAPS = 0,     // tap replicas P[s][ph][b][c][Hrep][Wp] (channels % 32 == 0)
-    TC_INPLACE = 1,  // 1x1 stride-1 unpadded, H*W % 4 == 0: x itself on a flat pixel grid
-    TC_IM2COL = 2,   // any other channel count: P[b][k][OH][Wp], one row per packed weight row
-};
-
-struct TcPlan {
-    int mode;
-    int64_t Wp, NPH, pad_top, Hrep, Lp, PS;  // PS: replica plane stride (elements)
-    int64_t Cr;                              // channels of the GEMM view (k rows per tap)
-    int rowoff[TC_MAX_KH], phase[TC_MAX_KH];
-};
-
-static void tc_plan(const ConvGeom& g, TcPlan* pl) {
+// cmul: channel multiple a tap replica needs (32 for the TF32 kernel's 32-deep k tiles; the FP32
+// TMA kernel takes any RSC layer, its 16-deep tiles lying inside one tap by the packing)
+void tc_plan(const ConvGeom& g, TcPlan* pl, int cmul) {
     for (int r = 0; r < TC_MAX_KH; ++r) pl->rowoff[r] = pl->phase[r] = 0;
     pl->NPH = 1;
     pl->pad_top = 0;
     if (g.KH == 1 && g.KW == 1 && g.SY == 1 && g.SX == 1 && g.PY == 0 && g.PX == 0 && (g.H * g.W) % 4 == 0 &&
-        g.x_bs % 4 == 0 && g.rsc && g.C % 32 == 0) {
+        g.x_bs % 4 == 0 && g.rsc && g.C % cmul == 0) {
         pl->mode = TC_INPLACE;
         pl->Wp = g.H * g.W;  // one flat row: pixel q of the image is output pixel q
         pl->Hrep = 1;
@@ -115,7 +103,7 @@ static void tc_plan(const ConvGeom& g, TcPlan* pl) {
     }
     pl->Wp = round_up(g.OW, 4);
     pl->Lp = round_up(g.OH * pl->Wp, 32);
-    if (!(g.rsc && g.C % 32 == 0)) {
+    if (!(g.rsc && g.C % cmul == 0)) {
         pl->mode = TC_IM2COL;
         pl->Hrep = g.OH;
         pl->Cr = round_up(g.Kpad, 32);
@@ -147,7 +135,7 @@ static void tc_plan(const ConvGeom& g, TcPlan* pl) {
 // input window those need once (SX*3 + (KW-1)*DX + 1 <= 32 values) and writes one 16-byte quad
 // per s, values rounded to TF32.
 // SXC, DXC: compile-time column stride and dilation (0 = taken from SX, DX at run time)
-template <int SXC, int DXC>
+template <int SXC, int DXC, bool ROUND>
 __global__ void k_tc_repack_taps(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C,
                                  int H, int W, int KW, int SY, int SX_, int DX_, int PX, int NPH, int pad_top,
                                  int Hrep, int Wp, int OW, int PS) {
@@ -167,7 +155,8 @@ __global__ void k_tc_repack_taps(const float* __restrict__ x, long long x_bs, fl
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
         const int ix = ix0 + t;
-        win[t] = (t < span && rok && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+        float v = (t < span && rok && (unsigned)ix < (unsigned)W) ? __ldg(src + ix) : 0.f;
+        win[t] = ROUND ? tc::to_tf32_rna(v) : v;
     }
     const long long plane_z = (long long)ph * B + b;  // z of kernel column s is s*NPH*B + plane_z
 #pragma unroll
@@ -193,6 +182,7 @@ __global__ void k_tc_repack_taps(const float* __restrict__ x, long long x_bs, fl
 
 // im2col rows P[b][k][OH][Wp] in the k order of the packed weights (RSC with Cpad channels per
 // tap, or CRS), rows past the real K zero; values rounded to TF32.
+template <bool ROUND>
 __global__ void k_tc_repack_im2col(const float* __restrict__ x, long long x_bs, float* __restrict__ P, int B, int C,
                                    int H, int W, int KH, int KW, int SY, int SX, int DY, int DX, int PY, int PX,
                                    int rsc, int Cpad, int Kreal, int Cr, int OH, int OW, int Wp, int PS) {
@@ -224,7 +214,8 @@ __global__ void k_tc_repack_im2col(const float* __restrict__ x, long long x_bs, 
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
             const int xx = x0 + t, ix = xx * SX + s * DX - PX;
-            v[t] = (rok && xx < OW && (unsigned)ix < (unsigned)W) ? tc::to_tf32_rna(__ldg(src + ix)) : 0.f;
+            const float u = (rok && xx < OW && (unsigned)ix < (unsigned)W) ? __ldg(src + ix) : 0.f;
+            v[t] = ROUND ? tc::to_tf32_rna(u) : u;
         }
         *reinterpret_cast<float4*>(P + (long long)pk * PS + oy * Wp + x0) = make_float4(v[0], v[1], v[2], v[3]);
     }
@@ -632,8 +623,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // fp32 tensor map, 128-byte swizzle with 32-byte atoms, zero fill out of bounds
-static int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                      const uint32_t* box) {
+int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                      const uint32_t* box, CUtensorMapSwizzle sw) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(TB_ERR_CUDA, "tensor-core conv: cuTensorMapEncodeTiled is not available");
     cuuint64_t d[4], s[3];
@@ -641,7 +632,7 @@ static int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_
     for (int i = 0; i < rank; ++i) d[i] = dims[i], bx[i] = box[i];
     for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, s, bx, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "tensor-core conv: cuTensorMapEncodeTiled failed (%d)", (int)r);
     return TB_OK;
@@ -651,7 +642,7 @@ bool conv_tc_supported(const ConvGeom& g) {
     // one output pixel per image (a connected layer) would fill one row of a 32-pixel group
     if (g.KH > TC_MAX_KH || g.SY > 4 || g.OH * g.OW == 1) return false;
     TcPlan pl;
-    tc_plan(g, &pl);
+    tc_plan(g, &pl, 32);
     if (pl.mode == TC_TAPS && (g.KW > 8 || g.SX * 3 + (g.KW - 1) * g.DX + 1 > 32 || pl.NPH * g.B * g.C > 65535))
         return false;
     return pl.Cr <= 4096 && g.B * pl.Lp < ((int64_t)1 << 31) - TC_BM &&
@@ -659,7 +650,7 @@ bool conv_tc_supported(const ConvGeom& g) {
 }
 
 // Replica floats of a plan (rounded to 64 floats, so the split-K partials after it stay aligned).
-static int64_t replica_floats(const ConvGeom& g, const TcPlan& pl) {
+int64_t replica_floats(const ConvGeom& g, const TcPlan& pl) {
     int64_t n;
     if (pl.mode == TC_INPLACE) {
         // x that is not 16-byte aligned is copied into a tap replica instead
@@ -678,7 +669,7 @@ constexpr int64_t TC_PART_CAP = (int64_t)1 << 25;
 
 int64_t conv_tc_scratch_floats(const ConvGeom& g) {
     TcPlan pl;
-    tc_plan(g, &pl);
+    tc_plan(g, &pl, 32);
     return replica_floats(g, pl) + TC_PART_CAP;
 }
 
@@ -765,24 +756,26 @@ static TcShape choose_shape(const ConvGeom& g, int64_t npix, int ktiles, int sms
     return best;
 }
 
-int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
-                   const float* bn_scale, const float* bn_mean, const float* bn_var, const float* res, float* y,
-                   int act, int yolo_classes, float* scratch, int64_t* launches, unsigned long long* phases) {
-    if (!conv_tc_supported(g)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: unsupported geometry");
-    if (g.B == 0) return TB_OK;
-    TcPlan pl;
-    tc_plan(g, &pl);
+// The A operand of a conv (pixels x k) as TMA maps: x in place (1x1 stride-1 layers), tap
+// replicas or im2col rows built into `scratch` (values rounded to TF32 when `round`).  Maps: a4
+// copies 4 32-pixel groups x box_k channels, a1 one group, `tail` a bounds-checked group of an
+// in-place x; swizzle `sw`.  Shared by the TF32 kernel and the FP32 TMA kernel.
+int tc_prepare_a(tb_ctx* ctx, const ConvGeom& g, const float* x, float* scratch, bool round, int box_k, int cmul,
+                 CUtensorMapSwizzle sw, CUtensorMap* a4, CUtensorMap* a1, CUtensorMap* tail, TcPlan* plo,
+                 int* kmaps_o, int* g_full_o, int64_t* launches) {
+    TcPlan& pl = *plo;
+    tc_plan(g, &pl, cmul);
     if (pl.mode == TC_INPLACE && !aligned16(x)) {  // same result through a (1-tap) replica
         ConvGeom g2 = g;
         g2.x_bs = g.x_bs + 1;  // any stride that is not a multiple of 4 selects the replica plan
-        tc_plan(g2, &pl);
+        tc_plan(g2, &pl, cmul);
     }
-    TcMaps maps;
-    memset(&maps, 0, sizeof(maps));
     int r;
-    int kmaps = 1;  // A maps in use (one per distinct kernel row for tap replicas)
-    const uint32_t b4[4] = {32, 32, 4, 1}, b1[4] = {32, 32, 1, 1};
-    int g_full = 1 << 30;
+    int& kmaps = *kmaps_o;  // A maps in use (one per distinct kernel row for tap replicas)
+    int& g_full = *g_full_o;
+    kmaps = 1;
+    g_full = 1 << 30;
+    const uint32_t b4[4] = {32, (uint32_t)box_k, 4, 1}, b1[4] = {32, (uint32_t)box_k, 1, 1};
     if (pl.mode == TC_INPLACE) {
         // x itself: (32 pixels, channel, 32-pixel group, image); a partial last group of an
         // image goes through the bounds-checked (pixel, channel, image) tail map
@@ -790,21 +783,21 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
         g_full = (int)(HW / 32);
         const uint64_t dims[4] = {32, (uint64_t)g.C, (uint64_t)std::max<int64_t>(g_full, 1), (uint64_t)g.B};
         const uint64_t st[3] = {(uint64_t)HW * 4, 128, (uint64_t)g.x_bs * 4};
-        r = encode_map(&maps.a4[0], x, 4, dims, st, b4);
-        if (r == TB_OK) r = encode_map(&maps.a1[0], x, 4, dims, st, b1);
+        r = encode_map(&a4[0], x, 4, dims, st, b4, sw);
+        if (r == TB_OK) r = encode_map(&a1[0], x, 4, dims, st, b1, sw);
         const uint64_t td[3] = {(uint64_t)HW, (uint64_t)g.C, (uint64_t)g.B};
         const uint64_t ts[2] = {(uint64_t)HW * 4, (uint64_t)g.x_bs * 4};
-        const uint32_t tb[3] = {32, 32, 1};
-        if (r == TB_OK) r = encode_map(&maps.tail, x, 3, td, ts, tb);
+        const uint32_t tb[3] = {32, (uint32_t)box_k, 1};
+        if (r == TB_OK) r = encode_map(tail, x, 3, td, ts, tb, sw);
         if (r != TB_OK) return r;
     } else {
         if (!scratch || !aligned16(scratch))
-            return fail(TB_ERR_INVALID, "tensor-core conv: this geometry needs a 16-byte-aligned replica buffer");
+            return fail(TB_ERR_INVALID, "conv: this geometry needs a 16-byte-aligned replica buffer");
         int64_t Z;
         if (pl.mode == TC_IM2COL) {
             Z = g.B;
             const int64_t total = g.B * pl.Cr * g.OH * (pl.Wp / 4);
-            k_tc_repack_im2col<<<grid_for(total, 256, ctx->sm_count, 4), 256, 0, ctx->stream>>>(
+            (round ? k_tc_repack_im2col<true> : k_tc_repack_im2col<false>)<<<grid_for(total, 256, ctx->sm_count, 4), 256, 0, ctx->stream>>>(
                 x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KH, (int)g.KW, (int)g.SY,
                 (int)g.SX, (int)g.DY, (int)g.DX, (int)g.PY, (int)g.PX, g.rsc ? 1 : 0, (int)g.Cpad,
                 (int)(g.rsc ? g.KH * g.KW * g.Cpad : g.C * g.KH * g.KW), (int)pl.Cr, (int)g.OH, (int)g.OW,
@@ -813,9 +806,9 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
             Z = g.KW * pl.NPH * g.B;
             const int64_t rows4 = pl.Hrep * (pl.Wp / 4);
             dim3 rg((unsigned)ceil_div(rows4, 256), (unsigned)(pl.NPH * g.B * g.C));
-            auto kern = (g.SX == 1 && g.DX == 1)   ? k_tc_repack_taps<1, 1>
-                        : (g.SX == 2 && g.DX == 1) ? k_tc_repack_taps<2, 1>
-                                                   : k_tc_repack_taps<0, 0>;
+            auto kern = (g.SX == 1 && g.DX == 1)   ? (round ? k_tc_repack_taps<1, 1, true> : k_tc_repack_taps<1, 1, false>)
+                        : (g.SX == 2 && g.DX == 1) ? (round ? k_tc_repack_taps<2, 1, true> : k_tc_repack_taps<2, 1, false>)
+                                                   : (round ? k_tc_repack_taps<0, 0, true> : k_tc_repack_taps<0, 0, false>);
             kern<<<rg, 256, 0, ctx->stream>>>(x, g.x_bs, scratch, (int)g.B, (int)g.C, (int)g.H, (int)g.W, (int)g.KW,
                                               (int)g.SY, (int)g.SX, (int)g.DX, (int)g.PX, (int)pl.NPH,
                                               (int)pl.pad_top, (int)pl.Hrep, (int)pl.Wp, (int)g.OW, (int)pl.PS);
@@ -830,12 +823,27 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
         const uint64_t st[3] = {(uint64_t)pl.PS * 4, 128, (uint64_t)(pl.Cr * pl.PS) * 4};
         for (int k = 0; k < kmaps; ++k) {
             const float* base = scratch + (int64_t)pl.rowoff[k] * pl.Wp;
-            r = encode_map(&maps.a4[k], base, 4, dims, st, b4);
-            if (r == TB_OK) r = encode_map(&maps.a1[k], base, 4, dims, st, b1);
+            r = encode_map(&a4[k], base, 4, dims, st, b4, sw);
+            if (r == TB_OK) r = encode_map(&a1[k], base, 4, dims, st, b1, sw);
             if (r != TB_OK) return r;
         }
     }
 
+    return TB_OK;
+}
+
+int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
+                   const float* bn_scale, const float* bn_mean, const float* bn_var, const float* res, float* y,
+                   int act, int yolo_classes, float* scratch, int64_t* launches, unsigned long long* phases) {
+    if (!conv_tc_supported(g)) return fail(TB_ERR_UNSUPPORTED, "tensor-core conv: unsupported geometry");
+    if (g.B == 0) return TB_OK;
+    TcPlan pl;
+    TcMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    int kmaps = 1, g_full = 1 << 30;
+    int r = tc_prepare_a(ctx, g, x, scratch, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, maps.a4, maps.a1,
+                         &maps.tail, &pl, &kmaps, &g_full, launches);
+    if (r != TB_OK) return r;
     TcParams p{};
     p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
     p.res = res; p.y = y; p.status = ctx->d_status; p.phases = phases;
@@ -882,12 +890,12 @@ int conv_tc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
         const uint64_t dims[3] = {32, (uint64_t)g.Kpad, (uint64_t)(g.Mpad / 32)};
         const uint64_t st[2] = {(uint64_t)g.Mpad * 4, 128};
         const uint32_t box[3] = {32, 32, (uint32_t)(bn / 32 / sh.ctas)};  // this CTA's filters
-        r = encode_map(&maps.b, wp, 3, dims, st, box);
+        r = encode_map(&maps.b, wp, 3, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     } else {
         const uint64_t dims[2] = {(uint64_t)g.Mpad, (uint64_t)g.Kpad};
         const uint64_t st[1] = {(uint64_t)g.Mpad * 4};
         const uint32_t box[2] = {32, 32};
-        r = encode_map(&maps.b, wp, 2, dims, st, box);
+        r = encode_map(&maps.b, wp, 2, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     }
     if (r != TB_OK) return r;
     if (sh.ctas == 1) {

@@ -11,6 +11,8 @@
 #pragma once
 #include "conv.cuh"
 
+#include <cuda.h>
+
 namespace tbi {
 namespace tc {
 
@@ -342,4 +344,30 @@ __device__ __forceinline__ void tma_load_4d_g(unsigned dst, const void* tmap, ui
 }
 
 }  // namespace tc
+
+// ---- A-operand planning shared by the TF32 kernel and the FP32 TMA kernel (conv_tc.cu) ----
+constexpr int TC_MAX_KH = 8;
+// How the A operand is laid out for one geometry.
+enum TcMode {
+    TC_TAPS = 0,     // tap replicas P[s][ph][b][c][Hrep][Wp] (channels % 32 == 0)
+    TC_INPLACE = 1,  // 1x1 stride-1 unpadded, H*W % 4 == 0: x itself on a flat pixel grid
+    TC_IM2COL = 2,   // any other channel count: P[b][k][OH][Wp], one row per packed weight row
+};
+
+struct TcPlan {
+    int mode;
+    int64_t Wp, NPH, pad_top, Hrep, Lp, PS;  // PS: replica plane stride (elements)
+    int64_t Cr;                              // channels of the GEMM view (k rows per tap)
+    int rowoff[TC_MAX_KH], phase[TC_MAX_KH];
+};
+
+void tc_plan(const ConvGeom& g, TcPlan* pl, int cmul);
+// replica floats of a plan, rounded up to 64
+int64_t replica_floats(const ConvGeom& g, const TcPlan& pl);
+// fp32 tensor map (swizzle `sw`, zero fill out of bounds)
+int encode_map(CUtensorMap* m, const float* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+               const uint32_t* box, CUtensorMapSwizzle sw);
+int tc_prepare_a(tb_ctx* ctx, const ConvGeom& g, const float* x, float* scratch, bool round, int box_k, int cmul,
+                 CUtensorMapSwizzle sw, CUtensorMap* a4, CUtensorMap* a1, CUtensorMap* tail, TcPlan* plo,
+                 int* kmaps_o, int* g_full_o, int64_t* launches);
 }  // namespace tbi

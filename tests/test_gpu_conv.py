@@ -85,11 +85,12 @@ def test_all_activations(ctx):
 
 
 @pytest.mark.parametrize("cfg", ["128,128,1", "64,128,1", "64,64,1", "32,256,1", "128,128,3", "64,128,5",
-                                 "64,64,2", "32,256,4"])
+                                 "64,64,2", "32,256,4", "128,128,1,1", "128,128,3,1"])
 def test_every_tile_and_split_configuration(ctx, cfg, monkeypatch):
     """Each CTA tile and split-K count (pinned through the TB_CONV_FORCE test hook), on a
     strided RSC layer, a stride-1 RSC layer, a CRS layer and a vectorised 1x1 layer; each twice,
-    so the split-K arrival counters are seen to reset."""
+    so the split-K arrival counters are seen to reset.  A fourth field 1 selects the TMA-fed
+    kernel (RSC and 1x1 layers; the CRS layer keeps the gather kernel)."""
     monkeypatch.setenv("TB_CONV_FORCE", cfg)
     rng = np.random.default_rng(11)
     for (B, C, H, F, k, s, p) in [(2, 32, 26, 64, 3, 2, 1), (1, 64, 20, 128, 3, 1, 1), (1, 3, 21, 16, 3, 1, 1),
