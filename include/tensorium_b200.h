@@ -248,6 +248,17 @@ int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_he
                    int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
                    int64_t relative, int64_t letter, int64_t capacity,
                    tb_detection* dets, float* prob, int64_t* counts_host);
+/* Class-wise non-maximum suppression on the detections tb_yolo_detect wrote, replacing
+ * TDetectionsHelper.doNMSSort (source/ntypes.pas:1621-1649): for every image and class, the
+ * detections with a non-zero probability of the class are taken in order of decreasing
+ * probability; each one not yet suppressed zeroes the class probability of every later one
+ * whose box IoU with it (box_iou, source/ntypes.pas:1059-1108) exceeds `thresh`. Detections
+ * with objectness 0 take no part. prob is updated in place; the records keep their order (the
+ * reference leaves them sorted by the last class). Equal probabilities are taken in detection
+ * order (the reference's quicksort leaves their order to its partition history). At most 8192
+ * detections per image (min(counts_host[b], capacity)). Asynchronous on the context stream. */
+int tb_yolo_nms(tb_ctx* ctx, int64_t batch, int64_t capacity, const int64_t* counts_host, int64_t classes,
+                float thresh, const tb_detection* dets, float* prob);
 
 /* ---- XNOR binary convolution (TXNORConvolutionLayer, source/nxnorconvolutionlayer.pas) --- */
 #define TB_XNOR_PAD_BIT0 0   /* padding pixels are bit 0 (= -1), as im2col_cpu_custom_bin :232-316 */

@@ -510,6 +510,106 @@ void or_xnor_conv(int64_t batch, int64_t c, int64_t h, int64_t w, int64_t filter
     }
 }
 
+
+// ---- NMS: TDetectionsHelper.doNMSSort (source/ntypes.pas:1621-1649), with box_iou
+// (source/ntypes.pas:1059-1108), TDetectionsHelper.Comparer (:1554-1566) and
+// TTools<T>.QuickSort (source/ntensors.pas:2483-2526). The record array is represented by a
+// permutation of detection indices: QuickSort swaps records, the comparator reads prob /
+// objectness through them, so swapping indices is the same algorithm. Output: probs (in the
+// original detection order) with the suppressed (detection, class) entries zeroed; order
+// receives the final record order (the reference leaves the array in that order).
+static float nms_overlap(float x1, float w1, float x2, float w2) {
+    const float l1 = x1 - w1 / 2.0f, l2 = x2 - w2 / 2.0f;
+    const float left = (l1 > l2) ? l1 : l2;
+    const float r1 = x1 + w1 / 2.0f, r2 = x2 + w2 / 2.0f;
+    const float right = (r1 < r2) ? r1 : r2;
+    return right - left;
+}
+
+static float nms_iou(const float* a, const float* b) {
+    const float w = nms_overlap(a[0], a[2], b[0], b[2]);
+    const float h = nms_overlap(a[1], a[3], b[1], b[3]);
+    const float i = (w < 0.0f || h < 0.0f) ? 0.0f : w * h;
+    const float i2 = i;  // box_union recomputes the same intersection
+    const float u = a[2] * a[3] + b[2] * b[3] - i2;
+    if (i == 0.0f || u == 0.0f) return 0.0f;
+    return i / u;
+}
+
+struct NmsCtx {
+    const float* probs;
+    const float* obj;
+    int64_t classes;
+    int64_t sort_class;
+};
+
+// Comparer: 1 when a sorts after b (smaller prob / objectness), -1 before, 0 equal
+static int nms_cmp(const NmsCtx& c, int64_t a, int64_t b) {
+    float diff;
+    if (c.sort_class >= 0)
+        diff = c.probs[a * c.classes + c.sort_class] - c.probs[b * c.classes + c.sort_class];
+    else
+        diff = c.obj[a] - c.obj[b];
+    if (diff < 0) return 1;
+    if (diff > 0) return -1;
+    return 0;
+}
+
+static void nms_quicksort(const NmsCtx& c, int64_t* arr, int64_t L, int64_t R) {
+    do {
+        int64_t I = L, J = R;
+        const int64_t P = arr[(L + R) >> 1];
+        do {
+            while (I <= R && nms_cmp(c, P, arr[I]) > 0) ++I;
+            while (J >= 0 && nms_cmp(c, P, arr[J]) < 0) --J;
+            if (I <= J) {
+                const int64_t q = arr[I];
+                arr[I] = arr[J];
+                arr[J] = q;
+                ++I;
+                --J;
+            }
+        } while (I <= J);
+        if (J - L < R - I) {
+            if (L < J) nms_quicksort(c, arr, L, J);
+            L = I;
+        } else {
+            if (I < R) nms_quicksort(c, arr, I, R);
+            R = J;
+        }
+    } while (L < R);
+}
+
+void or_nms_sort(int64_t n, int64_t classes, const float* boxes, const float* objectness, float* probs,
+                 float thresh, int64_t* order) {
+    std::vector<int64_t> arr(n);
+    for (int64_t i = 0; i < n; ++i) arr[i] = i;
+    // detections with objectness 0 go to the end (swap with the last, re-examine the swapped-in one)
+    int64_t total = n - 1, k = total, i = 0;
+    while (i <= k) {
+        if (objectness[arr[i]] == 0.0f) {
+            std::swap(arr[i], arr[k]);
+            --k;
+            --i;
+        }
+        ++i;
+    }
+    total = k + 1;
+    NmsCtx c{probs, objectness, classes, -1};
+    for (int64_t cl = 0; cl < classes; ++cl) {
+        c.sort_class = cl;
+        if (total > 0) nms_quicksort(c, arr.data(), 0, total - 1);
+        for (int64_t a = 0; a < total; ++a) {
+            if (probs[arr[a] * classes + cl] == 0.0f) continue;
+            const float* ba = boxes + arr[a] * 4;
+            for (int64_t b = a + 1; b < total; ++b)
+                if (nms_iou(ba, boxes + arr[b] * 4) > thresh) probs[arr[b] * classes + cl] = 0.0f;
+        }
+    }
+    if (order)
+        for (int64_t j = 0; j < n; ++j) order[j] = arr[j];
+}
+
 int64_t or_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -29,7 +29,8 @@ def build() -> Path:
 
 
 def _load():
-    if not LIB_PATH.exists():
+    src = HERE / "oracle.cpp"
+    if not LIB_PATH.exists() or (src.exists() and src.stat().st_mtime > LIB_PATH.stat().st_mtime):
         build()
     lib = C.CDLL(str(LIB_PATH))
     P, I, F = C.c_void_p, C.c_int64, C.c_float
@@ -51,6 +52,7 @@ def _load():
         "or_avgpool": [I, I, I, I, P, P],
         "or_xnor_mean": [I, I, P, P],
         "or_xnor_conv": [I] * 9 + [P, P, P, P, P],
+        "or_nms_sort": [I, I, P, P, P, F, P],
         "or_num_threads": [],
         "or_set_threads": [I],
     }
@@ -158,6 +160,18 @@ def yolo_detections(out, b, n, classes, h, w, mask, anchors, img_w, img_h, net_w
                                  _p(boxes), _p(meta), _p(probs))
     k = min(cnt, capacity)
     return cnt, boxes[:k], meta[:k], probs[:k]
+
+
+def nms_sort(boxes, objectness, probs, thresh):
+    """TDetectionsHelper.doNMSSort: probs (n x classes) with the suppressed entries zeroed, in the
+    original detection order, and the final record order the reference leaves."""
+    boxes = f32(boxes).reshape(-1, 4)
+    obj = f32(objectness)
+    probs = f32(probs).copy()
+    n, classes = probs.shape
+    order = np.zeros(n, np.int64)
+    lib.or_nms_sort(n, classes, _p(boxes), _p(obj), _p(probs), thresh, _p(order))
+    return probs, order
 
 
 def connected(x, w, b, act):

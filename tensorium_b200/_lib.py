@@ -104,6 +104,7 @@ SIGNATURES = {
     "tb_yolo_fwd": [P, I64, I64, I64, I64, I64, P, P, F32],
     "tb_yolo_detect": [P, I64, I64, C.POINTER(YoloHead), I64, I64, I64, I64, F32, I64, I64, I64,
                        P, P, PI64],
+    "tb_yolo_nms": [P, I64, I64, PI64, I64, F32, P, P],
     "tb_xnor_packed_weights_count": [I64, I64, I64, PI64],
     "tb_xnor_pack_weights": [P, I64, I64, I64, P, P, P],
     "tb_xnor_conv_fwd": [P, I64, I64, I64, I64, I64, I64, I64, I64, I64, P, P, P, P, I64, P, P],

@@ -5,6 +5,7 @@
 #include "common.cuh"
 
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 using namespace tbi;
@@ -220,6 +221,145 @@ extern "C" int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const
         int64_t t = 0;
         for (int64_t h = 0; h < n_heads; ++h) t += hc[(size_t)(b * n_heads + h)];
         counts_host[b] = t;
+    }
+    return TB_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Class-wise NMS: TDetectionsHelper.doNMSSort (source/ntypes.pas:1621-1649) on the device.
+// One block per (class) and launch per image: the candidates of the class (objectness > 0,
+// prob > 0) are sorted by probability, highest first, in shared memory (bitonic sort; equal
+// probabilities in detection order), then walked in that order: a candidate that is still
+// unsuppressed zeroes the class probability of every later candidate whose box IoU with it
+// exceeds the threshold (the inner comparisons run in parallel, one barrier per candidate).
+// The reference sorts the whole record array with an unstable quicksort that carries the
+// previous class's order, so among exactly equal probabilities its order is the partition
+// history's; this keeps the detection order for them.  It also leaves the records sorted by the
+// last class; this leaves them in place.  Box IoU as box_iou (source/ntypes.pas:1059-1108).
+// ---------------------------------------------------------------------------------------
+namespace {
+
+constexpr int NMS_THREADS = 256;
+constexpr int NMS_MAX = 8192;  // detections per image one block can sort in shared memory
+
+__device__ __forceinline__ float nms_overlap(float x1, float w1, float x2, float w2) {
+    const float l1 = __fsub_rn(x1, w1 * 0.5f), l2 = __fsub_rn(x2, w2 * 0.5f);
+    const float left = l1 > l2 ? l1 : l2;
+    const float r1 = __fadd_rn(x1, w1 * 0.5f), r2 = __fadd_rn(x2, w2 * 0.5f);
+    const float right = r1 < r2 ? r1 : r2;
+    return __fsub_rn(right, left);
+}
+
+__device__ __forceinline__ float nms_iou(const tb_detection& a, const tb_detection& b) {
+    const float w = nms_overlap(a.x, a.w, b.x, b.w);
+    const float h = nms_overlap(a.y, a.h, b.y, b.h);
+    const float i = (w < 0.0f || h < 0.0f) ? 0.0f : __fmul_rn(w, h);
+    const float u = __fsub_rn(__fadd_rn(__fmul_rn(a.w, a.h), __fmul_rn(b.w, b.h)), i);
+    if (i == 0.0f || u == 0.0f) return 0.0f;
+    return __fdiv_rn(i, u);
+}
+
+// (ka, ia) comes before (kb, ib): higher probability first, then lower detection index
+__device__ __forceinline__ bool nms_before(float ka, int ia, float kb, int ib) {
+    return ka > kb || (ka == kb && ia < ib);
+}
+
+__global__ void __launch_bounds__(NMS_THREADS)
+    k_yolo_nms(const tb_detection* __restrict__ dets, float* __restrict__ prob, int n, int classes, int P,
+               float thresh) {
+    extern __shared__ __align__(16) unsigned char nsm[];
+    float* key = reinterpret_cast<float*>(nsm);
+    int* idx = reinterpret_cast<int*>(key + P);
+    unsigned char* supp = reinterpret_cast<unsigned char*>(idx + P);
+    __shared__ int m_sh;
+    const int k = blockIdx.x, tid = threadIdx.x;
+    if (tid == 0) m_sh = 0;
+    __syncthreads();
+    for (int j = tid; j < n; j += NMS_THREADS) {  // candidates, in any slot order (sorted below)
+        const float pk = prob[(long long)j * classes + k];
+        if (dets[j].objectness != 0.0f && pk != 0.0f) {
+            const int s = atomicAdd(&m_sh, 1);
+            key[s] = pk;
+            idx[s] = j;
+        }
+    }
+    __syncthreads();
+    const int m = m_sh;
+    if (m < 2) return;  // nothing to suppress
+    int P2 = 2;
+    while (P2 < m) P2 <<= 1;
+    for (int s = m + tid; s < P2; s += NMS_THREADS) {
+        key[s] = -1.0f;  // below every probability
+        idx[s] = 0x7fffffff;
+    }
+    __syncthreads();
+    for (int size = 2; size <= P2; size <<= 1) {  // bitonic sort into "before" order
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int t = tid; t < P2 / 2; t += NMS_THREADS) {
+                const int lo = 2 * t - (t & (stride - 1)), hi = lo + stride;
+                const bool up = (lo & size) == 0;  // this run ends in "before" order
+                const bool swap = up ? nms_before(key[hi], idx[hi], key[lo], idx[lo])
+                                     : nms_before(key[lo], idx[lo], key[hi], idx[hi]);
+                if (swap) {
+                    const float tk = key[lo];
+                    key[lo] = key[hi];
+                    key[hi] = tk;
+                    const int ti = idx[lo];
+                    idx[lo] = idx[hi];
+                    idx[hi] = ti;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int s = tid; s < m; s += NMS_THREADS) supp[s] = 0;
+    __syncthreads();
+    for (int i = 0; i < m - 1; ++i) {
+        if (!supp[i]) {  // uniform: read after the barrier that ended the previous step
+            const tb_detection a = dets[idx[i]];
+            for (int j = i + 1 + tid; j < m; j += NMS_THREADS)
+                if (nms_iou(a, dets[idx[j]]) > thresh) supp[j] = 1;
+        }
+        __syncthreads();
+    }
+    for (int s = tid; s < m; s += NMS_THREADS)
+        if (supp[s]) prob[(long long)idx[s] * classes + k] = 0.0f;
+}
+
+}  // namespace
+
+extern "C" int tb_yolo_nms(tb_ctx* ctx, int64_t batch, int64_t capacity, const int64_t* counts_host, int64_t classes,
+                           float thresh, const tb_detection* dets, float* prob) {
+    TB_ENTER(ctx);
+    if (batch < 0 || capacity < 0 || classes <= 0 || (batch > 0 && !counts_host))
+        return fail(TB_ERR_INVALID, "nms: bad arguments");
+    if (batch == 0 || capacity == 0) return TB_OK;
+    if (!dets || !prob) return fail(TB_ERR_INVALID, "nms: null detections or probabilities");
+    if (classes > 65535) return fail(TB_ERR_UNSUPPORTED, "nms: more than 65535 classes");
+    static std::mutex mu;
+    static bool done[64] = {false};
+    const int smem_max = NMS_MAX * 9;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (ctx->device < 64 && !done[ctx->device]) {
+            cudaError_t e = cudaFuncSetAttribute(k_yolo_nms, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(nms)");
+            done[ctx->device] = true;
+        }
+    }
+    for (int64_t b = 0; b < batch; ++b) {
+        const int64_t n = counts_host[b] < capacity ? counts_host[b] : capacity;
+        if (n < 0) return fail(TB_ERR_INVALID, "nms: negative count");
+        if (n > NMS_MAX)
+            return fail(TB_ERR_UNSUPPORTED, "nms: %lld detections in image %lld (at most %d)", (long long)n,
+                        (long long)b, NMS_MAX);
+        if (n < 2) continue;
+        int P = 2;
+        while (P < n) P <<= 1;
+        k_yolo_nms<<<(unsigned)classes, NMS_THREADS, (size_t)P * 9, ctx->stream>>>(
+            dets + b * capacity, prob + b * capacity * classes, (int)n, (int)classes, P, thresh);
+        int r = check_launch("k_yolo_nms");
+        if (r != TB_OK) return r;
     }
     return TB_OK;
 }

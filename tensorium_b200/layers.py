@@ -250,7 +250,7 @@ DET_DTYPE = np.dtype([("x", "<f4"), ("y", "<f4"), ("w", "<f4"), ("h", "<f4"), ("
 
 
 def get_detections(ctx: Context, heads, outputs, batch, img_w, img_h, net_w, net_h, thresh,
-                   relative=True, letter=False, capacity=4096):
+                   relative=True, letter=False, capacity=4096, nms=None):
     """TNNet.Detections for every image (source/nnet.pas:584-677): detection records, class
     probabilities and counts, extracted on the GPU in the reference order."""
     hs = (YoloHead * len(heads))(*[h.head(o) for h, o in zip(heads, outputs)])
@@ -260,8 +260,19 @@ def get_detections(ctx: Context, heads, outputs, batch, img_w, img_h, net_w, net
     counts = (C.c_int64 * batch)()
     check(lib.tb_yolo_detect(ctx.handle, batch, len(heads), hs, img_w, img_h, net_w, net_h, thresh,
                              1 if relative else 0, 1 if letter else 0, capacity, ptr(dets), ptr(prob), counts))
+    if nms is not None:  # TDetectionsHelper.doNMSSort(classes, nms) on the device
+        check(lib.tb_yolo_nms(ctx.handle, batch, capacity, counts, classes, nms, ptr(dets), ptr(prob)))
     recs = dets.cpu().numpy().view(DET_DTYPE).reshape(batch, capacity)
     return recs, prob.cpu().numpy().reshape(batch, capacity, classes), np.array(counts[:], np.int64)
+
+
+def nms_sort(ctx: Context, dets: torch.Tensor, prob: torch.Tensor, counts, capacity: int, classes: int,
+             thresh: float = 0.45):
+    """TDetectionsHelper.doNMSSort on device records (tb_detection bytes, batch*capacity) and
+    probabilities (batch*capacity x classes), in place."""
+    batch = len(counts)
+    c = (C.c_int64 * batch)(*[int(v) for v in counts])
+    check(lib.tb_yolo_nms(ctx.handle, batch, capacity, c, classes, thresh, ptr(dets), ptr(prob)))
 
 
 class TXNORConvolutionLayer(TBaseLayer):

@@ -118,12 +118,13 @@ class TNNet:
             outs.append(self.output(i))
         return heads, outs
 
-    def detections(self, img_w, img_h, thresh=0.45, relative=True, letter=False, capacity=4096):
-        """TNNet.Detections over every yolo layer, extracted on the GPU."""
+    def detections(self, img_w, img_h, thresh=0.45, relative=True, letter=False, capacity=4096, nms=None):
+        """TNNet.Detections over every yolo layer, extracted on the GPU; with nms = a threshold,
+        followed by TDetectionsHelper.doNMSSort on the GPU (the sample's detections.doNMSSort)."""
         heads, outs = self.yolo_heads()
         net_c, net_h, net_w = self.input_shape
         return get_detections(self.ctx, heads, outs, self.batch, img_w, img_h, net_w, net_h, thresh,
-                              relative, letter, capacity)
+                              relative, letter, capacity, nms)
 
     def profile(self, x: torch.Tensor) -> np.ndarray:
         """Device milliseconds of every layer in one eager forward (CUDA events)."""

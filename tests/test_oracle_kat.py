@@ -172,3 +172,22 @@ def test_xnor_zero_pad_mode_equals_sign_convolution():
     ref = naive_conv(np.where(x > 0, 1.0, -1.0).astype(np.float32), np.where(w > 0, 1.0, -1.0).astype(np.float32), 1, 1)
     assert np.array_equal(cnt, ref.astype(np.int32))
     assert np.array_equal(y, cnt.astype(np.float32) * mean[None, :, None, None])
+
+
+def test_nms_sort_known_answers():
+    """TDetectionsHelper.doNMSSort restated: per class, the higher-probability box of an
+    overlapping pair keeps its probability, the other's is zeroed; disjoint boxes and other
+    classes are untouched; objectness-0 records take no part."""
+    boxes = np.array([[0.50, 0.50, 0.20, 0.20],   # 0
+                      [0.52, 0.50, 0.20, 0.20],   # 1 overlaps 0 (IoU ~0.82)
+                      [0.10, 0.10, 0.05, 0.05],   # 2 disjoint
+                      [0.51, 0.50, 0.20, 0.20]],  # 3 overlaps 0 and 1, objectness 0
+                     np.float32)
+    obj = np.array([0.9, 0.8, 0.7, 0.0], np.float32)
+    probs = np.array([[0.6, 0.0], [0.7, 0.3], [0.5, 0.4], [0.0, 0.0]], np.float32)
+    out, order = O.nms_sort(boxes, obj, probs, 0.45)
+    assert np.array_equal(out, np.array([[0.0, 0.0], [0.7, 0.3], [0.5, 0.4], [0.0, 0.0]], np.float32))
+    assert order[-1] == 3  # the objectness-0 record went to the end
+    # above the IoU threshold nothing is suppressed
+    out2, _ = O.nms_sort(boxes, obj, probs, 0.9)
+    assert np.array_equal(out2, probs)
