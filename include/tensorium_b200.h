@@ -350,6 +350,57 @@ int tb_net_flops(tb_net* net, double* flops);
  * (layer_count entries; 0 for layers fused into their neighbour). Blocks. */
 int tb_net_profile(tb_net* net, const float* x, double* ms_out);
 
+/* Network shape as created: batch and the per-image input shape. */
+int tb_net_input_shape(tb_net* net, int64_t* batch, int64_t* channels, int64_t* height,
+                       int64_t* width);
+/* One layer's description (host-side; valid before and after finalize). Fields that do not apply
+ * to the layer's type are 0. */
+typedef struct tb_layer_info {
+    int64_t type;                      /* TB_LAYER_* */
+    int64_t c, h, w;                   /* input shape per image */
+    int64_t out_c, out_h, out_w;       /* output shape per image */
+    int64_t filters, ksize, stride, pad, activation, batch_normalize;  /* conv / connected / maxpool */
+    int64_t from;                      /* shortcut: absolute source layer */
+    int64_t n_inputs;                  /* route: number of inputs (TB_PARAM_ROUTE_INPUTS) */
+    int64_t classes, n, total_anchors; /* yolo */
+    int64_t groups;                    /* softmax */
+    float scale;                       /* upsample scale, yolo scale_x_y, softmax temperature */
+    float reserved;
+    int64_t weights_count;             /* floats in TB_PARAM_WEIGHTS */
+} tb_layer_info;
+int tb_net_layer_info(tb_net* net, int64_t layer, tb_layer_info* out);
+/* Copy a layer's host-side parameter array into dst (float, or int64 for the two index arrays).
+ * dst == NULL only reports the element count. BN arrays are empty once batchnorm is folded. */
+#define TB_PARAM_WEIGHTS       0
+#define TB_PARAM_BIASES        1
+#define TB_PARAM_SCALES        2
+#define TB_PARAM_ROLLING_MEAN  3
+#define TB_PARAM_ROLLING_VAR   4
+#define TB_PARAM_ROUTE_INPUTS  5   /* int64, absolute layer indices */
+#define TB_PARAM_YOLO_MASK     6   /* int64 */
+#define TB_PARAM_YOLO_ANCHORS  7   /* float, 2 per anchor */
+int tb_net_layer_param(tb_net* net, int64_t layer, int64_t which, void* dst, int64_t capacity,
+                       int64_t* count);
+
+/* ---- darknet model files (TDarknetParser, source/nparser.pas) ------------------------------ */
+/* TDarknetParser.Create + loadWeights (source/nparser.pas:782-940, 1275-1340): parse a darknet
+ * .cfg file into a new, unfinalized tb_net and, when weights_path is not NULL, read a darknet
+ * .weights file into it (cutoff > 0: only the first cutoff layers, as loadWeights' cutoff).
+ * batch > 0 overrides the [net] batch the way TDarknetParser.Create does (it applies when
+ * batch / subdivisions * subdivisions of the cfg differs from it). ctx may be NULL for a
+ * host-only net. Supported sections: [net], [convolutional], [connected] (batchnorm folded on
+ * load), [maxpool], [avgpool], [softmax], [route], [shortcut], [upsample], [yolo], [dropout]
+ * (identity at inference, kept as a one-input route so layer indices match the cfg); any other
+ * section or option value outside the executor's scope returns TB_ERR_UNSUPPORTED naming it.
+ * Layers past the end of the weights file keep zero weights (the reference stops at EOF); a
+ * file that ends inside a layer's arrays is TB_ERR_INVALID. */
+int tb_darknet_load(tb_ctx* ctx, const char* cfg_path, const char* weights_path, int64_t batch,
+                    int64_t cutoff, tb_net** out);
+/* TDarknetParser.saveWeights (source/nparser.pas:1394-1440): header major 0, minor 2, revision 5,
+ * 64-bit seen, then per conv layer biases, [scales, rolling mean, rolling variance when its
+ * batchnorm is not folded], weights; per connected layer biases, weights. */
+int tb_darknet_save_weights(tb_net* net, const char* weights_path, int64_t seen);
+
 /* ---- diagnostics -------------------------------------------------------------------------- */
 /* FP32 FFMA throughput of this GPU (TFLOP/s) from a register-resident FMA loop on every SM;
  * the roofline denominator of the FP32 CUDA-core conv path (no reference counterpart). Blocks. */

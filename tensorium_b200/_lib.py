@@ -63,6 +63,19 @@ class YoloHead(C.Structure):
                 ("anchors_host", C.c_void_p), ("new_coords", C.c_int64)]
 
 
+class LayerInfo(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "type", "c", "h", "w", "out_c", "out_h", "out_w", "filters", "ksize", "stride", "pad",
+        "activation", "batch_normalize", "from_", "n_inputs", "classes", "n", "total_anchors",
+        "groups")] + [("scale", C.c_float), ("reserved", C.c_float), ("weights_count", C.c_int64)]
+
+
+# TB_LAYER_* / TB_PARAM_* (include/tensorium_b200.h)
+LAYER_TYPES = {1: "conv", 2: "shortcut", 3: "route", 4: "upsample", 5: "yolo", 6: "maxpool",
+               7: "connected", 8: "softmax", 9: "avgpool"}
+PARAM = {"weights": 0, "biases": 1, "scales": 2, "mean": 3, "var": 4, "route_inputs": 5,
+         "yolo_mask": 6, "yolo_anchors": 7}
+
 P = C.c_void_p
 I64 = C.c_int64
 F32 = C.c_float
@@ -131,6 +144,11 @@ SIGNATURES = {
     "tb_net_launch_count": [P, PI64],
     "tb_net_flops": [P, C.POINTER(C.c_double)],
     "tb_net_profile": [P, P, C.POINTER(C.c_double)],
+    "tb_net_input_shape": [P, PI64, PI64, PI64, PI64],
+    "tb_net_layer_info": [P, I64, C.POINTER(LayerInfo)],
+    "tb_net_layer_param": [P, I64, I64, P, I64, PI64],
+    "tb_darknet_load": [P, C.c_char_p, C.c_char_p, I64, I64, C.POINTER(P)],
+    "tb_darknet_save_weights": [P, C.c_char_p, I64],
     "tb_diag_fp32_fma_tflops": [P, C.POINTER(C.c_double)],
     "tb_diag_popc_tbitmac": [P, C.POINTER(C.c_double)],
     "tb_diag_tc_mma_rate": [P, I64, C.POINTER(C.c_double), C.POINTER(C.c_double)],

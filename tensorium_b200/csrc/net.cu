@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <memory>
 #include <vector>
 
@@ -316,19 +317,21 @@ void free_graph(tb_net* net) {
 extern "C" {
 
 int tb_net_create(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t height, int64_t width, tb_net** out) {
-    TB_ENTER(ctx);
+    // ctx may be NULL: a host-only net that can be built, inspected and saved, not finalized
+    if (ctx) TB_ENTER(ctx);
     if (!out || batch <= 0 || channels <= 0 || height <= 0 || width <= 0)
         return fail(TB_ERR_INVALID, "tb_net_create: bad arguments");
     tb_net* n = new tb_net();
     n->ctx = ctx;
     n->batch = batch; n->c = channels; n->h = height; n->w = width;
-    n->math_mode = ctx->math_mode;
+    n->math_mode = ctx ? ctx->math_mode : TB_MATH_FP32;
     *out = n;
     return TB_OK;
 }
 
 int tb_net_destroy(tb_net* net) {
     if (!net) return TB_OK;
+    if (!net->ctx) { delete net; return TB_OK; }
     enter(net->ctx);
     cudaStreamSynchronize(net->ctx->stream);
     free_graph(net);
@@ -490,6 +493,7 @@ int tb_net_fuse_batchnorm(tb_net* net) {
 
 int tb_net_finalize(tb_net* net, int64_t math_mode) {
     if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (!net->ctx) return fail(TB_ERR_STATE, "net was created without a context (host-only)");
     TB_ENTER(net->ctx);
     if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
     if (net->layers.empty()) return fail(TB_ERR_INVALID, "empty net");
@@ -685,6 +689,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
 
 int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
     if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (!net->ctx) return fail(TB_ERR_STATE, "net was created without a context (host-only)");
     TB_ENTER(net->ctx);
     if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
     if (!x) return fail(TB_ERR_INVALID, "null input");
@@ -722,6 +727,7 @@ int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
 
 int tb_net_profile(tb_net* net, const float* x, double* ms_out) {
     if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (!net->ctx) return fail(TB_ERR_STATE, "net was created without a context (host-only)");
     TB_ENTER(net->ctx);
     if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
     if (!x || !ms_out) return fail(TB_ERR_INVALID, "null argument");
@@ -778,6 +784,65 @@ int tb_net_flops(tb_net* net, double* flops) {
     if (!net || !flops) return fail(TB_ERR_INVALID, "null argument");
     if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
     *flops = net->flops;
+    return TB_OK;
+}
+
+int tb_net_input_shape(tb_net* net, int64_t* batch, int64_t* channels, int64_t* height, int64_t* width) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (batch) *batch = net->batch;
+    if (channels) *channels = net->c;
+    if (height) *height = net->h;
+    if (width) *width = net->w;
+    return TB_OK;
+}
+
+int tb_net_layer_info(tb_net* net, int64_t layer, tb_layer_info* out) {
+    if (!net || !out) return fail(TB_ERR_INVALID, "null argument");
+    if (layer < 0 || layer >= (int64_t)net->layers.size()) return fail(TB_ERR_INVALID, "layer out of range");
+    int r = infer_shapes(net);
+    if (r != TB_OK) return r;
+    const Layer& L = *net->layers[layer];
+    tb_layer_info d{};
+    d.type = L.type;
+    d.c = L.c; d.h = L.h; d.w = L.w;
+    d.out_c = L.oc; d.out_h = L.oh; d.out_w = L.ow;
+    d.filters = L.filters; d.ksize = L.ksize; d.stride = L.stride; d.pad = L.pad;
+    d.activation = L.act; d.batch_normalize = L.bn ? 1 : 0;
+    d.from = L.from;
+    d.n_inputs = (int64_t)L.inputs.size();
+    d.classes = L.classes; d.n = L.n; d.total_anchors = (int64_t)L.anchors.size() / 2;
+    d.groups = L.groups;
+    d.scale = L.type == TB_LAYER_UPSAMPLE ? L.up_scale
+            : L.type == TB_LAYER_YOLO     ? L.scale_xy
+            : L.type == TB_LAYER_SOFTMAX  ? L.temperature : 0.0f;
+    d.weights_count = (int64_t)L.weights.size();
+    *out = d;
+    return TB_OK;
+}
+
+int tb_net_layer_param(tb_net* net, int64_t layer, int64_t which, void* dst, int64_t capacity,
+                       int64_t* count) {
+    if (!net) return fail(TB_ERR_INVALID, "null net");
+    if (layer < 0 || layer >= (int64_t)net->layers.size()) return fail(TB_ERR_INVALID, "layer out of range");
+    const Layer& L = *net->layers[layer];
+    const void* src = nullptr;
+    int64_t n = 0, esz = 4;
+    switch (which) {
+    case TB_PARAM_WEIGHTS:       src = L.weights.data(); n = (int64_t)L.weights.size(); break;
+    case TB_PARAM_BIASES:        src = L.biases.data();  n = (int64_t)L.biases.size();  break;
+    case TB_PARAM_SCALES:        src = L.scales.data();  n = L.bn ? (int64_t)L.scales.size() : 0; break;
+    case TB_PARAM_ROLLING_MEAN:  src = L.mean.data();    n = L.bn ? (int64_t)L.mean.size() : 0;   break;
+    case TB_PARAM_ROLLING_VAR:   src = L.var.data();     n = L.bn ? (int64_t)L.var.size() : 0;    break;
+    case TB_PARAM_ROUTE_INPUTS:  src = L.inputs.data();  n = (int64_t)L.inputs.size(); esz = 8; break;
+    case TB_PARAM_YOLO_MASK:     src = L.mask.data();    n = (int64_t)L.mask.size();   esz = 8; break;
+    case TB_PARAM_YOLO_ANCHORS:  src = L.anchors.data(); n = (int64_t)L.anchors.size(); break;
+    default: return fail(TB_ERR_INVALID, "unknown parameter %lld", (long long)which);
+    }
+    if (count) *count = n;
+    if (!dst) return TB_OK;
+    if (capacity < n) return fail(TB_ERR_INVALID, "parameter holds %lld elements, capacity %lld",
+                                  (long long)n, (long long)capacity);
+    if (n) std::memcpy(dst, src, (size_t)(n * esz));
     return TB_OK;
 }
 

@@ -11,7 +11,7 @@ import ctypes as C
 import numpy as np
 import torch
 
-from ._lib import MATH_FP32, check, lib
+from ._lib import LAYER_TYPES, MATH_FP32, PARAM, LayerInfo, check, lib
 from .context import Context, ptr
 from .layers import TYoloLayer, get_detections
 from .synth import layer_shapes
@@ -76,6 +76,87 @@ class TNNet:
             check(lib.tb_net_add_avgpool(h))
         else:
             raise ValueError(f"layer {i}: unknown type {t}")
+
+    # -- darknet model files ---------------------------------------------------------------
+    @classmethod
+    def from_darknet(cls, ctx, cfg_path, weights_path=None, batch: int = 0, cutoff: int = 0,
+                     fuse_batchnorm: bool = True, fusion: bool = True, math_mode: int = MATH_FP32):
+        """TDarknetParser.Create(cfg, batch) + loadWeights(weights, cutoff)
+        (source/nparser.pas:782-940, 1275-1340), parsed and read by the library
+        (tb_darknet_load).  ctx = None gives a host-only net (inspect, save; no forward)."""
+        self = cls.__new__(cls)
+        self.ctx = ctx
+        self.handle = C.c_void_p()
+        check(lib.tb_darknet_load(ctx.handle if ctx is not None else None, str(cfg_path).encode(),
+                                  None if weights_path is None else str(weights_path).encode(),
+                                  int(batch), int(cutoff), C.byref(self.handle)))
+        b, c, h, w = (C.c_int64() for _ in range(4))
+        check(lib.tb_net_input_shape(self.handle, C.byref(b), C.byref(c), C.byref(h), C.byref(w)))
+        self.batch, self.input_shape = b.value, (c.value, h.value, w.value)
+        self.specs = self.layer_specs(params=False)
+        self.shapes = [s.pop("_out") for s in self.specs]
+        self.yolo_layers = [i for i, s in enumerate(self.specs) if s["type"] == "yolo"]
+        if ctx is None:
+            return self
+        ctx.adopt(self)
+        check(lib.tb_net_set_fusion(self.handle, 1 if fusion else 0))
+        if fuse_batchnorm:
+            check(lib.tb_net_fuse_batchnorm(self.handle))
+        check(lib.tb_net_finalize(self.handle, math_mode))
+        return self
+
+    def layer_specs(self, params: bool = True):
+        """The net's layers as layer specifications (the dicts tensorium_b200.synth builds), read
+        back from the library; params=True copies the host-side weight arrays too.  Each spec
+        also carries "_out", the layer's output shape (c, h, w)."""
+        n = C.c_int64()
+        check(lib.tb_net_layer_count(self.handle, C.byref(n)))
+        return [self._spec_of(i, params) for i in range(n.value)]
+
+    def _param(self, i, name, dtype=np.float32):
+        cnt = C.c_int64()
+        check(lib.tb_net_layer_param(self.handle, i, PARAM[name], None, 0, C.byref(cnt)))
+        a = np.empty(cnt.value, dtype)
+        check(lib.tb_net_layer_param(self.handle, i, PARAM[name], a.ctypes.data_as(C.c_void_p), cnt.value, None))
+        return a
+
+    def _spec_of(self, i, params):
+        d = LayerInfo()
+        check(lib.tb_net_layer_info(self.handle, i, C.byref(d)))
+        t = LAYER_TYPES[d.type]
+        s = {"type": t, "_out": (d.out_c, d.out_h, d.out_w)}
+        if t == "conv":
+            s.update(filters=d.filters, size=d.ksize, stride=d.stride, pad=d.pad, activation=d.activation,
+                     batch_normalize=bool(d.batch_normalize))
+            if params:
+                s["weights"] = self._param(i, "weights").reshape(d.filters, -1)
+                s["biases"] = self._param(i, "biases")
+                if d.batch_normalize:
+                    s["scales"], s["mean"], s["var"] = (self._param(i, k) for k in ("scales", "mean", "var"))
+        elif t == "connected":
+            s.update(outputs=d.filters, activation=d.activation)
+            if params:
+                s["weights"] = self._param(i, "weights").reshape(d.filters, -1)
+                s["biases"] = self._param(i, "biases")
+        elif t == "shortcut":
+            s.update({"from": d.from_, "activation": d.activation})
+        elif t == "route":
+            s["layers"] = [int(v) for v in self._param(i, "route_inputs", np.int64)]
+        elif t == "upsample":
+            s.update(stride=d.stride, scale=d.scale)
+        elif t == "yolo":
+            s.update(classes=d.classes, mask=[int(v) for v in self._param(i, "yolo_mask", np.int64)],
+                     anchors=self._param(i, "yolo_anchors"), scale_xy=d.scale)
+        elif t == "maxpool":
+            s.update(size=d.ksize, stride=d.stride, padding=d.pad)
+        elif t == "softmax":
+            s.update(groups=d.groups, temperature=d.scale)
+        return s
+
+    def save_weights(self, path, seen: int = 0) -> None:
+        """TDarknetParser.saveWeights (source/nparser.pas:1394-1440) of the host-side arrays
+        (batchnorm arrays only for conv layers whose batchnorm is not folded)."""
+        check(lib.tb_darknet_save_weights(self.handle, str(path).encode(), int(seen)))
 
     # -- execution ----------------------------------------------------------------------
     def forward(self, x: torch.Tensor, use_graph: bool = True) -> None:
@@ -145,7 +226,7 @@ class TNNet:
         return n.value
 
     def close(self):
-        if self.handle and self.ctx.handle:
+        if self.handle and (self.ctx is None or self.ctx.handle):
             lib.tb_net_destroy(self.handle)
             self.handle = C.c_void_p()
 
