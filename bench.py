@@ -443,6 +443,23 @@ def kernel_suite(ctx, hbm_gbs):
         lambda: check(lib.tb_yolo_fwd(ctx.handle, 64, 3, 80, 52, 52, ptr(x), ptr(y), 1.0)),
         "TYoloLayer.forward (source/nyololayer.pas:786-825)")
     del x, y
+    # input pipeline: 64 decoded full-HD RGB frames letterboxed into a 416x416 batch
+    from tensorium_b200._lib import PIXEL_FPC, Image
+    n_img, ih, iw = 64, 1080, 1920
+    frames = torch.randint(0, 256, (n_img, ih, iw, 3), dtype=torch.uint8, device=dev, generator=g)
+    xin = torch.empty((n_img, 3, 416, 416), device=dev)
+    descs = (Image * n_img)(*[Image(frames[i].data_ptr(), iw, ih, iw * 3, 3, 0) for i in range(n_img)])
+    nh = ih * 416 // iw
+    hs = np.float32((ih - 1) / (nh - 1))
+    iy = (np.arange(nh, dtype=np.float32) * hs).astype(np.int64)
+    rows = set(iy.tolist()) | set((iy[:-1] + 1).tolist())  # the last row reads one source row
+    add("k_images_to_tensor", f"{n_img}x{ih}x{iw}x3 u8 -> letterbox {n_img}x3x416x416",
+        n_img * len(rows) * iw * 3 + xin.numel() * 4,
+        lambda: check(lib.tb_images_to_tensor(ctx.handle, n_img, descs, 416, 416, 1, PIXEL_FPC, ptr(xin),
+                                              0, None, None)),
+        "TImageData.loadFromFile + letterBoxEx + toTensor (source/ntypes.pas:651-694,837-943), "
+        "CPU-only in the reference; bytes = source rows the row pass reads + fp32 output")
+    del frames, xin
     torch.cuda.empty_cache()
 
     # XNOR conv: C_in = C_out in {128..1024}, 3x3 s1 p1, batch 64; its

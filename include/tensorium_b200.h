@@ -382,6 +382,31 @@ int tb_net_layer_info(tb_net* net, int64_t layer, tb_layer_info* out);
 int tb_net_layer_param(tb_net* net, int64_t layer, int64_t which, void* dst, int64_t capacity,
                        int64_t* count);
 
+/* ---- input pipeline (TImageData, source/ntypes.pas) ---------------------------------------- */
+/* A decoded 8-bit image in device memory: rows of width pixels, row_stride bytes apart, each
+ * pixel bytes_per_pixel bytes (1: gray, 3: RGB / BGR, 4: RGBA / BGRA; alpha is ignored). */
+typedef struct tb_image {
+    const uint8_t* pixels;
+    int64_t width, height, row_stride, bytes_per_pixel;
+    int64_t bgr;                /* 1: bytes in B, G, R order */
+} tb_image;
+/* Byte-to-float scale of the pixel values. TB_PIXEL_FPC: v * 257 / 65280, what the FPC build's
+ * TImageData.loadFromFile gives (FPImage widens a byte to 16 bits as v * 257, the reference
+ * divides by $ff00; source/ntypes.pas:684-690). TB_PIXEL_255: v / 255 (the Delphi build, :713-719). */
+#define TB_PIXEL_FPC 0
+#define TB_PIXEL_255 1
+/* TImageData.loadFromFile + resize or letterBoxEx + toTensor for a batch of images
+ * (source/ntypes.pas:651-657, 669-694, 837-897, 922-943), on the device, bit-exact with the
+ * reference's single-precision arithmetic: image i becomes planes [3][out_h][out_w] at
+ * out + i * out_batch_stride (0 = 3 * out_h * out_w), ready to be the network's input.
+ * keep_aspect = 0: resize to out_w x out_h (the YOLO sample's img.resize); 1: letterBoxEx
+ * (aspect kept, centred, border 0.5). ratio_out (n floats) and placement_out (n x 4 int64: resized
+ * width, height, x offset, y offset) are host arrays, may be NULL. Resized sides must be >= 2.
+ * Asynchronous on the context stream. */
+int tb_images_to_tensor(tb_ctx* ctx, int64_t n, const tb_image* images_host, int64_t out_w,
+                        int64_t out_h, int64_t keep_aspect, int64_t pixel_scale, float* out,
+                        int64_t out_batch_stride, float* ratio_out, int64_t* placement_out);
+
 /* ---- darknet model files (TDarknetParser, source/nparser.pas) ------------------------------ */
 /* TDarknetParser.Create + loadWeights (source/nparser.pas:782-940, 1275-1340): parse a darknet
  * .cfg file into a new, unfinalized tb_net and, when weights_path is not NULL, read a darknet

@@ -610,6 +610,95 @@ void or_nms_sort(int64_t n, int64_t classes, const float* boxes, const float* ob
         for (int64_t j = 0; j < n; ++j) order[j] = arr[j];
 }
 
+// ---------------------------------------------------------------------------------------
+// input images (source/ntypes.pas TImageData)
+// ---------------------------------------------------------------------------------------
+// TImageData.loadFromFile (:669-694, FPC build): planar RGB floats from the decoder's colours.
+// FPImage (FreePascal's fcl-image, not part of the reference) holds 16-bit channels and widens
+// an 8-bit value v to v * 257; the reference divides by $ff00, so a pixel byte becomes
+// v * 257 / 65280 (double division, rounded to single on the store). The Delphi build
+// (:696-724) divides the 8-bit value by $ff: pixel_scale 1.
+// src: interleaved rows (row_stride bytes apart), bpp bytes per pixel (1 gray, 3, 4), bgr:
+// byte order B, G, R. out: [3][h][w].
+void or_image_from_bytes(int64_t w, int64_t h, const uint8_t* src, int64_t row_stride, int64_t bpp,
+                         int64_t bgr, int64_t pixel_scale, float* out) {
+    const int64_t plane = w * h;
+    for (int64_t y = 0; y < h; ++y)
+        for (int64_t x = 0; x < w; ++x) {
+            const uint8_t* p = src + y * row_stride + x * bpp;
+            int v[3];
+            if (bpp == 1) v[0] = v[1] = v[2] = p[0];
+            else if (bgr) { v[0] = p[2]; v[1] = p[1]; v[2] = p[0]; }
+            else { v[0] = p[0]; v[1] = p[1]; v[2] = p[2]; }
+            for (int k = 0; k < 3; ++k)
+                out[k * plane + y * w + x] = pixel_scale == 0 ? (float)((double)(v[k] * 257) / 65280.0)
+                                                              : (float)((double)v[k] / 255.0);
+        }
+}
+
+// TImageData.resize (:837-897): separable bilinear, columns first into `part` [c][h][aw], then
+// rows. Single-precision arithmetic; w_scale / h_scale are integer quotients stored to single.
+void or_resize(int64_t c, int64_t h, int64_t w, const float* src, int64_t aw, int64_t ah, float* out) {
+    std::vector<float> part((size_t)(c * h * aw));
+    const float w_scale = (float)((double)(w - 1) / (double)(aw - 1));
+    const float h_scale = (float)((double)(h - 1) / (double)(ah - 1));
+    for (int64_t k = 0; k < c; ++k)
+        for (int64_t r = 0; r < h; ++r)
+            for (int64_t cc = 0; cc < aw; ++cc) {
+                float val;
+                if (cc == aw - 1 || w == 1) {
+                    val = src[(k * h + r) * w + (w - 1)];
+                } else {
+                    const float sx = (float)cc * w_scale;
+                    const int64_t ix = (int64_t)sx;  // trunc
+                    const float dx = sx - (float)ix;
+                    val = (1.0f - dx) * src[(k * h + r) * w + ix] + dx * src[(k * h + r) * w + ix + 1];
+                }
+                part[(size_t)((k * h + r) * aw + cc)] = val;
+            }
+    for (int64_t k = 0; k < c; ++k)
+        for (int64_t r = 0; r < ah; ++r) {
+            const float sy = (float)r * h_scale;
+            const int64_t iy = (int64_t)sy;
+            const float dy = sy - (float)iy;
+            for (int64_t cc = 0; cc < aw; ++cc)
+                out[(k * ah + r) * aw + cc] = (1.0f - dy) * part[(size_t)((k * h + iy) * aw + cc)];
+            if (r == ah - 1 || h == 1) continue;
+            for (int64_t cc = 0; cc < aw; ++cc)
+                out[(k * ah + r) * aw + cc] = out[(k * ah + r) * aw + cc] + dy * part[(size_t)((k * h + iy + 1) * aw + cc)];
+        }
+}
+
+// TImageData.letterBoxEx (:922-943): keep the aspect ratio, resize, embed centred into an
+// image filled with 0.5. meta_out: new_w, new_h, dx, dy; ratio_out: the scale (single).
+void or_letterbox(int64_t c, int64_t h, int64_t w, const float* src, int64_t aw, int64_t ah, float* out,
+                  int64_t* meta_out, float* ratio_out) {
+    int64_t new_w = w, new_h = h;
+    float ratio;
+    if ((double)aw / (double)w < (double)ah / (double)h) {
+        new_w = aw;
+        new_h = (h * aw) / w;
+        ratio = (float)((double)aw / (double)w);
+    } else {
+        new_h = ah;
+        new_w = (w * ah) / h;
+        ratio = (float)((double)ah / (double)h);
+    }
+    std::vector<float> resized((size_t)(c * new_h * new_w));
+    or_resize(c, h, w, src, new_w, new_h, resized.data());
+    for (int64_t i = 0; i < c * ah * aw; ++i) out[i] = 0.5f;
+    const int64_t dx = (aw - new_w) / 2, dy = (ah - new_h) / 2;
+    for (int64_t k = 0; k < c; ++k)
+        for (int64_t y = 0; y < new_h; ++y)
+            for (int64_t x = 0; x < new_w; ++x) {
+                const int64_t ox = dx + x, oy = dy + y;  // Setpixels drops out-of-range writes
+                if (ox < 0 || oy < 0 || ox >= aw || oy >= ah) continue;
+                out[(k * ah + oy) * aw + ox] = resized[(size_t)((k * new_h + y) * new_w + x)];
+            }
+    if (meta_out) { meta_out[0] = new_w; meta_out[1] = new_h; meta_out[2] = dx; meta_out[3] = dy; }
+    if (ratio_out) *ratio_out = ratio;
+}
+
 int64_t or_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -53,6 +53,9 @@ def _load():
         "or_xnor_mean": [I, I, P, P],
         "or_xnor_conv": [I] * 9 + [P, P, P, P, P],
         "or_nms_sort": [I, I, P, P, P, F, P],
+        "or_image_from_bytes": [I, I, P, I, I, I, I, P],
+        "or_resize": [I, I, I, P, I, I, P],
+        "or_letterbox": [I, I, I, P, I, I, P, P, P],
         "or_num_threads": [],
         "or_set_threads": [I],
     }
@@ -172,6 +175,37 @@ def nms_sort(boxes, objectness, probs, thresh):
     order = np.zeros(n, np.int64)
     lib.or_nms_sort(n, classes, _p(boxes), _p(obj), _p(probs), thresh, _p(order))
     return probs, order
+
+
+def image_from_bytes(img, bgr=False, pixel_scale=0):
+    """TImageData.loadFromFile's conversion of an 8-bit image [h][w] or [h][w][bpp] to planar
+    floats [3][h][w] (pixel_scale 0: v*257/65280 as the FPC build, 1: v/255 as the Delphi build)."""
+    img = np.ascontiguousarray(img, np.uint8)
+    h, w = img.shape[:2]
+    bpp = 1 if img.ndim == 2 else img.shape[2]
+    out = np.empty((3, h, w), np.float32)
+    lib.or_image_from_bytes(w, h, _p(img), w * bpp, bpp, 1 if bgr else 0, pixel_scale, _p(out))
+    return out
+
+
+def resize(x, aw, ah):
+    """TImageData.resize of a planar image [c][h][w] to [c][ah][aw]."""
+    x = f32(x)
+    c, h, w = x.shape
+    out = np.empty((c, ah, aw), np.float32)
+    lib.or_resize(c, h, w, _p(x), aw, ah, _p(out))
+    return out
+
+
+def letterbox(x, aw, ah):
+    """TImageData.letterBoxEx: (image [c][ah][aw], ratio, (new_w, new_h, dx, dy))."""
+    x = f32(x)
+    c, h, w = x.shape
+    out = np.empty((c, ah, aw), np.float32)
+    meta = np.zeros(4, np.int64)
+    ratio = np.zeros(1, np.float32)
+    lib.or_letterbox(c, h, w, _p(x), aw, ah, _p(out), _p(meta), _p(ratio))
+    return out, float(ratio[0]), tuple(int(v) for v in meta)
 
 
 def connected(x, w, b, act):

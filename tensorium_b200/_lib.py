@@ -63,6 +63,15 @@ class YoloHead(C.Structure):
                 ("anchors_host", C.c_void_p), ("new_coords", C.c_int64)]
 
 
+class Image(C.Structure):
+    _fields_ = [("pixels", C.c_void_p), ("width", C.c_int64), ("height", C.c_int64),
+                ("row_stride", C.c_int64), ("bytes_per_pixel", C.c_int64), ("bgr", C.c_int64)]
+
+
+PIXEL_FPC = 0
+PIXEL_255 = 1
+
+
 class LayerInfo(C.Structure):
     _fields_ = [(n, C.c_int64) for n in (
         "type", "c", "h", "w", "out_c", "out_h", "out_w", "filters", "ksize", "stride", "pad",
@@ -147,6 +156,8 @@ SIGNATURES = {
     "tb_net_input_shape": [P, PI64, PI64, PI64, PI64],
     "tb_net_layer_info": [P, I64, C.POINTER(LayerInfo)],
     "tb_net_layer_param": [P, I64, I64, P, I64, PI64],
+    "tb_images_to_tensor": [P, I64, C.POINTER(Image), I64, I64, I64, I64, P, I64,
+                            C.POINTER(C.c_float), PI64],
     "tb_darknet_load": [P, C.c_char_p, C.c_char_p, I64, I64, C.POINTER(P)],
     "tb_darknet_save_weights": [P, C.c_char_p, I64],
     "tb_diag_fp32_fma_tflops": [P, C.POINTER(C.c_double)],

@@ -183,6 +183,25 @@ class TNNet:
         layers = layers if layers is not None else [len(self.specs) - 1]
         return [self.output(l).cpu().numpy() for l in layers]
 
+    def predict_images(self, images, letterbox: bool = False, layers=None, pipeline=None):
+        """The YOLO sample's per-image loop (img.resize or letterBoxEx, then predict;
+        Samples/FPC/MSCOCO_Yolo/MSCOCOYolo.pas:348-350,454) for a whole batch of decoded 8-bit
+        images: bytes to the GPU, resized / letterboxed into the input on the GPU, forward.
+        Returns the outputs like predict, and the ratios and placements of the images."""
+        from .image import ImagePipeline
+        if pipeline is None:
+            pipeline = getattr(self, "_pipeline", None) or ImagePipeline(self.ctx)
+            self._pipeline = pipeline
+        c, h, w = self.input_shape
+        assert c == 3 and len(images) == self.batch, (c, len(images))
+        if getattr(self, "_x", None) is None or tuple(self._x.shape) != (self.batch,) + self.input_shape:
+            self._x = torch.empty((self.batch,) + self.input_shape, dtype=torch.float32,
+                                  device=self.ctx.torch_device)
+        _, ratios, place = pipeline.to_tensor(images, w, h, letterbox, out=self._x)
+        self.forward(self._x)
+        layers = layers if layers is not None else [len(self.specs) - 1]
+        return [self.output(l).cpu().numpy() for l in layers], ratios, place
+
     def staging(self, x_host):
         if getattr(self, "_x", None) is None or tuple(self._x.shape) != tuple(x_host.shape):
             self._x = torch.empty(x_host.shape, dtype=torch.float32, device=self.ctx.torch_device)
