@@ -80,6 +80,12 @@ int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
 int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
+// Direct convolution for short reductions (C*KH*KW <= 32, CRS-packed weights, no residual, no
+// fused yolo): the first layer of an image network (conv_direct.cu).
+bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes);
+int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
+                       const float* bn_scale, const float* bn_mean, const float* bn_var, float* y, int act,
+                       int64_t* launches);
 // Split-K partial floats this call would need (0 when it does not split), for a given x.
 // allow_tma = false: only the gather kernels (callers whose scratch cannot hold a replica)
 int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x, bool allow_tma = true);

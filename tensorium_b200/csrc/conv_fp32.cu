@@ -256,6 +256,8 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt,
                      int64_t tile_cnt_len, bool allow_tma) {
     if (g.B == 0) return TB_OK;
+    if (conv_direct_supported(g, res, yolo_classes) && !getenv("TB_CONV_FORCE"))
+        return conv_direct_launch(ctx, g, x, wp, bias, bn_scale, bn_mean, bn_var, y, act, launches);
     TileCfg t = choose_tiles(ctx, g, aligned16(x), allow_tma);
     return launch_with(ctx, g, t, x, wp, bias, bn_scale, bn_mean, bn_var, res, y, act, yolo_classes,
                        ws, ws_floats, launches, tile_cnt, tile_cnt_len);
@@ -265,7 +267,7 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
 // fastest; later launches of the same geometry use it.  Blocks; allocates the workspace the
 // candidates need (not during stream capture).
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y) {
-    if (g.B == 0) return TB_OK;
+    if (g.B == 0 || conv_direct_supported(g, nullptr, 0)) return TB_OK;
     const int mode = conv_mode_of(g, aligned16(x));
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int cfgs[4][2] = {{128, 128}, {64, 128}, {64, 64}, {32, 256}};

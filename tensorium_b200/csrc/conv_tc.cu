@@ -229,6 +229,23 @@ __global__ void k_round_tf32(float* __restrict__ p, long long n) {
 // The epilogue of one pixel for 4 consecutive filters, for the less common cases (unfused batchnorm,
 // yolo logistic, activations other than leaky / linear); out of line to keep the kernel small.
 static __device__ __noinline__ float4 tc_epilogue4_f(float4 o, int f0, int F, const ConvParams ep) {
+    if (ep.yolo_classes > 0 && !ep.bn_mean) {
+        // fused yolo activation (TYoloLayer.forward: logistic on entries 0, 1, 4..): the result
+        // is rounded to TF32, so the logistic runs in single precision here (the FP32 path keeps
+        // the reference's double-precision exp)
+        const int period = ep.yolo_classes + 5;
+        int e = f0 % period;
+        float v[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int f = min(f0 + i, F - 1);
+            float t = ep.bias ? __fadd_rn(v[i], ep.bias[f]) : v[i];
+            if (e != 2 && e != 3) t = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-t)));
+            v[i] = t;
+            e = e + 1 == period ? 0 : e + 1;
+        }
+        return make_float4(v[0], v[1], v[2], v[3]);
+    }
     // filters f0 .. f0+3, clamped to F-1 (values past the last filter are never stored)
     o.x = conv_epilogue(o.x, min(f0, F - 1), ep);
     o.y = conv_epilogue(o.y, min(f0 + 1, F - 1), ep);

@@ -103,3 +103,41 @@ def test_every_tile_and_split_configuration(ctx, cfg, monkeypatch):
         y2 = run_layer(ctx, x, w, b, F, k, s, p, 9)
         assert np.array_equal(y1, y2)
         assert worst_map_err(y1, ref, B * F) <= FP32_TOL, (cfg, C)
+
+
+DIRECT_CASES = [  # (B, C, H, F, k, s, p, dil): reductions of <= 32 on the direct kernel
+    (2, 3, 416, 32, 3, 1, 1, 1),     # YOLOv3 layer 0 / config 0
+    (2, 3, 33, 16, 3, 2, 1, 1),      # stride 2, odd size
+    (8, 1, 28, 32, 5, 1, 2, 1),      # MNIST conv1
+    (1, 2, 20, 100, 3, 1, 2, 2),     # dilation 2, F not a multiple of 8
+    (3, 4, 9, 128, 2, 1, 0, 1),      # even kernel, no padding, F = 128
+]
+
+
+@pytest.mark.parametrize("B,C,H,F,k,s,p,dil", DIRECT_CASES)
+def test_direct_kernel_is_bit_exact(ctx, B, C, H, F, k, s, p, dil):
+    """The direct kernel runs the reference's dot product (one FMA per k, ascending, from 0) and
+    epilogue in the same order, so it equals the oracle bit for bit; the GEMM kernel on the same
+    layer (pinned with TB_CONV_FORCE) agrees within the FP32 tolerance."""
+    rng = np.random.default_rng(B * 100 + C * 10 + F)
+    x = rng.uniform(0, 1, (B, C, H, H)).astype(np.float32)
+    w = (rng.standard_normal((F, C * k * k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    b = rng.standard_normal(F).astype(np.float32) * 0.1
+    for act in (9, 4, 0):
+        y = run_layer(ctx, x, w, b, F, k, s, p, act, dil=dil)
+        ref = O.conv2d(x, w, b, F, k, s, p, act, dilation=dil)
+        assert np.array_equal(y, ref), (act, np.abs(y - ref).max())
+
+
+def test_direct_kernel_against_gemm_kernel(ctx, monkeypatch):
+    rng = np.random.default_rng(3)
+    x = rng.uniform(0, 1, (2, 3, 64, 64)).astype(np.float32)
+    w = (rng.standard_normal((32, 27)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(32).astype(np.float32) * 0.1
+    bn = (np.ones(32, np.float32), (rng.standard_normal(32) * 0.1).astype(np.float32),
+          rng.uniform(0.5, 1.5, 32).astype(np.float32))
+    y = run_layer(ctx, x, w, b, 32, 3, 1, 1, 9, bn=bn)
+    monkeypatch.setenv("TB_CONV_FORCE", "32,256,1")
+    g = run_layer(ctx, x, w, b, 32, 3, 1, 1, 9, bn=bn)
+    ref = O.conv2d(x, w, b, 32, 3, 1, 1, 9, bn=bn)
+    assert worst_map_err(y, ref, 64) <= FP32_TOL and worst_map_err(g, ref, 64) <= FP32_TOL
