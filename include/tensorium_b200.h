@@ -151,6 +151,22 @@ int tb_conv_pack_weights_tf32(tb_ctx* ctx, const tb_conv_desc* d, const float* w
  * (TB_MATH_TF32 and channels % 32 == 0), 0 when it runs the FP32 kernel: which packing the
  * caller should hand it (no reference counterpart). */
 int tb_conv_uses_tensor_cores(const tb_conv_desc* d, int64_t math_mode, int64_t* yes);
+/* ---- TF32 tensor-core conv on NHWC activations (no reference counterpart: the layout the
+ * B200 tensor-core path uses inside a network) ----
+ * x is [batch][h][w][...] with x_pixel_stride floats per pixel (x points at the conv's first
+ * input channel; a multiple of 4); y is NHWC with y_pixel_stride floats per pixel (y at the
+ * output's first channel) or, with y_pixel_stride == 0, NCHW with the descriptor's
+ * out_batch_stride. The residual (NHWC, res_pixel_stride) is added after the activation, the
+ * shortcut order. Weights are packed by tb_conv_pack_weights_nhwc ([F][KH][KW][C rounded up to
+ * 32], rounded to TF32). Operands are read as TF32; outputs are rounded to TF32. Geometries the
+ * kernel cannot take (corner or tap offsets outside the im2col map's range, inputs under 128 KB)
+ * return TB_ERR_UNSUPPORTED. The descriptor's in/res batch strides are ignored. */
+int tb_conv_nhwc_packed_count(const tb_conv_desc* d, int64_t* count);
+int tb_conv_pack_weights_nhwc(tb_ctx* ctx, const tb_conv_desc* d, const float* weights_host_or_dev,
+                              float* packed);
+int tb_conv2d_fwd_nhwc(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
+                       const float* packed_w, const float* bias, const float* residual,
+                       int64_t res_pixel_stride, float* y, int64_t y_pixel_stride);
 /* Host helper: fold batchnorm into weights and biases in place, the arithmetic of
  * TBaseConvolutionalLayer.fuseBatchNorm (source/nConvolutionLayer.pas:102-126). */
 int tb_conv_fold_bn(int64_t filters, int64_t filter_size, float* weights_host, float* biases_host,

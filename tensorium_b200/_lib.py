@@ -116,6 +116,9 @@ SIGNATURES = {
     "tb_conv_uses_tensor_cores": [C.POINTER(ConvDesc), I64, PI64],
     "tb_conv_pack_weights_tf32": [P, C.POINTER(ConvDesc), P, P],
     "tb_conv_fold_bn": [I64, I64, P, P, P, P, P],
+    "tb_conv_nhwc_packed_count": [C.POINTER(ConvDesc), PI64],
+    "tb_conv_pack_weights_nhwc": [P, C.POINTER(ConvDesc), P, P],
+    "tb_conv2d_fwd_nhwc": [P, C.POINTER(ConvDesc), P, I64, P, P, P, I64, P, I64],
     "tb_conv_autotune": [P, C.POINTER(ConvDesc), P, P, P],
     "tb_conv2d_fwd": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P, I64],
     "tb_conv2d_fwd_noalloc": [P, C.POINTER(ConvDesc), P, P, P, P, P, P, P, P],

@@ -80,6 +80,13 @@ int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
 int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
+// TF32 tensor-core conv on NHWC activations with the A operand fetched by TMA im2col (conv_nhwc.cu).
+int64_t conv_nhwc_packed_count(const ConvGeom& g);
+bool conv_nhwc_supported(const ConvGeom& g, int64_t x_ps);
+int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp);
+int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
+                     const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
+                     int yolo_classes, unsigned long long* phases);
 // Direct convolution for short reductions (C*KH*KW <= 32, CRS-packed weights, no residual, no
 // fused yolo): the first layer of an image network (conv_direct.cu).
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes);

@@ -1,0 +1,471 @@
+// conv_nhwc.cu -- TF32 tensor-core convolution on NHWC activations, A operand fetched by TMA in
+// im2col mode.
+//
+// The NCHW tensor-core kernel (conv_tc.cu) first copies its input into tap replicas, because a
+// tap shift along W moves an NCHW pixel row by one float, which no TMA box can start at. With the
+// channels innermost (NHWC) the pixel is an outer dimension: TMA's im2col mode walks 128
+// consecutive output pixels (across row and image ends) and loads, for one kernel tap and 32
+// channels, each pixel's input window start shifted by the tap offset, zero-filling whatever falls
+// in the padding. So the operand tile arrives K-major (32 channels = one 128-byte swizzled row per
+// pixel) straight from the activations: no replica pass, no padded pixel grid.
+//
+// Roles as in the NCHW kernel: warp 0 one thread issues the TMA ring (A by im2col, B = packed
+// weights [F][KH][KW][Cp] K-major by a tiled 2-D map); warp 1 owns TMEM and one thread issues
+// tcgen05.mma kind::tf32 (M = 128 pixels, N = BN filters, K = 8) into one of two accumulators;
+// warps 2-9 run the epilogue of the previous tile while the next one accumulates. TMEM lane =
+// pixel, so a thread holds 16 consecutive filters of one pixel after a 16-column load: NHWC
+// stores are four 16-byte vectors per thread, NCHW stores (the yolo head convs) one float per
+// filter with the warp's 32 lanes writing 32 consecutive pixels. No shared-memory transpose.
+// Outputs are rounded to TF32 (nearest), so the next layer's operands are exact TF32 values.
+// Every wait is bounded; on timeout the kernel sets the context status word, drains what is in
+// flight, frees TMEM and returns.
+#include "conv_tc.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+namespace tbi {
+
+namespace {
+
+constexpr int NH_BM = 128, NH_BK = 32, NH_THREADS = 320;
+constexpr int NH_A_BYTES = NH_BM * NH_BK * 4;  // 16 KB: 128 pixels x 32 channels
+
+struct NhwcParams {
+    const float* __restrict__ bias;
+    const float* __restrict__ res;  // NHWC, at the residual's channel offset (or null)
+    float* __restrict__ y;          // NHWC: at the output's channel offset; NCHW: image 0, filter 0
+    int* status;
+    unsigned long long* phases;
+    long long npix;                 // B * OH * OW
+    long long y_bs;                 // NCHW output: floats between images
+    int OW, OHW, SX, SY, PX, PY, KW, DX, DY;
+    int F, csteps, ktiles;
+    int tiles_n, tiles_total;
+    int out_nchw;
+    int y_ps, r_ps;                 // NHWC pixel strides (floats) of the output and residual
+    int vec;                        // NHWC: y / res 16-byte aligned and strides % 4 == 0
+    int act, yolo_classes;
+};
+
+struct NhwcMaps {
+    CUtensorMap a;  // im2col view of x: (C, W, H, N), 32 channels x 128 pixels per copy
+    CUtensorMap b;  // packed weights (k, filter), box 32 x BN
+};
+
+// K-major, 128-byte swizzle (layout type 2): rows of 32 fp32 along K, 8-row groups 1024 bytes apart
+__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
+    d |= (uint64_t)1 << 46;            // version (Blackwell)
+    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+    return d;
+}
+
+// instruction descriptor: F32 accumulate, TF32 A and B, both K-major, M x N
+__host__ __device__ constexpr uint32_t idesc_tf32_k(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_im2col_4d(unsigned dst, const void* tmap, uint64_t* bar, int c, int w,
+                                                   int h, int n, uint16_t ow, uint16_t oh) {
+    unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(b), "r"(c), "r"(w), "r"(h), "r"(n), "h"(ow), "h"(oh)
+        : "memory");
+}
+
+__device__ __forceinline__ float nh_act(float o, int f, const NhwcParams& p) {
+    if (p.yolo_classes > 0) {  // fused yolo activation (logistic on entries 0, 1, 4..), single precision
+        const int e = f % (p.yolo_classes + 5);
+        return (e != 2 && e != 3) ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-o))) : o;
+    }
+    if (p.act == TB_ACT_LEAKY) return o < 0.f ? __fmul_rn(o, 0.1f) : o;  // rounded to TF32 after
+    if (p.act == TB_ACT_LINEAR) return o;
+    return tb_activate_dev(o, p.act);
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_constant__ NhwcMaps maps, const NhwcParams p) {
+    constexpr int B_BYTES = BN * NH_BK * 4;
+    constexpr int STAGE_BYTES = NH_A_BYTES + B_BYTES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024 - ((unsigned)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const unsigned sbase = (unsigned)__cvta_generic_to_shared(smem);
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(&full_bar[s], 1);
+            tc::mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&tfull_bar[b], 1);
+            tc::mbar_init(&tempty_bar[b], 8);  // one arrival per epilogue warp
+        }
+        tc::mbar_init(&drain_bar, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
+    }
+    if (warp == 1) tc::tmem_alloc(&tmem_base, 2 * BN);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem0 = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int it = 0;
+            bool ok = true;
+            const long long c_start = clock64();
+            long long c_wait = 0;
+            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+                const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
+                const long long m0 = (long long)mt * NH_BM;
+                const int n0 = (int)(m0 / p.OHW);
+                const int q = (int)(m0 - (long long)n0 * p.OHW);
+                const int oy = q / p.OW, ox = q - oy * p.OW;
+                const int w0 = ox * p.SX - p.PX, h0 = oy * p.SY - p.PY;
+                int r = 0, s = 0, c0 = 0;
+                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                    const int st = it % STAGES, use = it / STAGES;
+                    const long long c0w = clock64();
+                    if (use > 0 && !tc::mbar_wait_bounded(&empty_bar[st], (use - 1) & 1, &abort_flag, p.status, 921)) {
+                        ok = false;
+                        break;
+                    }
+                    c_wait += clock64() - c0w;
+                    tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES);
+                    const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + NH_A_BYTES;
+                    tma_load_im2col_4d(sa, &maps.a, &full_bar[st], c0 * NH_BK, w0, h0, n0, (uint16_t)(s * p.DX),
+                                       (uint16_t)(r * p.DY));
+                    tc::tma_load_2d(sb, &maps.b, &full_bar[st], kt * NH_BK, nt * BN);
+                    if (++c0 == p.csteps) {  // next 32-channel step, then the next tap
+                        c0 = 0;
+                        if (++s == p.KW) s = 0, ++r;
+                    }
+                }
+            }
+            if (p.phases) {
+                p.phases[blockIdx.x * 12 + 0] = clock64() - c_start;
+                p.phases[blockIdx.x * 12 + 1] = c_wait;
+            }
+            if (!ok) {  // let the copies already issued land before the CTA exits
+                for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+                    tc::mbar_wait_limit(&full_bar[j % STAGES], (j / STAGES) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_tf32_k(NH_BM, BN);
+            int it = 0, tl = 0;
+            bool ok = true, issued = false;
+            const long long c_start = clock64();
+            long long c_wf = 0, c_we = 0;
+            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x, ++tl) {
+                const int buf = tl & 1, u = tl >> 1;
+                long long c0w = clock64();
+                if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 922)) break;
+                c_we += clock64() - c0w;
+                tc::tc_fence_after();
+                const uint32_t d = tmem0 + buf * BN;
+                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                    const int st = it % STAGES, use = it / STAGES;
+                    c0w = clock64();
+                    if (!tc::mbar_wait_bounded(&full_bar[st], use & 1, &abort_flag, p.status, 923)) {
+                        ok = false;
+                        break;
+                    }
+                    c_wf += clock64() - c0w;
+                    tc::tc_fence_after();
+                    const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + NH_A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < NH_BK / 8; ++kk)
+                        tc::mma_tf32(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
+                                     (kt || kk) ? 1u : 0u);
+                    issued = true;
+                    tc::mma_commit(&empty_bar[st]);
+                }
+                if (ok) tc::mma_commit(&tfull_bar[buf]);
+            }
+            if (p.phases) {
+                p.phases[blockIdx.x * 12 + 2] = clock64() - c_start;
+                p.phases[blockIdx.x * 12 + 3] = c_wf;
+                p.phases[blockIdx.x * 12 + 4] = c_we;
+            }
+            if (issued) {  // every MMA has finished before TMEM is freed
+                tc::mma_commit(&drain_bar);
+                tc::mbar_wait_limit(&drain_bar, 0);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2-9) ----------------
+        const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 2) >> 2;  // 16-filter slabs half, half + 2, ...
+        int tl = 0;
+        const long long c_start = clock64();
+        long long c_wt = 0, c_st = 0;
+        for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++tl) {
+            const int buf = tl & 1, u = tl >> 1;
+            const long long c0w = clock64();
+            const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 924);
+            c_wt += clock64() - c0w;
+            if (tc::epi_any(!ok)) break;  // tcgen05.ld is warp-collective: all epilogue warps leave together
+            tc::tc_fence_after();
+            const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
+            const long long m = (long long)mt * NH_BM + quarter * 32 + lane;  // this lane's pixel
+            const bool valid = m < p.npix;
+            const long long b = valid ? m / p.OHW : 0;
+            const int q = valid ? (int)(m - b * p.OHW) : 0;
+            float* yp = p.out_nchw ? p.y + b * p.y_bs + q : p.y + (valid ? m : 0) * p.y_ps;
+            const float* rp = p.res ? p.res + (valid ? m : 0) * p.r_ps : nullptr;
+            const uint32_t taddr = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
+            const long long c0l = clock64();
+            uint32_t vr[16];
+            if (half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
+#pragma unroll 1
+            for (int sl = half; sl < BN / 16; sl += 2) {
+                tc::tmem_wait16(vr);
+                float v[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(vr[i]);
+                // the next slab's TMEM load runs while this slab is finished and stored
+                if (sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
+                const int fb = nt * BN + sl * 16;
+                const bool full = fb + 16 <= p.F;
+                float rv[16];
+                if (rp && valid) {
+                    if (p.vec && full) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 r4 = __ldg(reinterpret_cast<const float4*>(rp + fb + i));
+                            rv[i] = r4.x; rv[i + 1] = r4.y; rv[i + 2] = r4.z; rv[i + 3] = r4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) rv[i] = fb + i < p.F ? __ldg(rp + fb + i) : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int f = min(fb + i, p.F - 1);
+                    float o = v[i];
+                    if (p.bias) o = __fadd_rn(o, __ldg(p.bias + f));
+                    o = nh_act(o, f, p);
+                    if (rp) o = __fadd_rn(o, rv[i]);
+                    v[i] = tc::to_tf32_rna(o);
+                }
+                if (valid) {
+                    if (p.out_nchw) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (fb + i < p.F) __stcs(yp + (long long)(fb + i) * p.OHW, v[i]);
+                    } else if (p.vec && full) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            __stcs(reinterpret_cast<float4*>(yp + fb + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (fb + i < p.F) yp[fb + i] = v[i];
+                    }
+                }
+            }
+            c_st += clock64() - c0l;
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);  // this warp's TMEM reads are done
+        }
+        if (p.phases && warp == 2 && lane == 0) {
+            p.phases[blockIdx.x * 12 + 5] = clock64() - c_start;
+            p.phases[blockIdx.x * 12 + 6] = c_wt;
+            p.phases[blockIdx.x * 12 + 7] = tl;
+            p.phases[blockIdx.x * 12 + 9] = c_st;
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem0, 2 * BN);
+    }
+}
+
+// packed weights for the NHWC kernel: wp[f][(r * KW + s) * Cp + c] = tf32(w[f][c][r][s]), zero for c >= C
+__global__ void k_pack_nhwc(const float* __restrict__ w, float* __restrict__ wp, int F, int C, int KH, int KW,
+                            int Cp) {
+    const long long kp = (long long)KH * KW * Cp, total = (long long)F * kp;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int f = (int)(i / kp);
+        const int k = (int)(i - (long long)f * kp);
+        const int rs = k / Cp, c = k - rs * Cp;
+        const int r = rs / KW, s = rs - r * KW;
+        wp[i] = c < C ? tc::to_tf32_rna(w[(((long long)f * C + c) * KH + r) * KW + s]) : 0.0f;
+    }
+}
+
+PFN_cuTensorMapEncodeIm2col_v12000 im2col_encoder() {
+    static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(f);
+    });
+    return fn;
+}
+
+template <int BN, int STAGES>
+constexpr int nh_smem() { return STAGES * (NH_A_BYTES + BN * NH_BK * 4) + 1024; }
+
+template <int BN, int STAGES>
+int nh_launch(tb_ctx* ctx, const NhwcMaps& maps, const NhwcParams& p) {
+    constexpr int smem = nh_smem<BN, STAGES>();
+    static bool attr = false;
+    if (!attr) {
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+    }
+    const int grid = std::min(p.tiles_total, ctx->sm_count);
+    k_conv_nhwc<BN, STAGES><<<grid, NH_THREADS, smem, ctx->stream>>>(maps, p);
+    return check_launch("k_conv_nhwc");
+}
+
+}  // namespace
+
+int64_t conv_nhwc_packed_count(const ConvGeom& g) { return g.F * g.KH * g.KW * round_up(g.C, 32); }
+
+bool conv_nhwc_supported(const ConvGeom& g, int64_t x_ps) {
+    // im2col corner and offset fields of a 4-D map: corners in [-128, 127], offsets < 256
+    const int64_t upx = g.PX - (g.KW - 1) * g.DX, upy = g.PY - (g.KH - 1) * g.DY;
+    if (g.PX > 128 || g.PY > 128 || upx < -128 || upx > 127 || upy < -128 || upy > 127) return false;
+    if ((g.KW - 1) * g.DX > 255 || (g.KH - 1) * g.DY > 255 || g.SX > 8 || g.SY > 8) return false;
+    if (x_ps < g.C || x_ps % 4 != 0) return false;  // TMA strides are multiples of 16 bytes
+    // small tensors keep the NCHW path (the im2col map is only used on tensors of >= 128 KB)
+    if (g.B * g.H * g.W * x_ps * 4 < (128 << 10)) return false;
+    return g.B * g.OH * g.OW < ((int64_t)1 << 31) - NH_BM && g.F <= 65535 && g.OH * g.OW > 1;
+}
+
+int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp) {
+    const int64_t total = conv_nhwc_packed_count(g);
+    k_pack_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)g.F, (int)g.C, (int)g.KH,
+                                                                              (int)g.KW, (int)round_up(g.C, 32));
+    return check_launch("k_pack_nhwc");
+}
+
+// x: NHWC with pixel stride x_ps (floats; x points at channel 0 of the conv's input);
+// y: NHWC with pixel stride y_ps when y_ps > 0 (y at the output's channel offset), else NCHW
+// with batch stride g.y_bs; res: NHWC with pixel stride r_ps (or null).
+int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
+                     const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
+                     int yolo_classes, unsigned long long* phases) {
+    if (!conv_nhwc_supported(g, x_ps)) return fail(TB_ERR_UNSUPPORTED, "NHWC tensor-core conv: unsupported geometry");
+    if (g.B == 0) return TB_OK;
+    if (!aligned16(x) || !aligned16(wp)) return fail(TB_ERR_INVALID, "NHWC conv: x and weights must be 16-byte aligned");
+    if (y_ps > 0 && y_ps < g.F) return fail(TB_ERR_INVALID, "NHWC conv: output pixel stride below the filter count");
+    auto enc = im2col_encoder();
+    if (!enc) return fail(TB_ERR_CUDA, "NHWC conv: cuTensorMapEncodeIm2col is not available");
+    const int64_t Cp = round_up(g.C, 32);
+    NhwcMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    {
+        cuuint64_t dims[4] = {(cuuint64_t)g.C, (cuuint64_t)g.W, (cuuint64_t)g.H, (cuuint64_t)g.B};
+        cuuint64_t strides[3] = {(cuuint64_t)(x_ps * 4), (cuuint64_t)(g.W * x_ps * 4), (cuuint64_t)(g.H * g.W * x_ps * 4)};
+        int lower[2] = {(int)-g.PX, (int)-g.PY};
+        int upper[2] = {(int)(g.PX - (g.KW - 1) * g.DX), (int)(g.PY - (g.KH - 1) * g.DY)};
+        cuuint32_t es[4] = {1, (cuuint32_t)g.SX, (cuuint32_t)g.SY, 1};
+        CUresult r = enc(&maps.a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(x), dims, strides, lower,
+                         upper, NH_BK, NH_BM, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "NHWC conv: cuTensorMapEncodeIm2col failed (%d)", (int)r);
+    }
+    // tile width: the widest of 256 / 128 / 64 filters that does not leave most of a tile empty
+    const int bn = g.F > 128 ? 256 : g.F > 64 ? 128 : 64;
+    {
+        const uint64_t dims[2] = {(uint64_t)(g.KH * g.KW * Cp), (uint64_t)g.F};
+        const uint64_t strides[1] = {(uint64_t)(g.KH * g.KW * Cp * 4)};
+        const uint32_t box[2] = {(uint32_t)NH_BK, (uint32_t)bn};
+        int r = encode_map(&maps.b, wp, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (r != TB_OK) return r;
+    }
+    NhwcParams p{};
+    p.bias = bias; p.res = res; p.y = y; p.status = ctx->d_status; p.phases = phases;
+    p.npix = g.B * g.OH * g.OW;
+    p.y_bs = g.y_bs;
+    p.OW = (int)g.OW; p.OHW = (int)(g.OH * g.OW);
+    p.SX = (int)g.SX; p.SY = (int)g.SY; p.PX = (int)g.PX; p.PY = (int)g.PY;
+    p.KW = (int)g.KW; p.DX = (int)g.DX; p.DY = (int)g.DY;
+    p.F = (int)g.F;
+    p.csteps = (int)(Cp / NH_BK);
+    p.ktiles = (int)(g.KH * g.KW * p.csteps);
+    p.tiles_n = (int)ceil_div(g.F, bn);
+    p.tiles_total = (int)(ceil_div(p.npix, NH_BM) * p.tiles_n);
+    p.out_nchw = y_ps > 0 ? 0 : 1;
+    p.y_ps = (int)y_ps;
+    p.r_ps = (int)r_ps;
+    p.vec = y_ps % 4 == 0 && aligned16(y) && (!res || (r_ps % 4 == 0 && aligned16(res))) ? 1 : 0;
+    p.act = act;
+    p.yolo_classes = yolo_classes;
+    if (bn == 256) return nh_launch<256, 4>(ctx, maps, p);
+    if (bn == 128) return nh_launch<128, 6>(ctx, maps, p);
+    return nh_launch<64, 8>(ctx, maps, p);
+}
+
+}  // namespace tbi
+
+using namespace tbi;
+
+extern "C" {
+
+int tb_conv_nhwc_packed_count(const tb_conv_desc* d, int64_t* count) {
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!count) return fail(TB_ERR_INVALID, "null count");
+    *count = conv_nhwc_packed_count(g);
+    return TB_OK;
+}
+
+int tb_conv_pack_weights_nhwc(tb_ctx* ctx, const tb_conv_desc* d, const float* weights, float* packed) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!weights || !packed) return fail(TB_ERR_INVALID, "NHWC pack: null pointer");
+    if (!aligned16(packed)) return fail(TB_ERR_INVALID, "NHWC pack: packed buffer must be 16-byte aligned");
+    return conv_nhwc_pack(ctx, g, weights, packed);
+}
+
+int tb_conv2d_fwd_nhwc(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
+                       const float* packed_w, const float* bias, const float* residual, int64_t res_pixel_stride,
+                       float* y, int64_t y_pixel_stride) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!x || !packed_w || !y) return fail(TB_ERR_INVALID, "NHWC conv: null x, weights or y");
+    if (residual && y_pixel_stride <= 0) return fail(TB_ERR_INVALID, "NHWC conv: a residual needs an NHWC output");
+    if (!act_supported(d->activation)) return fail(TB_ERR_UNSUPPORTED, "NHWC conv: activation not supported");
+    return conv_nhwc_launch(ctx, g, x, x_pixel_stride, packed_w, bias, residual, res_pixel_stride, y,
+                            y_pixel_stride, (int)d->activation, 0, nullptr);
+}
+
+}  // extern "C"
