@@ -463,6 +463,10 @@ int tb_diag_tc_mma_rate(tb_ctx* ctx, int64_t kmajor, double* tflops, double* cyc
  * 0, 0 (no reference counterpart). Blocks. */
 int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y,
                            double* out12);
+/* The same counters for one launch of the NHWC tensor-core conv (tb_conv2d_fwd_nhwc's kernel;
+ * entry 8 and 10 are 0). Blocks. */
+int tb_diag_conv_nhwc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
+                             const float* packed_w, float* y, int64_t y_pixel_stride, double* out12);
 
 #ifdef __cplusplus
 }

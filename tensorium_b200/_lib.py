@@ -167,6 +167,7 @@ SIGNATURES = {
     "tb_diag_popc_tbitmac": [P, C.POINTER(C.c_double)],
     "tb_diag_tc_mma_rate": [P, I64, C.POINTER(C.c_double), C.POINTER(C.c_double)],
     "tb_diag_conv_tc_phases": [P, P, P, P, P, C.POINTER(C.c_double)],
+    "tb_diag_conv_nhwc_phases": [P, P, P, I64, P, P, I64, C.POINTER(C.c_double)],
 }
 _RESTYPES = {"tb_get_stream": P}
 

@@ -27,6 +27,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace tbi {
 
@@ -49,13 +50,17 @@ struct NhwcParams {
     int out_nchw;
     int y_ps, r_ps;                 // NHWC pixel strides (floats) of the output and residual
     int vec;                        // NHWC: y / res 16-byte aligned and strides % 4 == 0
+    int tma_out;                    // NHWC output written by TMA tensor stores (maps.y)
     int act, yolo_classes;
 };
 
 struct NhwcMaps {
     CUtensorMap a;  // im2col view of x: (C, W, H, N), 32 channels x 128 pixels per copy
     CUtensorMap b;  // packed weights (k, filter), box 32 x BN
+    CUtensorMap y;  // NHWC output (filter, pixel), box 16 x 32, 64-byte swizzle (tma_out)
 };
+
+constexpr int NH_STG_BYTES = 8 * 2 * 32 * 64;  // per epilogue warp: two 32-pixel x 16-filter slabs
 
 // K-major, 128-byte swizzle (layout type 2): rows of 32 fp32 along K, 8-row groups 1024 bytes apart
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
@@ -81,6 +86,21 @@ __device__ __forceinline__ void tma_load_im2col_4d(unsigned dst, const void* tma
         " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};\n" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(b), "r"(c), "r"(w), "r"(h), "r"(n), "h"(ow), "h"(oh)
         : "memory");
+}
+
+// shared -> global tensor store of one box, tracked as a bulk group of this thread
+__device__ __forceinline__ void tma_store_2d(const void* tmap, unsigned src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+}
+
+// wait until at most n of this thread's bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ float nh_act(float o, int f, const NhwcParams& p) {
@@ -218,9 +238,19 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         // ---------------- epilogue (warps 2-9) ----------------
         const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31
         const int half = (warp - 2) >> 2;  // 16-filter slabs half, half + 2, ...
+        // this warp's two staging slabs (32 pixel rows x 64 bytes each, 64-byte swizzle: the
+        // 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3), which the TMA store undoes)
+        const unsigned stg0 = sbase + STAGES * STAGE_BYTES + (warp - 2) * 2 * 2048;
+        // the common epilogue (bias, then leaky or linear, residual) is decided once here: read
+        // per value from the parameter space, these flags cost a dependent constant load each
+        const bool fast = p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
+        const bool leaky = p.act == TB_ACT_LEAKY;
+        const float* __restrict__ bias = p.bias;
+        const int Fm1 = p.F - 1;
+        int sbuf = 0;
         int tl = 0;
         const long long c_start = clock64();
-        long long c_wt = 0, c_st = 0;
+        long long c_wt = 0, c_st = 0, c_ldw = 0, c_math = 0;
         for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
@@ -238,15 +268,17 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             const uint32_t taddr = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
             const long long c0l = clock64();
             uint32_t vr[16];
-            if (half < BN / 16) tc::tmem_ld16_issue(taddr + half * 16, vr);
 #pragma unroll 1
             for (int sl = half; sl < BN / 16; sl += 2) {
+                const long long q0 = clock64();
+                tc::tmem_ld16_issue(taddr + sl * 16, vr);
                 tc::tmem_wait16(vr);
+                const long long q1 = clock64();
+                c_ldw += q1 - q0;
                 float v[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(vr[i]);
                 // the next slab's TMEM load runs while this slab is finished and stored
-                if (sl + 2 < BN / 16) tc::tmem_ld16_issue(taddr + (sl + 2) * 16, vr);
                 const int fb = nt * BN + sl * 16;
                 const bool full = fb + 16 <= p.F;
                 float rv[16];
@@ -262,16 +294,49 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         for (int i = 0; i < 16; ++i) rv[i] = fb + i < p.F ? __ldg(rp + fb + i) : 0.f;
                     }
                 }
+                if (fast) {  // bias, leaky or linear, residual: flags held in registers
+                    float bv[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int f = min(fb + i, p.F - 1);
-                    float o = v[i];
-                    if (p.bias) o = __fadd_rn(o, __ldg(p.bias + f));
-                    o = nh_act(o, f, p);
-                    if (rp) o = __fadd_rn(o, rv[i]);
-                    v[i] = tc::to_tf32_rna(o);
+                    for (int i = 0; i < 16; ++i) bv[i] = bias ? __ldg(bias + min(fb + i, Fm1)) : 0.f;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float o = v[i];
+                        if (bias) o = __fadd_rn(o, bv[i]);
+                        if (leaky && o < 0.f) o = __fmul_rn(o, 0.1f);  // rounded to TF32 below
+                        if (rp) o = __fadd_rn(o, rv[i]);
+                        v[i] = tc::to_tf32_rna(o);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int f = min(fb + i, Fm1);
+                        float o = v[i];
+                        if (bias) o = __fadd_rn(o, __ldg(bias + f));
+                        o = nh_act(o, f, p);
+                        if (rp) o = __fadd_rn(o, rv[i]);
+                        v[i] = tc::to_tf32_rna(o);
+                    }
                 }
-                if (valid) {
+                const long long q2 = clock64();
+                c_math += q2 - q1;
+                if (p.tma_out) {
+                    // stage the slab, then one lane stores it as a 16 x 32 box (the map clips
+                    // filters >= F and pixels past the end)
+                    const unsigned slab = stg0 + sbuf * 2048;
+                    if (lane == 0) bulk_wait_read<1>();  // the store that last read this slab is done
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const unsigned a = slab + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4);
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(a), "f"(v[4 * c]),
+                                     "f"(v[4 * c + 1]), "f"(v[4 * c + 2]), "f"(v[4 * c + 3])
+                                     : "memory");
+                    }
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) tma_store_2d(&maps.y, slab, fb, (int)((long long)mt * NH_BM + quarter * 32));
+                    sbuf ^= 1;
+                } else if (valid) {
                     if (p.out_nchw) {
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
@@ -292,11 +357,14 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);  // this warp's TMEM reads are done
         }
+        if (lane == 0) bulk_wait_read<0>();  // the shared-memory slabs are read before the CTA exits
         if (p.phases && warp == 2 && lane == 0) {
             p.phases[blockIdx.x * 12 + 5] = clock64() - c_start;
             p.phases[blockIdx.x * 12 + 6] = c_wt;
             p.phases[blockIdx.x * 12 + 7] = tl;
             p.phases[blockIdx.x * 12 + 9] = c_st;
+            p.phases[blockIdx.x * 12 + 8] = c_ldw;
+            p.phases[blockIdx.x * 12 + 10] = c_math;
         }
     }
     tc::tc_fence_before();
@@ -334,7 +402,7 @@ PFN_cuTensorMapEncodeIm2col_v12000 im2col_encoder() {
 }
 
 template <int BN, int STAGES>
-constexpr int nh_smem() { return STAGES * (NH_A_BYTES + BN * NH_BK * 4) + 1024; }
+constexpr int nh_smem() { return STAGES * (NH_A_BYTES + BN * NH_BK * 4) + NH_STG_BYTES + 1024; }
 
 template <int BN, int STAGES>
 int nh_launch(tb_ctx* ctx, const NhwcMaps& maps, const NhwcParams& p) {
@@ -407,6 +475,14 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
         if (r != TB_OK) return r;
     }
     NhwcParams p{};
+    if (y_ps > 0 && y_ps % 4 == 0 && aligned16(y)) {
+        const uint64_t dims[2] = {(uint64_t)g.F, (uint64_t)(g.B * g.OH * g.OW)};
+        const uint64_t strides[1] = {(uint64_t)(y_ps * 4)};
+        const uint32_t box[2] = {16, 32};
+        int r = encode_map(&maps.y, y, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (r != TB_OK) return r;
+        p.tma_out = 1;
+    }
     p.bias = bias; p.res = res; p.y = y; p.status = ctx->d_status; p.phases = phases;
     p.npix = g.B * g.OH * g.OW;
     p.y_bs = g.y_bs;
@@ -466,6 +542,36 @@ int tb_conv2d_fwd_nhwc(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64
     if (!act_supported(d->activation)) return fail(TB_ERR_UNSUPPORTED, "NHWC conv: activation not supported");
     return conv_nhwc_launch(ctx, g, x, x_pixel_stride, packed_w, bias, residual, res_pixel_stride, y,
                             y_pixel_stride, (int)d->activation, 0, nullptr);
+}
+
+int tb_diag_conv_nhwc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
+                             const float* packed_w, float* y, int64_t y_pixel_stride, double* out12) {
+    TB_ENTER(ctx);
+    ConvGeom g;
+    int r = conv_geom(d, &g);
+    if (r != TB_OK) return r;
+    if (!x || !packed_w || !y || !out12) return fail(TB_ERR_INVALID, "NHWC conv phases: null pointer");
+    const int n = ctx->sm_count * 12;
+    unsigned long long* dph = nullptr;
+    TB_CHECK_CUDA(cudaMalloc(&dph, n * sizeof(unsigned long long)));
+    cudaMemsetAsync(dph, 0, n * sizeof(unsigned long long), ctx->stream);
+    r = conv_nhwc_launch(ctx, g, x, x_pixel_stride, packed_w, nullptr, nullptr, 0, y, y_pixel_stride,
+                         (int)d->activation, 0, dph);
+    std::vector<unsigned long long> h(n);
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), dph, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(dph);
+    if (r != TB_OK) return r;
+    if (e != cudaSuccess) return cuda_fail(e, "NHWC conv phases");
+    int ctas = 0;
+    for (int i = 0; i < 12; ++i) out12[i] = 0;
+    for (int c = 0; c < ctx->sm_count; ++c) {
+        if (h[c * 12 + 0] == 0) continue;
+        ++ctas;
+        for (int i = 0; i < 12; ++i) out12[i] += (double)h[c * 12 + i];
+    }
+    for (int i = 0; i < 12 && ctas; ++i) out12[i] /= ctas;
+    return TB_OK;
 }
 
 }  // extern "C"
