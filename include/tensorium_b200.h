@@ -355,6 +355,12 @@ int tb_net_forward(tb_net* net, const float* x, int64_t use_graph);
 /* Device pointer / element count of a layer's output (per batch) and its batch stride. */
 int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* count_per_image,
                         int64_t* batch_stride);
+/* Layout of a layer's output: *pixel_stride = 0 for NCHW ([batch][c][h][w], batch stride as
+ * tb_net_layer_output reports); > 0 for NHWC ([batch][h][w][pixel_stride], the layer's channels
+ * first in each pixel). A TF32 network of convs, shortcuts, routes, upsamples and fused yolo
+ * heads keeps its activations NHWC (its yolo outputs stay NCHW); set TB_NET_NHWC=0 before
+ * tb_net_finalize to keep every activation NCHW. */
+int tb_net_layer_layout(tb_net* net, int64_t layer, int64_t* pixel_stride);
 int tb_net_layer_count(tb_net* net, int64_t* count);
 /* Device launches the last tb_net_forward issued (graph replay counts its kernel nodes). */
 int tb_net_launch_count(tb_net* net, int64_t* count);

@@ -153,6 +153,7 @@ SIGNATURES = {
     "tb_net_forward": [P, P, I64],
     "tb_net_layer_output": [P, I64, C.POINTER(P), PI64, PI64],
     "tb_net_layer_count": [P, PI64],
+    "tb_net_layer_layout": [P, I64, PI64],
     "tb_net_launch_count": [P, PI64],
     "tb_net_flops": [P, C.POINTER(C.c_double)],
     "tb_net_profile": [P, P, C.POINTER(C.c_double)],

@@ -87,6 +87,19 @@ int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp);
 int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
                      const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
                      int yolo_classes, unsigned long long* phases);
+// NHWC data-movement layers of the network's NHWC plan (nhwc_layers.cu); strides in floats per pixel.
+int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, int64_t x_bs,
+                   float* y, int64_t ps);
+// first layer with C * KH * KW <= 32: receptive fields as 32 channels of a 1x1 conv, and its weights
+int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
+                      int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
+                      const float* x, int64_t x_bs, float* y);
+int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp);
+int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, int64_t s, float scale,
+                  const float* x, int64_t xps, float* y, int64_t yps);
+int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps, float* y, int64_t yps);
+int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t aps, const float* b, int64_t bps,
+                  float* y, int64_t yps, int act);
 // Direct convolution for short reductions (C*KH*KW <= 32, CRS-packed weights, no residual, no
 // fused yolo): the first layer of an image network (conv_direct.cu).
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes);

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         const bool leaky = p.act == TB_ACT_LEAKY;
         const float* __restrict__ bias = p.bias;
         const int Fm1 = p.F - 1;
+        const int period = p.yolo_classes > 0 ? p.yolo_classes + 5 : 0;
         int sbuf = 0;
         int tl = 0;
         const long long c_start = clock64();
@@ -305,6 +306,16 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         if (leaky && o < 0.f) o = __fmul_rn(o, 0.1f);  // rounded to TF32 below
                         if (rp) o = __fadd_rn(o, rv[i]);
                         v[i] = tc::to_tf32_rna(o);
+                    }
+                } else if (period) {  // fused yolo head: logistic on entries 0, 1, 4.. of each anchor
+                    int e = fb % period;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float o = v[i];
+                        if (bias) o = __fadd_rn(o, __ldg(bias + min(fb + i, Fm1)));
+                        if (e != 2 && e != 3) o = __frcp_rn(__fadd_rn(1.0f, __expf(-o)));  // rounded to TF32 below
+                        v[i] = tc::to_tf32_rna(o);
+                        e = e + 1 == period ? 0 : e + 1;
                     }
                 } else {
 #pragma unroll

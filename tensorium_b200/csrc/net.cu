@@ -29,6 +29,7 @@ namespace {
 struct View {
     float* ptr = nullptr;
     int64_t bs = 0;  // elements between images
+    int64_t ps = 0;  // 0: NCHW; > 0: NHWC with ps floats per pixel (ptr at the first channel)
 };
 
 struct Layer {
@@ -81,7 +82,26 @@ struct tb_net {
     int64_t launches = 0, graph_launches = 0;
     double flops = 0.0;
     std::vector<float*> allocs;
+    // NHWC plan (TF32 networks made of convs, shortcuts, routes, upsamples and fused yolo heads):
+    // activations are NHWC, every conv runs on the NHWC tensor-core kernel, the input is
+    // converted into x_nhwc (x_ps floats per pixel) first and the yolo heads are written NCHW
+    bool nhwc = false;
+    float* x_nhwc = nullptr;
+    int64_t x_ps = 0;
+    // the first conv with C * KH * KW <= 32 runs as a 1x1 conv over its receptive fields
+    // (x_nhwc holds [batch][oh][ow][32], made by the input conversion)
+    bool first_im2col = false;
 };
+
+namespace {
+// geometry of the first layer run as a 1x1 conv over 32 receptive-field channels
+ConvGeom first_as_1x1(const ConvGeom& g) {
+    ConvGeom f = g;
+    f.C = 32; f.H = g.OH; f.W = g.OW;
+    f.KH = f.KW = 1; f.SY = f.SX = 1; f.PY = f.PX = 0; f.DY = f.DX = 1;
+    return f;
+}
+}  // namespace
 
 namespace {
 
@@ -208,6 +228,13 @@ void desc_of(const tb_net* net, const Layer& L, tb_conv_desc* d) {
 View input_view(tb_net* net, int64_t i, const float* x) {
     if (i == 0) {
         View v;
+        if (net->nhwc) {
+            v.ptr = net->x_nhwc;
+            v.ps = net->x_ps;
+            const Layer& L0 = *net->layers[0];
+            v.bs = (net->first_im2col ? L0.oh * L0.ow : net->h * net->w) * net->x_ps;
+            return v;
+        }
         v.ptr = const_cast<float*>(x);
         v.bs = net->c * net->h * net->w;
         return v;
@@ -215,7 +242,70 @@ View input_view(tb_net* net, int64_t i, const float* x) {
     return net->layers[i - 1]->out;
 }
 
+// One layer of the NHWC plan.
+int run_layer_nhwc(tb_net* net, int64_t i, const float* x) {
+    tb_ctx* ctx = net->ctx;
+    Layer& L = *net->layers[i];
+    const int64_t B = net->batch;
+    int r;
+    if (i == 0) {  // the network input, NCHW, into the NHWC staging buffer (or its receptive fields)
+        if (net->first_im2col)
+            r = nhwc_im2col_first(ctx, B, net->c, net->h, net->w, L.ksize, L.ksize, L.stride, L.stride, L.pad, L.pad,
+                                  1, 1, L.oh, L.ow, x, net->c * net->h * net->w, net->x_nhwc);
+        else
+            r = nhwc_from_nchw(ctx, B, net->c, net->h, net->w, x, net->c * net->h * net->w, net->x_nhwc, net->x_ps);
+        if (r != TB_OK) return r;
+        net->launches++;
+    }
+    if (L.absorbed) return TB_OK;
+    View in = input_view(net, i, x);
+    switch (L.type) {
+    case TB_LAYER_CONV: {
+        tb_conv_desc d;
+        desc_of(net, L, &d);
+        const Layer& T = *net->layers[L.target];
+        d.out_batch_stride = T.out.bs;
+        ConvGeom g;
+        r = conv_geom(&d, &g);
+        if (r != TB_OK) return r;
+        if (i == 0 && net->first_im2col) g = first_as_1x1(g);
+        const float* res = nullptr;
+        int64_t rps = 0;
+        if (L.fuse_res >= 0) {
+            res = net->layers[L.fuse_res]->out.ptr;
+            rps = net->layers[L.fuse_res]->out.ps;
+        }
+        net->launches++;
+        return conv_nhwc_launch(ctx, g, in.ptr, in.ps, L.d_wp, L.d_bias, res, rps, T.out.ptr, T.out.ps, (int)L.act,
+                                (int)L.fuse_yolo, nullptr);
+    }
+    case TB_LAYER_SHORTCUT: {
+        const Layer& F = *net->layers[L.from];
+        net->launches++;
+        return nhwc_shortcut(ctx, B * L.oh * L.ow, L.oc, in.ptr, in.ps, F.out.ptr, F.out.ps, L.out.ptr, L.out.ps,
+                             (int)L.act);
+    }
+    case TB_LAYER_ROUTE: {
+        if (L.route_zero_copy) return TB_OK;
+        int64_t off = 0;
+        for (int64_t j : L.inputs) {
+            const Layer& S = *net->layers[j];
+            r = nhwc_copy(ctx, B * L.oh * L.ow, S.oc, S.out.ptr, S.out.ps, L.out.ptr + off, L.out.ps);
+            if (r != TB_OK) return r;
+            net->launches++;
+            off += S.oc;
+        }
+        return TB_OK;
+    }
+    case TB_LAYER_UPSAMPLE:
+        net->launches++;
+        return nhwc_upsample(ctx, B, L.c, L.h, L.w, L.stride, L.up_scale, in.ptr, in.ps, L.out.ptr, L.out.ps);
+    }
+    return fail(TB_ERR_STATE, "layer %lld: not on the NHWC plan", (long long)i);
+}
+
 int run_layer(tb_net* net, int64_t i, const float* x) {
+    if (net->nhwc) return run_layer_nhwc(net, i, x);
     tb_ctx* ctx = net->ctx;
     Layer& L = *net->layers[i];
     if (L.absorbed) return TB_OK;
@@ -525,6 +615,64 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             }
         }
     }
+    // 1b. the NHWC plan: a TF32 network made only of convs (batchnorm folded, geometries the
+    //     NHWC tensor-core kernel takes), shortcuts, routes of 4-channel-multiple inputs,
+    //     upsamples and fused yolo heads runs every activation in NHWC (TB_NET_NHWC=0: off)
+    net->nhwc = false;
+    net->first_im2col = false;
+    {
+        const char* ev = getenv("TB_NET_NHWC");
+        bool ok = math_mode == TB_MATH_TF32 && net->fusion && !(ev && ev[0] == '0');
+        for (int64_t i = 0; ok && i < n; ++i) {
+            const Layer& L = *net->layers[i];
+            switch (L.type) {
+            case TB_LAYER_CONV: {
+                tb_conv_desc d;
+                desc_of(net, L, &d);
+                ConvGeom g;
+                if (L.bn || conv_geom(&d, &g) != TB_OK) { ok = false; break; }
+                if (i == 0 && L.c * L.ksize * L.ksize <= 32) {
+                    net->first_im2col = true;
+                    if (!conv_nhwc_supported(first_as_1x1(g), 32)) ok = false;
+                } else {
+                    const int64_t xps = i == 0 ? round_up(net->c, 4) : round_up(L.c, 4);
+                    if (!conv_nhwc_supported(g, xps) || (L.c % 4 && i > 0)) ok = false;
+                }
+                const Layer& T = *net->layers[L.target];
+                if (T.type != TB_LAYER_YOLO && L.oc % 4) ok = false;
+                break;
+            }
+            case TB_LAYER_SHORTCUT:
+            case TB_LAYER_UPSAMPLE:
+                if (L.oc % 4) ok = false;
+                break;
+            case TB_LAYER_ROUTE:
+                for (int64_t j : L.inputs)
+                    if (net->layers[j]->oc % 4 || net->layers[j]->type == TB_LAYER_YOLO) ok = false;
+                break;
+            case TB_LAYER_YOLO:
+                if (!L.absorbed) ok = false;
+                break;
+            default:
+                ok = false;
+            }
+        }
+        net->nhwc = ok;
+        if (!ok) net->first_im2col = false;
+    }
+    // floats per image and batch / pixel strides of a layer's own output buffer
+    auto own_view = [&](Layer& L, float* ptr, int64_t channels_total) {
+        View v;
+        v.ptr = ptr;
+        if (net->nhwc && L.type != TB_LAYER_YOLO) {
+            v.ps = round_up(channels_total, 4);
+            v.bs = L.oh * L.ow * v.ps;
+        } else {
+            v.bs = channels_total * L.oh * L.ow;
+        }
+        return v;
+    };
+
     // producer[j]: the layer whose kernel writes j's output
     std::vector<int64_t> producer((size_t)n);
     for (int64_t i = 0; i < n; ++i) producer[i] = i;
@@ -561,11 +709,11 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     for (int64_t i = 0; i < n; ++i) {
         Layer& L = *net->layers[i];
         if (L.type != TB_LAYER_ROUTE || L.inputs.size() == 1) continue;
-        L.own_floats = B * L.per_image();
+        L.out = own_view(L, nullptr, L.oc);
+        L.own_floats = B * L.out.bs;
         L.own = alloc(L.own_floats);
         if (!L.own) return err;
         L.out.ptr = L.own;
-        L.out.bs = L.per_image();
         placed[i] = true;
         bool all = net->fusion;
         for (int64_t j : L.inputs)
@@ -579,10 +727,10 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             int64_t off = 0;
             for (int64_t j : L.inputs) {
                 Layer& S = *net->layers[j];
+                S.out = L.out;  // NHWC: a channel slice; NCHW: a block of whole channel planes
                 S.out.ptr = L.own + off;
-                S.out.bs = L.per_image();
                 placed[j] = true;
-                off += S.per_image();
+                off += net->nhwc ? S.oc : S.per_image();
             }
             L.route_zero_copy = true;
         }
@@ -600,12 +748,18 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             placed[i] = true;
             continue;
         }
-        L.own_floats = B * L.per_image();
+        L.out = own_view(L, nullptr, L.oc);
+        L.own_floats = B * L.out.bs;
         L.own = alloc(L.own_floats);
         if (!L.own) return err;
         L.out.ptr = L.own;
-        L.out.bs = L.per_image();
         placed[i] = true;
+    }
+    if (net->nhwc) {
+        const Layer& L0 = *net->layers[0];
+        net->x_ps = net->first_im2col ? 32 : round_up(net->c, 4);
+        net->x_nhwc = alloc(B * (net->first_im2col ? L0.oh * L0.ow : net->h * net->w) * net->x_ps);
+        if (!net->x_nhwc) return err;
     }
     for (int64_t i = 0; i < n; ++i) {
         Layer& L = *net->layers[i];
@@ -625,11 +779,21 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         if (r != TB_OK) return r;
         float* raw = dev_upload(net, L.weights, &err);
         if (!raw) return err;
-        L.d_wp = alloc(g.Kpad * g.Mpad);
-        if (!L.d_wp) return err;
-        r = tb_conv_pack_weights(net->ctx, &d, raw, L.d_wp);
-        if (r == TB_OK && net->math_mode == TB_MATH_TF32 && conv_tc_supported(g))
-            r = conv_tc_round_weights(net->ctx, L.d_wp, g.Kpad * g.Mpad);
+        if (net->nhwc && i == 0 && net->first_im2col) {
+            L.d_wp = alloc(g.F * 32);
+            if (!L.d_wp) return err;
+            r = nhwc_pack_first(net->ctx, g.F, g.C, g.KH, g.KW, raw, L.d_wp);
+        } else if (net->nhwc) {
+            L.d_wp = alloc(conv_nhwc_packed_count(g));
+            if (!L.d_wp) return err;
+            r = conv_nhwc_pack(net->ctx, g, raw, L.d_wp);
+        } else {
+            L.d_wp = alloc(g.Kpad * g.Mpad);
+            if (!L.d_wp) return err;
+            r = tb_conv_pack_weights(net->ctx, &d, raw, L.d_wp);
+            if (r == TB_OK && net->math_mode == TB_MATH_TF32 && conv_tc_supported(g))
+                r = conv_tc_round_weights(net->ctx, L.d_wp, g.Kpad * g.Mpad);
+        }
         if (r != TB_OK) return r;
         L.d_bias = dev_upload(net, L.biases, &err);
         if (err != TB_OK) return err;
@@ -645,7 +809,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     // 4. measure the tile / split choices of every conv geometry on the real buffers
     //    (TB_AUTOTUNE=0 keeps the cost model)
     const char* at = getenv("TB_AUTOTUNE");
-    if (!(at && at[0] == '0')) {
+    if (!(at && at[0] == '0') && !net->nhwc) {
         for (int64_t i = 0; i < n; ++i) {
             Layer& L = *net->layers[i];
             if (L.type != TB_LAYER_CONV && L.type != TB_LAYER_CONNECTED) continue;
@@ -765,6 +929,14 @@ int tb_net_layer_output(tb_net* net, int64_t layer, const float** ptr, int64_t* 
     if (ptr) *ptr = L.out.ptr;
     if (count) *count = L.per_image();
     if (bs) *bs = L.out.bs;
+    return TB_OK;
+}
+
+int tb_net_layer_layout(tb_net* net, int64_t layer, int64_t* pixel_stride) {
+    if (!net || !pixel_stride) return fail(TB_ERR_INVALID, "null argument");
+    if (!net->finalized) return fail(TB_ERR_STATE, "net not finalized");
+    if (layer < 0 || layer >= (int64_t)net->layers.size()) return fail(TB_ERR_INVALID, "layer out of range");
+    *pixel_stride = net->layers[layer]->out.ps;
     return TB_OK;
 }
 

@@ -1,0 +1,180 @@
+// nhwc_layers.cu -- the data-movement layers of a network that runs its tensor-core convs on NHWC
+// activations (net.cu's NHWC plan): input conversion, upsample, route copy and shortcut on
+// [batch][h][w][pixel stride] buffers, where a layer's channels may be a slice of a wider
+// (concatenation) buffer. Same arithmetic as the NCHW kernels: upsample multiplies by the scale
+// (source/nupsamplelayer.pas:83-113), shortcut adds then activates (source/naddlayer.pas:667-725),
+// route copies (source/nconcatlayer.pas:93-119).
+#include "common.cuh"
+
+namespace tbi {
+
+namespace {
+
+// x: NCHW [b][c][h][w] (batch stride x_bs) -> y: NHWC, pixel stride ps >= c, channels c..ps-1
+// zero; values rounded to TF32 (nearest), as every activation the tensor cores read
+__global__ void k_nchw_to_nhwc(int64_t npix, int c, int hw, int ps, const float* __restrict__ x, int64_t x_bs,
+                               float* __restrict__ y) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npix * ps;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t pix = i / ps;
+        const int ch = (int)(i - pix * ps);
+        const int64_t b = pix / hw;
+        const int q = (int)(pix - b * hw);
+        float v = ch < c ? __ldg(x + b * x_bs + (int64_t)ch * hw + q) : 0.0f;
+        uint32_t u = __float_as_uint(v);  // round to nearest TF32 (ties away), finite values only
+        if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+        y[i] = __uint_as_float(u);
+    }
+}
+
+// upsample: y[b][oy][ox][ch] = scale * x[b][oy/s][ox/s][ch], 4 channels per thread
+__global__ void k_upsample_nhwc4(int64_t total4, int c4, int w, int h, int s, float scale,
+                                 const float4* __restrict__ x, int xps4, float4* __restrict__ y, int yps4) {
+    const int ow = w * s, oh = h * s;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t opix = i / c4;
+        const int q = (int)(i - opix * c4);
+        const int ox = (int)(opix % ow);
+        const int64_t t = opix / ow;
+        const int oy = (int)(t % oh);
+        const int64_t b = t / oh;
+        const float4 v = __ldg(x + ((b * h + oy / s) * w + ox / s) * xps4 + q);
+        y[opix * yps4 + q] = make_float4(scale * v.x, scale * v.y, scale * v.z, scale * v.w);
+    }
+}
+
+// copy c channels per pixel between two pixel strides (route slices)
+__global__ void k_copy_nhwc4(int64_t total4, int c4, const float4* __restrict__ x, int xps4, float4* __restrict__ y,
+                             int yps4) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t pix = i / c4;
+        const int q = (int)(i - pix * c4);
+        y[pix * yps4 + q] = __ldg(x + pix * xps4 + q);
+    }
+}
+
+// shortcut: out = act(a + b)
+__global__ void k_shortcut_nhwc(int64_t total, int c, const float* __restrict__ a, int aps,
+                                const float* __restrict__ b, int bps, float* __restrict__ y, int yps, int act) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t pix = i / c;
+        const int ch = (int)(i - pix * c);
+        float v = __fadd_rn(__ldg(a + pix * aps + ch), __ldg(b + pix * bps + ch));
+        if (act != TB_ACT_LINEAR) v = tb_activate_dev(v, act);
+        y[pix * yps + ch] = v;
+    }
+}
+
+// The first layer of an image network (C * KH * KW <= 32) as a 1x1 conv over 32 "channels": output
+// pixel (b, oy, ox) gets its whole receptive field, k = (r * KW + s) * C + c, zero past K and in
+// the padding, rounded to TF32. One k tile instead of KH * KW mostly empty ones.
+__global__ void k_im2col_first(int64_t npix, int C, int H, int W, int KW, int K, int OW, int OHW, int SY, int SX,
+                               int PY, int PX, int DY, int DX, const float* __restrict__ x, int64_t x_bs,
+                               float* __restrict__ y) {
+    // one thread per output pixel: the lanes of a warp read neighbouring pixels of the same tap
+    // (coalesced) and each writes its 128-byte row of 32 values
+    for (int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pix < npix; pix += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = pix / OHW;
+        const int q = (int)(pix - b * OHW);
+        const int oy = q / OW, ox = q - oy * OW;
+        const float* xb = x + b * x_bs;
+        float v[32];
+        int c = 0, r = 0, s = 0;  // k = (r * KW + s) * C + c, in order
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            float t = 0.0f;
+            if (k < K) {
+                const int iy = oy * SY - PY + r * DY, ix = ox * SX - PX + s * DX;
+                if (iy >= 0 && iy < H && ix >= 0 && ix < W) t = __ldg(xb + ((int64_t)c * H + iy) * W + ix);
+                if (++c == C) {
+                    c = 0;
+                    if (++s == KW) s = 0, ++r;
+                }
+            }
+            uint32_t u = __float_as_uint(t);
+            if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+            v[k] = __uint_as_float(u);
+        }
+        float4* yo = reinterpret_cast<float4*>(y + pix * 32);
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) __stcs(yo + k / 4, make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]));
+    }
+}
+
+// its weights: wp[f][k] = tf32(w[f][c][r][s]) for k = (r * KW + s) * C + c < K, zero up to 32
+__global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp, int F, int C, int KH, int KW) {
+    const int K = C * KH * KW;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < F * 32; i += gridDim.x * blockDim.x) {
+        const int f = i >> 5, k = i & 31;
+        float v = 0.0f;
+        if (k < K) {
+            const int rs = k / C, c = k - rs * C;
+            const int r = rs / KW, s = rs - r * KW;
+            v = w[(((int64_t)f * C + c) * KH + r) * KW + s];
+        }
+        uint32_t u = __float_as_uint(v);
+        if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+        wp[i] = __uint_as_float(u);
+    }
+}
+
+}  // namespace
+
+int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
+                      int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
+                      const float* x, int64_t x_bs, float* y) {
+    const int64_t npix = B * OH * OW;
+    if (npix == 0) return TB_OK;
+    k_im2col_first<<<grid_for(npix, 128, ctx->sm_count), 128, 0, ctx->stream>>>(
+        npix, (int)C, (int)H, (int)W, (int)KW, (int)(C * KH * KW), (int)OW, (int)(OH * OW), (int)SY, (int)SX,
+        (int)PY, (int)PX, (int)DY, (int)DX, x, x_bs, y);
+    return check_launch("k_im2col_first");
+}
+
+int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp) {
+    k_pack_first<<<grid_for(F * 32, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)F, (int)C, (int)KH, (int)KW);
+    return check_launch("k_pack_first");
+}
+
+int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, int64_t x_bs,
+                   float* y, int64_t ps) {
+    const int64_t npix = batch * h * w;
+    if (npix == 0) return TB_OK;
+    k_nchw_to_nhwc<<<grid_for(npix * ps, 256, ctx->sm_count), 256, 0, ctx->stream>>>(npix, (int)c, (int)(h * w),
+                                                                                     (int)ps, x, x_bs, y);
+    return check_launch("k_nchw_to_nhwc");
+}
+
+int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, int64_t s, float scale,
+                  const float* x, int64_t xps, float* y, int64_t yps) {
+    if (c % 4 || xps % 4 || yps % 4 || !aligned16(x) || !aligned16(y))
+        return fail(TB_ERR_STATE, "NHWC upsample: channels, strides and pointers must be 16-byte multiples");
+    const int64_t total4 = batch * h * s * w * s * (c / 4);
+    if (total4 == 0) return TB_OK;
+    k_upsample_nhwc4<<<grid_for(total4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        total4, (int)(c / 4), (int)w, (int)h, (int)s, scale, reinterpret_cast<const float4*>(x), (int)(xps / 4),
+        reinterpret_cast<float4*>(y), (int)(yps / 4));
+    return check_launch("k_upsample_nhwc4");
+}
+
+int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps, float* y, int64_t yps) {
+    if (c % 4 || xps % 4 || yps % 4 || !aligned16(x) || !aligned16(y))
+        return fail(TB_ERR_STATE, "NHWC copy: channels, strides and pointers must be 16-byte multiples");
+    const int64_t total4 = npix * (c / 4);
+    if (total4 == 0) return TB_OK;
+    k_copy_nhwc4<<<grid_for(total4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        total4, (int)(c / 4), reinterpret_cast<const float4*>(x), (int)(xps / 4), reinterpret_cast<float4*>(y),
+        (int)(yps / 4));
+    return check_launch("k_copy_nhwc4");
+}
+
+int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t aps, const float* b, int64_t bps,
+                  float* y, int64_t yps, int act) {
+    const int64_t total = npix * c;
+    if (total == 0) return TB_OK;
+    k_shortcut_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(total, (int)c, a, (int)aps, b,
+                                                                                  (int)bps, y, (int)yps, act);
+    return check_launch("k_shortcut_nhwc");
+}
+
+}  // namespace tbi

@@ -166,14 +166,23 @@ class TNNet:
         check(lib.tb_net_forward(self.handle, ptr(x), 1 if use_graph else 0))
 
     def output(self, layer: int = -1) -> torch.Tensor:
-        """Device view of a layer's output, [batch, per_image] (strided for route slices)."""
+        """A layer's output as [batch, per_image] in NCHW order: a device view (strided for route
+        slices), or, for an activation the executor keeps NHWC, an NCHW copy of it."""
         if layer < 0:
             layer += len(self.specs)
         p = C.c_void_p()
         n = C.c_int64()
         bs = C.c_int64()
         check(lib.tb_net_layer_output(self.handle, layer, C.byref(p), C.byref(n), C.byref(bs)))
-        return _view(p.value, self.batch, n.value, bs.value, self.ctx.torch_device)
+        ps = C.c_int64()
+        check(lib.tb_net_layer_layout(self.handle, layer, C.byref(ps)))
+        if ps.value == 0:
+            return _view(p.value, self.batch, n.value, bs.value, self.ctx.torch_device)
+        c, h, w = self.shapes[layer]
+        numel = (self.batch - 1) * bs.value + (h * w - 1) * ps.value + c
+        t = torch.as_tensor(_CAI(p.value, numel), device=self.ctx.torch_device)
+        nhwc = t.as_strided((self.batch, h, w, c), (bs.value, w * ps.value, ps.value, 1))
+        return nhwc.permute(0, 3, 1, 2).contiguous().reshape(self.batch, c * h * w)
 
     def predict(self, x_host: np.ndarray, layers=None):
         """TNNet.predict (source/nnet.pas:452-472): host input in, host outputs back

@@ -155,3 +155,45 @@ def test_tc_conv_every_tile_shape(ctx, shape, monkeypatch):
         ref = O.conv2d(x, w, b, F, k, s, p, 4)
         e = rel_l2_maps(y1, ref, B * F)
         assert 0.0 < e <= TF32_TOL, (shape, C, e)
+
+
+def test_yolov3_tf32_nhwc_plan(ctx):
+    """The fused TF32 YOLOv3 runs its activations NHWC (every conv on the NHWC tensor-core kernel,
+    A operand by TMA im2col): intermediate maps and the three yolo outputs within the TF32 bar of
+    the FP32 oracle, the same detection index sets away from the threshold band, and graph replay
+    equal to eager."""
+    import ctypes as C_
+    from tensorium_b200 import synth
+    from tensorium_b200._lib import lib
+    from tensorium_b200.net import TNNet
+    specs = synth.yolov3_specs()
+    shape = (3, 416, 416)
+    x = synth.input_images(3, "yolov3", 2, shape)
+    heads, raws, inner = [82, 94, 106], [81, 93, 105], [1, 36, 61, 85, 97]
+    ref = O.run_network(specs, x, keep=heads + raws + inner)
+    net = TNNet(ctx, specs, 2, shape, math_mode=MATH_TF32)
+    ps = C_.c_int64()
+    lib.tb_net_layer_layout(net.handle, 36, C_.byref(ps))
+    assert ps.value == 384  # NHWC, a 256-channel slice of the 384-channel route 97 buffer
+    xd = torch.from_numpy(x).to(ctx.torch_device)
+    net.forward(xd, use_graph=False)
+    for i in inner:  # per image, as the heads
+        e = rel_l2_maps(net.output(i).cpu().numpy(), ref[i], 2)
+        assert e <= TF32_TOL, (i, e)
+    eager = [net.output(h).clone() for h in heads]
+    thresh = 0.45
+    logit = np.log(thresh / (1 - thresh))
+    for h, r, got in zip(heads, raws, eager):
+        got = got.cpu().numpy()
+        e = rel_l2_maps(got, ref[h], 2)
+        assert e <= TF32_TOL, (h, e)
+        g = got.shape[-1] // 255
+        go, ro = got.reshape(2, 3, 85, g)[:, :, 4], ref[h].reshape(2, 3, 85, g)[:, :, 4]
+        xo = ref[r].reshape(2, 3, 85, g)[:, :, 4]
+        band = TF32_TOL * np.sqrt((xo ** 2).mean(axis=2, keepdims=True))
+        sure = np.abs(xo - logit) > 4 * band
+        assert np.array_equal((go > thresh)[sure], (ro > thresh)[sure]), h
+    net.forward(xd, use_graph=True)
+    for h, e in zip(heads, eager):
+        assert torch.equal(net.output(h), e)
+    net.close()
