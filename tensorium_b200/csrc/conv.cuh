@@ -87,6 +87,9 @@ int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp);
 int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
                      const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
                      int yolo_classes, unsigned long long* phases);
+int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps);
+int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp, float* y,
+                       int64_t y_ps);
 // NHWC data-movement layers of the network's NHWC plan (nhwc_layers.cu); strides in floats per pixel.
 int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, int64_t x_bs,
                    float* y, int64_t ps);

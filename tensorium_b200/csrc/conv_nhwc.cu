@@ -26,6 +26,9 @@
 
 #include <algorithm>
 #include <cstring>
+#include <cstdio>
+#include <cstdlib>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -47,6 +50,9 @@ struct NhwcParams {
     int OW, OHW, SX, SY, PX, PY, KW, DX, DY;
     int F, csteps, ktiles;
     int tiles_n, tiles_total;
+    int splits, kt_per_split, units;  // split-K: unit w = k range w % splits of tile w / splits
+    float* part;                      // split-K partial tiles [unit][128 pixels][BN]
+    int* tile_cnt;                    // split-K arrival counters, one per tile, left at 0
     int out_nchw;
     int y_ps, r_ps;                 // NHWC pixel strides (floats) of the output and residual
     int vec;                        // NHWC: y / res 16-byte aligned and strides % 4 == 0
@@ -122,6 +128,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
+    __shared__ volatile int last_unit;  // split-K: this CTA's unit is the last of its tile
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const unsigned sbase = (unsigned)__cvta_generic_to_shared(smem);
@@ -154,15 +161,18 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             bool ok = true;
             const long long c_start = clock64();
             long long c_wait = 0;
-            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+            for (int w = blockIdx.x; ok && w < p.units; w += gridDim.x) {
+                const int t = w / p.splits, z = w - t * p.splits;
+                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
                 const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
                 const long long m0 = (long long)mt * NH_BM;
                 const int n0 = (int)(m0 / p.OHW);
                 const int q = (int)(m0 - (long long)n0 * p.OHW);
                 const int oy = q / p.OW, ox = q - oy * p.OW;
                 const int w0 = ox * p.SX - p.PX, h0 = oy * p.SY - p.PY;
-                int r = 0, s = 0, c0 = 0;
-                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                const int rs0 = kb / p.csteps;  // tap (r, s) and channel step of k tile kb
+                int r = rs0 / p.KW, s = rs0 - r * p.KW, c0 = kb - rs0 * p.csteps;
+                for (int kt = kb; kt < ke; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
                     const long long c0w = clock64();
                     if (use > 0 && !tc::mbar_wait_bounded(&empty_bar[st], (use - 1) & 1, &abort_flag, p.status, 921)) {
@@ -198,14 +208,16 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             bool ok = true, issued = false;
             const long long c_start = clock64();
             long long c_wf = 0, c_we = 0;
-            for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x, ++tl) {
+            for (int w = blockIdx.x; ok && w < p.units; w += gridDim.x, ++tl) {
+                const int z = w % p.splits;
+                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
                 const int buf = tl & 1, u = tl >> 1;
                 long long c0w = clock64();
                 if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 922)) break;
                 c_we += clock64() - c0w;
                 tc::tc_fence_after();
                 const uint32_t d = tmem0 + buf * BN;
-                for (int kt = 0; kt < p.ktiles; ++kt, ++it) {
+                for (int kt = kb; kt < ke; ++kt, ++it) {
                     const int st = it % STAGES, use = it / STAGES;
                     c0w = clock64();
                     if (!tc::mbar_wait_bounded(&full_bar[st], use & 1, &abort_flag, p.status, 923)) {
@@ -218,7 +230,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
 #pragma unroll
                     for (int kk = 0; kk < NH_BK / 8; ++kk)
                         tc::mma_tf32(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
-                                     (kt || kk) ? 1u : 0u);
+                                     (kt != kb || kk) ? 1u : 0u);
                     issued = true;
                     tc::mma_commit(&empty_bar[st]);
                 }
@@ -252,13 +264,45 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         int tl = 0;
         const long long c_start = clock64();
         long long c_wt = 0, c_st = 0, c_ldw = 0, c_math = 0;
-        for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x, ++tl) {
+        for (int w = blockIdx.x; w < p.units; w += gridDim.x, ++tl) {
+            const int t = w / p.splits;
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
             const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 924);
             c_wt += clock64() - c0w;
             if (tc::epi_any(!ok)) break;  // tcgen05.ld is warp-collective: all epilogue warps leave together
             tc::tc_fence_after();
+            const bool from_tmem = p.splits == 1;
+            if (!from_tmem) {
+                // split-K: this unit's raw accumulator rows -> its partial tile, then free TMEM
+                float* prow = p.part + ((size_t)w * NH_BM + quarter * 32 + lane) * BN;
+                const uint32_t ta = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+                for (int sl = half; sl < BN / 16; sl += 2) {
+                    uint32_t pr[16];
+                    tc::tmem_ld16_issue(ta + sl * 16, pr);
+                    tc::tmem_wait16(pr);
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4)
+                        __stcg(reinterpret_cast<float4*>(prow + sl * 16 + i),
+                               make_float4(__uint_as_float(pr[i]), __uint_as_float(pr[i + 1]),
+                                           __uint_as_float(pr[i + 2]), __uint_as_float(pr[i + 3])));
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);
+                // the last unit of the tile to arrive sums the partials in split order
+                __threadfence();
+                tc::epi_sync();
+                if (warp == 2 && lane == 0) {
+                    const int prev = atomicAdd(&p.tile_cnt[t], 1);
+                    last_unit = prev == p.splits - 1;
+                    if (last_unit) p.tile_cnt[t] = 0;  // ready for the next launch
+                }
+                tc::epi_sync();
+                if (!last_unit) continue;
+                __threadfence();
+            }
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
             const long long m = (long long)mt * NH_BM + quarter * 32 + lane;  // this lane's pixel
             const bool valid = m < p.npix;
@@ -272,8 +316,27 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
 #pragma unroll 1
             for (int sl = half; sl < BN / 16; sl += 2) {
                 const long long q0 = clock64();
-                tc::tmem_ld16_issue(taddr + sl * 16, vr);
-                tc::tmem_wait16(vr);
+                if (from_tmem) {
+                    tc::tmem_ld16_issue(taddr + sl * 16, vr);
+                    tc::tmem_wait16(vr);
+                } else {  // sum of the tile's partials, split 0 first
+                    float acc[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+                    const float* pb = p.part + ((size_t)t * p.splits * NH_BM + quarter * 32 + lane) * BN + sl * 16;
+                    for (int zz = 0; zz < p.splits; ++zz) {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 q4 = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)zz * NH_BM * BN + i));
+                            acc[i] = __fadd_rn(acc[i], q4.x);
+                            acc[i + 1] = __fadd_rn(acc[i + 1], q4.y);
+                            acc[i + 2] = __fadd_rn(acc[i + 2], q4.z);
+                            acc[i + 3] = __fadd_rn(acc[i + 3], q4.w);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) vr[i] = __float_as_uint(acc[i]);
+                }
                 const long long q1 = clock64();
                 c_ldw += q1 - q0;
                 float v[16];
@@ -364,6 +427,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                 }
             }
             c_st += clock64() - c0l;
+            if (!from_tmem) continue;  // the accumulator was released after the partial was written
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);  // this warp's TMEM reads are done
@@ -423,7 +487,7 @@ int nh_launch(tb_ctx* ctx, const NhwcMaps& maps, const NhwcParams& p) {
         TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
-    const int grid = std::min(p.tiles_total, ctx->sm_count);
+    const int grid = std::min(p.units, ctx->sm_count);
     k_conv_nhwc<BN, STAGES><<<grid, NH_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch("k_conv_nhwc");
 }
@@ -448,6 +512,47 @@ int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp) {
     k_pack_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)g.F, (int)g.C, (int)g.KH,
                                                                               (int)g.KW, (int)round_up(g.C, 32));
     return check_launch("k_pack_nhwc");
+}
+
+// Tile shape of one NHWC conv launch: filters per tile and K splits.
+struct NhShape {
+    int bn, splits;
+};
+
+std::mutex g_nh_mu;
+std::map<std::vector<int64_t>, NhShape> g_nh_tuned;  // measured at network set-up
+thread_local const NhShape* t_nh_pin = nullptr;    // the autotuner's candidate under test
+
+std::vector<int64_t> nh_key(int device, const ConvGeom& g, int64_t x_ps) {
+    return {device, g.B, g.C, g.H, g.W, g.F, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX, x_ps};
+}
+
+int64_t nh_ktiles(const ConvGeom& g) { return g.KH * g.KW * (round_up(g.C, 32) / NH_BK); }
+
+// split-K partial tiles of a shape (floats)
+int64_t nh_part_floats(const ConvGeom& g, const NhShape& sh) {
+    if (sh.splits <= 1) return 0;
+    const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, sh.bn);
+    return tiles * sh.splits * NH_BM * sh.bn;
+}
+
+constexpr int64_t NH_PART_CAP = (int64_t)1 << 26;  // 256 MiB of partial tiles at most
+
+// default shape: the widest tile that does not leave most of it empty, no split
+NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : 64, 1}; }
+
+NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
+    if (t_nh_pin) return *t_nh_pin;
+    if (const char* f = getenv("TB_NHWC_FORCE")) {  // test hook: "BN,SPLITS"
+        NhShape sh{256, 1};
+        if (sscanf(f, "%d,%d", &sh.bn, &sh.splits) >= 1 && (sh.bn == 64 || sh.bn == 128 || sh.bn == 256)) {
+            if (sh.splits < 1) sh.splits = 1;
+            return sh;
+        }
+    }
+    std::lock_guard<std::mutex> lk(g_nh_mu);
+    auto it = g_nh_tuned.find(nh_key(ctx->device, g, x_ps));
+    return it != g_nh_tuned.end() ? it->second : nh_default(g);
 }
 
 // x: NHWC with pixel stride x_ps (floats; x points at channel 0 of the conv's input);
@@ -476,8 +581,16 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "NHWC conv: cuTensorMapEncodeIm2col failed (%d)", (int)r);
     }
-    // tile width: the widest of 256 / 128 / 64 filters that does not leave most of a tile empty
-    const int bn = g.F > 128 ? 256 : g.F > 64 ? 128 : 64;
+    NhShape sh = nh_choose(ctx, g, x_ps);
+    const int bn = sh.bn;
+    const int64_t ktiles = nh_ktiles(g);
+    const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
+    if (sh.splits > ktiles) sh.splits = (int)ktiles;
+    const int kps = (int)ceil_div(ktiles, sh.splits);
+    sh.splits = (int)ceil_div(ktiles, kps);  // no empty split
+    if (sh.splits > 1 && (tiles > ctx->tile_cnt_len || nh_part_floats(g, sh) > NH_PART_CAP ||
+                          (size_t)nh_part_floats(g, sh) * sizeof(float) > ctx->ws_bytes))
+        sh.splits = 1;  // no room for the partial tiles or counters: one unit per tile
     {
         const uint64_t dims[2] = {(uint64_t)(g.KH * g.KW * Cp), (uint64_t)g.F};
         const uint64_t strides[1] = {(uint64_t)(g.KH * g.KW * Cp * 4)};
@@ -505,6 +618,11 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     p.ktiles = (int)(g.KH * g.KW * p.csteps);
     p.tiles_n = (int)ceil_div(g.F, bn);
     p.tiles_total = (int)(ceil_div(p.npix, NH_BM) * p.tiles_n);
+    p.splits = sh.splits;
+    p.kt_per_split = sh.splits > 1 ? (int)ceil_div(ktiles, sh.splits) : (int)ktiles;
+    p.units = p.tiles_total * p.splits;
+    p.part = sh.splits > 1 ? reinterpret_cast<float*>(ctx->ws) : nullptr;
+    p.tile_cnt = ctx->tile_cnt;
     p.out_nchw = y_ps > 0 ? 0 : 1;
     p.y_ps = (int)y_ps;
     p.r_ps = (int)r_ps;
@@ -514,6 +632,66 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     if (bn == 256) return nh_launch<256, 4>(ctx, maps, p);
     if (bn == 128) return nh_launch<128, 6>(ctx, maps, p);
     return nh_launch<64, 8>(ctx, maps, p);
+}
+
+// Workspace the NHWC conv of this geometry needs (split-K partials of its tuned shape).
+int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
+    return nh_part_floats(g, nh_choose(ctx, g, x_ps));
+}
+
+// Time the tile shapes (filters per tile x K splits) of this geometry on the given buffers
+// (bias and residual off) and keep the fastest for later launches. Blocks; grows the workspace.
+int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp, float* y,
+                       int64_t y_ps) {
+    if (g.B == 0 || !conv_nhwc_supported(g, x_ps)) return TB_OK;
+    const int64_t ktiles = nh_ktiles(g);
+    std::vector<NhShape> cands;
+    for (int bn : {64, 128, 256}) {
+        if (bn > 64 && bn / 2 >= g.F) continue;  // a tile at least half full
+        const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
+        for (int sp : {1, 2, 3, 4, 6, 8}) {
+            if (sp > 1 && (ktiles < 4 * sp || tiles > ctx->tile_cnt_len || tiles * sp > 4 * (int64_t)ctx->sm_count))
+                continue;
+            NhShape sh{bn, sp};
+            if (nh_part_floats(g, sh) > NH_PART_CAP) continue;
+            cands.push_back(sh);
+        }
+    }
+    if (cands.empty()) return TB_OK;
+    int64_t ws = 0;
+    for (const NhShape& c : cands) ws = std::max(ws, nh_part_floats(g, c));
+    int r = ensure_workspace(ctx, (size_t)std::max<int64_t>(ws, 1) * sizeof(float));
+    if (r != TB_OK) return r;
+    cudaEvent_t e0, e1;
+    TB_CHECK_CUDA(cudaEventCreate(&e0));
+    TB_CHECK_CUDA(cudaEventCreate(&e1));
+    float best_ms = 1e30f;
+    NhShape best = cands[0];
+    for (const NhShape& c : cands) {
+        t_nh_pin = &c;
+        r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr);
+        cudaEventRecord(e0, ctx->stream);
+        for (int rep = 0; rep < 3 && r == TB_OK; ++rep)
+            r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr);
+        cudaEventRecord(e1, ctx->stream);
+        t_nh_pin = nullptr;
+        cudaError_t e = cudaEventSynchronize(e1);
+        if (r != TB_OK) break;
+        if (e != cudaSuccess) { r = cuda_fail(e, "NHWC conv autotune"); break; }
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (getenv("TB_AUTOTUNE_VERBOSE"))
+            fprintf(stderr, "nhwc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d splits %d: %.4f ms\n",
+                    (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
+                    (long long)g.B, c.bn, c.splits, ms / 3);
+        if (ms < best_ms) best_ms = ms, best = c;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (r != TB_OK) return r;
+    std::lock_guard<std::mutex> lk(g_nh_mu);
+    g_nh_tuned[nh_key(ctx->device, g, x_ps)] = best;
+    return TB_OK;
 }
 
 }  // namespace tbi

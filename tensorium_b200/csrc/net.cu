@@ -809,6 +809,26 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     // 4. measure the tile / split choices of every conv geometry on the real buffers
     //    (TB_AUTOTUNE=0 keeps the cost model)
     const char* at = getenv("TB_AUTOTUNE");
+    if (net->nhwc) {  // NHWC plan: tile width and K splits of every conv, measured on its buffers
+        for (int64_t i = 0; i < n; ++i) {
+            Layer& L = *net->layers[i];
+            if (L.type != TB_LAYER_CONV) continue;
+            tb_conv_desc d;
+            desc_of(net, L, &d);
+            const Layer& T = *net->layers[L.target];
+            d.out_batch_stride = T.out.bs;
+            ConvGeom g;
+            r = conv_geom(&d, &g);
+            if (r != TB_OK) return r;
+            if (i == 0 && net->first_im2col) g = first_as_1x1(g);
+            const View in = input_view(net, i, nullptr);
+            if (!(at && at[0] == '0')) {
+                r = conv_nhwc_autotune(net->ctx, g, in.ptr, in.ps, L.d_wp, T.out.ptr, T.out.ps);
+                if (r != TB_OK) return r;
+            }
+            ws_floats = std::max(ws_floats, conv_nhwc_ws_floats(net->ctx, g, in.ps));
+        }
+    }
     if (!(at && at[0] == '0') && !net->nhwc) {
         for (int64_t i = 0; i < n; ++i) {
             Layer& L = *net->layers[i];

@@ -106,3 +106,24 @@ def test_nhwc_rejects_what_it_cannot_take(ctx):
     x = torch.zeros(1024, device=ctx.torch_device)
     rc = lib.tb_conv2d_fwd_nhwc(ctx.handle, C.byref(d), ptr(x), 8, ptr(x), None, None, 0, ptr(x), 8)
     assert rc < 0
+
+
+@pytest.mark.parametrize("shape", ["64,1", "128,1", "256,1", "256,3", "128,2", "64,4", "256,8"])
+def test_nhwc_every_tile_shape(ctx, shape, monkeypatch):
+    """Each (filters per tile, K splits) shape, pinned through the TB_NHWC_FORCE test hook; split
+    units are summed by the last arriving unit in split order, so two runs are identical."""
+    monkeypatch.setenv("TB_NHWC_FORCE", shape)
+    ctx.reserve(256 << 20)  # room for the split-K partial tiles
+    rng = np.random.default_rng(31)
+    for (B, Cc, H, F, k, s, p) in [(2, 128, 26, 256, 3, 1, 1), (8, 512, 13, 160, 3, 1, 1), (2, 64, 52, 96, 1, 1, 0),
+                                   (2, 64, 40, 72, 3, 2, 1)]:
+        x = rng.uniform(0, 1, (B, Cc, H, H)).astype(np.float32)
+        w = (rng.standard_normal((F, Cc * k * k)) * np.sqrt(2.0 / (Cc * k * k))).astype(np.float32)
+        b = rng.standard_normal(F).astype(np.float32) * 0.1
+        r = rng.standard_normal((B, F, (H + 2 * p - k) // s + 1, (H + 2 * p - k) // s + 1)).astype(np.float32)
+        y1 = run_nhwc(ctx, x, w, b, F, k, s, p, 9, residual=r)
+        y2 = run_nhwc(ctx, x, w, b, F, k, s, p, 9, residual=r)
+        assert np.array_equal(y1, y2), (shape, Cc)
+        ref = O.shortcut(O.conv2d(x, w, b, F, k, s, p, 9), r)
+        e = rel_l2_maps(y1, ref, B * F)
+        assert 0.0 < e <= TF32_TOL, (shape, Cc, e)
