@@ -41,7 +41,7 @@ METRIC = "YOLOv3-416 images/sec (FP32 path)"
 METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
 MATH_MODES = {"fp32": 0, "tf32": 1}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
-PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "conv_tc_yolov3_b8.json"
+PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "k_conv_nhwc_yolov3_b8.json"
 
 
 def dist_env():
@@ -352,13 +352,14 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
     out = {"metric": METRIC_TF32, "value": world * B * args.steps / (ms / 1e3), "unit": "images/s",
            "ms_per_step": ms / args.steps, "dtype": "tf32 operands rounded to nearest, fp32 accumulate",
            "gpu_launches": int(launches * args.steps),
-           "roofline": {"bound": "tensor", "kernel": "k_conv_tc (tcgen05 TF32) + tap-replica repack; layer 0 on conv_fp32_kernel",
+           "roofline": {"bound": "tensor", "kernel": "k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) + "
+                                                     "input / receptive-field conversion and NHWC upsample",
                         "achieved": achieved, "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
                         "peak_source": f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)",
                         "conv_ms_per_forward": conv_ms,
                         "traffic": (json.loads(PROFILE_SUMMARY_TF32.read_text()).get("dram_bytes_per_forward")
                                     if PROFILE_SUMMARY_TF32.exists() else None),
-                        "traffic_unit": "bytes per forward (ncu, summed over conv and repack launches)"},
+                        "traffic_unit": "bytes per forward (ncu, summed over every launch of one forward)"},
            "head_rel_l2_vs_fp32_path": errs, "heads": list(HEADS)}
     net.close()
     return out
@@ -517,6 +518,26 @@ def run_layer_mode(args):
     x = torch.rand((args.batch, c, h, w), device=ctx.torch_device)
     st = TNNetState(x)
     mm = MATH_MODES[args.math]
+    if args.nhwc:  # the NHWC tensor-core kernel (TF32) the TF32 network runs, through its C ABI
+        import ctypes as C
+        from tensorium_b200._lib import ConvDesc, check, lib
+        from tensorium_b200.context import ptr
+        oc, oh, ow = shapes[i]
+        d = ConvDesc(args.batch, c, h, w, s["filters"], s["size"], s["size"], s["stride"], s["stride"], s["pad"],
+                     s["pad"], 1, 1, s["activation"], 0, 0, 0)
+        cnt = C.c_int64()
+        check(lib.tb_conv_nhwc_packed_count(C.byref(d), C.byref(cnt)))
+        wd = torch.from_numpy(np.ascontiguousarray(s["weights"])).to(ctx.torch_device)
+        wp = torch.empty(cnt.value, device=ctx.torch_device)
+        check(lib.tb_conv_pack_weights_nhwc(ctx.handle, C.byref(d), ptr(wd), ptr(wp)))
+        xn = torch.rand((args.batch, h, w, c), device=ctx.torch_device)
+        yn = torch.empty((args.batch, oh, ow, oc), device=ctx.torch_device)
+
+        class _Nhwc:
+            @staticmethod
+            def forward(_st, math_mode=None):
+                check(lib.tb_conv2d_fwd_nhwc(ctx.handle, C.byref(d), ptr(xn), c, ptr(wp), None, None, 0, ptr(yn), oc))
+        L = _Nhwc
     for _ in range(args.warmup):
         L.forward(st, math_mode=mm)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -533,7 +554,7 @@ def run_layer_mode(args):
     ms = e0.elapsed_time(e1) / args.steps
     oc, oh, ow = shapes[i]
     flops = 2.0 * oc * oh * ow * c * s["size"] ** 2 * args.batch
-    print(json.dumps({"layer": i, "math": args.math, "shape": f"{c}x{h}x{w} -> {oc}x{oh}x{ow} k{s['size']} s{s['stride']}",
+    print(json.dumps({"layer": i, "math": args.math + (" nhwc" if args.nhwc else ""), "shape": f"{c}x{h}x{w} -> {oc}x{oh}x{ow} k{s['size']} s{s['stride']}",
                       "batch": args.batch, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
 
 
@@ -551,6 +572,7 @@ def main():
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
     ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
                     help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")
+    ap.add_argument("--nhwc", action="store_true", help="with --layer and --math tf32: the NHWC tensor-core kernel")
     ap.add_argument("--profile-window", action="store_true",
                     help="eager forwards inside cudaProfilerStart/Stop (for ncu --profile-from-start off); "
                          "the printed numbers are then not bench values")
