@@ -539,13 +539,13 @@ int64_t nh_part_floats(const ConvGeom& g, const NhShape& sh) {
 constexpr int64_t NH_PART_CAP = (int64_t)1 << 26;  // 256 MiB of partial tiles at most
 
 // default shape: the widest tile that does not leave most of it empty, no split
-NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : 64, 1}; }
+NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : g.F > 32 ? 64 : 32, 1}; }
 
 NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
     if (t_nh_pin) return *t_nh_pin;
     if (const char* f = getenv("TB_NHWC_FORCE")) {  // test hook: "BN,SPLITS"
         NhShape sh{256, 1};
-        if (sscanf(f, "%d,%d", &sh.bn, &sh.splits) >= 1 && (sh.bn == 64 || sh.bn == 128 || sh.bn == 256)) {
+        if (sscanf(f, "%d,%d", &sh.bn, &sh.splits) >= 1 && (sh.bn == 32 || sh.bn == 64 || sh.bn == 128 || sh.bn == 256)) {
             if (sh.splits < 1) sh.splits = 1;
             return sh;
         }
@@ -631,6 +631,7 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     p.yolo_classes = yolo_classes;
     if (bn == 256) return nh_launch<256, 4>(ctx, maps, p);
     if (bn == 128) return nh_launch<128, 6>(ctx, maps, p);
+    if (bn == 32) return nh_launch<32, 8>(ctx, maps, p);
     return nh_launch<64, 8>(ctx, maps, p);
 }
 
@@ -646,8 +647,8 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
     if (g.B == 0 || !conv_nhwc_supported(g, x_ps)) return TB_OK;
     const int64_t ktiles = nh_ktiles(g);
     std::vector<NhShape> cands;
-    for (int bn : {64, 128, 256}) {
-        if (bn > 64 && bn / 2 >= g.F) continue;  // a tile at least half full
+    for (int bn : {32, 64, 128, 256}) {
+        if (bn > 32 && bn / 2 >= g.F) continue;  // a tile at least half full
         const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
         for (int sp : {1, 2, 3, 4, 6, 8}) {
             if (sp > 1 && (ktiles < 4 * sp || tiles > ctx->tile_cnt_len || tiles * sp > 4 * (int64_t)ctx->sm_count))

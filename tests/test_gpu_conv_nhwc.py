@@ -108,7 +108,7 @@ def test_nhwc_rejects_what_it_cannot_take(ctx):
     assert rc < 0
 
 
-@pytest.mark.parametrize("shape", ["64,1", "128,1", "256,1", "256,3", "128,2", "64,4", "256,8"])
+@pytest.mark.parametrize("shape", ["32,1", "32,3", "64,1", "128,1", "256,1", "256,3", "128,2", "64,4", "256,8"])
 def test_nhwc_every_tile_shape(ctx, shape, monkeypatch):
     """Each (filters per tile, K splits) shape, pinned through the TB_NHWC_FORCE test hook; split
     units are summed by the last arriving unit in split order, so two runs are identical."""
