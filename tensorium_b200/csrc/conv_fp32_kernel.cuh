@@ -56,15 +56,26 @@ __device__ __forceinline__ ColQuad decode_quad(const ConvParams& p, long long nb
     return q;
 }
 
+// The epilogue of one value. simple: no unfused batchnorm, no yolo, leaky or linear -- then the
+// row's bias bm (0 without bias) and the flags come from registers the caller loaded once,
+// instead of re-reading the kernel parameters for every value.
+__device__ __forceinline__ float conv_epi_value(float v, int m, const ConvParams& p, bool simple, bool has_bias,
+                                                bool leaky, float bm) {
+    if (!simple) return conv_epilogue(v, m, p);
+    if (has_bias) v = __fadd_rn(v, bm);
+    return (leaky && v < 0.f) ? (float)(0.1 * (double)v) : v;  // activate_array's leaky
+}
+
 // Store the 4 outputs of column quad q in row m after the epilogue.
-__device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const ColQuad& q, const float* v) {
+__device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const ColQuad& q, const float* v,
+                                            bool simple, bool has_bias, bool leaky, float bm) {
     if (q.nvalid == 0) return;
     if (p.vec_out && q.nvalid == 4) {  // OHW % 4 == 0: the quad lies in one image, 16-byte aligned
         float4 o;
-        o.x = conv_epilogue(v[0], m, p);
-        o.y = conv_epilogue(v[1], m, p);
-        o.z = conv_epilogue(v[2], m, p);
-        o.w = conv_epilogue(v[3], m, p);
+        o.x = conv_epi_value(v[0], m, p, simple, has_bias, leaky, bm);
+        o.y = conv_epi_value(v[1], m, p, simple, has_bias, leaky, bm);
+        o.z = conv_epi_value(v[2], m, p, simple, has_bias, leaky, bm);
+        o.w = conv_epi_value(v[3], m, p, simple, has_bias, leaky, bm);
         const long long off = (long long)m * p.OHW + q.pix;
         if (p.res) {
             float4 r = *reinterpret_cast<const float4*>(p.res + q.b * p.r_bs + off);
@@ -82,7 +93,7 @@ __device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const Co
         if (k < q.nvalid) {
             while (pix >= p.OHW) { pix -= p.OHW; ++b; }
             const long long off = (long long)m * p.OHW + pix;
-            float o = conv_epilogue(v[k], m, p);
+            float o = conv_epi_value(v[k], m, p, simple, has_bias, leaky, bm);
             if (p.res) o = __fadd_rn(o, p.res[b * p.r_bs + off]);
             p.y[b * p.y_bs + off] = o;
             ++pix;
@@ -271,6 +282,9 @@ conv_fp32_kernel(const ConvParams p) {
 
     // ---- epilogue ----
     const ColQuad cq[2] = {decode_quad(p, n0 + tx * TN2), decode_quad(p, n0 + BN / 2 + tx * TN2)};
+    const bool simple = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
+    const bool has_bias = p.bias != nullptr, leaky = p.act == TB_ACT_LEAKY;
+    const float* __restrict__ biasp = p.bias;
     if (p.splits > 1) {
         // split-K: publish this split's partial tile, then the last CTA to arrive on the tile
         // sums all partials in split order 0..S-1 (deterministic, whatever the arrival order)
@@ -330,7 +344,7 @@ conv_fp32_kernel(const ConvParams p) {
                             if (nb + q < p.Ntot) v[q] = __fadd_rn(v[q], __ldcg(src + z * plane + q));
                     }
                 }
-                conv_store4(p, m, cq[g], v);
+                conv_store4(p, m, cq[g], v, simple, has_bias, leaky, has_bias ? __ldg(biasp + m) : 0.f);
             }
         }
         return;
@@ -339,11 +353,12 @@ conv_fp32_kernel(const ConvParams p) {
     for (int i = 0; i < TM; ++i) {
         int m = m0 + (i < TM2 ? ty * TM2 + i : BM / 2 + ty * TM2 + (i - TM2));
         if (m >= p.F) continue;
+        const float bm = has_bias ? __ldg(biasp + m) : 0.f;
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
             long long nb = n0 + g * (BN / 2) + tx * TN2;
             if (nb >= p.Ntot) continue;
-            conv_store4(p, m, cq[g], &acc[i][g * 4]);
+            conv_store4(p, m, cq[g], &acc[i][g * 4], simple, has_bias, leaky, bm);
         }
     }
 }
