@@ -143,4 +143,14 @@ __device__ __forceinline__ float conv_epilogue(float v, int m, const ConvParams&
     return v;
 }
 
+// The epilogue of one value. simple: no unfused batchnorm, no yolo, leaky or linear -- then the
+// row's bias bm (0 without bias) and the flags come from registers the caller loaded once,
+// instead of re-reading the kernel parameters for every value.
+__device__ __forceinline__ float conv_epi_value(float v, int m, const ConvParams& p, bool simple, bool has_bias,
+                                                bool leaky, float bm) {
+    if (!simple) return conv_epilogue(v, m, p);
+    if (has_bias) v = __fadd_rn(v, bm);
+    return (leaky && v < 0.f) ? (float)(0.1 * (double)v) : v;  // activate_array's leaky
+}
+
 }  // namespace tbi

@@ -56,16 +56,6 @@ __device__ __forceinline__ ColQuad decode_quad(const ConvParams& p, long long nb
     return q;
 }
 
-// The epilogue of one value. simple: no unfused batchnorm, no yolo, leaky or linear -- then the
-// row's bias bm (0 without bias) and the flags come from registers the caller loaded once,
-// instead of re-reading the kernel parameters for every value.
-__device__ __forceinline__ float conv_epi_value(float v, int m, const ConvParams& p, bool simple, bool has_bias,
-                                                bool leaky, float bm) {
-    if (!simple) return conv_epilogue(v, m, p);
-    if (has_bias) v = __fadd_rn(v, bm);
-    return (leaky && v < 0.f) ? (float)(0.1 * (double)v) : v;  // activate_array's leaky
-}
-
 // Store the 4 outputs of column quad q in row m after the epilogue.
 __device__ __forceinline__ void conv_store4(const ConvParams& p, int m, const ColQuad& q, const float* v,
                                             bool simple, bool has_bias, bool leaky, float bm) {

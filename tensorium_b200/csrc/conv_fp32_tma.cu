@@ -162,18 +162,21 @@ __global__ void __launch_bounds__(FT_THREADS, 2)
         cq[g].ox = ox;
         cq[g].nvalid = (ok && b < q.B && qq < q.OHWp) ? max(0, min(4, q.OW - ox)) : 0;
     }
+    const bool simple = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
+    const bool has_bias = p.bias != nullptr, leaky = p.act == TB_ACT_LEAKY;
     auto store4 = [&](int m, int g, const float* v) {
         const Quad& c = cq[g];
         if (c.nvalid == 0) return;
+        const float bm = has_bias ? __ldg(p.bias + m) : 0.f;
         const long long off = (long long)m * p.OHW + (long long)c.oy * q.OW + c.ox;
         float* yb = p.y + c.b * p.y_bs;
         const float* rb = p.res ? p.res + c.b * p.r_bs : nullptr;
         if (p.vec_out && c.nvalid == 4) {
             float4 o;
-            o.x = conv_epilogue(v[0], m, p);
-            o.y = conv_epilogue(v[1], m, p);
-            o.z = conv_epilogue(v[2], m, p);
-            o.w = conv_epilogue(v[3], m, p);
+            o.x = conv_epi_value(v[0], m, p, simple, has_bias, leaky, bm);
+            o.y = conv_epi_value(v[1], m, p, simple, has_bias, leaky, bm);
+            o.z = conv_epi_value(v[2], m, p, simple, has_bias, leaky, bm);
+            o.w = conv_epi_value(v[3], m, p, simple, has_bias, leaky, bm);
             if (rb) {
                 const float4 r = *reinterpret_cast<const float4*>(rb + off);
                 o.x = __fadd_rn(o.x, r.x);
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(FT_THREADS, 2)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             if (e < c.nvalid) {
-                float o = conv_epilogue(v[e], m, p);
+                float o = conv_epi_value(v[e], m, p, simple, has_bias, leaky, bm);
                 if (rb) o = __fadd_rn(o, rb[off + e]);
                 yb[off + e] = o;
             }
