@@ -9,7 +9,8 @@ collective (weak scaling).  Timing: W untimed steps, then K steps between a barr
 synchronize on both sides, CUDA events on the launching stream, max over ranks.
 
   value       images/s over all ranks, inputs resident in HBM (graph replay of the forward)
-  e2e         the same metric through TNNet.predict's path: pinned-host input -> H2D, forward,
+  e2e         the same metric through StreamPredictor (TNNet.predict for a stream of batches):
+              pinned-host input -> H2D, forward,
               D2H of the three yolo heads, every step
   roofline    the FP32 CUDA-core conv kernels: conv FLOPs of a forward / their summed device
               time (per-layer CUDA events), against the FFMA rate measured on this GPU
@@ -212,31 +213,28 @@ def run_ours(args):
     clocks = clk.summary()
     value = world * B * args.steps / (ms / 1e3)
 
-    # ---- end to end: pinned host in, heads out, every step ----
+    # ---- end to end: pinned host in, heads out, every step (StreamPredictor: the host copies of
+    #      step i+1 / i-1 overlap the forward of step i) ----
+    from tensorium_b200.net import StreamPredictor
     h_in = torch.from_numpy(x_host).pin_memory()
     h_outs = [torch.empty(net.output(h).shape, dtype=torch.float32).pin_memory() for h in HEADS]
-    d_in = torch.empty_like(x)
-    net.forward(d_in)  # captures the graph for this input buffer
-
-    def e2e_step():
-        d_in.copy_(h_in, non_blocking=True)
-        net.forward(d_in)
-        for h, o in zip(HEADS, h_outs):
-            o.copy_(net.output(h), non_blocking=True)
-
+    sp = StreamPredictor(net, HEADS)
     for _ in range(max(args.warmup, 1)):
-        e2e_step()
+        sp.submit(h_in, h_outs)
+    sp.wait()
     barrier()
     e0.record(stream)
     for _ in range(args.steps):
-        e2e_step()
+        sp.submit(h_in, h_outs)
+    stream.wait_stream(sp.copy)
     e1.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
     e2e = {"value": world * B * args.steps / (ms_e2e / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": int(h_in.numel() * 4),
            "d2h_bytes_per_step": int(sum(o.numel() * 4 for o in h_outs)),
-           "path": "pinned host -> H2D -> TNNet.forward (graph) -> D2H of the 3 yolo heads"}
+           "path": ("StreamPredictor: pinned host -> H2D (copy stream) -> TNNet.forward (graph) -> D2H of the "
+                    "3 yolo heads (copy stream), consecutive steps overlapped through double-buffered staging")}
 
     # ---- roofline of the conv kernels (per-layer CUDA events, eager forward) ----
     prof = np.zeros(len(specs))
@@ -256,14 +254,16 @@ def run_ours(args):
         fma = __import__("ctypes").c_double()
         from tensorium_b200._lib import check, lib
         check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
-        peak, bound, kernel = fma.value, "fp32", "conv_fp32_kernel (+ split-K fixup), all 75 convs of a forward"
+        peak, bound, kernel = fma.value, "fp32", ("conv_fp32_kernel (+ split-K fix-up) for 74 convs and "
+                                                  "k_conv_direct for the first, all 75 convs of a forward")
         peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
                        "and bf16 tensor peaks only")
     else:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         bf16 = peaks.get("bf16_tflops", 1590.0)
         peak, bound = bf16 / 2, "tensor"
-        kernel = "k_conv_tc (tcgen05 TF32) + tap-replica repack for 69 convs, conv_fp32_kernel for the rest"
+        kernel = ("k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) for all 75 convs "
+                  "+ the first layer's receptive-field conversion")
         peak_source = (f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)"
                        if "bf16_tflops" in peaks else "TF32 dense = half the fallback bf16 1590 TFLOP/s")
     roofline = {"bound": bound, "kernel": kernel,

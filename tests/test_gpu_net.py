@@ -132,3 +132,23 @@ def test_unfused_batchnorm_network(ctx):
     ref = O.run_network(specs, x, fuse_batchnorm=False, keep=[7])
     net = TNNet(ctx, specs, 4, (3, 32, 32), fuse_batchnorm=False)
     assert worst_map_err(net.predict(x, layers=[7])[0], ref[7], 4 * 512) <= FP32_TOL
+
+
+def test_stream_predictor_matches_predict(ctx):
+    """StreamPredictor (uploads / downloads overlapped with the forward) returns, for every
+    submitted batch, what predict returns for it."""
+    from tensorium_b200.net import StreamPredictor
+    specs = synth.cifar_specs()
+    net = TNNet(ctx, specs, 16, (3, 32, 32))
+    batches = [synth.input_images(20 + i, "cifar", 16, (3, 32, 32)) for i in range(5)]
+    want = [net.predict(b, layers=[9, 11]) for b in batches]
+    sp = StreamPredictor(net, [9, 11])
+    h_ins = [torch.from_numpy(b).pin_memory() for b in batches]
+    h_outs = [[torch.empty(net.output(l).shape).pin_memory() for l in (9, 11)] for _ in batches]
+    for hi, ho in zip(h_ins, h_outs):
+        sp.submit(hi, ho)
+    sp.wait()
+    for w, ho in zip(want, h_outs):
+        for a, b in zip(w, ho):
+            assert np.array_equal(a, b.numpy())
+    net.close()
