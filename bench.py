@@ -254,8 +254,8 @@ def run_ours(args):
         fma = __import__("ctypes").c_double()
         from tensorium_b200._lib import check, lib
         check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
-        peak, bound, kernel = fma.value, "fp32", ("conv_fp32_kernel (+ split-K fix-up) for 74 convs and "
-                                                  "k_conv_direct for the first, all 75 convs of a forward")
+        peak, bound, kernel = fma.value, "fp32", ("conv_fp32_kernel / k_conv_fp32_tma (+ split-K fix-up, "
+                                                  "tap replicas) for 74 convs and k_conv_direct for the first")
         peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
                        "and bf16 tensor peaks only")
     else:
