@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     } else {
         // ---------------- epilogue (warps 2-9) ----------------
         const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31
-        const int half = (warp - 2) >> 2;  // 16-filter slabs half, half + 2, ...
+        const int half = (warp - 2) >> 2;  // which half of the tile's filters this warp takes
         // this warp's two staging slabs (32 pixel rows x 64 bytes each, 64-byte swizzle: the
         // 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3), which the TMA store undoes)
         const unsigned stg0 = sbase + STAGES * STAGE_BYTES + (warp - 2) * 2 * 2048;
@@ -312,37 +312,14 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             const float* rp = p.res ? p.res + (valid ? m : 0) * p.r_ps : nullptr;
             const uint32_t taddr = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
             const long long c0l = clock64();
-            uint32_t vr[16];
-#pragma unroll 1
-            for (int sl = half; sl < BN / 16; sl += 2) {
-                const long long q0 = clock64();
-                if (from_tmem) {
-                    tc::tmem_ld16_issue(taddr + sl * 16, vr);
-                    tc::tmem_wait16(vr);
-                } else {  // sum of the tile's partials, split 0 first
-                    float acc[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-                    const float* pb = p.part + ((size_t)t * p.splits * NH_BM + quarter * 32 + lane) * BN + sl * 16;
-                    for (int zz = 0; zz < p.splits; ++zz) {
-#pragma unroll
-                        for (int i = 0; i < 16; i += 4) {
-                            const float4 q4 = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)zz * NH_BM * BN + i));
-                            acc[i] = __fadd_rn(acc[i], q4.x);
-                            acc[i + 1] = __fadd_rn(acc[i + 1], q4.y);
-                            acc[i + 2] = __fadd_rn(acc[i + 2], q4.z);
-                            acc[i + 3] = __fadd_rn(acc[i + 3], q4.w);
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) vr[i] = __float_as_uint(acc[i]);
-                }
-                const long long q1 = clock64();
-                c_ldw += q1 - q0;
+            // this warp's slabs are contiguous and taken two at a time through one 32-column TMEM
+            // load: one load latency per pair of slabs instead of one per slab
+            constexpr int PER = BN / 32;  // slabs per warp (the two warps of a lane window split the tile)
+            const int s_begin = half * PER;
+            auto process = [&](int sl, const float* vin) {
                 float v[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(vr[i]);
-                // the next slab's TMEM load runs while this slab is finished and stored
+                for (int i = 0; i < 16; ++i) v[i] = vin[i];
                 const int fb = nt * BN + sl * 16;
                 const bool full = fb + 16 <= p.F;
                 float rv[16];
@@ -391,8 +368,6 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         v[i] = tc::to_tf32_rna(o);
                     }
                 }
-                const long long q2 = clock64();
-                c_math += q2 - q1;
                 if (p.tma_out) {
                     // stage the slab, then one lane stores it as a 16 x 32 box (the map clips
                     // filters >= F and pixels past the end)
@@ -425,6 +400,43 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                             if (fb + i < p.F) yp[fb + i] = v[i];
                     }
                 }
+            };
+            // the tile's accumulator columns [c0, c0 + n): from TMEM, or the sum of the split-K
+            // partials in split order
+            auto fetch = [&](int c0, float* out, int n) {
+                if (from_tmem) {
+                    if (n == 32) tc::tmem_ld32(taddr + c0, out);
+                    else tc::tmem_ld16(taddr + c0, out);
+                    return;
+                }
+                for (int i = 0; i < n; ++i) out[i] = 0.f;
+                const float* pb = p.part + ((size_t)t * p.splits * NH_BM + quarter * 32 + lane) * BN + c0;
+                for (int zz = 0; zz < p.splits; ++zz) {
+                    for (int i = 0; i < n; i += 4) {
+                        const float4 q4 = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)zz * NH_BM * BN + i));
+                        out[i] = __fadd_rn(out[i], q4.x);
+                        out[i + 1] = __fadd_rn(out[i + 1], q4.y);
+                        out[i + 2] = __fadd_rn(out[i + 2], q4.z);
+                        out[i + 3] = __fadd_rn(out[i + 3], q4.w);
+                    }
+                }
+            };
+            if constexpr (PER >= 2) {
+#pragma unroll 1
+                for (int sl = s_begin; sl < s_begin + PER; sl += 2) {
+                    float vv[32];
+                    const long long q0 = clock64();
+                    fetch(sl * 16, vv, 32);
+                    c_ldw += clock64() - q0;
+                    process(sl, vv);
+                    process(sl + 1, vv + 16);
+                }
+            } else {
+                float vv[16];
+                const long long q0 = clock64();
+                fetch(s_begin * 16, vv, 16);
+                c_ldw += clock64() - q0;
+                process(s_begin, vv);
             }
             c_st += clock64() - c0l;
             if (!from_tmem) continue;  // the accumulator was released after the partial was written
