@@ -226,15 +226,15 @@ def run_ours(args):
     e0.record(stream)
     for _ in range(args.steps):
         sp.submit(h_in, h_outs)
-    stream.wait_stream(sp.copy)
+    stream.wait_stream(sp.download)
     e1.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
     e2e = {"value": world * B * args.steps / (ms_e2e / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": int(h_in.numel() * 4),
            "d2h_bytes_per_step": int(sum(o.numel() * 4 for o in h_outs)),
-           "path": ("StreamPredictor: pinned host -> H2D (copy stream) -> TNNet.forward (graph) -> D2H of the "
-                    "3 yolo heads (copy stream), consecutive steps overlapped through double-buffered staging")}
+           "path": ("StreamPredictor: pinned host -> H2D (upload stream) -> TNNet.forward (graph) -> D2H of the "
+                    "3 yolo heads (download stream), consecutive steps overlapped through double-buffered staging")}
 
     # ---- roofline of the conv kernels (per-layer CUDA events, eager forward) ----
     prof = np.zeros(len(specs))

@@ -269,9 +269,10 @@ class StreamPredictor:
     """TNNet.predict for a stream of batches, with the host copies overlapped with the forward.
 
     Each ``submit(h_in, h_outs)`` schedules, for one batch: the host-to-device copy of ``h_in``
-    (pinned) on a copy stream, the forward (CUDA graph) on the compute stream once the copy has
+    (pinned) on an upload stream, the forward (CUDA graph) on the compute stream once the copy has
     landed, on-device copies of the requested outputs into one of two staging sets, and their
-    device-to-host copies into ``h_outs`` (pinned) on the copy stream. With two input and two output
+    device-to-host copies into ``h_outs`` (pinned) on a download stream (a separate stream, so
+    that an upload never queues behind a download that waits for the previous forward). With two input and two output
     staging buffers, batch i+1's upload and batch i-1's download run while batch i computes.
     ``wait()`` blocks until every submitted batch has landed in its host buffers. The forward sees a
     fixed input buffer (one graph); each batch reaches it by a device-to-device copy.
@@ -287,7 +288,8 @@ class StreamPredictor:
         self.d_out = [[torch.empty(net.output(l).shape, dtype=torch.float32, device=dev) for l in self.layers]
                       for _ in range(2)]
         self.compute = torch.cuda.current_stream(dev)
-        self.copy = torch.cuda.Stream(device=dev)
+        self.upload = torch.cuda.Stream(device=dev)
+        self.download = torch.cuda.Stream(device=dev)
         self.ev_h2d = [torch.cuda.Event() for _ in range(2)]
         self.ev_in_free = [torch.cuda.Event() for _ in range(2)]
         self.ev_out_ready = [torch.cuda.Event() for _ in range(2)]
@@ -299,11 +301,11 @@ class StreamPredictor:
     def submit(self, h_in: torch.Tensor, h_outs) -> None:
         k = self.i & 1
         self.i += 1
-        with torch.cuda.stream(self.copy):
+        with torch.cuda.stream(self.upload):
             if self.used[k]:
-                self.copy.wait_event(self.ev_in_free[k])
+                self.upload.wait_event(self.ev_in_free[k])
             self.d_in[k].copy_(h_in, non_blocking=True)
-            self.ev_h2d[k].record(self.copy)
+            self.ev_h2d[k].record(self.upload)
         self.compute.wait_event(self.ev_h2d[k])
         self.x.copy_(self.d_in[k])
         self.ev_in_free[k].record(self.compute)
@@ -313,16 +315,17 @@ class StreamPredictor:
         for l, d in zip(self.layers, self.d_out[k]):
             d.copy_(self.net.output(l))
         self.ev_out_ready[k].record(self.compute)
-        with torch.cuda.stream(self.copy):
-            self.copy.wait_event(self.ev_out_ready[k])
+        with torch.cuda.stream(self.download):
+            self.download.wait_event(self.ev_out_ready[k])
             for o, d in zip(h_outs, self.d_out[k]):
                 o.copy_(d, non_blocking=True)
-            self.ev_out_free[k].record(self.copy)
+            self.ev_out_free[k].record(self.download)
         self.used[k] = True
 
     def wait(self) -> None:
-        self.copy.synchronize()
+        self.upload.synchronize()
         self.compute.synchronize()
+        self.download.synchronize()
 
 
 class _CAI:
