@@ -160,7 +160,9 @@ __global__ void k_yolo(int entries, int hw, int vec4, const float* __restrict__ 
     const bool logi = e != 2 && e != 3, sxy = e < 2 && scale_xy != 1.0f;
     const int64_t base = (int64_t)blockIdx.y * hw;
     auto f = [&](float v) {
-        if (logi) v = tb_logistic(v);
+        // logistic_activate in double, as tb_logistic, inlined here: a call per element cost
+        // more than the memory traffic it hides behind
+        if (logi) v = (float)(1.0 / (1.0 + exp(-(double)v)));
         if (sxy) v = __fadd_rn(__fmul_rn(v, scale_xy), bias_xy);
         return v;
     };
