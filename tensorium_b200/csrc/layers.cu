@@ -93,19 +93,33 @@ __global__ void k_upsample(int64_t total, int c, int h, int w, int s, float scal
 __global__ void k_upsample2(int64_t total2, int c, int h, int w, float scale,
                             const float* __restrict__ x, float* __restrict__ y, int64_t y_bs) {
     const int ow = 2 * w, oh = 2 * h, half = w / 2;
-    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total2;
-         o += (int64_t)gridDim.x * blockDim.x) {
-        int xq = (int)(o % half);
-        int64_t t = o / half;
-        int iy = (int)(t % h);
-        int64_t cc = t / h;
-        int64_t b = cc / c, ch = cc - b * c;
-        float2 v = *reinterpret_cast<const float2*>(x + (cc * h + iy) * w + 2 * xq);
-        float a = scale * v.x, bb = scale * v.y;
-        float4 o4 = make_float4(a, a, bb, bb);
-        float* dst = y + b * y_bs + (ch * oh + 2 * iy) * (int64_t)ow + 4 * xq;
-        *reinterpret_cast<float4*>(dst) = o4;
-        *reinterpret_cast<float4*>(dst + ow) = o4;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t o0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o0 < total2; o0 += 4 * step) {
+        float2 v[4];  // four input pairs per thread per round, loads first
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t o = o0 + r * step;
+            if (o < total2) {
+                const int xq = (int)(o % half);
+                const int64_t t = o / half;
+                v[r] = __ldcs(reinterpret_cast<const float2*>(x + t * w + 2 * xq));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t o = o0 + r * step;
+            if (o >= total2) break;
+            const int xq = (int)(o % half);
+            const int64_t t = o / half;
+            const int iy = (int)(t % h);
+            const int64_t cc = t / h;
+            const int64_t b = cc / c, ch = cc - b * c;
+            const float a = scale * v[r].x, bb = scale * v[r].y;
+            const float4 o4 = make_float4(a, a, bb, bb);
+            float* dst = y + b * y_bs + (ch * oh + 2 * iy) * (int64_t)ow + 4 * xq;
+            __stcs(reinterpret_cast<float4*>(dst), o4);
+            __stcs(reinterpret_cast<float4*>(dst + ow), o4);
+        }
     }
 }
 
@@ -123,24 +137,50 @@ __global__ void k_copy_rows(int64_t batch, int64_t n, const float* __restrict__ 
 __global__ void k_copy_rows4(int64_t batch, int64_t n4, const float4* __restrict__ src, int64_t src_bs4,
                              float4* __restrict__ dst, int64_t dst_bs4) {
     const int64_t total = batch * n4;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        int64_t b = i / n4, e = i - b * n4;
-        dst[b * dst_bs4 + e] = src[b * src_bs4 + e];
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * step) {
+        float4 v[4];  // four vectors per thread per round, loads first
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t i = i0 + r * step;
+            if (i < total) {
+                const int64_t b = i / n4, e = i - b * n4;
+                v[r] = __ldcs(src + b * src_bs4 + e);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t i = i0 + r * step;
+            if (i >= total) break;
+            const int64_t b = i / n4, e = i - b * n4;
+            __stcs(dst + b * dst_bs4 + e, v[r]);
+        }
     }
 }
 
 // ---- shortcut: y = act(a + b) (source/naddlayer.pas:696-699) ----
 __global__ void k_shortcut4(int64_t n4, const float4* __restrict__ a, const float4* __restrict__ b,
                             float4* __restrict__ y, int act) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float4 u = a[i], v = b[i], o;
-        o.x = tb_activate_dev(u.x + v.x, act);
-        o.y = tb_activate_dev(u.y + v.y, act);
-        o.z = tb_activate_dev(u.z + v.z, act);
-        o.w = tb_activate_dev(u.w + v.w, act);
-        y[i] = o;
+    // four vectors per thread per round, all loads issued before any use (more bytes in flight)
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * step) {
+        float4 u[4], v[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t i = i0 + r * step;
+            if (i < n4) u[r] = __ldcs(a + i), v[r] = __ldcs(b + i);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t i = i0 + r * step;
+            if (i >= n4) break;
+            float4 o;
+            o.x = tb_activate_dev(u[r].x + v[r].x, act);
+            o.y = tb_activate_dev(u[r].y + v[r].y, act);
+            o.z = tb_activate_dev(u[r].z + v[r].z, act);
+            o.w = tb_activate_dev(u[r].w + v[r].w, act);
+            __stcs(y + i, o);
+        }
     }
 }
 
