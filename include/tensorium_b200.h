@@ -470,7 +470,8 @@ int tb_diag_tc_mma_rate(tb_ctx* ctx, int64_t kmajor, double* tflops, double* cyc
 int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w, float* y,
                            double* out12);
 /* The same counters for one launch of the NHWC tensor-core conv (tb_conv2d_fwd_nhwc's kernel;
- * entry 8 and 10 are 0). Blocks. */
+ * entry 8 = epilogue cycles in TMEM loads or split-K partial sums, entry 9 = all per-tile
+ * epilogue work, entry 10 = 0). Blocks. */
 int tb_diag_conv_nhwc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
                              const float* packed_w, float* y, int64_t y_pixel_stride, double* out12);
 

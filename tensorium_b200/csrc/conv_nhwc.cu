@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         int sbuf = 0;
         int tl = 0;
         const long long c_start = clock64();
-        long long c_wt = 0, c_st = 0, c_ldw = 0, c_math = 0;
+        long long c_wt = 0, c_st = 0, c_ldw = 0;
         for (int w = blockIdx.x; w < p.units; w += gridDim.x, ++tl) {
             const int t = w / p.splits;
             const int buf = tl & 1, u = tl >> 1;
@@ -451,7 +451,6 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             p.phases[blockIdx.x * 12 + 7] = tl;
             p.phases[blockIdx.x * 12 + 9] = c_st;
             p.phases[blockIdx.x * 12 + 8] = c_ldw;
-            p.phases[blockIdx.x * 12 + 10] = c_math;
         }
     }
     tc::tc_fence_before();
