@@ -107,9 +107,19 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def host_threads():
+    """Every host core this process may run on, whatever OMP_NUM_THREADS says (torchrun sets it
+    to 1 for each rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(specs, seconds=12.0, max_images=16):
     """The CPU oracle on this host's cores, one image at a time, for about `seconds`."""
     from oracle import oracle as O
+    O.set_threads(host_threads())
     x = None
     n, t0 = 0, time.perf_counter()
     while n < max_images and (n == 0 or time.perf_counter() - t0 < seconds):
@@ -121,6 +131,7 @@ def cpu_baseline(specs, seconds=12.0, max_images=16):
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "images/s", "cores": O.num_threads(), "kind": "port",
+            "host_cores": os.cpu_count(), "cpu": cpu_model(),
             "sample": f"{n} YOLOv3-416 images at batch 1 (per-image oracle: im2col + k-ascending FMA "
                       f"SGEMM over rows, OpenMP, AVX2), {dt:.1f} s"}
 
@@ -141,6 +152,7 @@ def run_reference(args):
         return
     from tensorium_b200 import synth
     from oracle import oracle as O
+    O.set_threads(host_threads())
     specs = synth.yolov3_specs()
     xs = synth.input_images(3, "yolov3", 4, INPUT)
     for w in range(args.warmup):
@@ -158,7 +170,7 @@ def run_reference(args):
                        "sample_per_step": "1 image (CPU)"},
             "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "cpu_baseline": {"value": v, "unit": "images/s", "cores": O.num_threads(), "kind": "port",
-                             "cpu": cpu_model(),
+                             "host_cores": os.cpu_count(), "cpu": cpu_model(),
                              "sample": "1 YOLOv3-416 image per step through the CPU restatement of the "
                                        "reference path (the FreePascal reference cannot be built here)"}}
     print(json.dumps(line), flush=True)

@@ -63,8 +63,13 @@ extern "C" {
 #define TB_ACT_SELU     15
 
 /* ---- math modes of the convolution mainloop ---------------------------------------- */
-#define TB_MATH_FP32  0   /* FP32 CUDA-core FMA mainloop (reference-faithful, default) */
+#define TB_MATH_FP32  0   /* FP32 CUDA-core mainloop in the reference's order: one FMA per k,
+                             k ascending as im2col rows (c, kh, kw), no split of K -- results
+                             bit-identical to the reference CPU path (default) */
 #define TB_MATH_TF32  1   /* tcgen05 tensor-core mainloop, TF32 operands, FP32 accumulate */
+#define TB_MATH_FP32_TILED 2  /* FP32 CUDA-core mainloop with the summation reordered (k tiles
+                             in (kh, kw, c) order, split-K with partial sums in scratch): within
+                             the reference's 1e-4 per map, not bit-identical */
 
 /* ---- context ------------------------------------------------------------------------- */
 typedef struct tb_ctx tb_ctx;
@@ -100,6 +105,8 @@ int tb_memcpy_h2d(tb_ctx* ctx, void* dst, const void* src_host, int64_t bytes);
 int tb_memcpy_d2h(tb_ctx* ctx, void* dst_host, const void* src, int64_t bytes);
 /* Grow the split-K workspace to at least `bytes` (allocates; call before graph capture). */
 int tb_workspace_reserve(tb_ctx* ctx, int64_t bytes);
+/* Bytes the context's scratch workspace holds now (no counterpart in the reference). */
+int tb_workspace_size(tb_ctx* ctx, int64_t* bytes);
 
 /* ---- elementwise / BLAS-1 helpers used by the layers on the path -------------------- */
 /* TNNCuda.ActivateArray(N, x, offset, activation) (source/nncuda.pas:108). */
@@ -194,11 +201,14 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
 /* tb_conv2d_fwd without any device allocation, for callers that cannot call cudaMalloc
  * (device memory handed out up front by an arena, an allocator held by another component, or
  * a loop where an allocation's latency or failure is not acceptable). No counterpart in the
- * reference. Same arguments and results as tb_conv2d_fwd with the FP32 mainloop; the split-K
- * scratch is a fixed array inside the library (16 MiB of partial sums + 16384 tile counters,
- * held on every GPU that loads the library until exit). A layer whose split needs more scratch
- * than that is rejected with TB_ERR_INVALID. The first call on a device looks up the array's
- * device address; make that first call before any stream capture. All calls share the one
+ * reference. Same arguments as tb_conv2d_fwd and the results of tb_conv2d_fwd with
+ * math_mode TB_MATH_FP32_TILED (the tiled kernels with split-K); the split-K scratch is a fixed
+ * array inside the library (16 MiB of partial sums + 16384 tile counters, held on every GPU that
+ * loads the library until exit). A layer whose chosen split needs more scratch than that runs
+ * with its split lowered until the partial sums fit (split 1 needs none); a split pinned through
+ * the TB_CONV_FORCE test hook that does not fit is rejected with TB_ERR_INVALID. The first call
+ * on a device looks up the array's device address; make that first call before any stream
+ * capture; cudaDeviceReset of that device is not supported afterwards. All calls share the one
  * array: calls that overlap on the GPU (other streams, other contexts on the same device) race. */
 int tb_conv2d_fwd_noalloc(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const float* packed_w,
                           const float* bias, const float* bn_scale, const float* bn_mean,
@@ -306,6 +316,94 @@ int tb_softmax_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t groups, f
 /* TAvgPoolLayer.forward (source/navgpoollayer.pas:60-84): y[b][c] = mean over h*w. */
 int tb_avgpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int64_t w,
                    const float* x, float* y);
+
+/* ---- TNNCuda method shims --------------------------------------------------------------
+ * One function per TNNCuda<single> method the forward layers call, with that method's argument
+ * list in the same order (source/nncuda.pas:100-151), preceded by the context that stands in
+ * for the global `cuda` object: SizeInt -> int64_t, single -> float, boolean / longint ->
+ * int32_t, TCUMem -> device pointer.  A Pascal TNNCuda replacement forwards each method with a
+ * one-line call.  Results follow the reference's CPU routines (the library's parity target):
+ * the GEMMs keep cblas_sgemm's orders (s_nn / s_tn: C = beta*C then one FMA of alpha*a per k
+ * ascending; s_nt: sdot_avx2's eight lanes; s_tt: sequential sum of (alpha*a)*b).  The GEMM
+ * shims are correctness shims (one thread per output); tb_conv2d_fwd is the fast conv path.
+ * Training-direction calls (upSample with isForward = 0) return TB_ERR_UNSUPPORTED. */
+/* createDeviceBuffer(N bytes) / freeDeviceBuffer (source/nncuda.pas:103-104, 488-497). */
+int tbcompat_createDeviceBuffer(tb_ctx* ctx, int64_t N, void** mem);
+int tbcompat_freeDeviceBuffer(tb_ctx* ctx, void* mem);
+/* readBuffer / writeBuffer (source/nncuda.pas:105-106): blocking copies of bufferSize bytes. */
+int tbcompat_readBuffer(tb_ctx* ctx, const void* mem, int64_t bufferSize, void* buffer);
+int tbcompat_writeBuffer(tb_ctx* ctx, void* mem, int64_t bufferSize, const void* buffer);
+/* finish (source/nncuda.pas:153, 1575-1584). */
+int tbcompat_finish(tb_ctx* ctx);
+/* ActivateArray(N, x, offset, activation) (source/nncuda.pas:108, 524-580). */
+int tbcompat_ActivateArray(tb_ctx* ctx, int64_t N, float* x, int64_t offset, int32_t activation);
+/* forwardBias(dstSize, dst, offset, srcSize, src, incb, batch) (source/nncuda.pas:111, 582-600):
+ * dst[offset + i] += src[((i / block) % srcSize) * incb], block = dstSize / (srcSize*batch). */
+int tbcompat_forwardBias(tb_ctx* ctx, int64_t dstSize, float* dst, int64_t offset, int64_t srcSize,
+                         const float* src, int64_t incb, int64_t batch);
+/* forwardScale(dstSize, dst, offset, scaleSize, scale, incb, batch) (source/nncuda.pas:145,
+ * 1468-1488): dst[offset + i] *= scale[f]. */
+int tbcompat_forwardScale(tb_ctx* ctx, int64_t dstSize, float* dst, int64_t offset, int64_t scaleSize,
+                          const float* scale, int64_t incb, int64_t batch);
+/* forwardScaleAdd(dstSize, dst, offset, scaleSize, scales, biases, incb, batch) (source/
+ * nncuda.pas:146, 1490-1508): dst = dst*scales[f] + biases[f], two roundings. */
+int tbcompat_forwardScaleAdd(tb_ctx* ctx, int64_t dstSize, float* dst, int64_t offset, int64_t scaleSize,
+                             const float* scales, const float* biases, int64_t incb, int64_t batch);
+/* normalize(srcSize, dstSize, groups, means, meansStride, vars, varsStride, dst, dstOffset)
+ * (source/nncuda.pas:141, 1371-1393): dst[g][i][j] = (dst - means[i*meansStride]) /
+ * max(sqrt(vars[i*varsStride]), 1e-6) as blockNormalize (source/ntensors.pas:8693-8718). */
+int tbcompat_normalize(tb_ctx* ctx, int64_t srcSize, int64_t dstSize, int64_t groups, const float* means,
+                       int64_t meansStride, const float* vars, int64_t varsStride, float* dst, int64_t dstOffset);
+/* gemm(transA, transB, M, N, K, ALPHA, A, aOffset, lda, B, bOffset, ldb, BETA, C, cOffset, ldc)
+ * (source/nncuda.pas:112, 624-808): row-major C = ALPHA*op(A)*op(B) + BETA*C. */
+int tbcompat_gemm(tb_ctx* ctx, int32_t transA, int32_t transB, int64_t M, int64_t N, int64_t K, float ALPHA,
+                  const float* A, int64_t aOffset, int64_t lda, const float* B, int64_t bOffset, int64_t ldb,
+                  float BETA, float* C, int64_t cOffset, int64_t ldc);
+/* gemmStridedBatched(..., strideA, ..., strideB, ..., strideC, batchCount) (source/nncuda.pas:
+ * 119, 809-896): batchCount GEMMs, matrices strideA / strideB / strideC elements apart. */
+int tbcompat_gemmStridedBatched(tb_ctx* ctx, int32_t transA, int32_t transB, int64_t M, int64_t N, int64_t K,
+                                float ALPHA, const float* A, int64_t aOffset, int64_t lda, int64_t strideA,
+                                const float* B, int64_t bOffset, int64_t ldb, int64_t strideB, float BETA, float* C,
+                                int64_t cOffset, int64_t ldc, int64_t strideC, int64_t batchCount);
+/* addvv (source/nncuda.pas:120, 897-915). */
+int tbcompat_addvv(tb_ctx* ctx, int64_t N, const float* src1, int64_t src1Offset, int64_t inca, const float* src2,
+                   int64_t src2Offset, int64_t incb, float* dst, int64_t dstOffset, int64_t incc);
+/* fill (source/nncuda.pas:128, 1017-1035). */
+int tbcompat_fill(tb_ctx* ctx, int64_t N, float* x, int64_t offset, float val, int64_t stride);
+/* copy (source/nncuda.pas:129, 1037-1054). */
+int tbcompat_copy(tb_ctx* ctx, int64_t N, const float* src, int64_t srcOffset, int64_t inca, float* dst,
+                  int64_t dstOffset, int64_t incb);
+/* fmavss(N, src, offset, scalar, bias, dst) (source/nncuda.pas:137, 1288-1305): dst = src*scalar + bias. */
+int tbcompat_fmavss(tb_ctx* ctx, int64_t N, float* src, int64_t offset, float scalar, float bias, float* dst);
+/* softmaxBatch(N, input, iOffset, batch, batch_size, groups, group_size, stride, temp, output,
+ * oOffset) (source/nncuda.pas:130, 1056-1086). */
+int tbcompat_softmaxBatch(tb_ctx* ctx, int64_t N, const float* input, int64_t iOffset, int64_t batch,
+                          int64_t batch_size, int64_t groups, int64_t group_size, int64_t stride, float temp,
+                          float* output, int64_t oOffset);
+/* forwardMaxPool(aBatch, outC, outH, outW, input, c, h, w, stride_x, stride_y, padding,
+ * kernelSize, indexes, output) (source/nncuda.pas:132, 1088-1142); indexes are int64. */
+int tbcompat_forwardMaxPool(tb_ctx* ctx, int64_t aBatch, int64_t outC, int64_t outH, int64_t outW,
+                            const float* input, int64_t c, int64_t h, int64_t w, int64_t stride_x, int64_t stride_y,
+                            int64_t padding, int64_t kernelSize, int64_t* indexes, float* output);
+/* im2col(aChannels, aHeight, aWidth, kernelHeight, kernelWidth, padHeight, padWidth, strideY,
+ * strideX, dilationY, dilationX, im, imOffset, col, colOffset) (source/nncuda.pas:134,
+ * 1144-1190): col[(c*kh + r)*kw + s][oy*ow + ox], the CPU sim2Col layout. */
+int tbcompat_im2col(tb_ctx* ctx, int64_t aChannels, int64_t aHeight, int64_t aWidth, int64_t kernelHeight,
+                    int64_t kernelWidth, int64_t padHeight, int64_t padWidth, int64_t strideY, int64_t strideX,
+                    int64_t dilationY, int64_t dilationX, const float* im, int64_t imOffset, float* col,
+                    int64_t colOffset);
+/* upSample(aBatch, aChannels, outHeight, outWidth, in, stride, isForward, scale, out, zeroIn)
+ * (source/nncuda.pas:136, 1267-1286); outHeight / outWidth are the INPUT's size, as the
+ * reference passes them. */
+int tbcompat_upSample(tb_ctx* ctx, int64_t aBatch, int64_t aChannels, int64_t outHeight, int64_t outWidth,
+                      const float* in, int64_t stride, int32_t isForward, float scale, float* out, int32_t zeroIn);
+
+/* Unfused batchnorm layer (TBaseLayer.batchNorm inference, source/nbaselayer.pas:336-370, the
+ * cuda.normalize -> forwardScale -> forwardBias sequence of :620-643) in one pass over
+ * [batch][channels][spatial]: y = ((x - mean)/max(sqrt(var), 1e-6))*scale + bias, three
+ * roundings. scales / biases may be NULL (1 / 0). y may equal x. */
+int tb_bn_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t spatial, const float* x, const float* mean,
+              const float* variance, const float* scales, const float* biases, float* y);
 
 /* ---- whole-network executor (TNNet.forward / predict, source/nnet.pas:275-317,452-472) --- */
 typedef struct tb_net tb_net;

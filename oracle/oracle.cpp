@@ -65,8 +65,9 @@ static inline float act_scalar(float x, int a) {
         if (x > 4) return (float)(0.01 * ((double)x - 4) + 1);
         return (float)(0.125 * (double)x + 0.5);
     case acREVLEAKY:
-    case acLEAKY:  // activate_array :555-566: if x<0 then x := 0.1*x
-        return x < 0 ? (float)(0.1 * (double)x) : x;
+    case acLEAKY:  // activate_array :555-566 -> leaky_array (:234-267, the USE_AVX2 build every
+                   // sample project defines): x < 0 -> x * f with f: single = 0.1 (vmulps)
+        return x < 0 ? x * 0.1f : x;
     case acELU:
         return (float)((x >= 0 ? (double)x : 0.0) + (x < 0 ? std::exp((double)x) - 1.0 : 0.0));
     case acLOGGY:
@@ -154,8 +155,21 @@ void or_sgemm_nn(int64_t M, int64_t N, int64_t K, float alpha, const float* A, i
     }
 }
 
-// SGEMM NT: sgemm_nt -> s_nt (source/ntensors.pas:1957-2005): C[i,j] += alpha*sdot(A_i, B_j),
-// sdot_pas order (sequential, separate multiply and add).
+// SGEMM NT: sgemm_nt -> s_nt (source/ntensors.pas:1957-2005): C[i,j] = beta*C[i,j] +
+// alpha*sdot(A_i, B_j).  sdot is sdot_avx2 (source/ntensors.pas:1233-1306, SIMD_REGS = 8) in the
+// USE_AVX2 build every sample project defines: eight lane sums, lane l taking k = l, l+8, ...
+// with one fused multiply-add each (the masked tail block adds its k = 8*floor(K/8) + l to lane
+// l), then lanes l and l+4 are added (vextractf128 + vaddps) and the four sums reduced by two
+// vhaddps: ((s0+s1) + (s2+s3)).
+// ---------------------------------------------------------------------------------------
+static inline float sdot_avx2_order(int64_t K, const float* a, const float* b) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t k = 0; k < K; ++k) lane[k & 7] = std::fmaf(a[k], b[k], lane[k & 7]);
+    float t[4];
+    for (int l = 0; l < 4; ++l) t[l] = lane[l] + lane[l + 4];
+    return (t[0] + t[1]) + (t[2] + t[3]);
+}
+
 void or_sgemm_nt(int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
                  const float* B, int64_t ldb, float beta, float* C, int64_t ldc) {
 #pragma omp parallel for schedule(static)
@@ -164,11 +178,41 @@ void or_sgemm_nt(int64_t M, int64_t N, int64_t K, float alpha, const float* A, i
         if (beta != 1.0f)
             for (int64_t j = 0; j < N; ++j) c[j] = c[j] * beta;
         for (int64_t j = 0; j < N; ++j) {
-            const float* a = A + i * lda;
-            const float* b = B + j * ldb;
-            float s = 0.0f;
-            for (int64_t k = 0; k < K; ++k) s = s + a[k] * b[k];
-            c[j] = c[j] + alpha * s;
+            const float s = alpha * sdot_avx2_order(K, A + i * lda, B + j * ldb);
+            c[j] = c[j] + s;
+        }
+    }
+}
+
+// SGEMM TN: sgemm_tn -> s_tn (source/ntensors.pas:2007-2040): per row i and k ascending,
+// saxpy(N, alpha*A[k*lda + i], B_k, C_i) -- one FMA per k, as s_nn.
+void or_sgemm_tn(int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
+                 const float* B, int64_t ldb, float beta, float* C, int64_t ldc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < M; ++i) {
+        float* c = C + i * ldc;
+        if (beta != 1.0f)
+            for (int64_t j = 0; j < N; ++j) c[j] = c[j] * beta;
+        for (int64_t k = 0; k < K; ++k) saxpy_fma(N, alpha * A[k * lda + i], B + k * ldb, c);
+    }
+}
+
+// SGEMM TT: sgemm_tt -> s_tt (source/ntensors.pas:2159-2183): sum := sum + ALPHA*A[i + kk*lda]*
+// B[kk + j*ldb] (single products, left to right), C += sum.
+void or_sgemm_tt(int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
+                 const float* B, int64_t ldb, float beta, float* C, int64_t ldc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < M; ++i) {
+        float* c = C + i * ldc;
+        if (beta != 1.0f)
+            for (int64_t j = 0; j < N; ++j) c[j] = c[j] * beta;
+        for (int64_t j = 0; j < N; ++j) {
+            float sum = 0.0f;
+            for (int64_t k = 0; k < K; ++k) {
+                const float t = alpha * A[i + k * lda];
+                sum = sum + t * B[k + j * ldb];
+            }
+            c[j] = c[j] + sum;
         }
     }
 }
@@ -433,15 +477,25 @@ void or_softmax(int64_t batch, int64_t inputs, int64_t groups, float temp, const
         }
 }
 
-// Global average pool: TAvgPoolLayer.forward (source/navgpoollayer.pas:60-84); the sum is
-// sequential here (the reference's TTensor.Sum order is SIMD-dependent).
+// Global average pool: TAvgPoolLayer.forward (source/navgpoollayer.pas:60-84): Sum(1, h*w,
+// offset) / (h*w).  TTensor<single>.sumv is vsSumI (source/ntensors.pas:3624-3634), which on an
+// AVX2 CPU with unit stride is vssum_avx2 (:3592-3620): eight lane sums over the whole blocks of
+// 8 (vaddps), lanes l and l+4 added, two haddps ((s0+s1) + (s2+s3)), then the N mod 8 tail added
+// one by one.
+static inline float vssum_avx2_order(int64_t n, const float* a) {
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int64_t nb = n / 8 * 8;
+    for (int64_t k = 0; k < nb; ++k) lane[k & 7] = lane[k & 7] + a[k];
+    float t[4];
+    for (int l = 0; l < 4; ++l) t[l] = lane[l] + lane[l + 4];
+    float s = (t[0] + t[1]) + (t[2] + t[3]);
+    for (int64_t k = nb; k < n; ++k) s = s + a[k];
+    return s;
+}
+
 void or_avgpool(int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, float* y) {
     const int64_t im = h * w;
-    for (int64_t i = 0; i < batch * c; ++i) {
-        float s = 0.0f;
-        for (int64_t j = 0; j < im; ++j) s = s + x[i * im + j];
-        y[i] = s / (float)im;
-    }
+    for (int64_t i = 0; i < batch * c; ++i) y[i] = vssum_avx2_order(im, x + i * im) / (float)im;
 }
 
 // ---------------------------------------------------------------------------------------

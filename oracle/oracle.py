@@ -39,6 +39,8 @@ def _load():
         "or_im2col": [I] * 11 + [P, P],
         "or_sgemm_nn": [I, I, I, F, P, I, P, I, F, P, I],
         "or_sgemm_nt": [I, I, I, F, P, I, P, I, F, P, I],
+        "or_sgemm_tn": [I, I, I, F, P, I, P, I, F, P, I],
+        "or_sgemm_tt": [I, I, I, F, P, I, P, I, F, P, I],
         "or_fuse_bn": [I, I, P, P, P, P, P],
         "or_conv2d_fwd": [I] * 13 + [P, P, P, P, P, P, I, P],
         "or_maxpool": [I] * 8 + [P, P, P],
@@ -80,6 +82,16 @@ def _p(a):
 
 def f32(a):
     return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def sgemm(trans_a, trans_b, M, N, K, alpha, A, lda, B, ldb, beta, Cm, ldc):
+    """cblas_sgemm (row major) in the reference CPU routines' orders; returns the updated C."""
+    A, B = f32(A), f32(B)
+    out = f32(Cm).copy()
+    fn = {(0, 0): lib.or_sgemm_nn, (0, 1): lib.or_sgemm_nt, (1, 0): lib.or_sgemm_tn,
+          (1, 1): lib.or_sgemm_tt}[(int(bool(trans_a)), int(bool(trans_b)))]
+    fn(M, N, K, alpha, _p(A), lda, _p(B), ldb, beta, _p(out), ldc)
+    return out
 
 
 # ---- single layers ----------------------------------------------------------------------

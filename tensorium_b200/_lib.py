@@ -29,6 +29,7 @@ ACT = {
 
 MATH_FP32 = 0
 MATH_TF32 = 1
+MATH_FP32_TILED = 2  # FP32 with the summation reordered (tiles, split-K): not bit-exact
 
 XNOR_PAD_BIT0 = 0
 XNOR_PAD_ZERO = 1
@@ -104,12 +105,36 @@ SIGNATURES = {
     "tb_memcpy_h2d": [P, P, P, I64],
     "tb_memcpy_d2h": [P, P, P, I64],
     "tb_workspace_reserve": [P, I64],
+    "tb_workspace_size": [P, C.POINTER(I64)],
     "tb_activate": [P, I64, P, I64, I64],
     "tb_forward_bias": [P, I64, P, I64, I64, P, I64, I64],
     "tb_copy": [P, I64, P, I64, I64, P, I64, I64],
     "tb_fill": [P, I64, P, I64, F32, I64],
     "tb_addvv": [P, I64, P, I64, I64, P, I64, I64, P, I64, I64],
     "tb_fmavss": [P, I64, P, I64, F32, F32, P],
+    "tb_bn_fwd": [P, I64, I64, I64, P, P, P, P, P, P],
+    # TNNCuda method shims (argument lists of source/nncuda.pas:100-151)
+    "tbcompat_createDeviceBuffer": [P, I64, C.POINTER(P)],
+    "tbcompat_freeDeviceBuffer": [P, P],
+    "tbcompat_readBuffer": [P, P, I64, P],
+    "tbcompat_writeBuffer": [P, P, I64, P],
+    "tbcompat_finish": [P],
+    "tbcompat_ActivateArray": [P, I64, P, I64, C.c_int32],
+    "tbcompat_forwardBias": [P, I64, P, I64, I64, P, I64, I64],
+    "tbcompat_forwardScale": [P, I64, P, I64, I64, P, I64, I64],
+    "tbcompat_forwardScaleAdd": [P, I64, P, I64, I64, P, P, I64, I64],
+    "tbcompat_normalize": [P, I64, I64, I64, P, I64, P, I64, P, I64],
+    "tbcompat_gemm": [P, C.c_int32, C.c_int32, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P, I64, I64],
+    "tbcompat_gemmStridedBatched": [P, C.c_int32, C.c_int32, I64, I64, I64, F32, P, I64, I64, I64, P, I64, I64,
+                                    I64, F32, P, I64, I64, I64, I64],
+    "tbcompat_addvv": [P, I64, P, I64, I64, P, I64, I64, P, I64, I64],
+    "tbcompat_fill": [P, I64, P, I64, F32, I64],
+    "tbcompat_copy": [P, I64, P, I64, I64, P, I64, I64],
+    "tbcompat_fmavss": [P, I64, P, I64, F32, F32, P],
+    "tbcompat_softmaxBatch": [P, I64, P, I64, I64, I64, I64, I64, I64, F32, P, I64],
+    "tbcompat_forwardMaxPool": [P, I64, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, P, P],
+    "tbcompat_im2col": [P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, P, I64, P, I64],
+    "tbcompat_upSample": [P, I64, I64, I64, I64, P, I64, C.c_int32, F32, P, C.c_int32],
     "tb_conv_out_shape": [C.POINTER(ConvDesc), PI64, PI64],
     "tb_conv_packed_weights_count": [C.POINTER(ConvDesc), PI64],
     "tb_conv_pack_weights": [P, C.POINTER(ConvDesc), P, P],

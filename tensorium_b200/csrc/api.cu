@@ -367,6 +367,12 @@ int tb_memcpy_d2h(tb_ctx* ctx, void* dst, const void* src, int64_t bytes) {
     return TB_OK;
 }
 
+int tb_workspace_size(tb_ctx* ctx, int64_t* bytes) {
+    if (!ctx || !bytes) return fail(TB_ERR_INVALID, "tb_workspace_size: null argument");
+    *bytes = (int64_t)ctx->ws_bytes;
+    return TB_OK;
+}
+
 int tb_workspace_reserve(tb_ctx* ctx, int64_t bytes) {
     TB_ENTER(ctx);
     if (bytes < 0) return fail(TB_ERR_INVALID, "negative workspace size");

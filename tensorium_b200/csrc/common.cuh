@@ -80,7 +80,7 @@ static __device__ __noinline__ float tb_activate_slow(float x, int a);
 
 // Common activations inline, the rest out of line (keeps the unrolled conv epilogues small).
 __device__ __forceinline__ float tb_activate_dev(float x, int a) {
-    if (a == TB_ACT_LEAKY || a == TB_ACT_REVLEAKY) return x < 0.f ? (float)(0.1 * (double)x) : x;
+    if (a == TB_ACT_LEAKY || a == TB_ACT_REVLEAKY) return x < 0.f ? __fmul_rn(x, 0.1f) : x;
     if (a == TB_ACT_LINEAR) return x;
     if (a == TB_ACT_RELU) return x > 0.f ? x : x * 0.0f;
     return tb_activate_slow(x, a);
@@ -105,7 +105,7 @@ static __device__ __noinline__ float tb_activate_slow(float x, int a) {
         if (x > 4.f) return (float)(0.01 * ((double)x - 4.0) + 1.0);
         return (float)(0.125 * (double)x + 0.5);
     case TB_ACT_REVLEAKY:
-    case TB_ACT_LEAKY: return x < 0.f ? (float)(0.1 * (double)x) : x;
+    case TB_ACT_LEAKY: return x < 0.f ? __fmul_rn(x, 0.1f) : x;  // leaky_array: single multiply by 0.1f
     case TB_ACT_ELU:
         return (float)((x >= 0.f ? (double)x : 0.0) + (x < 0.f ? exp((double)x) - 1.0 : 0.0));
     case TB_ACT_LOGGY: return (float)(2.0 / (1.0 + exp(-(double)x)) - 1.0);

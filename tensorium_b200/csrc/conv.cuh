@@ -44,6 +44,7 @@ struct ConvParams {
     int ktiles, kt_per_split, splits;
     int act, yolo_classes;
     int vec_out;  // 1: OHW, y_bs, r_bs multiples of 4 and y/res 16-byte aligned
+    int wrsc;     // packed weight order: 1 = RSC (k = (r*kw + s)*Cpad + c), 0 = CRS
 };
 
 inline bool conv_is_rsc(int64_t C, int64_t KH, int64_t KW) {
@@ -60,6 +61,17 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
                      const float* bn_var, const float* res, float* y, int act, int yolo_classes,
                      float* ws, int64_t ws_floats, int64_t* launches, int* tile_cnt = nullptr,
                      int64_t tile_cnt_len = 0, bool allow_tma = true);
+// Order-exact FP32 conv (conv_exact.cu): the reference's k order and one FMA chain per output
+// (fma = false: the connected layer's separate multiply and add), no split of K, no scratch.
+bool conv_exact_supported(const ConvGeom& g);
+int conv_exact_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
+                      const float* bn_scale, const float* bn_mean, const float* bn_var, const float* res, float* y,
+                      int act, int yolo_classes, bool fma, int64_t* launches);
+int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y, bool fma);
+// Connected layer in the reference's sdot_avx2 order (layers.cu): g is a 1x1 conv over 1x1 inputs.
+int fc_sdot_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
+                   const float* bn_scale, const float* bn_mean, const float* bn_var, float* y, int act,
+                   int64_t* launches);
 // TF32 tensor-core path (conv_tc.cu): convolutions with channels % 32 == 0 (any stride, dilation).
 bool conv_tc_supported(const ConvGeom& g);
 int64_t conv_tc_scratch_floats(const ConvGeom& g);
@@ -112,6 +124,10 @@ int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
 // Split-K partial floats this call would need (0 when it does not split), for a given x.
 // allow_tma = false: only the gather kernels (callers whose scratch cannot hold a replica)
 int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x, bool allow_tma = true);
+// The same for a caller-provided scratch of cap_floats partials and cap_tiles counters (the gather
+// kernels, K split lowered until it fits; a split pinned by TB_CONV_FORCE is kept).
+int64_t conv_fp32_ws_floats_fit(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t cap_floats,
+                                int64_t cap_tiles);
 
 // Floats of split-K workspace the FP32 path needs for this geometry (0 if it does not split).
 int64_t conv_fp32_ws_floats(tb_ctx* ctx, const ConvGeom& g);
@@ -150,7 +166,7 @@ __device__ __forceinline__ float conv_epi_value(float v, int m, const ConvParams
                                                 bool leaky, float bm) {
     if (!simple) return conv_epilogue(v, m, p);
     if (has_bias) v = __fadd_rn(v, bm);
-    return (leaky && v < 0.f) ? (float)(0.1 * (double)v) : v;  // activate_array's leaky
+    return (leaky && v < 0.f) ? __fmul_rn(v, 0.1f) : v;  // activate_array's leaky (leaky_array: v * 0.1f)
 }
 
 }  // namespace tbi

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
                         float o = acc[q][j];
                         if (simple) {  // bias, then leaky or linear (the common first layer)
                             if (p.bias) o = __fadd_rn(o, bias);
-                            if (p.act == TB_ACT_LEAKY && o < 0.f) o = (float)(0.1 * (double)o);
+                            if (p.act == TB_ACT_LEAKY && o < 0.f) o = __fmul_rn(o, 0.1f);
                         } else {
                             o = conv_epilogue(o, f, p);
                         }

@@ -1,0 +1,9 @@
+// conv_exact_128x128.cu -- instantiation of the order-exact FP32 conv for the 128 x 128 CTA tile
+// (thread tile 8 x 8).
+#include "conv_exact.cuh"
+
+namespace tbi {
+int exact_launch_128x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma) {
+    return exact_launch_modes<128, 128, 8>(ctx, p, grid, mode, fma);
+}
+}  // namespace tbi

@@ -1,0 +1,9 @@
+// conv_exact_64x128.cu -- instantiation of the order-exact FP32 conv for the 64 x 128 CTA tile
+// (thread tile 8 x 8).
+#include "conv_exact.cuh"
+
+namespace tbi {
+int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma) {
+    return exact_launch_modes<64, 128, 8>(ctx, p, grid, mode, fma);
+}
+}  // namespace tbi

@@ -187,6 +187,30 @@ int64_t conv_fp32_ws_floats_for(tb_ctx* ctx, const ConvGeom& g, const float* x, 
     return ws_floats_of(g, choose_tiles(ctx, g, aligned16(x), allow_tma));
 }
 
+// A caller-provided scratch of cap_floats partial sums and cap_tiles counters: keep the chosen
+// tile but lower its K split to the largest count whose partial planes fit (down to 1, which
+// needs none).  A split pinned through TB_CONV_FORCE is kept as it is.
+static TileCfg fit_to_scratch(const ConvGeom& g, TileCfg t, int64_t cap_floats, int64_t cap_tiles) {
+    if (t.tma || t.splits <= 1 || getenv("TB_CONV_FORCE")) return t;
+    const int64_t ktiles = g.Kpad / CONV_BK;
+    const int64_t tiles = ceil_div(g.F, t.BM) * ceil_div(g.B * g.OH * g.OW, t.BN);
+    for (int64_t sp = t.splits; sp >= 1; --sp) {
+        const int64_t kps = ceil_div(ktiles, sp);
+        const int64_t s2 = ceil_div(ktiles, kps);
+        if (s2 == 1 || (s2 * g.F * g.B * g.OH * g.OW <= cap_floats && tiles <= cap_tiles)) {
+            t.splits = (int)s2;
+            t.kt_per_split = (int)kps;
+            return t;
+        }
+    }
+    return t;
+}
+
+int64_t conv_fp32_ws_floats_fit(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t cap_floats,
+                                int64_t cap_tiles) {
+    return ws_floats_of(g, fit_to_scratch(g, choose_tiles(ctx, g, aligned16(x), false), cap_floats, cap_tiles));
+}
+
 static int launch_with(tb_ctx* ctx, const ConvGeom& g, const TileCfg& t, const float* x, const float* wp,
                        const float* bias, const float* bn_scale, const float* bn_mean,
                        const float* bn_var, const float* res, float* y, int act, int yolo_classes,
@@ -259,6 +283,7 @@ int conv_fp32_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
     if (conv_direct_supported(g, res, yolo_classes) && !getenv("TB_CONV_FORCE"))
         return conv_direct_launch(ctx, g, x, wp, bias, bn_scale, bn_mean, bn_var, y, act, launches);
     TileCfg t = choose_tiles(ctx, g, aligned16(x), allow_tma);
+    if (ws) t = fit_to_scratch(g, t, ws_floats, tile_cnt ? tile_cnt_len : ctx->tile_cnt_len);
     return launch_with(ctx, g, t, x, wp, bias, bn_scale, bn_mean, bn_var, res, y, act, yolo_classes,
                        ws, ws_floats, launches, tile_cnt, tile_cnt_len);
 }
@@ -416,6 +441,8 @@ int tb_conv_autotune(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const f
     int r = conv_geom(d, &g);
     if (r != TB_OK) return r;
     if (!x || !packed_w || !y) return fail(TB_ERR_INVALID, "conv autotune: null pointer");
+    if (ctx->math_mode != TB_MATH_FP32_TILED && conv_exact_supported(g))
+        return conv_exact_autotune(ctx, g, x, packed_w, y, true);
     return conv_fp32_autotune(ctx, g, x, packed_w, y);
 }
 
@@ -433,7 +460,7 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
     if (!act_supported(d->activation))
         return fail(TB_ERR_UNSUPPORTED, "conv: activation %lld not supported", (long long)d->activation);
     if (math_mode < 0) math_mode = ctx->math_mode;
-    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32)
+    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32 && math_mode != TB_MATH_FP32_TILED)
         return fail(TB_ERR_UNSUPPORTED, "conv: math mode %lld is not available in this build", (long long)math_mode);
     if (math_mode == TB_MATH_TF32 && conv_tc_supported(g)) {
         r = ensure_workspace(ctx, (size_t)conv_tc_scratch_floats(g) * sizeof(float));
@@ -441,6 +468,9 @@ int tb_conv2d_fwd(tb_ctx* ctx, const tb_conv_desc* d, const float* x, const floa
         return conv_tc_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
                               (int)d->activation, 0, reinterpret_cast<float*>(ctx->ws), nullptr);
     }
+    if (math_mode != TB_MATH_FP32_TILED && conv_exact_supported(g))
+        return conv_exact_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
+                                 (int)d->activation, 0, true, nullptr);
     return conv_fp32_launch(ctx, g, x, packed_w, bias, bn_scale, bn_mean, bn_variance, residual, y,
                             (int)d->activation, 0, nullptr, 0, nullptr);
 }

@@ -4,9 +4,12 @@
 // Some hosts cannot call cudaMalloc at the point where they run a layer: a process whose
 // device memory is handed out up front by a framework's arena, code running while another
 // component holds the allocator, or a real-time loop where an allocation's latency (or
-// failure) is not acceptable.  tb_conv2d_fwd may grow the context's workspace for split-K
-// partial sums; this variant instead keeps that scratch (partial sums and the per-tile arrival
-// counters) in one fixed array in device memory that is part of the library image.
+// failure) is not acceptable.  tb_conv2d_fwd with TB_MATH_FP32_TILED may grow the context's
+// workspace for split-K partial sums; this variant runs the same tiled kernels but keeps that
+// scratch (partial sums and the per-tile arrival counters) in one fixed array in device memory
+// that is part of the library image.  (The default FP32 path, TB_MATH_FP32, needs no scratch.)
+// The array's device address is cached per device index for the life of the process; the
+// library does not support cudaDeviceReset of a device it has run this entry point on.
 #include "conv.cuh"
 
 #include <mutex>
@@ -57,11 +60,13 @@ extern "C" int tb_conv2d_fwd_noalloc(tb_ctx* ctx, const tb_conv_desc* d, const f
     if (!aligned16(packed_w)) return fail(TB_ERR_INVALID, "noalloc conv: packed weights must be 16-byte aligned");
     if (!act_supported(d->activation))
         return fail(TB_ERR_UNSUPPORTED, "noalloc conv: activation %lld not supported", (long long)d->activation);
-    const int64_t need = conv_fp32_ws_floats_for(ctx, g, x, false);
+    // the tile's K split is lowered until its partial sums fit the static scratch (split 1 needs
+    // none); only a split pinned through the TB_CONV_FORCE test hook can still exceed it
+    const int64_t need = conv_fp32_ws_floats_fit(ctx, g, x, NOALLOC_PARTIAL_FLOATS, NOALLOC_COUNTERS);
     if (need > NOALLOC_PARTIAL_FLOATS)
         return fail(TB_ERR_INVALID,
-                    "noalloc conv: this layer needs %lld bytes of split-K scratch; the static scratch holds "
-                    "%lld bytes (use tb_conv2d_fwd, or a smaller batch)",
+                    "noalloc conv: the pinned split needs %lld bytes of split-K scratch; the static scratch holds "
+                    "%lld bytes",
                     (long long)need * 4, (long long)NOALLOC_PARTIAL_FLOATS * 4);
     unsigned char* base = nullptr;
     r = scratch_address(ctx->device, &base);

@@ -244,13 +244,23 @@ __global__ void k_softmax(int64_t groups_total, int n, int groups, int64_t input
     }
 }
 
-// ---- global average pool (source/navgpoollayer.pas:60-84), sequential sum per channel ----
+// ---- global average pool (source/navgpoollayer.pas:60-84): Sum / (h*w), the sum in the order
+// of vssum_avx2 (source/ntensors.pas:3592-3620), which vsSumI uses on AVX2 CPUs: eight lane sums
+// over the whole blocks of 8, (l0+l4) .. (l3+l7), two horizontal adds, then the tail in order ----
 __global__ void k_avgpool(int64_t total, int im, const float* __restrict__ x, float* __restrict__ y) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float* p = x + i * im;
-        float s = 0.0f;
-        for (int j = 0; j < im; ++j) s = __fadd_rn(s, p[j]);
+        float lane[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int nb = im / 8 * 8;
+        for (int j = 0; j < nb; j += 8)
+#pragma unroll
+            for (int l = 0; l < 8; ++l) lane[l] = __fadd_rn(lane[l], p[j + l]);
+        float t[4];
+#pragma unroll
+        for (int l = 0; l < 4; ++l) t[l] = __fadd_rn(lane[l], lane[l + 4]);
+        float s = __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
+        for (int j = nb; j < im; ++j) s = __fadd_rn(s, p[j]);
         y[i] = __fdiv_rn(s, (float)im);
     }
 }
@@ -405,6 +415,63 @@ int tb_avgpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int6
     return check_launch("k_avgpool");
 }
 
+}  // extern "C"
+
+namespace tbi {
+
+// TConnectedLayer.forward (source/nconnectedlayer.pas:157-184): y = x * W^T through sgemm_nt, whose
+// dot product is sdot_avx2 (source/ntensors.pas:1233-1306) in the USE_AVX2 build the samples use:
+// eight lane sums (lane l: k = l, l+8, ..., one FMA each), then (l0+l4) ... and two horizontal
+// adds.  One thread per output keeps those eight lanes in registers; the block stages 64-deep k
+// chunks of 8 images' inputs and 32 outputs' packed weights (Wp[k][m]) in shared memory.
+__global__ void __launch_bounds__(256) k_fc_sdot8(const ConvParams p, int batch, int inputs) {
+    __shared__ float Xs[8][64];
+    __shared__ float Ws[64][32];
+    const int tid = threadIdx.x, ol = tid & 31, bl = tid >> 5;
+    const int o = blockIdx.x * 32 + ol, b = blockIdx.y * 8 + bl;
+    float lane[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < inputs; k0 += 64) {
+        for (int e = tid; e < 8 * 64; e += 256) {
+            const int bb = blockIdx.y * 8 + e / 64, kk = k0 + (e & 63);
+            Xs[e / 64][e & 63] = (bb < batch && kk < inputs) ? p.x[(long long)bb * p.x_bs + kk] : 0.f;
+        }
+        for (int e = tid; e < 64 * 32; e += 256) {
+            const int kk = k0 + e / 32, oo = blockIdx.x * 32 + (e & 31);
+            Ws[e / 32][e & 31] = (kk < inputs && oo < p.F) ? p.w[(long long)kk * p.Mpad + oo] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 64; ++kk) lane[kk & 7] = fmaf(Xs[bl][kk], Ws[kk][ol], lane[kk & 7]);
+        __syncthreads();
+    }
+    if (o >= p.F || b >= batch) return;
+    float t[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) t[l] = __fadd_rn(lane[l], lane[l + 4]);
+    const float s = __fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3]));
+    p.y[(long long)b * p.y_bs + o] = conv_epilogue(__fadd_rn(0.f, s), o, p);  // C := 0*C + alpha*sdot
+}
+
+int fc_sdot_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
+                   const float* bn_scale, const float* bn_mean, const float* bn_var, float* y, int act,
+                   int64_t* launches) {
+    if (g.B == 0) return TB_OK;
+    if (g.KH != 1 || g.KW != 1 || g.H != 1 || g.W != 1 || g.SY != 1 || g.SX != 1 || g.PY != 0 || g.PX != 0)
+        return fail(TB_ERR_INVALID, "fc: not a 1x1 layer over 1x1 inputs");
+    ConvParams p{};
+    p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
+    p.y = y; p.F = (int)g.F; p.Mpad = (int)g.Mpad; p.x_bs = g.x_bs; p.y_bs = g.y_bs; p.act = act;
+    dim3 grid((unsigned)ceil_div(g.F, 32), (unsigned)ceil_div(g.B, 8));
+    if (grid.y > 65535) return fail(TB_ERR_INVALID, "fc: batch too large");
+    k_fc_sdot8<<<grid, 256, 0, ctx->stream>>>(p, (int)g.B, (int)g.C);
+    if (launches) ++*launches;
+    return check_launch("k_fc_sdot8");
+}
+
+}  // namespace tbi
+
+extern "C" {
+
 int tb_fc_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t outputs, const float* x,
               const float* packed_w, const float* bias, int64_t activation, float* y) {
     TB_ENTER(ctx);
@@ -412,7 +479,13 @@ int tb_fc_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t outputs, const
     d.batch = batch; d.channels = inputs; d.height = 1; d.width = 1;
     d.filters = outputs; d.kernel_h = 1; d.kernel_w = 1; d.stride_y = 1; d.stride_x = 1;
     d.activation = activation;
-    return tb_conv2d_fwd(ctx, &d, x, packed_w, bias, nullptr, nullptr, nullptr, nullptr, y, TB_MATH_FP32);
+    if (batch == 0) return TB_OK;
+    if (!x || !packed_w || !y) return fail(TB_ERR_INVALID, "fc: null x, weights or y");
+    if (!act_supported(activation)) return fail(TB_ERR_UNSUPPORTED, "fc: activation %lld not supported", (long long)activation);
+    ConvGeom g;
+    int r = conv_geom(&d, &g);
+    if (r != TB_OK) return r;
+    return fc_sdot_launch(ctx, g, x, packed_w, bias, nullptr, nullptr, nullptr, y, (int)activation, nullptr);
 }
 
 }  // extern "C"

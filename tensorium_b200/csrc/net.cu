@@ -332,6 +332,14 @@ int run_layer(tb_net* net, int64_t i, const float* x) {
             return conv_tc_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
                                   L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
                                   (int)L.act, (int)L.fuse_yolo, reinterpret_cast<float*>(ctx->ws), &net->launches);
+        if (L.type == TB_LAYER_CONNECTED && net->math_mode != TB_MATH_FP32_TILED)
+            return fc_sdot_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
+                                  L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, T.out.ptr, (int)L.act,
+                                  &net->launches);
+        if (net->math_mode != TB_MATH_FP32_TILED && conv_exact_supported(g))
+            return conv_exact_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
+                                     L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
+                                     (int)L.act, (int)L.fuse_yolo, true, &net->launches);
         return conv_fp32_launch(ctx, g, in.ptr, L.d_wp, L.d_bias, L.bn ? L.d_scale : nullptr,
                                 L.bn ? L.d_mean : nullptr, L.bn ? L.d_var : nullptr, res, T.out.ptr,
                                 (int)L.act, (int)L.fuse_yolo, nullptr, 0, &net->launches);
@@ -587,7 +595,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     TB_ENTER(net->ctx);
     if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
     if (net->layers.empty()) return fail(TB_ERR_INVALID, "empty net");
-    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32)
+    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32 && math_mode != TB_MATH_FP32_TILED)
         return fail(TB_ERR_UNSUPPORTED, "net: math mode %lld is not available in this build", (long long)math_mode);
     net->math_mode = math_mode;
     int r = infer_shapes(net);
@@ -803,7 +811,8 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             L.d_var = dev_upload(net, L.var, &err);
             if (err != TB_OK) return err;
         }
-        ws_floats = std::max(ws_floats, conv_fp32_ws_floats(net->ctx, g));
+        if (net->math_mode == TB_MATH_FP32_TILED || !conv_exact_supported(g))
+            ws_floats = std::max(ws_floats, conv_fp32_ws_floats(net->ctx, g));
         net->flops += 2.0 * (double)g.F * (double)(g.B * g.OH * g.OW) * (double)(g.C * g.KH * g.KW);
     }
     // 4. measure the tile / split choices of every conv geometry on the real buffers
@@ -854,6 +863,13 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             if (net->math_mode == TB_MATH_TF32 && conv_tc_supported(g)) {
                 ws_floats = std::max(ws_floats, conv_tc_scratch_floats(g));
                 r = conv_tc_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr);
+                if (tmp) cudaFree(tmp);
+                if (r != TB_OK) return r;
+                continue;
+            }
+            if (net->math_mode != TB_MATH_FP32_TILED) {  // the order-exact kernels need no workspace
+                r = L.type == TB_LAYER_CONNECTED ? TB_OK
+                                                 : conv_exact_autotune(net->ctx, g, in.ptr, L.d_wp, T.out.ptr, true);
                 if (tmp) cudaFree(tmp);
                 if (r != TB_OK) return r;
                 continue;

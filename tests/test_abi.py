@@ -13,7 +13,7 @@ from tensorium_b200._lib import ConvDesc, check, lib
 def header_functions():
     text = (ROOT / "include" / "tensorium_b200.h").read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(?:int|void\s*\*|const char\s*\*)\s*(tb_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(?:int|void\s*\*|const char\s*\*)\s*(tb(?:compat)?_\w+)\s*\(", text)))
 
 
 def test_every_declared_symbol_is_exported():
@@ -83,3 +83,11 @@ def test_init_without_gpu_fails_cleanly():
     h = C.c_void_p()
     rc = lib.tb_init(0, None, C.byref(h))
     assert rc < 0 and not h.value
+
+
+def test_integration_unit_declares_every_function():
+    """The Pascal binding unit in INTEGRATION.md declares every function of the header."""
+    text = (ROOT / "INTEGRATION.md").read_text()
+    declared = set(re.findall(r"function (tb(?:compat)?_\w+)\b[^;]*;[^\n]*external libB200", text))
+    missing = set(header_functions()) - declared
+    assert not missing, sorted(missing)

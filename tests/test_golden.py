@@ -7,7 +7,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from conftest import FP32_TOL, worst_map_err, yolo_err
+from conftest import assert_bit_exact, assert_yolo_parity
 from oracle import oracle as O
 from tensorium_b200 import synth
 
@@ -56,9 +56,9 @@ def test_gpu_matches_golden_network(ctx):
         got = net.output(i).cpu().numpy()
         ref = G[f"net_{i}"]
         if s["type"] == "yolo":
-            assert yolo_err(got, ref, G[f"net_{i - 1}"], 3, 3) <= 1.0, i
+            assert_yolo_parity(got.reshape(ref.shape), ref, 3, 3, i)
         else:
-            assert worst_map_err(got, ref, 2 * shapes[i][0]) <= FP32_TOL, i
+            assert_bit_exact(got.reshape(ref.shape), ref, 2 * shapes[i][0], i)
     recs, probs, counts = net.detections(640, 480, 0.5, relative=False, letter=True, capacity=4096)
     # heads: the last yolo layer only in the golden record (image 0)
     heads, outs = net.yolo_heads()

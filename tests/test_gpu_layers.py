@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import FP32_TOL, max_rel_err, worst_map_err
+from conftest import assert_bit_exact
 from oracle import oracle as O
 from tensorium_b200._lib import check, lib
 from tensorium_b200.context import ptr
@@ -98,7 +98,7 @@ def test_softmax_avgpool_connected(ctx):
     b = rng.standard_normal(1024).astype(np.float32) * 0.1
     fc = TConnectedLayer(256, 1, 3136, 1024, "relu", w, b).bind(ctx)
     yf = fc.forward(TNNetState(dev(ctx, xi))).cpu().numpy()
-    assert worst_map_err(yf, O.connected(xi, w, b, 1), 256) <= FP32_TOL
+    assert_bit_exact(yf, O.connected(xi, w, b, 1), 256, "connected (sdot_avx2 order)")
 
 
 @pytest.mark.parametrize("C,S,B", [(128, 13, 2), (256, 26, 1), (64, 7, 3), (40, 9, 2)])
@@ -145,3 +145,25 @@ def test_detections_match_oracle_order_and_values(ctx):
         got_box = np.c_[r["x"], r["y"], r["w"], r["h"], r["objectness"]]
         np.testing.assert_allclose(got_box, np.concatenate(exp_boxes), rtol=1e-6, atol=1e-6)
         assert np.array_equal(probs[b, :total], np.concatenate(exp_probs))
+
+
+@pytest.mark.parametrize("C", [128, 256, 512, 1024])
+@pytest.mark.parametrize("S", [52, 26, 13])
+def test_xnor_config4_batch64(ctx, C, S):
+    """BASELINE config 4 at its full size: C_in = C_out = C, 3x3 s1 p1, S x S, batch 64.  The
+    serial oracle checks images 0, 31 and 63 of the batch-64 launch bit for bit (popcounts and
+    scaled outputs, the reference's bit-0 padding)."""
+    B = 64
+    rng = np.random.default_rng(1000 + C + S)
+    w = rng.standard_normal((C, C * 9)).astype(np.float32)
+    g = torch.Generator(device=ctx.torch_device).manual_seed(C * 100 + S)
+    x = torch.randn((B, C, S, S), generator=g, device=ctx.torch_device)
+    L = TXNORConvolutionLayer(B, S, S, C, C, 3, 1, 1, "linear", 0)
+    L.upload(ctx, w)
+    cnt = torch.empty((B, C, S, S), dtype=torch.int32, device=ctx.torch_device)
+    y = L.forward(TNNetState(x), counts=cnt)
+    mean = O.xnor_mean(w)
+    for b in (0, 31, 63):
+        rc, ry = O.xnor_conv(x[b:b + 1].cpu().numpy(), w, mean, C, 3, 1, 1, 0)
+        assert np.array_equal(cnt[b:b + 1].cpu().numpy(), rc), b
+        assert np.array_equal(y[b:b + 1].cpu().numpy(), ry), b

@@ -67,13 +67,13 @@ def test_bias_bn_and_leaky_follow_the_reference_formulas():
     sd = np.sqrt(var.astype(np.float64)).astype(np.float32)
     t = ((x - mu[None, :, None, None]) / sd[None, :, None, None]).astype(np.float32)
     t = (t * sc[None, :, None, None]).astype(np.float32) + b[None, :, None, None]
-    expect = np.where(t < 0, (0.1 * t.astype(np.float64)).astype(np.float32), t)
+    expect = np.where(t < 0, t * np.float32(0.1), t)
     assert np.array_equal(y, expect)
 
 
 def test_activation_forms():
     x = np.array([-3.0, -0.5, -0.0, 0.0, 0.5, 7.0], np.float32)
-    assert np.array_equal(O.activate(x, LEAKY), np.where(x < 0, (0.1 * x.astype(np.float64)).astype(np.float32), x))
+    assert np.array_equal(O.activate(x, LEAKY), np.where(x < 0, x * np.float32(0.1), x))
     lg = (1.0 / (1.0 + np.exp(-x.astype(np.float64)))).astype(np.float32)
     assert np.array_equal(O.activate(x, LOGISTIC), lg)
     assert np.array_equal(O.activate(x, RELU), np.maximum(x, 0) * (x > 0))
