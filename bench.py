@@ -40,7 +40,7 @@ INPUT = (3, 416, 416)
 HEADS = (82, 94, 106)
 METRIC = "YOLOv3-416 images/sec (FP32 path)"
 METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
-MATH_MODES = {"fp32": 0, "tf32": 1}
+MATH_MODES = {"fp32": 0, "tf32": 1, "fp32_tiled": 2}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
 PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "k_conv_nhwc_yolov3_b8.json"
 
@@ -225,28 +225,67 @@ def run_ours(args):
     clocks = clk.summary()
     value = world * B * args.steps / (ms / 1e3)
 
-    # ---- end to end: pinned host in, heads out, every step (StreamPredictor: the host copies of
-    #      step i+1 / i-1 overlap the forward of step i) ----
-    from tensorium_b200.net import StreamPredictor
+    # ---- end to end through the public API, every step: pinned host images -> H2D (upload stream,
+    #      the next step's copy overlapping this step's forward) -> TNNet.forward (graph) -> GPU
+    #      detection extraction -> NCCL gather of every rank's detections to rank 0 through the C
+    #      ABI (tb_group_gather) -> D2H of the gathered detections on rank 0 ----
     h_in = torch.from_numpy(x_host).pin_memory()
-    h_outs = [torch.empty(net.output(h).shape, dtype=torch.float32).pin_memory() for h in HEADS]
-    sp = StreamPredictor(net, HEADS)
-    for _ in range(max(args.warmup, 1)):
-        sp.submit(h_in, h_outs)
-    sp.wait()
+    gat = tbd.DetectionGather(net, world, rank, capacity=1024, thresh=0.45)
+    upload = torch.cuda.Stream(local)
+    x_fixed = torch.empty_like(x)  # the forward's one input buffer (one CUDA graph)
+    d_in = [torch.empty_like(x), torch.empty_like(x)]
+    ev_h2d = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_free = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def upload_into(k, wait_free):
+        with torch.cuda.stream(upload):
+            if wait_free:
+                upload.wait_event(ev_free[k])
+            d_in[k].copy_(h_in, non_blocking=True)
+            ev_h2d[k].record(upload)
+
+    def e2e_steps(n):
+        upload_into(0, False)
+        for k in range(n):
+            cur = k % 2
+            stream.wait_event(ev_h2d[cur])
+            x_fixed.copy_(d_in[cur])
+            ev_free[cur].record(stream)
+            if k + 1 < n:  # the next step's upload overlaps this step's forward
+                upload_into(1 - cur, k >= 1)
+            net.forward(x_fixed)
+            gat.step(download=True)
+
+    e2e_steps(max(args.warmup, 1))
     barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gather_ms = []
     e0.record(stream)
-    for _ in range(args.steps):
-        sp.submit(h_in, h_outs)
-    stream.wait_stream(sp.download)
+    e2e_steps(args.steps)
     e1.record(stream)
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+    # the gather alone (device time of detection extraction + NCCL gather + D2H), max over ranks
+    for _ in range(5):
+        barrier()
+        g0.record(stream)
+        gat.step(download=True)
+        g1.record(stream)
+        barrier()
+        gather_ms.append(g0.elapsed_time(g1))
+    gathered = gat.unpack()
     e2e = {"value": world * B * args.steps / (ms_e2e / 1e3), "unit": "images/s",
            "h2d_bytes_per_step": int(h_in.numel() * 4),
-           "d2h_bytes_per_step": int(sum(o.numel() * 4 for o in h_outs)),
-           "path": ("StreamPredictor: pinned host -> H2D (upload stream) -> TNNet.forward (graph) -> D2H of the "
-                    "3 yolo heads (download stream), consecutive steps overlapped through double-buffered staging")}
+           "d2h_bytes_per_step": int(gat.d2h_bytes),
+           "detect_and_gather_ms": max_over_ranks(float(np.median(gather_ms))),
+           "gathered_on_rank0": {"images": len(gathered) if gathered is not None else None,
+                                 "boxes": int(sum(len(r) for r in gathered)) if gathered is not None else None,
+                                 "bytes": int(gat.d2h_bytes), "capacity_per_image": gat.capacity,
+                                 "thresh": gat.thresh},
+           "path": ("pinned host -> H2D (upload stream, overlapping the previous forward) -> TNNet.forward "
+                    "(graph) -> tb_yolo_detect -> tb_group_gather (NCCL, C ABI) of every rank's records "
+                    "+ counts to rank 0 -> D2H on rank 0, every step")}
+    gat.close()
 
     # ---- roofline of the conv kernels (per-layer CUDA events, eager forward) ----
     prof = np.zeros(len(specs))
@@ -266,8 +305,9 @@ def run_ours(args):
         fma = __import__("ctypes").c_double()
         from tensorium_b200._lib import check, lib
         check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
-        peak, bound, kernel = fma.value, "fp32", ("conv_fp32_kernel / k_conv_fp32_tma (+ split-K fix-up, "
-                                                  "tap replicas) for 74 convs and k_conv_direct for the first")
+        peak, bound, kernel = fma.value, "fp32", ("k_conv_exact (order-exact FP32 implicit GEMM, bit-identical "
+                                                  "to the reference CPU path) for 74 convs and k_conv_direct for "
+                                                  "the first")
         peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
                        "and bf16 tensor peaks only")
     else:
@@ -285,12 +325,6 @@ def run_ours(args):
                 "algorithmic_flops_per_forward": conv_flops, "conv_ms_per_forward": conv_ms,
                 "all_layers_ms_per_forward": total_ms}
 
-    # detections of this rank's images, gathered to rank 0 in global image order (outside the
-    # timed region; NCCL carries only this final gather)
-    net.forward(x)
-    recs, probs, counts = net.detections(416, 416, 0.45, capacity=16384)
-    gathered = tbd.gather_detections(tbd.detections_per_image(recs, probs, counts, 16384))
-
     line = {"metric": METRIC if args.math == "fp32" else METRIC_TF32, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.math == "fp32" else "tf32 (fp32 accumulate)",
@@ -301,10 +335,7 @@ def run_ours(args):
                        "input": "3x416x416", "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2: each step streams ~1.3 GB of activations per GPU"},
             "e2e": e2e, "roofline": roofline, "clocks": clocks,
-            "gpu_launches": int(launches_per_step * args.steps),
-            "detections": {"images_gathered_on_rank0": len(gathered) if gathered is not None else None,
-                           "boxes": int(sum(len(r) for r, _ in gathered)) if gathered is not None else None,
-                           "thresh": 0.45}}
+            "gpu_launches": int(launches_per_step * args.steps)}
     if args.math == "fp32" and not args.no_tf32_block:
         line["tf32_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream)
     if world == 1 and not args.no_kernel_suite:
@@ -582,7 +613,7 @@ def main():
     ap.add_argument("--no-kernel-suite", action="store_true", help="skip the memory-bound / XNOR kernel suite")
     ap.add_argument("--suite", choices=["kernels"], default=None, help="run only the kernel suite")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
-    ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
+    ap.add_argument("--math", choices=["fp32", "tf32", "fp32_tiled"], default="fp32",
                     help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")
     ap.add_argument("--nhwc", action="store_true", help="with --layer and --math tf32: the NHWC tensor-core kernel")
     ap.add_argument("--profile-window", action="store_true",

@@ -405,6 +405,36 @@ int tbcompat_upSample(tb_ctx* ctx, int64_t aBatch, int64_t aChannels, int64_t ou
 int tb_bn_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t spatial, const float* x, const float* mean,
               const float* variance, const float* scales, const float* biases, float* y);
 
+/* ---- multi-GPU group (NCCL) ------------------------------------------------------------
+ * Inference shards by image: each GPU runs the whole network on its slice of the batch, and the
+ * only exchange is the final gather of per-GPU results (detection records, counts, logits) to
+ * rank 0. The reference has no multi-GPU path (source/nConvolutionLayer.pas:472 marks it as
+ * future work); these entry points are new. NCCL (libnccl.so.2) is loaded on first use. */
+typedef struct tb_group tb_group;
+/* NCCL loads; *nccl_version = its version code (may be NULL). TB_ERR_UNSUPPORTED without NCCL. */
+int tb_group_available(int64_t* nccl_version);
+/* One process drives ngpu GPUs: a context per device (tb_group_context) and NCCL communicators
+ * over them (ncclCommInitAll). Ranks follow `devices`. */
+int tb_group_init(int64_t ngpu, const int64_t* devices, tb_group** out);
+/* One process per GPU: rank 0 makes the 128-byte id, the caller hands it to every rank. */
+int tb_group_unique_id(void* id_out);
+/* This process's rank over ctx's GPU. Non-blocking NCCL initialisation with a deadline of
+ * timeout_ms: if a rank never joins, every waiting rank aborts its communicator and returns
+ * TB_ERR_TIMEOUT (the same deadline bounds every later tb_group_gather). */
+int tb_group_init_rank(tb_ctx* ctx, int64_t nranks, int64_t rank, const void* id, int64_t timeout_ms,
+                       tb_group** out);
+/* Group size, global rank of this process's first GPU, GPUs this process drives. */
+int tb_group_size(tb_group* g, int64_t* nranks, int64_t* first_local_rank, int64_t* local_gpus);
+/* Context of local GPU `local` (tb_group_init groups own them; do not shut them down). */
+int tb_group_context(tb_group* g, int64_t local, tb_ctx** ctx);
+/* Gather to rank 0: rank r sends bytes_per_rank[r] bytes (every rank passes the whole array)
+ * from its device buffer send_local[i] (i = local GPU index), and rank 0 receives them back to
+ * back in rank order at recv_root (device memory of rank 0's GPU; ignored on other ranks).
+ * Blocks until this process's part is complete, within the group's deadline (then the
+ * communicators are aborted and TB_ERR_TIMEOUT returned; the group is unusable afterwards). */
+int tb_group_gather(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank, void* recv_root);
+int tb_group_destroy(tb_group* g);
+
 /* ---- whole-network executor (TNNet.forward / predict, source/nnet.pas:275-317,452-472) --- */
 typedef struct tb_net tb_net;
 #define TB_LAYER_CONV      1

@@ -113,6 +113,14 @@ SIGNATURES = {
     "tb_addvv": [P, I64, P, I64, I64, P, I64, I64, P, I64, I64],
     "tb_fmavss": [P, I64, P, I64, F32, F32, P],
     "tb_bn_fwd": [P, I64, I64, I64, P, P, P, P, P, P],
+    "tb_group_available": [PI64],
+    "tb_group_init": [I64, PI64, C.POINTER(P)],
+    "tb_group_unique_id": [P],
+    "tb_group_init_rank": [P, I64, I64, P, I64, C.POINTER(P)],
+    "tb_group_size": [P, PI64, PI64, PI64],
+    "tb_group_context": [P, I64, C.POINTER(P)],
+    "tb_group_gather": [P, C.POINTER(P), PI64, P],
+    "tb_group_destroy": [P],
     # TNNCuda method shims (argument lists of source/nncuda.pas:100-151)
     "tbcompat_createDeviceBuffer": [P, I64, C.POINTER(P)],
     "tbcompat_freeDeviceBuffer": [P, P],

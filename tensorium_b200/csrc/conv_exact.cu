@@ -15,6 +15,13 @@ struct ExactTile {
 };
 constexpr ExactTile kTiles[] = {{128, 128, 256}, {64, 128, 128}, {128, 64, 128}, {64, 64, 64}, {32, 128, 128}};
 constexpr int kNumTiles = 5;
+constexpr int kNumVariants = 4;  // stage-depth variants (ExactShape) of the 3x3 and 1x1-vector modes
+
+// configurations: t = variant * kNumTiles + tile
+int num_configs(int mode, bool fma) {
+    if (mode == EX_3X3) return kNumVariants * kNumTiles;
+    return (mode == EX_1X1V && fma) ? 3 * kNumTiles : kNumTiles;
+}
 
 int exact_mode_of(const ConvGeom& g, const float* x) {
     if (g.KH == 1 && g.KW == 1) {
@@ -27,18 +34,20 @@ int exact_mode_of(const ConvGeom& g, const float* x) {
     return EX_GEN;
 }
 
+// tile index t of kTiles plus a stage-depth variant (ExactShape) in t / kNumTiles
 int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool fma) {
-    switch (t) {
-    case 0: return exact_launch_128x128(ctx, p, grid, mode, fma);
-    case 1: return exact_launch_64x128(ctx, p, grid, mode, fma);
-    case 2: return exact_launch_128x64(ctx, p, grid, mode, fma);
-    case 3: return exact_launch_64x64(ctx, p, grid, mode, fma);
-    default: return exact_launch_32x128(ctx, p, grid, mode, fma);
+    const int var = t / kNumTiles;
+    switch (t % kNumTiles) {
+    case 0: return exact_launch_128x128(ctx, p, grid, mode, fma, var);
+    case 1: return exact_launch_64x128(ctx, p, grid, mode, fma, var);
+    case 2: return exact_launch_128x64(ctx, p, grid, mode, fma, var);
+    case 3: return exact_launch_64x64(ctx, p, grid, mode, fma, var);
+    default: return exact_launch_32x128(ctx, p, grid, mode, fma, var);
     }
 }
 
 bool tile_admissible(int t, int64_t M) {
-    const int BM = kTiles[t].BM;
+    const int BM = kTiles[t % kNumTiles].BM;
     if (M <= 32) return BM == 32;
     if (M <= 64) return BM <= 64;
     return BM >= 64;
@@ -47,7 +56,7 @@ bool tile_admissible(int t, int64_t M) {
 // Wave model: an SM that receives k CTAs of a tile runs them at a rate that grows with the warps
 // resident (full from 12 warps up); the layer ends with the busiest SM.
 double model_cost(tb_ctx* ctx, int t, const ConvGeom& g, int mode) {
-    const ExactTile& T = kTiles[t];
+    const ExactTile& T = kTiles[t % kNumTiles];
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int64_t tiles = ceil_div(M, T.BM) * ceil_div(N, T.BN);
     ConvParams dummy{};
@@ -58,7 +67,7 @@ double model_cost(tb_ctx* ctx, int t, const ConvGeom& g, int mode) {
     const int64_t resident = std::min<int64_t>(per_sm, occ);
     const double warps = (double)resident * T.NT / 32.0;
     const double rate = std::min(1.0, warps / 12.0);
-    const double eff = (T.BM == 128 && T.BN == 128) ? 1.0 : (T.BM == 32 ? 0.85 : (T.BM * T.BN == 8192 ? 0.95 : 0.9));
+    const double eff = (T.BM * T.BN >= 16384) ? 1.0 : (T.BM == 32 ? 0.85 : (T.BM * T.BN == 8192 ? 0.95 : 0.9));
     return (double)rounds * resident * T.BM * T.BN / (rate * eff);
 }
 
@@ -71,10 +80,12 @@ std::vector<int64_t> key_of(const tb_ctx* ctx, const ConvGeom& g, int mode, bool
 }
 
 int choose_tile(tb_ctx* ctx, const ConvGeom& g, int mode, bool fma) {
-    // test hook: TB_EXACT_FORCE=<tile index 0..4> pins the CTA tile (parity tests of every tile)
+    // test hook: TB_EXACT_FORCE=<configuration> pins the CTA tile (index % 5) and stage-depth
+    // variant (index / 5) for the parity tests of every configuration
     if (const char* f = getenv("TB_EXACT_FORCE")) {
         int t = atoi(f);
-        if (t >= 0 && t < kNumTiles && tile_admissible(t, g.F)) return t;
+        if (t >= 0 && t < num_configs(mode, fma) && tile_admissible(t, g.F)) return t;
+        if (t >= 0 && tile_admissible(t % kNumTiles, g.F)) return t % kNumTiles;
     }
     {
         std::lock_guard<std::mutex> lk(g_mu);
@@ -114,7 +125,7 @@ ConvParams params_of(const ConvGeom& g, const float* x, const float* wp, const f
 }
 
 int launch_tile(tb_ctx* ctx, int t, const ConvGeom& g, const ConvParams& p, int mode, bool fma) {
-    const ExactTile& T = kTiles[t];
+    const ExactTile& T = kTiles[t % kNumTiles];
     dim3 grid((unsigned)ceil_div(p.Ntot, T.BN), (unsigned)ceil_div(g.F, T.BM), 1);
     if (grid.y > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     return run_tile(ctx, t, p, grid, mode, fma);
@@ -158,7 +169,7 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
     TB_CHECK_CUDA(cudaEventCreate(&e1));
     float best_ms = 1e30f;
     int best = -1, rc = TB_OK;
-    for (int t = 0; t < kNumTiles && rc == TB_OK; ++t) {
+    for (int t = 0; t < num_configs(mode, fma) && rc == TB_OK; ++t) {
         if (!tile_admissible(t, g.F)) continue;
         rc = launch_tile(ctx, t, g, p, mode, fma);  // warm-up
         if (rc != TB_OK) break;
@@ -171,9 +182,9 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
         float ms = 0.f;
         cudaEventElapsedTime(&ms, e0, e1);
         if (getenv("TB_AUTOTUNE_VERBOSE"))
-            fprintf(stderr, "exact autotune C%lld H%lld F%lld k%lld s%lld B%lld: tile %dx%d mode %d: %.4f ms\n",
+            fprintf(stderr, "exact autotune C%lld H%lld F%lld k%lld s%lld B%lld: tile %dx%d var %d mode %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY, (long long)g.B,
-                    kTiles[t].BM, kTiles[t].BN, mode, ms / 3);
+                    kTiles[t % kNumTiles].BM, kTiles[t % kNumTiles].BN, t / kNumTiles, mode, ms / 3);
         if (ms < best_ms) { best_ms = ms; best = t; }
     }
     cudaEventDestroy(e0);

@@ -31,32 +31,37 @@ namespace tbi {
 enum ExactMode { EX_1X1V = 0, EX_1X1 = 1, EX_3X3 = 2, EX_GEN = 3 };
 constexpr int EX_GEN_TAPS = 25;  // generic tap loop: kernel windows of at most 25 taps
 
-template <int MODE, int G>
+// VAR selects the stage depth: 0 = 2 channels (3x3) / 16 channels (1x1) per stage, 4-deep ring;
+// 1 = twice the channels per stage, 3-deep ring; 2 = the channels of 0, 3-deep ring; 3 = as 0,
+// compiled for one resident CTA per SM (no register cap from occupancy).
+template <int MODE, int G, int VAR = 0>
 struct ExactShape {
-    static constexpr int STAGES = MODE == EX_GEN ? 3 : 4;
-    static constexpr int KSMAX = MODE == EX_3X3 ? 18 : (MODE == EX_GEN ? G * EX_GEN_TAPS : 16);
-    static constexpr int CC = MODE == EX_3X3 ? 2 : (MODE == EX_GEN ? G : 16);  // channels per stage
+    static constexpr int STAGES = (MODE == EX_GEN || VAR > 0) ? 3 : 4;
+    static constexpr int CC = MODE == EX_3X3 ? (VAR == 1 ? 4 : 2) : (MODE == EX_GEN ? G : (VAR == 1 ? 32 : 16));
+    static constexpr int KSMAX = MODE == EX_3X3 ? 9 * CC : (MODE == EX_GEN ? G * EX_GEN_TAPS : CC);
 };
 
-template <int BM, int BN, int TM>
-__host__ __device__ constexpr int exact_threads() { return (BM / TM) * (BN / 8); }
+template <int BM, int BN, int TM, int TN>
+__host__ __device__ constexpr int exact_threads() { return (BM / TM) * (BN / TN); }
 
-inline int exact_smem_bytes(int BM, int BN, int NT, int mode) {
-    const int G = NT / BN;
-    int st = 4, ks = 16;
-    if (mode == EX_3X3) ks = 18;
-    if (mode == EX_GEN) { st = 3; ks = G * EX_GEN_TAPS; }
-    return st * ks * (BM + BN) * 4;
+template <int MODE, int G, int VAR>
+inline int exact_smem_bytes(int BM, int BN) {
+    using S = ExactShape<MODE, G, VAR>;
+    return S::STAGES * S::KSMAX * (BM + BN) * 4;
 }
 
-template <int BM, int BN, int TM, int MODE, bool FMA>
-__global__ void __launch_bounds__(exact_threads<BM, BN, TM>(), 512 / exact_threads<BM, BN, TM>())
+// TM x TN outputs per thread: filters in two TM/2 quads BM/2 apart, pixels in TN/4 quads BN*4/TN
+// apart (every shared-memory read a broadcast or a conflict-free float4).  TN = 16 tiles and VAR 3
+// are compiled without an occupancy-derived register cap.
+template <int BM, int BN, int TM, int TN, int MODE, bool FMA, int VAR>
+__global__ void __launch_bounds__(exact_threads<BM, BN, TM, TN>(),
+                                  (VAR == 3 || TN == 16) ? 1 : 512 / exact_threads<BM, BN, TM, TN>())
 k_conv_exact(const ConvParams p) {
-    constexpr int TN = 8, TX = BN / TN, TM2 = TM / 2;
-    constexpr int NT = exact_threads<BM, BN, TM>();
+    constexpr int TX = BN / TN, TM2 = TM / 2, NQ = TN / 4, QS = BN / NQ;
+    constexpr int NT = exact_threads<BM, BN, TM, TN>();
     constexpr int G = NT / BN;  // pixel-column groups of the activation loader
     static_assert(G == 1 || G == 2, "one or two threads per pixel column");
-    using S = ExactShape<MODE, G>;
+    using S = ExactShape<MODE, G, VAR>;
     constexpr int STAGES = S::STAGES, KSMAX = S::KSMAX, CC = S::CC;
     extern __shared__ __align__(16) float smem[];
     float* As = smem;                      // [STAGES][KSMAX][BM]
@@ -138,8 +143,8 @@ k_conv_exact(const ConvParams p) {
         pixoff = pixok ? iy0 * p.W + ix0 : 0;
     }
     // 1x1 vectorised: thread -> (pixel quad, channel rows v_r0 + i*VRG)
-    constexpr int BQ = BN / 4, VRG = NT / BQ, VIT = 16 / VRG;
-    static_assert(MODE != EX_1X1V || (NT % BQ == 0 && 16 % VRG == 0), "1x1 quads cover the tile");
+    constexpr int BQ = BN / 4, VRG = NT / BQ, VIT = CC / VRG;
+    static_assert(MODE != EX_1X1V || (NT % BQ == 0 && CC % VRG == 0), "1x1 quads cover the tile");
     const float* vq = p.x;
     bool vok = false;
     int v_r0 = 0;
@@ -155,7 +160,46 @@ k_conv_exact(const ConvParams p) {
         }
     }
 
+    // One copy ("item") of a stage: items 0 .. WIT-1 are this thread's weight rows, the rest its
+    // activation elements.  Called with compile-time i (unrolled loops), so every branch folds.
+    constexpr int RPG1 = CC / G, CPG3 = CC / G;
+    constexpr int NA = MODE == EX_1X1V ? VIT : (MODE == EX_1X1 ? RPG1 : (MODE == EX_3X3 ? 9 * CPG3 : 0));
+    constexpr int NITEMS = WIT + NA;
+    auto load_item = [&](int i, int st_idx, int buf) {
+        const int c0 = st_idx * CC;
+        if (i < WIT) {
+            const int row = w_r0 + i * RG;
+            if (row < KS) {
+                const bool ok = w_mok && c0 + w_cc[i] < p.C;
+                cp_async16(As + buf * KSMAX * BM + row * BM + 4 * w_mq,
+                           ok ? p.w + (long long)st_idx * wstep + w_off[i] : p.w, ok);
+            }
+            return;
+        }
+        const int a = i - WIT;
+        float* bs = Bs + buf * KSMAX * BN;
+        if (MODE == EX_1X1V) {
+            const int row = v_r0 + a * VRG;
+            const bool ok = vok && c0 + row < p.C;
+            cp_async16(bs + row * BN + 4 * (tid % BQ), ok ? vq + (long long)(c0 + row) * HW : p.x, ok);
+        } else if (MODE == EX_1X1) {
+            const int row = g * RPG1 + a;
+            const bool ok = pixok && c0 + row < p.C;
+            cp_async4(bs + row * BN + bcol, ok ? xb + (long long)(c0 + row) * HW + pixoff : p.x, ok);
+        } else if (MODE == EX_3X3) {
+            const int ch = g * CPG3 + a / 9, tap = a % 9, r = tap / 3, s = tap % 3;
+            const bool ok = c0 + ch < p.C && ((tapok >> tap) & 1u);
+            cp_async4(bs + (ch * 9 + tap) * BN + bcol, ok ? xb + (long long)(c0 + ch) * HW + rowoff[r] + coloff[s] : p.x,
+                      ok);
+        }
+    };
+
     auto load_stage = [&](int st_idx, int buf) {
+        if (MODE != EX_GEN) {
+#pragma unroll
+            for (int i = 0; i < NITEMS; ++i) load_item(i, st_idx, buf);
+            return;
+        }
         const int c0 = st_idx * CC;
         float* as = As + buf * KSMAX * BM;
         const float* wst = p.w + (long long)st_idx * wstep;
@@ -176,7 +220,7 @@ k_conv_exact(const ConvParams p) {
                 cp_async16(bs + row * BN + 4 * (tid % BQ), ok ? vq + (long long)(c0 + row) * HW : p.x, ok);
             }
         } else if (MODE == EX_1X1) {
-            constexpr int RPG = 16 / G;
+            constexpr int RPG = CC / G;
 #pragma unroll
             for (int j = 0; j < RPG; ++j) {
                 const int row = g * RPG + j;
@@ -184,7 +228,7 @@ k_conv_exact(const ConvParams p) {
                 cp_async4(bs + row * BN + bcol, ok ? xb + (long long)(c0 + row) * HW + pixoff : p.x, ok);
             }
         } else if (MODE == EX_3X3) {
-            constexpr int CPG = 2 / G;  // channels of this thread per stage
+            constexpr int CPG = CC / G;  // channels of this thread per stage
 #pragma unroll
             for (int cc = 0; cc < CPG; ++cc) {
                 const int ch = g * CPG + cc;
@@ -229,8 +273,9 @@ k_conv_exact(const ConvParams p) {
         float a[TM], bv[TN];
         *reinterpret_cast<AV*>(&a[0]) = *reinterpret_cast<const AV*>(as + ty * TM2);
         *reinterpret_cast<AV*>(&a[TM2]) = *reinterpret_cast<const AV*>(as + BM / 2 + ty * TM2);
-        *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bs + tx * 4);
-        *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bs + BN / 2 + tx * 4);
+#pragma unroll
+        for (int q = 0; q < NQ; ++q)
+            *reinterpret_cast<float4*>(&bv[4 * q]) = *reinterpret_cast<const float4*>(bs + q * QS + tx * 4);
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -240,7 +285,30 @@ k_conv_exact(const ConvParams p) {
             }
     };
 
-    for (int t = 0; t < nst; ++t) {
+    // non-generic modes: the copies of stage t + STAGES - 1 are spread over the k steps of stage t
+    // (IPK after each step), so the FMA stream is not held up by a burst of address arithmetic
+    constexpr int IPK = (NITEMS + KSMAX - 1) / KSMAX;
+    if (MODE != EX_GEN) {
+        for (int t = 0; t < nst; ++t) {
+            cp_async_wait<STAGES - 2>();
+            __syncthreads();
+            const int tn = t + STAGES - 1;
+            const bool more = tn < nst;
+            const int nbuf = tn % STAGES;
+            const float* as = As + (t % STAGES) * KSMAX * BM;
+            const float* bs = Bs + (t % STAGES) * KSMAX * BN;
+#pragma unroll
+            for (int kk = 0; kk < KSMAX; ++kk) {
+                kstep(as + kk * BM, bs + kk * BN);
+                if (more) {
+#pragma unroll
+                    for (int i = kk * IPK; i < (kk + 1) * IPK && i < NITEMS; ++i) load_item(i, tn, nbuf);
+                }
+            }
+            cp_async_commit();
+        }
+    }
+    for (int t = 0; MODE == EX_GEN && t < nst; ++t) {
         cp_async_wait<STAGES - 2>();
         __syncthreads();
         {
@@ -261,7 +329,9 @@ k_conv_exact(const ConvParams p) {
     cp_async_wait<0>();
 
     // ---- epilogue (the tiled kernel's, without split-K) ----
-    const ColQuad cq[2] = {decode_quad(p, n0 + tx * 4), decode_quad(p, n0 + BN / 2 + tx * 4)};
+    ColQuad cq[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) cq[q] = decode_quad(p, n0 + q * QS + tx * 4);
     const bool simple = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
     const bool has_bias = p.bias != nullptr, leaky = p.act == TB_ACT_LEAKY;
     const float* __restrict__ biasp = p.bias;
@@ -271,15 +341,15 @@ k_conv_exact(const ConvParams p) {
         if (m >= p.F) continue;
         const float bm = has_bias ? __ldg(biasp + m) : 0.f;
 #pragma unroll
-        for (int gq = 0; gq < 2; ++gq) conv_store4(p, m, cq[gq], &acc[i][gq * 4], simple, has_bias, leaky, bm);
+        for (int gq = 0; gq < NQ; ++gq) conv_store4(p, m, cq[gq], &acc[i][gq * 4], simple, has_bias, leaky, bm);
     }
 }
 
-template <int BM, int BN, int TM, int MODE, bool FMA>
+template <int BM, int BN, int TM, int TN, int MODE, bool FMA, int VAR>
 int exact_launch_one(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
-    constexpr int NT = exact_threads<BM, BN, TM>();
-    const int smem = exact_smem_bytes(BM, BN, NT, MODE);
-    auto kern = k_conv_exact<BM, BN, TM, MODE, FMA>;
+    constexpr int NT = exact_threads<BM, BN, TM, TN>();
+    const int smem = exact_smem_bytes<MODE, NT / BN, VAR>(BM, BN);
+    auto kern = k_conv_exact<BM, BN, TM, TN, MODE, FMA, VAR>;
     static std::mutex mu;
     static bool done[64] = {false};
     {
@@ -300,25 +370,32 @@ int exact_launch_one(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
     return check_launch("k_conv_exact");
 }
 
-template <int BM, int BN, int TM>
-int exact_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma) {
+// var: stage-depth variant (ExactShape) of the 3x3 and vectorised 1x1 modes
+template <int BM, int BN, int TM, int TN>
+int exact_launch_modes(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var) {
     switch (mode) {
     case EX_1X1V:
-        return fma ? exact_launch_one<BM, BN, TM, EX_1X1V, true>(ctx, p, grid)
-                   : exact_launch_one<BM, BN, TM, EX_1X1V, false>(ctx, p, grid);
+        if (!fma) return exact_launch_one<BM, BN, TM, TN, EX_1X1V, false, 0>(ctx, p, grid);
+        if (var == 1) return exact_launch_one<BM, BN, TM, TN, EX_1X1V, true, 1>(ctx, p, grid);
+        if (var == 2) return exact_launch_one<BM, BN, TM, TN, EX_1X1V, true, 2>(ctx, p, grid);
+        return exact_launch_one<BM, BN, TM, TN, EX_1X1V, true, 0>(ctx, p, grid);
     case EX_1X1:
-        return fma ? exact_launch_one<BM, BN, TM, EX_1X1, true>(ctx, p, grid)
-                   : exact_launch_one<BM, BN, TM, EX_1X1, false>(ctx, p, grid);
-    case EX_3X3: return exact_launch_one<BM, BN, TM, EX_3X3, true>(ctx, p, grid);
-    default: return exact_launch_one<BM, BN, TM, EX_GEN, true>(ctx, p, grid);
+        return fma ? exact_launch_one<BM, BN, TM, TN, EX_1X1, true, 0>(ctx, p, grid)
+                   : exact_launch_one<BM, BN, TM, TN, EX_1X1, false, 0>(ctx, p, grid);
+    case EX_3X3:
+        if (var == 1) return exact_launch_one<BM, BN, TM, TN, EX_3X3, true, 1>(ctx, p, grid);
+        if (var == 2) return exact_launch_one<BM, BN, TM, TN, EX_3X3, true, 2>(ctx, p, grid);
+        if (var == 3) return exact_launch_one<BM, BN, TM, TN, EX_3X3, true, 3>(ctx, p, grid);
+        return exact_launch_one<BM, BN, TM, TN, EX_3X3, true, 0>(ctx, p, grid);
+    default: return exact_launch_one<BM, BN, TM, TN, EX_GEN, true, 0>(ctx, p, grid);
     }
 }
 
 // one entry per tile shape (own translation units); grid.x == 0 returns resident CTAs per SM
-int exact_launch_128x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma);
-int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma);
-int exact_launch_128x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma);
-int exact_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma);
-int exact_launch_32x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma);
+int exact_launch_128x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+int exact_launch_128x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+int exact_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+int exact_launch_32x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
 
 }  // namespace tbi

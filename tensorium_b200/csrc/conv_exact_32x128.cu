@@ -3,7 +3,7 @@
 #include "conv_exact.cuh"
 
 namespace tbi {
-int exact_launch_32x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma) {
-    return exact_launch_modes<32, 128, 4>(ctx, p, grid, mode, fma);
+int exact_launch_32x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var) {
+    return exact_launch_modes<32, 128, 4, 8>(ctx, p, grid, mode, fma, var);
 }
 }  // namespace tbi

@@ -3,7 +3,7 @@
 #include "conv_exact.cuh"
 
 namespace tbi {
-int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma) {
-    return exact_launch_modes<64, 128, 8>(ctx, p, grid, mode, fma);
+int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var) {
+    return exact_launch_modes<64, 128, 8, 8>(ctx, p, grid, mode, fma, var);
 }
 }  // namespace tbi

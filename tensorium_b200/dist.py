@@ -67,3 +67,89 @@ def detections_per_image(recs: np.ndarray, probs: np.ndarray, counts: np.ndarray
         k = int(min(counts[b], capacity))
         out.append((recs[b, :k].copy(), probs[b, :k].copy()))
     return out
+
+
+class DetectionGather:
+    """The final exchange of a sharded forward, through the library's C ABI: every step, each rank
+    extracts its images' detections on its GPU (tb_yolo_detect: fixed-capacity records plus
+    counts) and tb_group_gather moves the packed buffers [counts (batch int64) | records
+    (batch*capacity tb_detection)] to rank 0 over NCCL, in rank order (= global image order).
+
+    The group is formed with tb_group_init_rank; torch.distributed only carries its 128-byte id
+    from rank 0 to the others.  With one rank the gather is a device copy."""
+
+    def __init__(self, net, world: int, rank: int, capacity: int = 1024, thresh: float = 0.45,
+                 timeout_ms: int = 120000):
+        import ctypes as C
+        from ._lib import Detection, YoloHead, check, lib
+        self._C, self._lib, self._check = C, lib, check
+        self.net, self.world, self.rank = net, world, rank
+        self.capacity, self.thresh = capacity, thresh
+        ctx = net.ctx
+        uid = (C.c_uint8 * 128)()
+        if rank == 0:
+            check(lib.tb_group_unique_id(uid))
+        if world > 1:
+            box = [bytes(uid)]
+            dist.broadcast_object_list(box, src=0)
+            uid = (C.c_uint8 * 128).from_buffer_copy(box[0])
+        self.group = C.c_void_p()
+        check(lib.tb_group_init_rank(ctx.handle, world, rank, uid, timeout_ms, C.byref(self.group)))
+        heads, outs = net.yolo_heads()
+        self.heads = heads
+        self.hs = (YoloHead * len(heads))(*[h.head(o) for h, o in zip(heads, outs)])
+        self.classes = max(h.classes for h in heads)
+        B = net.batch
+        self.rec_bytes = B * capacity * C.sizeof(Detection)
+        self.pack_bytes = 8 * B + self.rec_bytes
+        self.pack = torch.zeros(self.pack_bytes, dtype=torch.uint8, device=ctx.torch_device)
+        self.prob = torch.empty(B * capacity * self.classes, dtype=torch.float32, device=ctx.torch_device)
+        self.counts = (C.c_int64 * B)()
+        self.counts_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.sizes = (C.c_int64 * world)(*([self.pack_bytes] * world))
+        self.send = (C.c_void_p * 1)(self.pack.data_ptr())
+        if rank == 0:
+            self.out = torch.empty(world * self.pack_bytes, dtype=torch.uint8, device=ctx.torch_device)
+            self.host = torch.empty(world * self.pack_bytes, dtype=torch.uint8).pin_memory()
+        else:
+            self.out = self.host = None
+
+    def step(self, download: bool = True):
+        """Detections of the last forward, gathered on rank 0 (and, with download, copied to its
+        pinned host buffer asynchronously on the context's stream)."""
+        C, lib, check = self._C, self._lib, self._check
+        ctx = self.net.ctx
+        B = self.net.batch
+        check(lib.tb_yolo_detect(ctx.handle, B, len(self.heads), self.hs, 416, 416, 416, 416, self.thresh, 1, 0,
+                                 self.capacity, C.c_void_p(self.pack.data_ptr() + 8 * B),
+                                 C.c_void_p(self.prob.data_ptr()), self.counts))
+        self.counts_host.numpy()[:] = np.minimum(np.array(self.counts[:], np.int64), self.capacity)
+        self.pack[:8 * B].copy_(self.counts_host.view(torch.uint8), non_blocking=True)
+        out = C.c_void_p(self.out.data_ptr()) if self.out is not None else None
+        check(lib.tb_group_gather(self.group, self.send, self.sizes, out))
+        if download and self.host is not None:
+            self.host.copy_(self.out, non_blocking=True)
+
+    @property
+    def d2h_bytes(self) -> int:
+        return self.world * self.pack_bytes if self.rank == 0 else 0
+
+    def unpack(self):
+        """Rank 0, after the last step's copy completed: per global image, its detection records."""
+        from .layers import DET_DTYPE
+        if self.host is None:
+            return None
+        B, cap = self.net.batch, self.capacity
+        res = []
+        raw = self.host.numpy()
+        for r in range(self.world):
+            part = raw[r * self.pack_bytes:(r + 1) * self.pack_bytes]
+            counts = part[:8 * B].view(np.int64)
+            recs = part[8 * B:].view(DET_DTYPE).reshape(B, cap)
+            res.extend(recs[b, :int(counts[b])].copy() for b in range(B))
+        return res
+
+    def close(self):
+        if self.group:
+            self._lib.tb_group_destroy(self.group)
+            self.group = self._C.c_void_p()
