@@ -40,7 +40,7 @@ INPUT = (3, 416, 416)
 HEADS = (82, 94, 106)
 METRIC = "YOLOv3-416 images/sec (FP32 path)"
 METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
-MATH_MODES = {"fp32": 0, "tf32": 1, "fp32_tiled": 2}
+MATH_MODES = {"fp32": 0, "tf32": 1, "fp32_tiled": 2, "bf16split": 3}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
 PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "k_conv_nhwc_yolov3_b8.json"
 
@@ -230,7 +230,7 @@ def run_ours(args):
     #      detection extraction -> NCCL gather of every rank's detections to rank 0 through the C
     #      ABI (tb_group_gather) -> D2H of the gathered detections on rank 0 ----
     h_in = torch.from_numpy(x_host).pin_memory()
-    gat = tbd.DetectionGather(net, world, rank, capacity=1024, thresh=0.45)
+    gat = tbd.DetectionGather(net, world, rank, capacity=4096, thresh=0.45)
     upload = torch.cuda.Stream(local)
     x_fixed = torch.empty_like(x)  # the forward's one input buffer (one CUDA graph)
     d_in = [torch.empty_like(x), torch.empty_like(x)]
@@ -257,12 +257,14 @@ def run_ours(args):
             gat.step(download=True)
 
     e2e_steps(max(args.warmup, 1))
+    gat.wait()
     barrier()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     gather_ms = []
     e0.record(stream)
     e2e_steps(args.steps)
     e1.record(stream)
+    gat.wait()
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1))
     # the gather alone (device time of detection extraction + NCCL gather + D2H), max over ranks
@@ -271,6 +273,7 @@ def run_ours(args):
         g0.record(stream)
         gat.step(download=True)
         g1.record(stream)
+        gat.wait()
         barrier()
         gather_ms.append(g0.elapsed_time(g1))
     gathered = gat.unpack()
@@ -283,8 +286,8 @@ def run_ours(args):
                                  "bytes": int(gat.d2h_bytes), "capacity_per_image": gat.capacity,
                                  "thresh": gat.thresh},
            "path": ("pinned host -> H2D (upload stream, overlapping the previous forward) -> TNNet.forward "
-                    "(graph) -> tb_yolo_detect -> tb_group_gather (NCCL, C ABI) of every rank's records "
-                    "+ counts to rank 0 -> D2H on rank 0, every step")}
+                    "(graph) -> tb_yolo_detect_device -> tb_group_gather_async (NCCL, C ABI) of every rank's "
+                    "records + counts to rank 0 -> D2H on rank 0, every step, all queued behind the forward")}
     gat.close()
 
     # ---- roofline of the conv kernels (per-layer CUDA events, eager forward) ----
@@ -338,6 +341,9 @@ def run_ours(args):
             "gpu_launches": int(launches_per_step * args.steps)}
     if args.math == "fp32" and not args.no_tf32_block:
         line["tf32_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream)
+    if args.math == "fp32" and not args.no_configs:
+        line["other_configs"] = configs_block(args, ctx, world, rank, barrier, max_over_ranks, stream, peak,
+                                              cpu=(world == 1 and not args.no_cpu_baseline))
     if world == 1 and not args.no_kernel_suite:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         mem, xnor = kernel_suite(ctx, peaks.get("hbm_gbs", 6650.0))
@@ -354,6 +360,103 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def configs_block(args, ctx, world, rank, barrier, max_over_ranks, stream, fma_peak, cpu):
+    """BASELINE configs 0, 1, 2, YOLOv3 at batch 1 and the XNOR sweep (config 4), each on the FP32
+    path (bit-exact with the reference CPU path), timed like the headline (warm-up, CUDA events,
+    max over ranks), with the conv FLOP roofline against the measured FFMA rate and, on rank 0 at
+    N = 1, the CPU oracle on a bounded sample of the same workload."""
+    import torch
+    from tensorium_b200 import synth
+    from tensorium_b200.layers import TConvolutionalLayer, TNNetState
+    from tensorium_b200.net import TNNet
+    from oracle import oracle as O
+    if cpu:
+        O.set_threads(host_threads())
+    out = []
+
+    def timed(fn, steps):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / steps
+
+    def cpu_time(fn, min_s=2.0, max_reps=20):
+        fn()
+        t0, n = time.perf_counter(), 0
+        while n < max_reps and (n == 0 or time.perf_counter() - t0 < min_s):
+            fn()
+            n += 1
+        return (time.perf_counter() - t0) / n
+
+    def entry(name, workload, items, unit, ms, flops, cpu_s=None, cpu_items=None, sample=None, extra=None):
+        d = {"config": name, "workload": workload, "value": world * items / (ms / 1e3), "unit": unit,
+             "ms_per_step": ms, "n_gpus": world,
+             "roofline": {"bound": "fp32", "achieved": flops / (ms / 1e3) / 1e12, "peak": fma_peak,
+                          "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / fma_peak,
+                          "note": "whole step time (every layer) against the measured FFMA rate"}}
+        if cpu_s is not None:
+            d["cpu_baseline"] = {"value": cpu_items / cpu_s, "unit": unit, "cores": O.num_threads(), "kind": "port",
+                                 "sample": sample}
+        if extra:
+            d.update(extra)
+        out.append(d)
+
+    # config 0: one conv 3->32 3x3 + batchnorm (unfused, as TConvolutionalLayer.forward runs it) + leaky, 416x416
+    s0 = synth.config0_spec()[0]
+    L = TConvolutionalLayer(1, 416, 416, 3, 32, 1, 3, 1, 1, 1, 1, 9, True).bind(ctx)
+    L.weights, L.biases = s0["weights"], s0["biases"]
+    L.scales, L.rolling_mean, L.rolling_variance = s0["scales"], s0["mean"], s0["var"]
+    x0h = synth.input_images(0, "cfg0", 1, (3, 416, 416))
+    st0 = TNNetState(torch.from_numpy(x0h).to(ctx.torch_device))
+    ms = timed(lambda: L.forward(st0), 200)
+    cs = cpu_time(lambda: O.conv2d(x0h, s0["weights"], s0["biases"], 32, 3, 1, 1, 9,
+                                   bn=(s0["scales"], s0["mean"], s0["var"]))) if cpu else None
+    byts = (3 + 32) * 416 * 416 * 4
+    entry("config0", "conv 3->32 3x3 s1 p1 + batchnorm + leaky on 1x3x416x416", 1, "layers/s", ms, 0.2990e9, cs, 1,
+          "1 conv layer", {"hbm": {"bytes": byts, "achieved_gbs": byts / (ms / 1e3) / 1e9}})
+
+    # config 1: MNIST-shaped CNN, batch 256 per GPU
+    sp1 = synth.mnist_specs()
+    net1 = TNNet(ctx, sp1, 256, (1, 28, 28))
+    x1h = synth.input_images(1, "mnist", 256, (1, 28, 28))
+    x1 = torch.from_numpy(x1h).to(ctx.torch_device)
+    ms = timed(lambda: net1.forward(x1), 100)
+    cs = cpu_time(lambda: O.run_network(sp1, x1h[:64], keep=[6])) if cpu else None
+    f1 = synth.conv_flops(sp1, (1, 28, 28), 256) + 2 * 256 * (3136 * 1024 + 1024 * 10)
+    entry("config1", "MNIST-shaped CNN (conv5x5x32, maxpool, conv5x5x64, maxpool, fc 3136-1024, fc 1024-10, softmax), "
+          "batch 256 per GPU", 256, "images/s", ms, f1, cs, 64, "64 images through the oracle")
+    net1.close()
+
+    # config 2: CIFAR-shaped darknet CNN, batch 1024 sharded over the ranks
+    per = 1024 // world
+    sp2 = synth.cifar_specs()
+    net2 = TNNet(ctx, sp2, per, (3, 32, 32))
+    x2h = synth.input_images(2, "cifar", 1024, (3, 32, 32))[rank * per:(rank + 1) * per]
+    x2 = torch.from_numpy(np.ascontiguousarray(x2h)).to(ctx.torch_device)
+    ms = timed(lambda: net2.forward(x2), 20)
+    cs = cpu_time(lambda: O.run_network(sp2, x2h[:8], keep=[11])) if cpu else None
+    entry("config2", f"CIFAR-shaped darknet CNN, batch 1024 sharded over {world} GPU(s) ({per} per GPU)", per,
+          "images/s", ms, synth.conv_flops(sp2, (3, 32, 32), per), cs, 8, "8 images through the oracle")
+    net2.close()
+
+    # config 3 at batch 1: YOLOv3-416 latency
+    sp3 = synth.yolov3_specs()
+    net3 = TNNet(ctx, sp3, 1, INPUT)
+    x3 = torch.from_numpy(synth.input_images(3, "yolov3", 1, INPUT)).to(ctx.torch_device)
+    ms = timed(lambda: net3.forward(x3), 50)
+    entry("config3_batch1", "YOLOv3-416 forward, batch 1 per GPU (latency)", 1, "images/s", ms,
+          synth.conv_flops(sp3, INPUT, 1), None, None, None,
+          {"latency_ms": ms, "cpu_baseline_note": "the headline line's cpu_baseline is YOLOv3 at batch 1"})
+    net3.close()
+    return out
 
 
 def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, stream):
@@ -382,8 +485,10 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
     conv_ms = float(sum(prof[i] + (prof[i + 1] if i + 1 < len(specs) and specs[i + 1]["type"] in ("shortcut", "yolo") else 0.0)
                         for i, s in enumerate(specs) if s["type"] == "conv"))
     flops = synth.conv_flops(specs, INPUT, B)
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    bf16 = peaks.get("bf16_tflops", 1590.0)
+    import ctypes as C
+    from tensorium_b200._lib import check, lib
+    tc_rate, cyc = C.c_double(), C.c_double()
+    check(lib.tb_diag_tc_mma_rate(ctx.handle, 1, C.byref(tc_rate), C.byref(cyc)))
     achieved = flops / (conv_ms / 1e3) / 1e12
     # head error of the TF32 path against the FP32 path (relative L2 over the batch)
     net.forward(x)
@@ -397,8 +502,10 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
            "gpu_launches": int(launches * args.steps),
            "roofline": {"bound": "tensor", "kernel": "k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) + "
                                                      "input / receptive-field conversion and NHWC upsample",
-                        "achieved": achieved, "peak": bf16 / 2, "unit": "TFLOP/s", "frac": achieved / (bf16 / 2),
-                        "peak_source": f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)",
+                        "achieved": achieved, "peak": tc_rate.value, "unit": "TFLOP/s",
+                        "frac": achieved / tc_rate.value,
+                        "peak_source": ("TF32 tcgen05 MMA rate measured in this run with operands resident "
+                                        "(tb_diag_tc_mma_rate, M=128 N=256 K=8, at the current SM clock)"),
                         "conv_ms_per_forward": conv_ms,
                         "traffic": (json.loads(PROFILE_SUMMARY_TF32.read_text()).get("dram_bytes_per_forward")
                                     if PROFILE_SUMMARY_TF32.exists() else None),
@@ -554,6 +661,14 @@ def run_layer_mode(args):
     s = specs[i]
     assert s["type"] == "conv", f"layer {i} is a {s['type']}"
     c, h, w = shapes[i - 1] if i > 0 else INPUT
+    if args.shape:  # an arbitrary conv geometry C,H,F,k,stride (He-init weights)
+        c, h, f, k, st = (int(v) for v in args.shape.split(","))
+        w = h
+        s = synth.conv_spec(5, "shape", c, f, k, st, k // 2, 9, False)
+        specs = list(specs)
+        specs[i] = s
+        shapes = list(shapes)
+        shapes[i] = (f, (h + 2 * (k // 2) - k) // st + 1, (w + 2 * (k // 2) - k) // st + 1)
     ctx = Context(0)
     L = TConvolutionalLayer(args.batch, h, w, c, s["filters"], 1, s["size"], s["stride"], s["stride"], 1,
                             s["pad"], s["activation"], False).bind(ctx)
@@ -611,9 +726,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tf32-block", action="store_true", help="skip the TF32-path measurement of the default run")
     ap.add_argument("--no-kernel-suite", action="store_true", help="skip the memory-bound / XNOR kernel suite")
+    ap.add_argument("--no-configs", action="store_true", help="skip BASELINE configs 0, 1, 2 and YOLOv3 batch 1")
     ap.add_argument("--suite", choices=["kernels"], default=None, help="run only the kernel suite")
     ap.add_argument("--layer", type=int, default=None, help="time one YOLOv3 conv layer only")
-    ap.add_argument("--math", choices=["fp32", "tf32", "fp32_tiled"], default="fp32",
+    ap.add_argument("--shape", default=None, help="with --layer: replace its geometry by C,H,F,k,stride")
+    ap.add_argument("--math", choices=["fp32", "tf32", "fp32_tiled", "bf16split"], default="fp32",
                     help="conv mainloop: fp32 CUDA cores (reference-faithful) or tf32 tcgen05 tensor cores")
     ap.add_argument("--nhwc", action="store_true", help="with --layer and --math tf32: the NHWC tensor-core kernel")
     ap.add_argument("--profile-window", action="store_true",

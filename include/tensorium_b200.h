@@ -67,6 +67,11 @@ extern "C" {
                              k ascending as im2col rows (c, kh, kw), no split of K -- results
                              bit-identical to the reference CPU path (default) */
 #define TB_MATH_TF32  1   /* tcgen05 tensor-core mainloop, TF32 operands, FP32 accumulate */
+#define TB_MATH_BF16_SPLIT 3  /* tcgen05 kind::f16 tensor cores on BF16-split operands: every fp32
+                             value carried as a pair of bf16 (hi = bf16(v), lo = bf16(v - hi)), all
+                             four partial products accumulated in FP32 (~16-bit operand precision,
+                             twice the MMAs of TF32). Networks only (tb_net_finalize, NHWC plan);
+                             nets or layers that plan cannot take run on the FP32 path */
 #define TB_MATH_FP32_TILED 2  /* FP32 CUDA-core mainloop with the summation reordered (k tiles
                              in (kh, kw, c) order, split-K with partial sums in scratch): within
                              the reference's 1e-4 per map, not bit-identical */
@@ -274,6 +279,14 @@ int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_he
                    int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
                    int64_t relative, int64_t letter, int64_t capacity,
                    tb_detection* dets, float* prob, int64_t* counts_host);
+/* tb_yolo_detect without the host round trip (no counterpart in the reference): the per-image
+ * totals go to counts_dev (int64 [batch], device memory) and nothing waits, so detection
+ * extraction, a gather to rank 0 (tb_group_gather_async) and the copy of the result can be queued
+ * behind the forward. */
+int tb_yolo_detect_device(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads,
+                          int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
+                          int64_t relative, int64_t letter, int64_t capacity, tb_detection* dets, float* prob,
+                          int64_t* counts_dev);
 /* Class-wise non-maximum suppression on the detections tb_yolo_detect wrote, replacing
  * TDetectionsHelper.doNMSSort (source/ntypes.pas:1621-1649): for every image and class, the
  * detections with a non-zero probability of the class are taken in order of decreasing
@@ -433,6 +446,12 @@ int tb_group_context(tb_group* g, int64_t local, tb_ctx** ctx);
  * Blocks until this process's part is complete, within the group's deadline (then the
  * communicators are aborted and TB_ERR_TIMEOUT returned; the group is unusable afterwards). */
 int tb_group_gather(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank, void* recv_root);
+/* tb_group_gather split in two: enqueue the transfers on the local contexts' streams and return
+ * (they run in stream order after the work already queued), then wait, within the deadline, for
+ * the local streams to drain. */
+int tb_group_gather_async(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank,
+                          void* recv_root);
+int tb_group_wait(tb_group* g);
 int tb_group_destroy(tb_group* g);
 
 /* ---- whole-network executor (TNNet.forward / predict, source/nnet.pas:275-317,452-472) --- */

@@ -5,7 +5,7 @@ this package is the host-side mirror of the reference's layer / network API over
 library is loaded on first use of any of the names below (importing a submodule that needs it
 raises ImportError when it has not been built: there is no CPU fallback).
 """
-_EXPORTS = {"ACT": "_lib", "MATH_FP32": "_lib", "MATH_TF32": "_lib", "MATH_FP32_TILED": "_lib", "TBError": "_lib", "lib": "_lib",
+_EXPORTS = {"ACT": "_lib", "MATH_FP32": "_lib", "MATH_TF32": "_lib", "MATH_FP32_TILED": "_lib", "MATH_BF16_SPLIT": "_lib", "TBError": "_lib", "lib": "_lib",
             "Context": "context", "device_count": "context", "ptr": "context"}
 
 

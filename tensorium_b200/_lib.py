@@ -30,6 +30,7 @@ ACT = {
 MATH_FP32 = 0
 MATH_TF32 = 1
 MATH_FP32_TILED = 2  # FP32 with the summation reordered (tiles, split-K): not bit-exact
+MATH_BF16_SPLIT = 3  # tensor cores on bf16 (hi, lo) operand pairs, networks only
 
 XNOR_PAD_BIT0 = 0
 XNOR_PAD_ZERO = 1
@@ -120,6 +121,8 @@ SIGNATURES = {
     "tb_group_size": [P, PI64, PI64, PI64],
     "tb_group_context": [P, I64, C.POINTER(P)],
     "tb_group_gather": [P, C.POINTER(P), PI64, P],
+    "tb_group_gather_async": [P, C.POINTER(P), PI64, P],
+    "tb_group_wait": [P],
     "tb_group_destroy": [P],
     # TNNCuda method shims (argument lists of source/nncuda.pas:100-151)
     "tbcompat_createDeviceBuffer": [P, I64, C.POINTER(P)],
@@ -162,6 +165,8 @@ SIGNATURES = {
     "tb_yolo_fwd": [P, I64, I64, I64, I64, I64, P, P, F32],
     "tb_yolo_detect": [P, I64, I64, C.POINTER(YoloHead), I64, I64, I64, I64, F32, I64, I64, I64,
                        P, P, PI64],
+    "tb_yolo_detect_device": [P, I64, I64, C.POINTER(YoloHead), I64, I64, I64, I64, F32, I64, I64, I64,
+                       P, P, P],
     "tb_yolo_nms": [P, I64, I64, PI64, I64, F32, P, P],
     "tb_xnor_packed_weights_count": [I64, I64, I64, PI64],
     "tb_xnor_pack_weights": [P, I64, I64, I64, P, P, P],

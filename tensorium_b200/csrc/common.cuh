@@ -78,6 +78,33 @@ static __device__ __noinline__ float tb_logistic(float x) {
 
 static __device__ __noinline__ float tb_activate_slow(float x, int a);
 
+// Activation formats of the tensor-core networks (NHWC plan). TF32: each value an fp32 rounded to
+// nearest TF32 (what kind::tf32 reads). BF16 pair: each 32-bit slot holds two bf16, hi =
+// bf16(v) in the low half and lo = bf16(v - hi) in the high half, so a 32-channel fp32 row is a
+// 64-element bf16 row whose even / odd entries are the hi / lo parts (kind::f16 reads it as is).
+__device__ __forceinline__ float tb_tf32_rna(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+    return __uint_as_float(u);
+}
+__device__ __forceinline__ uint32_t tb_bf16_rn_bits(float x) {  // round to nearest even, finite x
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u) return u >> 16;
+    return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ float tb_pair_encode(float v) {
+    const uint32_t h = tb_bf16_rn_bits(v);
+    const float r = __fsub_rn(v, __uint_as_float(h << 16));
+    return __uint_as_float(h | (tb_bf16_rn_bits(r) << 16));
+}
+__device__ __forceinline__ float tb_pair_decode(float s) {
+    const uint32_t u = __float_as_uint(s);
+    return __fadd_rn(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+// store / load one activation in the network's format (pair = 0: TF32 rounding)
+__device__ __forceinline__ float tb_fmt_store(float v, int pair) { return pair ? tb_pair_encode(v) : tb_tf32_rna(v); }
+__device__ __forceinline__ float tb_fmt_load(float s, int pair) { return pair ? tb_pair_decode(s) : s; }
+
 // Common activations inline, the rest out of line (keeps the unrolled conv epilogues small).
 __device__ __forceinline__ float tb_activate_dev(float x, int a) {
     if (a == TB_ACT_LEAKY || a == TB_ACT_REVLEAKY) return x < 0.f ? __fmul_rn(x, 0.1f) : x;

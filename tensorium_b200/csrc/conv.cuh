@@ -93,28 +93,30 @@ int conv_tc_round_weights(tb_ctx* ctx, float* packed, int64_t n);
 // Measure the candidate (tile, split) choices of this geometry on x / y and keep the fastest.
 int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, float* y);
 // TF32 tensor-core conv on NHWC activations with the A operand fetched by TMA im2col (conv_nhwc.cu).
-int64_t conv_nhwc_packed_count(const ConvGeom& g);
+// pair = 1: BF16-split operands (activations as bf16 (hi, lo) pairs in 32-bit slots, weights as two
+// bf16 operands (hi, hi) and (lo, lo); kind::f16 MMAs accumulate all four partial products)
+int64_t conv_nhwc_packed_count(const ConvGeom& g, int pair = 0);
 bool conv_nhwc_supported(const ConvGeom& g, int64_t x_ps);
-int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp);
+int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp, int pair = 0);
 int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
                      const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
-                     int yolo_classes, unsigned long long* phases);
-int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps);
+                     int yolo_classes, unsigned long long* phases, int pair = 0);
+int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps, int pair = 0);
 int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp, float* y,
-                       int64_t y_ps);
+                       int64_t y_ps, int pair = 0);
 // NHWC data-movement layers of the network's NHWC plan (nhwc_layers.cu); strides in floats per pixel.
 int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, int64_t x_bs,
-                   float* y, int64_t ps);
+                   float* y, int64_t ps, int pair = 0);
 // first layer with C * KH * KW <= 32: receptive fields as 32 channels of a 1x1 conv, and its weights
 int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
                       int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
-                      const float* x, int64_t x_bs, float* y);
-int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp);
+                      const float* x, int64_t x_bs, float* y, int pair = 0);
+int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp, int pair = 0);
 int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, int64_t s, float scale,
-                  const float* x, int64_t xps, float* y, int64_t yps);
+                  const float* x, int64_t xps, float* y, int64_t yps, int pair = 0);
 int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps, float* y, int64_t yps);
 int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t aps, const float* b, int64_t bps,
-                  float* y, int64_t yps, int act);
+                  float* y, int64_t yps, int act, int pair = 0);
 // Direct convolution for short reductions (C*KH*KW <= 32, CRS-packed weights, no residual, no
 // fused yolo): the first layer of an image network (conv_direct.cu).
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes);

@@ -160,46 +160,7 @@ k_conv_exact(const ConvParams p) {
         }
     }
 
-    // One copy ("item") of a stage: items 0 .. WIT-1 are this thread's weight rows, the rest its
-    // activation elements.  Called with compile-time i (unrolled loops), so every branch folds.
-    constexpr int RPG1 = CC / G, CPG3 = CC / G;
-    constexpr int NA = MODE == EX_1X1V ? VIT : (MODE == EX_1X1 ? RPG1 : (MODE == EX_3X3 ? 9 * CPG3 : 0));
-    constexpr int NITEMS = WIT + NA;
-    auto load_item = [&](int i, int st_idx, int buf) {
-        const int c0 = st_idx * CC;
-        if (i < WIT) {
-            const int row = w_r0 + i * RG;
-            if (row < KS) {
-                const bool ok = w_mok && c0 + w_cc[i] < p.C;
-                cp_async16(As + buf * KSMAX * BM + row * BM + 4 * w_mq,
-                           ok ? p.w + (long long)st_idx * wstep + w_off[i] : p.w, ok);
-            }
-            return;
-        }
-        const int a = i - WIT;
-        float* bs = Bs + buf * KSMAX * BN;
-        if (MODE == EX_1X1V) {
-            const int row = v_r0 + a * VRG;
-            const bool ok = vok && c0 + row < p.C;
-            cp_async16(bs + row * BN + 4 * (tid % BQ), ok ? vq + (long long)(c0 + row) * HW : p.x, ok);
-        } else if (MODE == EX_1X1) {
-            const int row = g * RPG1 + a;
-            const bool ok = pixok && c0 + row < p.C;
-            cp_async4(bs + row * BN + bcol, ok ? xb + (long long)(c0 + row) * HW + pixoff : p.x, ok);
-        } else if (MODE == EX_3X3) {
-            const int ch = g * CPG3 + a / 9, tap = a % 9, r = tap / 3, s = tap % 3;
-            const bool ok = c0 + ch < p.C && ((tapok >> tap) & 1u);
-            cp_async4(bs + (ch * 9 + tap) * BN + bcol, ok ? xb + (long long)(c0 + ch) * HW + rowoff[r] + coloff[s] : p.x,
-                      ok);
-        }
-    };
-
     auto load_stage = [&](int st_idx, int buf) {
-        if (MODE != EX_GEN) {
-#pragma unroll
-            for (int i = 0; i < NITEMS; ++i) load_item(i, st_idx, buf);
-            return;
-        }
         const int c0 = st_idx * CC;
         float* as = As + buf * KSMAX * BM;
         const float* wst = p.w + (long long)st_idx * wstep;
@@ -285,30 +246,7 @@ k_conv_exact(const ConvParams p) {
             }
     };
 
-    // non-generic modes: the copies of stage t + STAGES - 1 are spread over the k steps of stage t
-    // (IPK after each step), so the FMA stream is not held up by a burst of address arithmetic
-    constexpr int IPK = (NITEMS + KSMAX - 1) / KSMAX;
-    if (MODE != EX_GEN) {
-        for (int t = 0; t < nst; ++t) {
-            cp_async_wait<STAGES - 2>();
-            __syncthreads();
-            const int tn = t + STAGES - 1;
-            const bool more = tn < nst;
-            const int nbuf = tn % STAGES;
-            const float* as = As + (t % STAGES) * KSMAX * BM;
-            const float* bs = Bs + (t % STAGES) * KSMAX * BN;
-#pragma unroll
-            for (int kk = 0; kk < KSMAX; ++kk) {
-                kstep(as + kk * BM, bs + kk * BN);
-                if (more) {
-#pragma unroll
-                    for (int i = kk * IPK; i < (kk + 1) * IPK && i < NITEMS; ++i) load_item(i, tn, nbuf);
-                }
-            }
-            cp_async_commit();
-        }
-    }
-    for (int t = 0; MODE == EX_GEN && t < nst; ++t) {
+    for (int t = 0; t < nst; ++t) {
         cp_async_wait<STAGES - 2>();
         __syncthreads();
         {

@@ -62,7 +62,8 @@ struct NhwcParams {
 
 struct NhwcMaps {
     CUtensorMap a;  // im2col view of x: (C, W, H, N), 32 channels x 128 pixels per copy
-    CUtensorMap b;  // packed weights (k, filter), box 32 x BN
+    CUtensorMap b;  // packed weights (k, filter), box 32 x BN (pair mode: the (hi, hi) operand)
+    CUtensorMap b2; // pair mode: the (lo, lo) weight operand
     CUtensorMap y;  // NHWC output (filter, pixel), box 16 x 32, 64-byte swizzle (tma_out)
 };
 
@@ -82,6 +83,10 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
 // instruction descriptor: F32 accumulate, TF32 A and B, both K-major, M x N
 __host__ __device__ constexpr uint32_t idesc_tf32_k(int M, int N) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// the same for kind::f16 with BF16 A and B
+__host__ __device__ constexpr uint32_t idesc_bf16_k(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void tma_load_im2col_4d(unsigned dst, const void* tmap, uint64_t* bar, int c, int w,
@@ -119,10 +124,14 @@ __device__ __forceinline__ float nh_act(float o, int f, const NhwcParams& p) {
     return tb_activate_dev(o, p.act);
 }
 
-template <int BN, int STAGES>
+// PAIR: BF16-split operands. The 32-bit activation slots hold bf16 (hi, lo) pairs, so the same
+// im2col box is a K-major tile of 64 bf16 (32 channels x (hi, lo)); the weights come as two
+// operands (hi, hi) and (lo, lo), and per 32 channels 4 + 4 kind::f16 MMAs (K = 16) accumulate
+// hi*w_hi + lo*w_hi + hi*w_lo + lo*w_lo = (hi + lo) * (w_hi + w_lo) in FP32.
+template <int BN, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_constant__ NhwcMaps maps, const NhwcParams p) {
     constexpr int B_BYTES = BN * NH_BK * 4;
-    constexpr int STAGE_BYTES = NH_A_BYTES + B_BYTES;
+    constexpr int STAGE_BYTES = NH_A_BYTES + (PAIR ? 2 : 1) * B_BYTES;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024 - ((unsigned)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
@@ -185,6 +194,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     tma_load_im2col_4d(sa, &maps.a, &full_bar[st], c0 * NH_BK, w0, h0, n0, (uint16_t)(s * p.DX),
                                        (uint16_t)(r * p.DY));
                     tc::tma_load_2d(sb, &maps.b, &full_bar[st], kt * NH_BK, nt * BN);
+                    if (PAIR) tc::tma_load_2d(sb + B_BYTES, &maps.b2, &full_bar[st], kt * NH_BK, nt * BN);
                     if (++c0 == p.csteps) {  // next 32-channel step, then the next tap
                         c0 = 0;
                         if (++s == p.KW) s = 0, ++r;
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = idesc_tf32_k(NH_BM, BN);
+            constexpr uint32_t idesc = PAIR ? idesc_bf16_k(NH_BM, BN) : idesc_tf32_k(NH_BM, BN);
             int it = 0, tl = 0;
             bool ok = true, issued = false;
             const long long c_start = clock64();
@@ -227,10 +237,21 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     c_wf += clock64() - c0w;
                     tc::tc_fence_after();
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + NH_A_BYTES;
+                    if (PAIR) {
 #pragma unroll
-                    for (int kk = 0; kk < NH_BK / 8; ++kk)
-                        tc::mma_tf32(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
-                                     (kt != kb || kk) ? 1u : 0u);
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc::mma_bf16(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
+                                         (kt != kb || kk) ? 1u : 0u);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc::mma_bf16(d, smem_desc_k_sw128(sa + kk * 32),
+                                         smem_desc_k_sw128(sb + B_BYTES + kk * 32), idesc, 1u);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < NH_BK / 8; ++kk)
+                            tc::mma_tf32(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
+                                         (kt != kb || kk) ? 1u : 0u);
+                    }
                     issued = true;
                     tc::mma_commit(&empty_bar[st]);
                 }
@@ -316,6 +337,9 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             // load: one load latency per pair of slabs instead of one per slab
             constexpr int PER = BN / 32;  // slabs per warp (the two warps of a lane window split the tile)
             const int s_begin = half * PER;
+            // TF32 mode rounds every output to TF32; pair mode writes NHWC outputs as bf16 pairs and
+            // the NCHW yolo outputs as plain fp32
+            auto store_fmt = [&](float o) { return PAIR ? (p.out_nchw ? o : tb_pair_encode(o)) : tc::to_tf32_rna(o); };
             auto process = [&](int sl, const float* vin) {
                 float v[16];
 #pragma unroll
@@ -328,11 +352,12 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
 #pragma unroll
                         for (int i = 0; i < 16; i += 4) {
                             const float4 r4 = __ldg(reinterpret_cast<const float4*>(rp + fb + i));
-                            rv[i] = r4.x; rv[i + 1] = r4.y; rv[i + 2] = r4.z; rv[i + 3] = r4.w;
+                            rv[i] = tb_fmt_load(r4.x, PAIR); rv[i + 1] = tb_fmt_load(r4.y, PAIR);
+                            rv[i + 2] = tb_fmt_load(r4.z, PAIR); rv[i + 3] = tb_fmt_load(r4.w, PAIR);
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) rv[i] = fb + i < p.F ? __ldg(rp + fb + i) : 0.f;
+                        for (int i = 0; i < 16; ++i) rv[i] = fb + i < p.F ? tb_fmt_load(__ldg(rp + fb + i), PAIR) : 0.f;
                     }
                 }
                 if (fast) {  // bias, leaky or linear, residual: flags held in registers
@@ -345,7 +370,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         if (bias) o = __fadd_rn(o, bv[i]);
                         if (leaky && o < 0.f) o = __fmul_rn(o, 0.1f);  // rounded to TF32 below
                         if (rp) o = __fadd_rn(o, rv[i]);
-                        v[i] = tc::to_tf32_rna(o);
+                        v[i] = store_fmt(o);
                     }
                 } else if (period) {  // fused yolo head: logistic on entries 0, 1, 4.. of each anchor
                     int e = fb % period;
@@ -354,7 +379,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         float o = v[i];
                         if (bias) o = __fadd_rn(o, __ldg(bias + min(fb + i, Fm1)));
                         if (e != 2 && e != 3) o = __frcp_rn(__fadd_rn(1.0f, __expf(-o)));  // rounded to TF32 below
-                        v[i] = tc::to_tf32_rna(o);
+                        v[i] = store_fmt(o);
                         e = e + 1 == period ? 0 : e + 1;
                     }
                 } else {
@@ -365,7 +390,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         if (bias) o = __fadd_rn(o, __ldg(bias + f));
                         o = nh_act(o, f, p);
                         if (rp) o = __fadd_rn(o, rv[i]);
-                        v[i] = tc::to_tf32_rna(o);
+                        v[i] = store_fmt(o);
                     }
                 }
                 if (p.tma_out) {
@@ -461,16 +486,24 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     }
 }
 
-// packed weights for the NHWC kernel: wp[f][(r * KW + s) * Cp + c] = tf32(w[f][c][r][s]), zero for c >= C
+// packed weights for the NHWC kernel: wp[f][(r * KW + s) * Cp + c] = tf32(w[f][c][r][s]), zero for c >= C;
+// pair mode: that array of (hi, hi) bf16 pairs, then one of (lo, lo)
 __global__ void k_pack_nhwc(const float* __restrict__ w, float* __restrict__ wp, int F, int C, int KH, int KW,
-                            int Cp) {
+                            int Cp, int pair) {
     const long long kp = (long long)KH * KW * Cp, total = (long long)F * kp;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         const int f = (int)(i / kp);
         const int k = (int)(i - (long long)f * kp);
         const int rs = k / Cp, c = k - rs * Cp;
         const int r = rs / KW, s = rs - r * KW;
-        wp[i] = c < C ? tc::to_tf32_rna(w[(((long long)f * C + c) * KH + r) * KW + s]) : 0.0f;
+        const float v = c < C ? w[(((long long)f * C + c) * KH + r) * KW + s] : 0.0f;
+        if (!pair) {
+            wp[i] = tc::to_tf32_rna(v);
+        } else {
+            const uint32_t e = __float_as_uint(tb_pair_encode(v)), hi = e & 0xffffu, lo = e >> 16;
+            wp[i] = __uint_as_float(hi | (hi << 16));
+            wp[total + i] = __uint_as_float(lo | (lo << 16));
+        }
     }
 }
 
@@ -487,25 +520,26 @@ PFN_cuTensorMapEncodeIm2col_v12000 im2col_encoder() {
     return fn;
 }
 
-template <int BN, int STAGES>
-constexpr int nh_smem() { return STAGES * (NH_A_BYTES + BN * NH_BK * 4) + NH_STG_BYTES + 1024; }
+template <int BN, int STAGES, bool PAIR>
+constexpr int nh_smem() { return STAGES * (NH_A_BYTES + (PAIR ? 2 : 1) * BN * NH_BK * 4) + NH_STG_BYTES + 1024; }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR>
 int nh_launch(tb_ctx* ctx, const NhwcMaps& maps, const NhwcParams& p) {
-    constexpr int smem = nh_smem<BN, STAGES>();
+    constexpr int smem = nh_smem<BN, STAGES, PAIR>();
+    static_assert(smem <= 232448, "shared memory per CTA");
     static bool attr = false;
     if (!attr) {
-        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
     const int grid = std::min(p.units, ctx->sm_count);
-    k_conv_nhwc<BN, STAGES><<<grid, NH_THREADS, smem, ctx->stream>>>(maps, p);
+    k_conv_nhwc<BN, STAGES, PAIR><<<grid, NH_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch("k_conv_nhwc");
 }
 
 }  // namespace
 
-int64_t conv_nhwc_packed_count(const ConvGeom& g) { return g.F * g.KH * g.KW * round_up(g.C, 32); }
+int64_t conv_nhwc_packed_count(const ConvGeom& g, int pair) { return (pair ? 2 : 1) * g.F * g.KH * g.KW * round_up(g.C, 32); }
 
 bool conv_nhwc_supported(const ConvGeom& g, int64_t x_ps) {
     // im2col corner and offset fields of a 4-D map: corners in [-128, 127], offsets < 256
@@ -518,10 +552,10 @@ bool conv_nhwc_supported(const ConvGeom& g, int64_t x_ps) {
     return g.B * g.OH * g.OW < ((int64_t)1 << 31) - NH_BM && g.F <= 65535 && g.OH * g.OW > 1;
 }
 
-int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp) {
-    const int64_t total = conv_nhwc_packed_count(g);
+int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp, int pair) {
+    const int64_t total = conv_nhwc_packed_count(g, 0);
     k_pack_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)g.F, (int)g.C, (int)g.KH,
-                                                                              (int)g.KW, (int)round_up(g.C, 32));
+                                                                              (int)g.KW, (int)round_up(g.C, 32), pair);
     return check_launch("k_pack_nhwc");
 }
 
@@ -534,8 +568,8 @@ std::mutex g_nh_mu;
 std::map<std::vector<int64_t>, NhShape> g_nh_tuned;  // measured at network set-up
 thread_local const NhShape* t_nh_pin = nullptr;    // the autotuner's candidate under test
 
-std::vector<int64_t> nh_key(int device, const ConvGeom& g, int64_t x_ps) {
-    return {device, g.B, g.C, g.H, g.W, g.F, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX, x_ps};
+std::vector<int64_t> nh_key(int device, const ConvGeom& g, int64_t x_ps, int pair) {
+    return {device, g.B, g.C, g.H, g.W, g.F, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX, x_ps, pair};
 }
 
 int64_t nh_ktiles(const ConvGeom& g) { return g.KH * g.KW * (round_up(g.C, 32) / NH_BK); }
@@ -552,7 +586,7 @@ constexpr int64_t NH_PART_CAP = (int64_t)1 << 26;  // 256 MiB of partial tiles a
 // default shape: the widest tile that does not leave most of it empty, no split
 NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : g.F > 32 ? 64 : 32, 1}; }
 
-NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
+NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps, int pair) {
     if (t_nh_pin) return *t_nh_pin;
     if (const char* f = getenv("TB_NHWC_FORCE")) {  // test hook: "BN,SPLITS"
         NhShape sh{256, 1};
@@ -562,7 +596,7 @@ NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
         }
     }
     std::lock_guard<std::mutex> lk(g_nh_mu);
-    auto it = g_nh_tuned.find(nh_key(ctx->device, g, x_ps));
+    auto it = g_nh_tuned.find(nh_key(ctx->device, g, x_ps, pair));
     return it != g_nh_tuned.end() ? it->second : nh_default(g);
 }
 
@@ -571,7 +605,7 @@ NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
 // with batch stride g.y_bs; res: NHWC with pixel stride r_ps (or null).
 int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp,
                      const float* bias, const float* res, int64_t r_ps, float* y, int64_t y_ps, int act,
-                     int yolo_classes, unsigned long long* phases) {
+                     int yolo_classes, unsigned long long* phases, int pair) {
     if (!conv_nhwc_supported(g, x_ps)) return fail(TB_ERR_UNSUPPORTED, "NHWC tensor-core conv: unsupported geometry");
     if (g.B == 0) return TB_OK;
     if (!aligned16(x) || !aligned16(wp)) return fail(TB_ERR_INVALID, "NHWC conv: x and weights must be 16-byte aligned");
@@ -592,7 +626,7 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "NHWC conv: cuTensorMapEncodeIm2col failed (%d)", (int)r);
     }
-    NhShape sh = nh_choose(ctx, g, x_ps);
+    NhShape sh = nh_choose(ctx, g, x_ps, pair);
     const int bn = sh.bn;
     const int64_t ktiles = nh_ktiles(g);
     const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
@@ -608,6 +642,11 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
         const uint32_t box[2] = {(uint32_t)NH_BK, (uint32_t)bn};
         int r = encode_map(&maps.b, wp, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (r != TB_OK) return r;
+        if (pair) {  // the (lo, lo) operand follows the (hi, hi) one
+            r = encode_map(&maps.b2, wp + conv_nhwc_packed_count(g, 0), 2, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+            if (r != TB_OK) return r;
+        }
     }
     NhwcParams p{};
     if (y_ps > 0 && y_ps % 4 == 0 && aligned16(y)) {
@@ -640,21 +679,27 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     p.vec = y_ps % 4 == 0 && aligned16(y) && (!res || (r_ps % 4 == 0 && aligned16(res))) ? 1 : 0;
     p.act = act;
     p.yolo_classes = yolo_classes;
-    if (bn == 256) return nh_launch<256, 4>(ctx, maps, p);
-    if (bn == 128) return nh_launch<128, 6>(ctx, maps, p);
-    if (bn == 32) return nh_launch<32, 8>(ctx, maps, p);
-    return nh_launch<64, 8>(ctx, maps, p);
+    if (pair) {
+        if (bn == 256) return nh_launch<256, 2, true>(ctx, maps, p);
+        if (bn == 128) return nh_launch<128, 4, true>(ctx, maps, p);
+        if (bn == 32) return nh_launch<32, 8, true>(ctx, maps, p);
+        return nh_launch<64, 6, true>(ctx, maps, p);
+    }
+    if (bn == 256) return nh_launch<256, 4, false>(ctx, maps, p);
+    if (bn == 128) return nh_launch<128, 6, false>(ctx, maps, p);
+    if (bn == 32) return nh_launch<32, 8, false>(ctx, maps, p);
+    return nh_launch<64, 8, false>(ctx, maps, p);
 }
 
 // Workspace the NHWC conv of this geometry needs (split-K partials of its tuned shape).
-int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps) {
-    return nh_part_floats(g, nh_choose(ctx, g, x_ps));
+int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps, int pair) {
+    return nh_part_floats(g, nh_choose(ctx, g, x_ps, pair));
 }
 
 // Time the tile shapes (filters per tile x K splits) of this geometry on the given buffers
 // (bias and residual off) and keep the fastest for later launches. Blocks; grows the workspace.
 int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_ps, const float* wp, float* y,
-                       int64_t y_ps) {
+                       int64_t y_ps, int pair) {
     if (g.B == 0 || !conv_nhwc_supported(g, x_ps)) return TB_OK;
     const int64_t ktiles = nh_ktiles(g);
     std::vector<NhShape> cands;
@@ -681,10 +726,10 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
     NhShape best = cands[0];
     for (const NhShape& c : cands) {
         t_nh_pin = &c;
-        r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr);
+        r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr, pair);
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && r == TB_OK; ++rep)
-            r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr);
+            r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr, pair);
         cudaEventRecord(e1, ctx->stream);
         t_nh_pin = nullptr;
         cudaError_t e = cudaEventSynchronize(e1);
@@ -702,7 +747,7 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
     cudaEventDestroy(e1);
     if (r != TB_OK) return r;
     std::lock_guard<std::mutex> lk(g_nh_mu);
-    g_nh_tuned[nh_key(ctx->device, g, x_ps)] = best;
+    g_nh_tuned[nh_key(ctx->device, g, x_ps, pair)] = best;
     return TB_OK;
 }
 

@@ -137,6 +137,15 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t desc_a, uint6
         "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
+// kind::f16 with BF16 A and B (both operands of one MMA the same type), FP32 accumulate
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
 // arrive on `bar` once every tcgen05 op issued so far by this thread has completed
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     unsigned a = (unsigned)__cvta_generic_to_shared(bar);

@@ -253,7 +253,8 @@ int tb_group_context(tb_group* g, int64_t local, tb_ctx** ctx) {
     return TB_OK;
 }
 
-int tb_group_gather(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank, void* recv_root) {
+int tb_group_gather_async(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank,
+                          void* recv_root) {
     if (!g || !send_local || !bytes_per_rank) return fail(TB_ERR_INVALID, "tb_group_gather: bad arguments");
     if (g->broken) return fail(TB_ERR_STATE, "tb_group_gather: the group was aborted after a timeout");
     const NcclApi* api = nccl();
@@ -290,7 +291,18 @@ int tb_group_gather(tb_group* g, const void* const* send_local, const int64_t* b
     r = api->groupEnd();
     if (rc != TB_OK) return rc;
     if (r != kNcclSuccess && r != kNcclInProgress) return nccl_fail(api, r, "ncclGroupEnd");
-    return wait_group(g, true, "tb_group_gather");
+    return wait_group(g, false, "tb_group_gather");  // enqueued (non-blocking communicators)
+}
+
+int tb_group_wait(tb_group* g) {
+    if (!g) return fail(TB_ERR_INVALID, "null group");
+    if (g->broken) return fail(TB_ERR_STATE, "tb_group_wait: the group was aborted after a timeout");
+    return wait_group(g, true, "tb_group_wait");
+}
+
+int tb_group_gather(tb_group* g, const void* const* send_local, const int64_t* bytes_per_rank, void* recv_root) {
+    int r = tb_group_gather_async(g, send_local, bytes_per_rank, recv_root);
+    return r != TB_OK ? r : tb_group_wait(g);
 }
 
 int tb_group_destroy(tb_group* g) {

@@ -86,6 +86,7 @@ struct tb_net {
     // activations are NHWC, every conv runs on the NHWC tensor-core kernel, the input is
     // converted into x_nhwc (x_ps floats per pixel) first and the yolo heads are written NCHW
     bool nhwc = false;
+    int pair = 0;  // NHWC plan in BF16-split mode: activations as bf16 (hi, lo) pairs
     float* x_nhwc = nullptr;
     int64_t x_ps = 0;
     // the first conv with C * KH * KW <= 32 runs as a 1x1 conv over its receptive fields
@@ -251,9 +252,10 @@ int run_layer_nhwc(tb_net* net, int64_t i, const float* x) {
     if (i == 0) {  // the network input, NCHW, into the NHWC staging buffer (or its receptive fields)
         if (net->first_im2col)
             r = nhwc_im2col_first(ctx, B, net->c, net->h, net->w, L.ksize, L.ksize, L.stride, L.stride, L.pad, L.pad,
-                                  1, 1, L.oh, L.ow, x, net->c * net->h * net->w, net->x_nhwc);
+                                  1, 1, L.oh, L.ow, x, net->c * net->h * net->w, net->x_nhwc, net->pair);
         else
-            r = nhwc_from_nchw(ctx, B, net->c, net->h, net->w, x, net->c * net->h * net->w, net->x_nhwc, net->x_ps);
+            r = nhwc_from_nchw(ctx, B, net->c, net->h, net->w, x, net->c * net->h * net->w, net->x_nhwc, net->x_ps,
+                               net->pair);
         if (r != TB_OK) return r;
         net->launches++;
     }
@@ -277,13 +279,13 @@ int run_layer_nhwc(tb_net* net, int64_t i, const float* x) {
         }
         net->launches++;
         return conv_nhwc_launch(ctx, g, in.ptr, in.ps, L.d_wp, L.d_bias, res, rps, T.out.ptr, T.out.ps, (int)L.act,
-                                (int)L.fuse_yolo, nullptr);
+                                (int)L.fuse_yolo, nullptr, net->pair);
     }
     case TB_LAYER_SHORTCUT: {
         const Layer& F = *net->layers[L.from];
         net->launches++;
         return nhwc_shortcut(ctx, B * L.oh * L.ow, L.oc, in.ptr, in.ps, F.out.ptr, F.out.ps, L.out.ptr, L.out.ps,
-                             (int)L.act);
+                             (int)L.act, net->pair);
     }
     case TB_LAYER_ROUTE: {
         if (L.route_zero_copy) return TB_OK;
@@ -299,7 +301,8 @@ int run_layer_nhwc(tb_net* net, int64_t i, const float* x) {
     }
     case TB_LAYER_UPSAMPLE:
         net->launches++;
-        return nhwc_upsample(ctx, B, L.c, L.h, L.w, L.stride, L.up_scale, in.ptr, in.ps, L.out.ptr, L.out.ps);
+        return nhwc_upsample(ctx, B, L.c, L.h, L.w, L.stride, L.up_scale, in.ptr, in.ps, L.out.ptr, L.out.ps,
+                             net->pair);
     }
     return fail(TB_ERR_STATE, "layer %lld: not on the NHWC plan", (long long)i);
 }
@@ -595,7 +598,8 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     TB_ENTER(net->ctx);
     if (net->finalized) return fail(TB_ERR_STATE, "net already finalized");
     if (net->layers.empty()) return fail(TB_ERR_INVALID, "empty net");
-    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32 && math_mode != TB_MATH_FP32_TILED)
+    if (math_mode != TB_MATH_FP32 && math_mode != TB_MATH_TF32 && math_mode != TB_MATH_FP32_TILED &&
+        math_mode != TB_MATH_BF16_SPLIT)
         return fail(TB_ERR_UNSUPPORTED, "net: math mode %lld is not available in this build", (long long)math_mode);
     net->math_mode = math_mode;
     int r = infer_shapes(net);
@@ -630,7 +634,8 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     net->first_im2col = false;
     {
         const char* ev = getenv("TB_NET_NHWC");
-        bool ok = math_mode == TB_MATH_TF32 && net->fusion && !(ev && ev[0] == '0');
+        const bool tc_mode = math_mode == TB_MATH_TF32 || math_mode == TB_MATH_BF16_SPLIT;
+        bool ok = tc_mode && net->fusion && !(ev && ev[0] == '0');
         for (int64_t i = 0; ok && i < n; ++i) {
             const Layer& L = *net->layers[i];
             switch (L.type) {
@@ -651,8 +656,10 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
                 break;
             }
             case TB_LAYER_SHORTCUT:
-            case TB_LAYER_UPSAMPLE:
                 if (L.oc % 4) ok = false;
+                break;
+            case TB_LAYER_UPSAMPLE:  // bf16 pairs are copied bit for bit: a scale needs decoding
+                if (L.oc % 4 || (math_mode == TB_MATH_BF16_SPLIT && L.up_scale != 1.0f)) ok = false;
                 break;
             case TB_LAYER_ROUTE:
                 for (int64_t j : L.inputs)
@@ -666,6 +673,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             }
         }
         net->nhwc = ok;
+        net->pair = ok && math_mode == TB_MATH_BF16_SPLIT ? 1 : 0;
         if (!ok) net->first_im2col = false;
     }
     // floats per image and batch / pixel strides of a layer's own output buffer
@@ -788,13 +796,13 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         float* raw = dev_upload(net, L.weights, &err);
         if (!raw) return err;
         if (net->nhwc && i == 0 && net->first_im2col) {
-            L.d_wp = alloc(g.F * 32);
+            L.d_wp = alloc(g.F * 32 * (net->pair ? 2 : 1));
             if (!L.d_wp) return err;
-            r = nhwc_pack_first(net->ctx, g.F, g.C, g.KH, g.KW, raw, L.d_wp);
+            r = nhwc_pack_first(net->ctx, g.F, g.C, g.KH, g.KW, raw, L.d_wp, net->pair);
         } else if (net->nhwc) {
-            L.d_wp = alloc(conv_nhwc_packed_count(g));
+            L.d_wp = alloc(conv_nhwc_packed_count(g, net->pair));
             if (!L.d_wp) return err;
-            r = conv_nhwc_pack(net->ctx, g, raw, L.d_wp);
+            r = conv_nhwc_pack(net->ctx, g, raw, L.d_wp, net->pair);
         } else {
             L.d_wp = alloc(g.Kpad * g.Mpad);
             if (!L.d_wp) return err;
@@ -832,10 +840,10 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
             if (i == 0 && net->first_im2col) g = first_as_1x1(g);
             const View in = input_view(net, i, nullptr);
             if (!(at && at[0] == '0')) {
-                r = conv_nhwc_autotune(net->ctx, g, in.ptr, in.ps, L.d_wp, T.out.ptr, T.out.ps);
+                r = conv_nhwc_autotune(net->ctx, g, in.ptr, in.ps, L.d_wp, T.out.ptr, T.out.ps, net->pair);
                 if (r != TB_OK) return r;
             }
-            ws_floats = std::max(ws_floats, conv_nhwc_ws_floats(net->ctx, g, in.ps));
+            ws_floats = std::max(ws_floats, conv_nhwc_ws_floats(net->ctx, g, in.ps, net->pair));
         }
     }
     if (!(at && at[0] == '0') && !net->nhwc) {

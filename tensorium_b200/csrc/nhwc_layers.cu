@@ -13,17 +13,15 @@ namespace {
 // x: NCHW [b][c][h][w] (batch stride x_bs) -> y: NHWC, pixel stride ps >= c, channels c..ps-1
 // zero; values rounded to TF32 (nearest), as every activation the tensor cores read
 __global__ void k_nchw_to_nhwc(int64_t npix, int c, int hw, int ps, const float* __restrict__ x, int64_t x_bs,
-                               float* __restrict__ y) {
+                               float* __restrict__ y, int pair) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npix * ps;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t pix = i / ps;
         const int ch = (int)(i - pix * ps);
         const int64_t b = pix / hw;
         const int q = (int)(pix - b * hw);
-        float v = ch < c ? __ldg(x + b * x_bs + (int64_t)ch * hw + q) : 0.0f;
-        uint32_t u = __float_as_uint(v);  // round to nearest TF32 (ties away), finite values only
-        if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
-        y[i] = __uint_as_float(u);
+        const float v = ch < c ? __ldg(x + b * x_bs + (int64_t)ch * hw + q) : 0.0f;
+        y[i] = tb_fmt_store(v, pair);
     }
 }
 
@@ -53,15 +51,16 @@ __global__ void k_copy_nhwc4(int64_t total4, int c4, const float4* __restrict__ 
     }
 }
 
-// shortcut: out = act(a + b)
+// shortcut: out = act(a + b) (bf16 pairs decoded, added in fp32, encoded again)
 __global__ void k_shortcut_nhwc(int64_t total, int c, const float* __restrict__ a, int aps,
-                                const float* __restrict__ b, int bps, float* __restrict__ y, int yps, int act) {
+                                const float* __restrict__ b, int bps, float* __restrict__ y, int yps, int act,
+                                int pair) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t pix = i / c;
         const int ch = (int)(i - pix * c);
-        float v = __fadd_rn(__ldg(a + pix * aps + ch), __ldg(b + pix * bps + ch));
+        float v = __fadd_rn(tb_fmt_load(__ldg(a + pix * aps + ch), pair), tb_fmt_load(__ldg(b + pix * bps + ch), pair));
         if (act != TB_ACT_LINEAR) v = tb_activate_dev(v, act);
-        y[pix * yps + ch] = v;
+        y[pix * yps + ch] = pair ? tb_pair_encode(v) : v;
     }
 }
 
@@ -70,7 +69,7 @@ __global__ void k_shortcut_nhwc(int64_t total, int c, const float* __restrict__ 
 // the padding, rounded to TF32. One k tile instead of KH * KW mostly empty ones.
 __global__ void k_im2col_first(int64_t npix, int C, int H, int W, int KW, int K, int OW, int OHW, int SY, int SX,
                                int PY, int PX, int DY, int DX, const float* __restrict__ x, int64_t x_bs,
-                               float* __restrict__ y) {
+                               float* __restrict__ y, int pair) {
     // one thread per output pixel: the lanes of a warp read neighbouring pixels of the same tap
     // (coalesced) and each writes its 128-byte row of 32 values
     for (int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pix < npix; pix += (int64_t)gridDim.x * blockDim.x) {
@@ -91,9 +90,7 @@ __global__ void k_im2col_first(int64_t npix, int C, int H, int W, int KW, int K,
                     if (++s == KW) s = 0, ++r;
                 }
             }
-            uint32_t u = __float_as_uint(t);
-            if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
-            v[k] = __uint_as_float(u);
+            v[k] = tb_fmt_store(t, pair);
         }
         float4* yo = reinterpret_cast<float4*>(y + pix * 32);
 #pragma unroll
@@ -101,8 +98,10 @@ __global__ void k_im2col_first(int64_t npix, int C, int H, int W, int KW, int K,
     }
 }
 
-// its weights: wp[f][k] = tf32(w[f][c][r][s]) for k = (r * KW + s) * C + c < K, zero up to 32
-__global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp, int F, int C, int KH, int KW) {
+// its weights: wp[f][k] = tf32(w[f][c][r][s]) for k = (r * KW + s) * C + c < K, zero up to 32; in
+// pair mode two such operands, [F][32] of (hi, hi) and then [F][32] of (lo, lo) bf16 pairs
+__global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp, int F, int C, int KH, int KW,
+                             int pair) {
     const int K = C * KH * KW;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < F * 32; i += gridDim.x * blockDim.x) {
         const int f = i >> 5, k = i & 31;
@@ -112,9 +111,13 @@ __global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp
             const int r = rs / KW, s = rs - r * KW;
             v = w[(((int64_t)f * C + c) * KH + r) * KW + s];
         }
-        uint32_t u = __float_as_uint(v);
-        if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
-        wp[i] = __uint_as_float(u);
+        if (!pair) {
+            wp[i] = tb_tf32_rna(v);
+        } else {
+            const uint32_t s = __float_as_uint(tb_pair_encode(v)), hi = s & 0xffffu, lo = s >> 16;
+            wp[i] = __uint_as_float(hi | (hi << 16));
+            wp[(int64_t)F * 32 + i] = __uint_as_float(lo | (lo << 16));
+        }
     }
 }
 
@@ -122,31 +125,33 @@ __global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp
 
 int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
                       int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
-                      const float* x, int64_t x_bs, float* y) {
+                      const float* x, int64_t x_bs, float* y, int pair) {
     const int64_t npix = B * OH * OW;
     if (npix == 0) return TB_OK;
     k_im2col_first<<<grid_for(npix, 128, ctx->sm_count), 128, 0, ctx->stream>>>(
         npix, (int)C, (int)H, (int)W, (int)KW, (int)(C * KH * KW), (int)OW, (int)(OH * OW), (int)SY, (int)SX,
-        (int)PY, (int)PX, (int)DY, (int)DX, x, x_bs, y);
+        (int)PY, (int)PX, (int)DY, (int)DX, x, x_bs, y, pair);
     return check_launch("k_im2col_first");
 }
 
-int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp) {
-    k_pack_first<<<grid_for(F * 32, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)F, (int)C, (int)KH, (int)KW);
+int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp, int pair) {
+    k_pack_first<<<grid_for(F * 32, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wp, (int)F, (int)C, (int)KH, (int)KW,
+                                                                                pair);
     return check_launch("k_pack_first");
 }
 
 int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, const float* x, int64_t x_bs,
-                   float* y, int64_t ps) {
+                   float* y, int64_t ps, int pair) {
     const int64_t npix = batch * h * w;
     if (npix == 0) return TB_OK;
     k_nchw_to_nhwc<<<grid_for(npix * ps, 256, ctx->sm_count), 256, 0, ctx->stream>>>(npix, (int)c, (int)(h * w),
-                                                                                     (int)ps, x, x_bs, y);
+                                                                                     (int)ps, x, x_bs, y, pair);
     return check_launch("k_nchw_to_nhwc");
 }
 
 int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, int64_t s, float scale,
-                  const float* x, int64_t xps, float* y, int64_t yps) {
+                  const float* x, int64_t xps, float* y, int64_t yps, int pair) {
+    if (pair && scale != 1.0f) return fail(TB_ERR_UNSUPPORTED, "NHWC upsample: bf16-pair activations need scale 1");
     if (c % 4 || xps % 4 || yps % 4 || !aligned16(x) || !aligned16(y))
         return fail(TB_ERR_STATE, "NHWC upsample: channels, strides and pointers must be 16-byte multiples");
     const int64_t total4 = batch * h * s * w * s * (c / 4);
@@ -169,11 +174,11 @@ int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps,
 }
 
 int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t aps, const float* b, int64_t bps,
-                  float* y, int64_t yps, int act) {
+                  float* y, int64_t yps, int act, int pair) {
     const int64_t total = npix * c;
     if (total == 0) return TB_OK;
     k_shortcut_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(total, (int)c, a, (int)aps, b,
-                                                                                  (int)bps, y, (int)yps, act);
+                                                                                  (int)bps, y, (int)yps, act, pair);
     return check_launch("k_shortcut_nhwc");
 }
 

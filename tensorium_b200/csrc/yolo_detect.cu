@@ -146,13 +146,45 @@ __global__ void __launch_bounds__(256) k_yolo_write(const DetectArgs a, const in
 
 }  // namespace
 
+// per image: the detections found over all heads (may exceed the capacity)
+__global__ void k_yolo_totals(const int* __restrict__ per_head, int n_heads, int batch, int64_t* __restrict__ out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= batch) return;
+    int64_t t = 0;
+    for (int h = 0; h < n_heads; ++h) t += per_head[b * n_heads + h];
+    out[b] = t;
+}
+
+static int yolo_detect_impl(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads, int64_t img_w,
+                            int64_t img_h, int64_t net_w, int64_t net_h, float thresh, int64_t relative,
+                            int64_t letter, int64_t capacity, tb_detection* dets, float* prob, int64_t* counts_host,
+                            int64_t* counts_dev);
+
 extern "C" int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads,
                               int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
                               int64_t relative, int64_t letter, int64_t capacity, tb_detection* dets,
                               float* prob, int64_t* counts_host) {
+    if (!counts_host) return fail(TB_ERR_INVALID, "yolo_detect: null counts");
+    return yolo_detect_impl(ctx, batch, n_heads, heads, img_w, img_h, net_w, net_h, thresh, relative, letter,
+                            capacity, dets, prob, counts_host, nullptr);
+}
+
+extern "C" int tb_yolo_detect_device(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads,
+                                     int64_t img_w, int64_t img_h, int64_t net_w, int64_t net_h, float thresh,
+                                     int64_t relative, int64_t letter, int64_t capacity, tb_detection* dets,
+                                     float* prob, int64_t* counts_dev) {
+    if (!counts_dev) return fail(TB_ERR_INVALID, "yolo_detect: null counts");
+    return yolo_detect_impl(ctx, batch, n_heads, heads, img_w, img_h, net_w, net_h, thresh, relative, letter,
+                            capacity, dets, prob, nullptr, counts_dev);
+}
+
+static int yolo_detect_impl(tb_ctx* ctx, int64_t batch, int64_t n_heads, const tb_yolo_head* heads, int64_t img_w,
+                            int64_t img_h, int64_t net_w, int64_t net_h, float thresh, int64_t relative,
+                            int64_t letter, int64_t capacity, tb_detection* dets, float* prob, int64_t* counts_host,
+                            int64_t* counts_dev) {
     TB_ENTER(ctx);
     if (batch < 0 || n_heads <= 0 || n_heads > MAX_HEADS || !heads || img_w <= 0 || img_h <= 0 ||
-        net_w <= 0 || net_h <= 0 || capacity < 0 || !counts_host || (capacity > 0 && !dets))
+        net_w <= 0 || net_h <= 0 || capacity < 0 || (capacity > 0 && !dets))
         return fail(TB_ERR_INVALID, "yolo_detect: bad arguments (at most %d heads)", MAX_HEADS);
     if (batch == 0) return TB_OK;
     if (batch > 65535) return fail(TB_ERR_INVALID, "yolo_detect: batch too large");
@@ -212,6 +244,11 @@ extern "C" int tb_yolo_detect(tb_ctx* ctx, int64_t batch, int64_t n_heads, const
         k_yolo_write<<<grid, 256, 0, ctx->stream>>>(a, d_counts, dets, prob, max_classes);
         r = check_launch("k_yolo_write");
         if (r != TB_OK) return r;
+    }
+    if (counts_dev) {  // per-image totals stay on the device; nothing waits
+        k_yolo_totals<<<(unsigned)ceil_div(batch, 128), 128, 0, ctx->stream>>>(d_counts, (int)n_heads, (int)batch,
+                                                                              counts_dev);
+        return check_launch("k_yolo_totals");
     }
     std::vector<int> hc((size_t)ncounts);
     TB_CHECK_CUDA(cudaMemcpyAsync(hc.data(), d_counts, sizeof(int) * (size_t)ncounts,

@@ -104,8 +104,6 @@ class DetectionGather:
         self.pack_bytes = 8 * B + self.rec_bytes
         self.pack = torch.zeros(self.pack_bytes, dtype=torch.uint8, device=ctx.torch_device)
         self.prob = torch.empty(B * capacity * self.classes, dtype=torch.float32, device=ctx.torch_device)
-        self.counts = (C.c_int64 * B)()
-        self.counts_host = torch.zeros(B, dtype=torch.int64).pin_memory()
         self.sizes = (C.c_int64 * world)(*([self.pack_bytes] * world))
         self.send = (C.c_void_p * 1)(self.pack.data_ptr())
         if rank == 0:
@@ -116,19 +114,23 @@ class DetectionGather:
 
     def step(self, download: bool = True):
         """Detections of the last forward, gathered on rank 0 (and, with download, copied to its
-        pinned host buffer asynchronously on the context's stream)."""
+        pinned host buffer), all queued on the context's stream behind the forward: the counts
+        stay on the device (tb_yolo_detect_device) and the NCCL gather is only enqueued
+        (tb_group_gather_async), so the host never waits inside a step.  wait() bounds the wait
+        for the queued transfers."""
         C, lib, check = self._C, self._lib, self._check
         ctx = self.net.ctx
         B = self.net.batch
-        check(lib.tb_yolo_detect(ctx.handle, B, len(self.heads), self.hs, 416, 416, 416, 416, self.thresh, 1, 0,
-                                 self.capacity, C.c_void_p(self.pack.data_ptr() + 8 * B),
-                                 C.c_void_p(self.prob.data_ptr()), self.counts))
-        self.counts_host.numpy()[:] = np.minimum(np.array(self.counts[:], np.int64), self.capacity)
-        self.pack[:8 * B].copy_(self.counts_host.view(torch.uint8), non_blocking=True)
+        check(lib.tb_yolo_detect_device(ctx.handle, B, len(self.heads), self.hs, 416, 416, 416, 416, self.thresh,
+                                        1, 0, self.capacity, C.c_void_p(self.pack.data_ptr() + 8 * B),
+                                        C.c_void_p(self.prob.data_ptr()), C.c_void_p(self.pack.data_ptr())))
         out = C.c_void_p(self.out.data_ptr()) if self.out is not None else None
-        check(lib.tb_group_gather(self.group, self.send, self.sizes, out))
+        check(lib.tb_group_gather_async(self.group, self.send, self.sizes, out))
         if download and self.host is not None:
             self.host.copy_(self.out, non_blocking=True)
+
+    def wait(self):
+        self._check(self._lib.tb_group_wait(self.group))
 
     @property
     def d2h_bytes(self) -> int:
@@ -144,7 +146,7 @@ class DetectionGather:
         raw = self.host.numpy()
         for r in range(self.world):
             part = raw[r * self.pack_bytes:(r + 1) * self.pack_bytes]
-            counts = part[:8 * B].view(np.int64)
+            counts = np.minimum(part[:8 * B].view(np.int64), cap)
             recs = part[8 * B:].view(DET_DTYPE).reshape(B, cap)
             res.extend(recs[b, :int(counts[b])].copy() for b in range(B))
         return res

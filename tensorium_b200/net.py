@@ -11,7 +11,7 @@ import ctypes as C
 import numpy as np
 import torch
 
-from ._lib import LAYER_TYPES, MATH_FP32, PARAM, LayerInfo, check, lib
+from ._lib import LAYER_TYPES, MATH_BF16_SPLIT, MATH_FP32, PARAM, LayerInfo, check, lib
 from .context import Context, ptr
 from .layers import TYoloLayer, get_detections
 from .synth import layer_shapes
@@ -25,6 +25,7 @@ class TNNet:
     def __init__(self, ctx: Context, specs, batch: int, input_shape, fuse_batchnorm: bool = True,
                  fusion: bool = True, math_mode: int = MATH_FP32):
         self.ctx = ctx
+        self.math_mode = int(math_mode)
         self.specs = specs
         self.batch = int(batch)
         self.input_shape = tuple(input_shape)
@@ -86,6 +87,7 @@ class TNNet:
         (tb_darknet_load).  ctx = None gives a host-only net (inspect, save; no forward)."""
         self = cls.__new__(cls)
         self.ctx = ctx
+        self.math_mode = int(math_mode)
         self.handle = C.c_void_p()
         check(lib.tb_darknet_load(ctx.handle if ctx is not None else None, str(cfg_path).encode(),
                                   None if weights_path is None else str(weights_path).encode(),
@@ -182,7 +184,13 @@ class TNNet:
         numel = (self.batch - 1) * bs.value + (h * w - 1) * ps.value + c
         t = torch.as_tensor(_CAI(p.value, numel), device=self.ctx.torch_device)
         nhwc = t.as_strided((self.batch, h, w, c), (bs.value, w * ps.value, ps.value, 1))
-        return nhwc.permute(0, 3, 1, 2).contiguous().reshape(self.batch, c * h * w)
+        out = nhwc.permute(0, 3, 1, 2).contiguous().reshape(self.batch, c * h * w)
+        if self.math_mode == MATH_BF16_SPLIT:  # 32-bit slots of bf16 (hi, lo) pairs: hi + lo
+            u = out.view(torch.int32)
+            hi = torch.bitwise_left_shift(u, 16).view(torch.float32)
+            lo = torch.bitwise_and(u, -65536).view(torch.float32)
+            out = hi + lo
+        return out
 
     def predict(self, x_host: np.ndarray, layers=None):
         """TNNet.predict (source/nnet.pas:452-472): host input in, host outputs back
