@@ -40,6 +40,7 @@ INPUT = (3, 416, 416)
 HEADS = (82, 94, 106)
 METRIC = "YOLOv3-416 images/sec (FP32 path)"
 METRIC_TF32 = "YOLOv3-416 images/sec (TF32 tensor-core path)"
+METRIC_BF16 = "YOLOv3-416 images/sec (BF16-split tensor-core path)"
 MATH_MODES = {"fp32": 0, "tf32": 1, "fp32_tiled": 2, "bf16split": 3}
 PROFILE_SUMMARY = ROOT / "profiles" / "conv_fp32_yolov3_b8.json"
 PROFILE_SUMMARY_TF32 = ROOT / "profiles" / "k_conv_nhwc_yolov3_b8.json"
@@ -328,9 +329,11 @@ def run_ours(args):
                 "algorithmic_flops_per_forward": conv_flops, "conv_ms_per_forward": conv_ms,
                 "all_layers_ms_per_forward": total_ms}
 
-    line = {"metric": METRIC if args.math == "fp32" else METRIC_TF32, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+    line = {"metric": {"fp32": METRIC, "tf32": METRIC_TF32, "bf16split": METRIC_BF16}.get(args.math, METRIC + " [" + args.math + "]"), "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.math == "fp32" else "tf32 (fp32 accumulate)",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": {"fp32": "f32", "fp32_tiled": "f32", "tf32": "tf32 (fp32 accumulate)",
+                      "bf16split": "bf16 (hi, lo) pairs (fp32 accumulate)"}[args.math],
             "data": "synthetic (seeded uniform images, random He-init weights, BN stats as config 0; "
                     "no dataset or .weights in the container)",
             "config": {"workload": "YOLOv3-416 forward (BASELINE config 3), batch 8 per GPU",
@@ -341,6 +344,8 @@ def run_ours(args):
             "gpu_launches": int(launches_per_step * args.steps)}
     if args.math == "fp32" and not args.no_tf32_block:
         line["tf32_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream)
+        line["bf16split_path"] = tf32_block(args, ctx, specs, x, net, world, barrier, max_over_ranks, stream,
+                                            mode="bf16split")
     if args.math == "fp32" and not args.no_configs:
         line["other_configs"] = configs_block(args, ctx, world, rank, barrier, max_over_ranks, stream, peak,
                                               cpu=(world == 1 and not args.no_cpu_baseline))
@@ -459,14 +464,15 @@ def configs_block(args, ctx, world, rank, barrier, max_over_ranks, stream, fma_p
     return out
 
 
-def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, stream):
-    """The same forward on the TF32 tensor-core path (BASELINE config 3's optional path), timed the
-    same way, with its head error against the FP32 path on the same images."""
+def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, stream, mode="tf32"):
+    """The same forward on a tensor-core path (BASELINE config 3's optional path: TF32, or the
+    BF16-split operands), timed the same way, with its head error against the FP32 path (which is
+    bit-identical to the reference CPU path) on the same images."""
     import torch
     from tensorium_b200 import synth
     from tensorium_b200.net import TNNet
     B = args.batch
-    net = TNNet(ctx, specs, B, INPUT, math_mode=MATH_MODES["tf32"])
+    net = TNNet(ctx, specs, B, INPUT, math_mode=MATH_MODES[mode])
     for _ in range(max(args.warmup, 1)):
         net.forward(x)
     launches = net.launch_count
@@ -497,14 +503,23 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
     for h in HEADS:  # yolo outputs (the head convs are fused into them)
         a, b = net.output(h).double(), net32.output(h).double()
         errs.append(float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b)))
-    out = {"metric": METRIC_TF32, "value": world * B * args.steps / (ms / 1e3), "unit": "images/s",
-           "ms_per_step": ms / args.steps, "dtype": "tf32 operands rounded to nearest, fp32 accumulate",
+    is_bf = mode == "bf16split"
+    out = {"metric": METRIC_BF16 if is_bf else METRIC_TF32, "value": world * B * args.steps / (ms / 1e3),
+           "unit": "images/s", "ms_per_step": ms / args.steps,
+           "dtype": ("bf16 (hi, lo) operand pairs, all four partial products, fp32 accumulate" if is_bf
+                     else "tf32 operands rounded to nearest, fp32 accumulate"),
            "gpu_launches": int(launches * args.steps),
-           "roofline": {"bound": "tensor", "kernel": "k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) + "
-                                                     "input / receptive-field conversion and NHWC upsample",
+           "roofline": {"bound": "tensor", "kernel": ("k_conv_nhwc<PAIR> (tcgen05 kind::f16, 8 MMAs per 32 channels) "
+                                                      if is_bf else "k_conv_nhwc (tcgen05 TF32, ") +
+                                                     "A by TMA im2col, NHWC activations) + input / receptive-field "
+                                                     "conversion and NHWC upsample",
                         "achieved": achieved, "peak": tc_rate.value, "unit": "TFLOP/s",
                         "frac": achieved / tc_rate.value,
                         "peak_source": ("TF32 tcgen05 MMA rate measured in this run with operands resident "
+                                        "(tb_diag_tc_mma_rate, M=128 N=256 K=8, at the current SM clock); the "
+                                        "BF16-split path issues twice the MMAs of TF32 per FLOP, so its MMA-time "
+                                        "fraction is twice this" if is_bf else
+                                        "TF32 tcgen05 MMA rate measured in this run with operands resident "
                                         "(tb_diag_tc_mma_rate, M=128 N=256 K=8, at the current SM clock)"),
                         "conv_ms_per_forward": conv_ms,
                         "traffic": (json.loads(PROFILE_SUMMARY_TF32.read_text()).get("dram_bytes_per_forward")

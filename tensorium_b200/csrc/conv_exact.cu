@@ -34,8 +34,14 @@ int exact_mode_of(const ConvGeom& g, const float* x) {
     return EX_GEN;
 }
 
+// configurations >= kWsBase: the warp-specialised kernel (conv_exact_ws.cu), 128 filters x 64 or
+// 128 pixels, 3x3 and vectorised 1x1 modes
+constexpr int kWsBase = 100;
+bool ws_mode(int mode, bool fma) { return fma && (mode == EX_3X3 || mode == EX_1X1V); }
+
 // tile index t of kTiles plus a stage-depth variant (ExactShape) in t / kNumTiles
 int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool fma) {
+    if (t >= kWsBase) return exact_ws_launch(ctx, p, grid, mode, t == kWsBase ? 64 : 128);
     const int var = t / kNumTiles;
     switch (t % kNumTiles) {
     case 0: return exact_launch_128x128(ctx, p, grid, mode, fma, var);
@@ -46,8 +52,12 @@ int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool 
     }
 }
 
+int tile_bm(int t) { return t >= kWsBase ? 128 : kTiles[t % kNumTiles].BM; }
+int tile_bn(int t) { return t >= kWsBase ? (t == kWsBase ? 64 : 128) : kTiles[t % kNumTiles].BN; }
+int tile_nt(int t) { return t >= kWsBase ? (t == kWsBase ? 128 : 256) : kTiles[t % kNumTiles].NT; }
+
 bool tile_admissible(int t, int64_t M) {
-    const int BM = kTiles[t % kNumTiles].BM;
+    const int BM = tile_bm(t);
     if (M <= 32) return BM == 32;
     if (M <= 64) return BM <= 64;
     return BM >= 64;
@@ -56,7 +66,7 @@ bool tile_admissible(int t, int64_t M) {
 // Wave model: an SM that receives k CTAs of a tile runs them at a rate that grows with the warps
 // resident (full from 12 warps up); the layer ends with the busiest SM.
 double model_cost(tb_ctx* ctx, int t, const ConvGeom& g, int mode) {
-    const ExactTile& T = kTiles[t % kNumTiles];
+    const ExactTile T{tile_bm(t), tile_bn(t), tile_nt(t)};
     const int64_t M = g.F, N = g.B * g.OH * g.OW;
     const int64_t tiles = ceil_div(M, T.BM) * ceil_div(N, T.BN);
     ConvParams dummy{};
@@ -84,6 +94,7 @@ int choose_tile(tb_ctx* ctx, const ConvGeom& g, int mode, bool fma) {
     // variant (index / 5) for the parity tests of every configuration
     if (const char* f = getenv("TB_EXACT_FORCE")) {
         int t = atoi(f);
+        if (t >= kWsBase && t <= kWsBase + 1 && ws_mode(mode, fma) && tile_admissible(t, g.F)) return t;
         if (t >= 0 && t < num_configs(mode, fma) && tile_admissible(t, g.F)) return t;
         if (t >= 0 && tile_admissible(t % kNumTiles, g.F)) return t % kNumTiles;
     }
@@ -125,7 +136,7 @@ ConvParams params_of(const ConvGeom& g, const float* x, const float* wp, const f
 }
 
 int launch_tile(tb_ctx* ctx, int t, const ConvGeom& g, const ConvParams& p, int mode, bool fma) {
-    const ExactTile& T = kTiles[t % kNumTiles];
+    const ExactTile T{tile_bm(t), tile_bn(t), tile_nt(t)};
     dim3 grid((unsigned)ceil_div(p.Ntot, T.BN), (unsigned)ceil_div(g.F, T.BM), 1);
     if (grid.y > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
     return run_tile(ctx, t, p, grid, mode, fma);
@@ -169,7 +180,11 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
     TB_CHECK_CUDA(cudaEventCreate(&e1));
     float best_ms = 1e30f;
     int best = -1, rc = TB_OK;
-    for (int t = 0; t < num_configs(mode, fma) && rc == TB_OK; ++t) {
+    std::vector<int> cfgs;
+    for (int t = 0; t < num_configs(mode, fma); ++t) cfgs.push_back(t);
+    if (ws_mode(mode, fma)) cfgs.push_back(kWsBase), cfgs.push_back(kWsBase + 1);
+    for (int t : cfgs) {
+        if (rc != TB_OK) break;
         if (!tile_admissible(t, g.F)) continue;
         rc = launch_tile(ctx, t, g, p, mode, fma);  // warm-up
         if (rc != TB_OK) break;
@@ -184,7 +199,7 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
         if (getenv("TB_AUTOTUNE_VERBOSE"))
             fprintf(stderr, "exact autotune C%lld H%lld F%lld k%lld s%lld B%lld: tile %dx%d var %d mode %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY, (long long)g.B,
-                    kTiles[t % kNumTiles].BM, kTiles[t % kNumTiles].BN, t / kNumTiles, mode, ms / 3);
+                    tile_bm(t), tile_bn(t), t >= kWsBase ? 9 : t / kNumTiles, mode, ms / 3);
         if (ms < best_ms) { best_ms = ms; best = t; }
     }
     cudaEventDestroy(e0);

@@ -295,7 +295,9 @@ class StreamPredictor:
         self.d_in = [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)]
         self.d_out = [[torch.empty(net.output(l).shape, dtype=torch.float32, device=dev) for l in self.layers]
                       for _ in range(2)]
-        self.compute = torch.cuda.current_stream(dev)
+        # the stream the context launches on (the forward's stream), whatever torch's current one is
+        raw = lib.tb_get_stream(net.ctx.handle)
+        self.compute = torch.cuda.ExternalStream(raw, device=dev) if raw else torch.cuda.default_stream(dev)
         self.upload = torch.cuda.Stream(device=dev)
         self.download = torch.cuda.Stream(device=dev)
         self.ev_h2d = [torch.cuda.Event() for _ in range(2)]
@@ -314,15 +316,16 @@ class StreamPredictor:
                 self.upload.wait_event(self.ev_in_free[k])
             self.d_in[k].copy_(h_in, non_blocking=True)
             self.ev_h2d[k].record(self.upload)
-        self.compute.wait_event(self.ev_h2d[k])
-        self.x.copy_(self.d_in[k])
-        self.ev_in_free[k].record(self.compute)
-        self.net.forward(self.x)
-        if self.used[k]:
-            self.compute.wait_event(self.ev_out_free[k])
-        for l, d in zip(self.layers, self.d_out[k]):
-            d.copy_(self.net.output(l))
-        self.ev_out_ready[k].record(self.compute)
+        with torch.cuda.stream(self.compute):
+            self.compute.wait_event(self.ev_h2d[k])
+            self.x.copy_(self.d_in[k])
+            self.ev_in_free[k].record(self.compute)
+            self.net.forward(self.x)
+            if self.used[k]:
+                self.compute.wait_event(self.ev_out_free[k])
+            for l, d in zip(self.layers, self.d_out[k]):
+                d.copy_(self.net.output(l))
+            self.ev_out_ready[k].record(self.compute)
         with torch.cuda.stream(self.download):
             self.download.wait_event(self.ev_out_ready[k])
             for o, d in zip(h_outs, self.d_out[k]):

@@ -62,11 +62,12 @@ def test_conv_bit_exact(ctx, B, C, H, F, k, s, p, dil):
         assert_bit_exact(y, ref, B * F, (B, C, H, F, k, s, act))
 
 
-@pytest.mark.parametrize("tile", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("tile", [0, 1, 2, 3, 4, 5, 10, 15, 17, 100, 101])
 def test_every_exact_tile(ctx, tile, monkeypatch):
-    """Each CTA tile of the order-exact kernel (TB_EXACT_FORCE pins it; a tile too wide for the
-    layer's filters falls back to an admissible one) on the 3x3, 1x1 vector, 1x1 gather and
-    generic-window modes, each twice."""
+    """Each configuration of the order-exact kernel (TB_EXACT_FORCE pins it: tile = index % 5,
+    stage-depth variant = index / 5, 100 / 101 the warp-specialised kernel with 64 / 128 pixels;
+    a configuration a layer cannot take falls back to an admissible one) on the 3x3, 1x1 vector,
+    1x1 gather and generic-window modes, each twice."""
     monkeypatch.setenv("TB_EXACT_FORCE", str(tile))
     for i, (B, C, H, F, k, s, p) in enumerate([(2, 32, 26, 64, 3, 2, 1), (1, 64, 20, 128, 3, 1, 1),
                                                (2, 64, 12, 96, 1, 1, 0), (2, 48, 13, 40, 1, 1, 0),
