@@ -17,12 +17,11 @@ namespace {
 constexpr int DIRECT_KMAX = 32;
 constexpr int DIRECT_FMAX = 128;
 constexpr int DIRECT_THREADS = 128;
-constexpr int DIRECT_PPT = 4;                     // output pixels per thread, DIRECT_THREADS apart
-constexpr int DIRECT_SEG = DIRECT_PPT * DIRECT_THREADS;  // output pixels of one row per block
+constexpr int DIRECT_SEG = 4 * DIRECT_THREADS;  // widest row segment of one block (4 pixels per thread)
 constexpr int DIRECT_SMEM_MAX = 96 * 1024;
 
-// Columns of one staged input row for a segment of DIRECT_SEG outputs.
-__host__ __device__ inline int direct_cols(int SX, int KW, int DX) { return (DIRECT_SEG - 1) * SX + (KW - 1) * DX + 1; }
+// Columns of one staged input row for a segment of seg outputs.
+__host__ __device__ inline int direct_cols(int SX, int KW, int DX, int seg) { return (seg - 1) * SX + (KW - 1) * DX + 1; }
 
 // One block: DIRECT_SEG consecutive output pixels of one output row of one image. The C x KH input
 // rows they read are staged in shared memory (zero where the window leaves the image), so the
@@ -31,19 +30,21 @@ __host__ __device__ inline int direct_cols(int SX, int KW, int DX) { return (DIR
 // plane) for every filter, 8 filters at a time: per k two 16-byte broadcast loads of weights and
 // 8 * DIRECT_PPT FMAs. KT > 0 fixes the reduction length at compile time (the common first layers:
 // 3x3x3 = 27, 1x5x5 = 25), which keeps the k loop free of per-iteration guards.
-template <int KT>  // KT > 0: the reduction length as a compile-time constant (0: runtime, <= DIRECT_KMAX)
+// PPT: output pixels per thread (4 for large images; 1 when that would leave the GPU short of blocks).
+template <int KT, int PPT>  // KT > 0: the reduction length as a compile-time constant (0: runtime, <= DIRECT_KMAX)
 __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams p, int segs) {
+    constexpr int DIRECT_PPT = PPT, SEG = PPT * DIRECT_THREADS;
     extern __shared__ __align__(16) float dsm[];
     float* wsm = dsm;                                   // [k][f] (DIRECT_FMAX per k)
     float* xs = dsm + DIRECT_KMAX * DIRECT_FMAX;        // [c * KH + r][cols]
     __shared__ int ktab[DIRECT_KMAX];                   // per k: offset in xs of the tap
     const int K = KT > 0 ? KT : p.C * p.KH * p.KW;
     const int F8 = (p.F + 7) & ~7;
-    const int cols = direct_cols(p.SX, p.KW, p.DX);
+    const int cols = direct_cols(p.SX, p.KW, p.DX, SEG);
     const int seg = blockIdx.x % segs;
     const int oy = (blockIdx.x / segs) % p.OH;
     const long long b = blockIdx.x / ((long long)segs * p.OH);
-    const int ox0 = seg * DIRECT_SEG;
+    const int ox0 = seg * SEG;
     for (int i = threadIdx.x; i < K * F8; i += blockDim.x) {
         const int k = i / F8, f = i - k * F8;
         wsm[k * DIRECT_FMAX + f] = f < p.F ? p.w[(long long)k * p.Mpad + f] : 0.0f;
@@ -99,6 +100,13 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
             if (f < p.F) {
                 float* yf = yrow + (long long)f * p.OHW;
                 const float bias = p.bias ? __ldg(p.bias + f) : 0.0f;
+                // unfused batchnorm (TBaseLayer.batchNorm, as conv_bn): the filter's constants once
+                float mean = 0.f, sd = 1.f, sc = 1.f;
+                if (p.bn_mean) {
+                    mean = __ldg(p.bn_mean + f);
+                    sd = fmaxf((float)sqrt((double)__ldg(p.bn_var + f)), 0.000001f);
+                    sc = p.bn_scale ? __ldg(p.bn_scale + f) : 1.0f;
+                }
 #pragma unroll
                 for (int q = 0; q < DIRECT_PPT; ++q) {
                     if (q < nq) {
@@ -106,6 +114,9 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
                         if (simple) {  // bias, then leaky or linear (the common first layer)
                             if (p.bias) o = __fadd_rn(o, bias);
                             if (p.act == TB_ACT_LEAKY && o < 0.f) o = __fmul_rn(o, 0.1f);
+                        } else if (p.bn_mean) {  // normalize, forwardScale, forwardBias, activation
+                            o = __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(o, mean), sd), sc), bias);
+                            if (p.act != TB_ACT_LINEAR) o = tb_activate_dev(o, p.act);
                         } else {
                             o = conv_epilogue(o, f, p);
                         }
@@ -120,7 +131,7 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
 }  // namespace
 
 static int64_t direct_smem(const ConvGeom& g) {
-    return (int64_t)(DIRECT_KMAX * DIRECT_FMAX + g.C * g.KH * direct_cols((int)g.SX, (int)g.KW, (int)g.DX)) * 4;
+    return (int64_t)(DIRECT_KMAX * DIRECT_FMAX + g.C * g.KH * direct_cols((int)g.SX, (int)g.KW, (int)g.DX, DIRECT_SEG)) * 4;
 }
 
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes) {
@@ -144,20 +155,33 @@ int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
     p.act = act;
     const long long npix = g.B * g.OH * g.OW;
     (void)npix;
-    const int segs = (int)ceil_div(g.OW, DIRECT_SEG);
+    // four pixels per thread while that still gives every SM a few blocks, else one
+    const bool wide = g.B * g.OH * ceil_div(g.OW, DIRECT_SEG) >= 4 * (int64_t)ctx->sm_count;
+    const int seg = wide ? DIRECT_SEG : DIRECT_THREADS;
+    const int segs = (int)ceil_div(g.OW, seg);
     const int64_t blocks = g.B * g.OH * segs;
-    const int64_t smem = direct_smem(g);
-    static bool attr = false;
-    if (!attr) {
-        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
-        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<27>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
-        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<25>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
-        attr = true;
+    const int64_t smem = (int64_t)(DIRECT_KMAX * DIRECT_FMAX + g.C * g.KH * direct_cols((int)g.SX, (int)g.KW, (int)g.DX, seg)) * 4;
+    static bool attr[64] = {false};
+    if (ctx->device < 64 && !attr[ctx->device]) {
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<0, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<27, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<25, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<27, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_direct<25, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, DIRECT_SMEM_MAX));
+        attr[ctx->device] = true;
     }
     const int64_t K = g.C * g.KH * g.KW;
-    if (K == 27) k_conv_direct<27><<<(unsigned)blocks, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-    else if (K == 25) k_conv_direct<25><<<(unsigned)blocks, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-    else k_conv_direct<0><<<(unsigned)blocks, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+    const unsigned nb = (unsigned)blocks;
+    if (wide) {
+        if (K == 27) k_conv_direct<27, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+        else if (K == 25) k_conv_direct<25, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+        else k_conv_direct<0, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+    } else {
+        if (K == 27) k_conv_direct<27, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+        else if (K == 25) k_conv_direct<25, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+        else k_conv_direct<0, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
+    }
     if (launches) ++*launches;
     return check_launch("k_conv_direct");
 }

@@ -38,9 +38,13 @@ int exact_mode_of(const ConvGeom& g, const float* x) {
 // 128 pixels, 3x3 and vectorised 1x1 modes
 constexpr int kWsBase = 100;
 bool ws_mode(int mode, bool fma) { return fma && (mode == EX_3X3 || mode == EX_1X1V); }
+// configurations 110 / 111: 32 outputs per thread, 64 x 64 (8 x 4) and 64 x 128 (4 x 8)
+constexpr int kSmallBase = 110;
 
 // tile index t of kTiles plus a stage-depth variant (ExactShape) in t / kNumTiles
 int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool fma) {
+    if (t == kSmallBase) return exact_launch_64x64n4(ctx, p, grid, mode, fma, 0);
+    if (t == kSmallBase + 1) return exact_launch_64x128m4(ctx, p, grid, mode, fma, 0);
     if (t >= kWsBase) return exact_ws_launch(ctx, p, grid, mode, t == kWsBase ? 64 : 128);
     const int var = t / kNumTiles;
     switch (t % kNumTiles) {
@@ -52,9 +56,21 @@ int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool 
     }
 }
 
-int tile_bm(int t) { return t >= kWsBase ? 128 : kTiles[t % kNumTiles].BM; }
-int tile_bn(int t) { return t >= kWsBase ? (t == kWsBase ? 64 : 128) : kTiles[t % kNumTiles].BN; }
-int tile_nt(int t) { return t >= kWsBase ? (t == kWsBase ? 128 : 256) : kTiles[t % kNumTiles].NT; }
+int tile_bm(int t) {
+    if (t == kSmallBase) return 64;
+    if (t == kSmallBase + 1) return 64;
+    return t >= kWsBase ? 128 : kTiles[t % kNumTiles].BM;
+}
+int tile_bn(int t) {
+    if (t == kSmallBase) return 64;
+    if (t == kSmallBase + 1) return 128;
+    return t >= kWsBase ? (t == kWsBase ? 64 : 128) : kTiles[t % kNumTiles].BN;
+}
+int tile_nt(int t) {
+    if (t == kSmallBase) return 128;
+    if (t == kSmallBase + 1) return 256;
+    return t >= kWsBase ? (t == kWsBase ? 128 : 256) : kTiles[t % kNumTiles].NT;
+}
 
 bool tile_admissible(int t, int64_t M) {
     const int BM = tile_bm(t);
@@ -95,6 +111,7 @@ int choose_tile(tb_ctx* ctx, const ConvGeom& g, int mode, bool fma) {
     if (const char* f = getenv("TB_EXACT_FORCE")) {
         int t = atoi(f);
         if (t >= kWsBase && t <= kWsBase + 1 && ws_mode(mode, fma) && tile_admissible(t, g.F)) return t;
+        if (t >= kSmallBase && t <= kSmallBase + 1 && tile_admissible(t, g.F)) return t;
         if (t >= 0 && t < num_configs(mode, fma) && tile_admissible(t, g.F)) return t;
         if (t >= 0 && tile_admissible(t % kNumTiles, g.F)) return t % kNumTiles;
     }
@@ -183,6 +200,8 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
     std::vector<int> cfgs;
     for (int t = 0; t < num_configs(mode, fma); ++t) cfgs.push_back(t);
     if (ws_mode(mode, fma)) cfgs.push_back(kWsBase), cfgs.push_back(kWsBase + 1);
+    cfgs.push_back(kSmallBase);
+    cfgs.push_back(kSmallBase + 1);
     for (int t : cfgs) {
         if (rc != TB_OK) break;
         if (!tile_admissible(t, g.F)) continue;
@@ -199,7 +218,7 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
         if (getenv("TB_AUTOTUNE_VERBOSE"))
             fprintf(stderr, "exact autotune C%lld H%lld F%lld k%lld s%lld B%lld: tile %dx%d var %d mode %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY, (long long)g.B,
-                    tile_bm(t), tile_bn(t), t >= kWsBase ? 9 : t / kNumTiles, mode, ms / 3);
+                    tile_bm(t), tile_bn(t), t >= kWsBase ? t : t / kNumTiles, mode, ms / 3);
         if (ms < best_ms) { best_ms = ms; best = t; }
     }
     cudaEventDestroy(e0);

@@ -335,6 +335,9 @@ int exact_launch_64x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, b
 int exact_launch_128x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
 int exact_launch_64x64(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
 int exact_launch_32x128(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+// 32 outputs per thread (conv_exact_small.cu)
+int exact_launch_64x64n4(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
+int exact_launch_64x128m4(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
 // warp-specialised variant (conv_exact_ws.cu): 128 filters x bn (64 or 128) pixels per CTA
 int exact_ws_launch(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, int bn);
 

@@ -62,7 +62,7 @@ def test_conv_bit_exact(ctx, B, C, H, F, k, s, p, dil):
         assert_bit_exact(y, ref, B * F, (B, C, H, F, k, s, act))
 
 
-@pytest.mark.parametrize("tile", [0, 1, 2, 3, 4, 5, 10, 15, 17, 100, 101])
+@pytest.mark.parametrize("tile", [0, 1, 2, 3, 4, 5, 10, 15, 17, 100, 101, 110, 111])
 def test_every_exact_tile(ctx, tile, monkeypatch):
     """Each configuration of the order-exact kernel (TB_EXACT_FORCE pins it: tile = index % 5,
     stage-depth variant = index / 5, 100 / 101 the warp-specialised kernel with 64 / 128 pixels;
