@@ -618,7 +618,8 @@ int tb_diag_conv_tc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, c
                            double* out12);
 /* The same counters for one launch of the NHWC tensor-core conv (tb_conv2d_fwd_nhwc's kernel;
  * entry 8 = epilogue cycles in TMEM loads or split-K partial sums, entry 9 = all per-tile
- * epilogue work, entry 10 = 0). Blocks. */
+ * epilogue work, entry 10 = the launch's span from the first CTA's start to the last CTA's end
+ * and entry 11 = the longest CTA, both in ns of the GPU's global timer). Blocks. */
 int tb_diag_conv_nhwc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x, int64_t x_pixel_stride,
                              const float* packed_w, float* y, int64_t y_pixel_stride, double* out12);
 

@@ -78,6 +78,20 @@ bool act_supported(int64_t a) {
     }
 }
 
+__global__ void k_stream_delay(unsigned long long ns) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int i = 0; i < (1 << 20); ++i) {  // bounded: ends after ns or ~1M polls, whichever first
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 >= ns) break;
+        __nanosleep(1000);
+    }
+}
+
+void stream_delay_us(tb_ctx* ctx, int us) {
+    k_stream_delay<<<1, 1, 0, ctx->stream>>>((unsigned long long)us * 1000ull);
+}
+
 }  // namespace tbi
 
 using namespace tbi;

@@ -7,6 +7,7 @@
 #include <string>
 #include <cstdio>
 #include <cstdarg>
+#include <utility>
 
 #include "../../include/tensorium_b200.h"
 
@@ -23,6 +24,8 @@ struct tb_ctx {
     cudaEvent_t fork = nullptr, join = nullptr;  // order own_stream work with `stream`
     int* tile_cnt = nullptr;                      // split-K arrival counters (zeroed, self-resetting)
     int64_t tile_cnt_len = 0;
+    int pdl = 0;  // launches through tbi::launch may overlap the previous kernel's tail (set while
+                  // a network forward is captured)
 };
 
 namespace tbi {
@@ -36,6 +39,41 @@ int enter(tb_ctx* ctx);
 int ensure_workspace(tb_ctx* ctx, size_t bytes);
 // Check the last launch.
 int check_launch(const char* what);
+// Keep the stream busy for about `us` microseconds (a bounded sleep on the GPU timer), so that the
+// launches a timing loop enqueues behind it start back to back: autotuners time device work, not
+// the host's launch overhead.
+void stream_delay_us(tb_ctx* ctx, int us);
+
+// Programmatic dependent launch. A kernel launched through `launch` while ctx->pdl is set may
+// start while the previous kernel on the stream is still running; it must execute
+// TB_GRID_DEP_ENTRY() before touching global memory that earlier kernels write or read: that waits
+// until every earlier kernel has completed and its writes are visible, then lets the next kernel
+// be scheduled. Outside such a launch the two instructions return at once.
+#define TB_GRID_DEP_ENTRY()                                                      \
+    do {                                                                         \
+        asm volatile("griddepcontrol.wait;\n" ::: "memory");                     \
+        asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");        \
+    } while (0)
+
+template <typename... KArgs, typename... Args>
+int launch(tb_ctx* ctx, const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    if (ctx->pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return check_launch(what);
+}
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }

@@ -33,6 +33,7 @@ __host__ __device__ inline int direct_cols(int SX, int KW, int DX, int seg) { re
 // PPT: output pixels per thread (4 for large images; 1 when that would leave the GPU short of blocks).
 template <int KT, int PPT>  // KT > 0: the reduction length as a compile-time constant (0: runtime, <= DIRECT_KMAX)
 __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams p, int segs) {
+    TB_GRID_DEP_ENTRY();
     constexpr int DIRECT_PPT = PPT, SEG = PPT * DIRECT_THREADS;
     extern __shared__ __align__(16) float dsm[];
     float* wsm = dsm;                                   // [k][f] (DIRECT_FMAX per k)
@@ -173,15 +174,10 @@ int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
     }
     const int64_t K = g.C * g.KH * g.KW;
     const unsigned nb = (unsigned)blocks;
-    if (wide) {
-        if (K == 27) k_conv_direct<27, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-        else if (K == 25) k_conv_direct<25, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-        else k_conv_direct<0, 4><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-    } else {
-        if (K == 27) k_conv_direct<27, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-        else if (K == 25) k_conv_direct<25, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-        else k_conv_direct<0, 1><<<nb, DIRECT_THREADS, (size_t)smem, ctx->stream>>>(p, segs);
-    }
+    auto kern = wide ? (K == 27 ? k_conv_direct<27, 4> : K == 25 ? k_conv_direct<25, 4> : k_conv_direct<0, 4>)
+                     : (K == 27 ? k_conv_direct<27, 1> : K == 25 ? k_conv_direct<25, 1> : k_conv_direct<0, 1>);
+    const int lr = launch(ctx, "k_conv_direct", kern, dim3(nb), dim3(DIRECT_THREADS), (size_t)smem, p, segs);
+    if (lr != TB_OK) return lr;
     if (launches) ++*launches;
     return check_launch("k_conv_direct");
 }

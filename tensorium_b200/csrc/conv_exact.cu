@@ -207,6 +207,7 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
         if (!tile_admissible(t, g.F)) continue;
         rc = launch_tile(ctx, t, g, p, mode, fma);  // warm-up
         if (rc != TB_OK) break;
+        stream_delay_us(ctx, 200);  // the timed launches queue behind it: device time only
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && rc == TB_OK; ++rep) rc = launch_tile(ctx, t, g, p, mode, fma);
         cudaEventRecord(e1, ctx->stream);

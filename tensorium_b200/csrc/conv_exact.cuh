@@ -66,6 +66,7 @@ k_conv_exact(const ConvParams p) {
     extern __shared__ __align__(16) float smem[];
     float* As = smem;                      // [STAGES][KSMAX][BM]
     float* Bs = smem + STAGES * KSMAX * BM;  // [STAGES][KSMAX][BN]
+    TB_GRID_DEP_ENTRY();
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
@@ -304,8 +305,7 @@ int exact_launch_one(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NT, smem) != cudaSuccess || n < 1) n = 1;
         return n;
     }
-    kern<<<grid, NT, smem, ctx->stream>>>(p);
-    return check_launch("k_conv_exact");
+    return launch(ctx, "k_conv_exact", kern, grid, dim3(NT), (size_t)smem, p);
 }
 
 // var: stage-depth variant (ExactShape) of the 3x3 and vectorised 1x1 modes

@@ -63,6 +63,7 @@ k_conv_exact_ws(const ConvParams p, int* status) {
     float* Bs = smem + S * KS * BM;  // [S][KS][BN]
     __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
     __shared__ volatile int abort_flag;
+    TB_GRID_DEP_ENTRY();
 
     const int tid = threadIdx.x;
     const int m0 = blockIdx.y * BM;
@@ -251,8 +252,7 @@ int ws_launch_one(tb_ctx* ctx, const ConvParams& p, dim3 grid) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, NT, smem) != cudaSuccess || n < 1) n = 1;
         return n;
     }
-    kern<<<grid, NT, smem, ctx->stream>>>(p, ctx->d_status);
-    return check_launch("k_conv_exact_ws");
+    return launch(ctx, "k_conv_exact_ws", kern, grid, dim3(NT), (size_t)smem, p, ctx->d_status);
 }
 
 }  // namespace

@@ -341,6 +341,7 @@ int conv_fp32_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const flo
             }
             break;
         }
+        stream_delay_us(ctx, 200);  // the timed launches queue behind it: device time only
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && rc == TB_OK; ++rep)
             rc = launch_with(ctx, g, t, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR,

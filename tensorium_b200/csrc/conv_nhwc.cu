@@ -50,8 +50,11 @@ struct NhwcParams {
     int OW, OHW, SX, SY, PX, PY, KW, DX, DY;
     int F, csteps, ktiles;
     int tiles_n, tiles_total;
-    int splits, kt_per_split, units;  // split-K: unit w = k range w % splits of tile w / splits
-    float* part;                      // split-K partial tiles [unit][128 pixels][BN]
+    // Work units: tiles 0 .. dp_tiles - 1 whole (unit w = tile w), then each remaining tile as
+    // `splits` K ranges of kt_per_split k tiles (unit dp_tiles + q: tile dp_tiles + q / splits,
+    // range q % splits), so the last partial wave of tiles is spread over every SM.
+    int dp_tiles, splits, kt_per_split, units;
+    float* part;                      // split units' partial tiles [q][BN / 4][128 pixels][4 filters]
     int* tile_cnt;                    // split-K arrival counters, one per tile, left at 0
     int out_nchw;
     int y_ps, r_ps;                 // NHWC pixel strides (floats) of the output and residual
@@ -66,6 +69,18 @@ struct NhwcMaps {
     CUtensorMap b2; // pair mode: the (lo, lo) weight operand
     CUtensorMap y;  // NHWC output (filter, pixel), box 16 x 32, 64-byte swizzle (tma_out)
 };
+
+// unit w of a launch: its tile, k tile range and partial slot (-1: a whole tile, stored directly)
+struct NhUnit {
+    int t, kb, ke, slot;
+};
+
+__device__ __forceinline__ NhUnit nh_unit(const NhwcParams& p, int w) {
+    if (w < p.dp_tiles) return NhUnit{w, 0, p.ktiles, -1};
+    const int q = w - p.dp_tiles, tq = q / p.splits, z = q - tq * p.splits;
+    const int kb = z * p.kt_per_split;
+    return NhUnit{p.dp_tiles + tq, kb, min(p.ktiles, kb + p.kt_per_split), q};
+}
 
 constexpr int NH_STG_BYTES = 8 * 2 * 32 * 64;  // per epilogue warp: two 32-pixel x 16-filter slabs
 
@@ -99,6 +114,23 @@ __device__ __forceinline__ void tma_load_im2col_4d(unsigned dst, const void* tma
         : "memory");
 }
 
+// the same for a CTA pair: the copy lands in this CTA's shared memory and its bytes are counted on
+// the mbarrier of the pair's even CTA
+template <int CTAS>
+__device__ __forceinline__ void tma_load_im2col_4d_g(unsigned dst, const void* tmap, uint64_t* bar, int c, int w,
+                                                     int h, int n, uint16_t ow, uint16_t oh) {
+    if constexpr (CTAS == 1) {
+        tma_load_im2col_4d(dst, tmap, bar, c, w, h, n, ow, oh);
+    } else {
+        asm volatile(
+            "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(tmap)), "r"(tc::tma_bar<2>(bar)), "r"(c), "r"(w), "r"(h), "r"(n), "h"(ow),
+            "h"(oh)
+            : "memory");
+    }
+}
+
 // shared -> global tensor store of one box, tracked as a bulk group of this thread
 __device__ __forceinline__ void tma_store_2d(const void* tmap, unsigned src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(
@@ -128,9 +160,17 @@ __device__ __forceinline__ float nh_act(float o, int f, const NhwcParams& p) {
 // im2col box is a K-major tile of 64 bf16 (32 channels x (hi, lo)); the weights come as two
 // operands (hi, hi) and (lo, lo), and per 32 channels 4 + 4 kind::f16 MMAs (K = 16) accumulate
 // hi*w_hi + lo*w_hi + hi*w_lo + lo*w_lo = (hi + lo) * (w_hi + w_lo) in FP32.
-template <int BN, int STAGES, bool PAIR>
+//
+// CTAS = 2: a cluster of two CTAs on two SMs computes a 256-pixel x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256). Each CTA loads its own 128 pixels of A and BN / 2 filters of
+// B (the MMA reads B half from each CTA's shared memory), so an SM receives 3/4 (BN = 256) of the
+// operand bytes per FLOP of a single-CTA tile; the even CTA's thread issues the MMAs and waits for
+// both CTAs' copies on its own barriers; each CTA's TMEM holds the accumulator rows of its pixels
+// and its epilogue warps store them. No split-K for pairs.
+template <int BN, int STAGES, bool PAIR, int CTAS>
 __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_constant__ NhwcMaps maps, const NhwcParams p) {
-    constexpr int B_BYTES = BN * NH_BK * 4;
+    constexpr int BNC = BN / CTAS;  // filters of B held by this CTA
+    constexpr int B_BYTES = BNC * NH_BK * 4;
     constexpr int STAGE_BYTES = NH_A_BYTES + (PAIR ? 2 : 1) * B_BYTES;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024 - ((unsigned)__cvta_generic_to_shared(smem_raw) & 1023)) & 1023);
@@ -140,7 +180,10 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     __shared__ volatile int last_unit;  // split-K: this CTA's unit is the last of its tile
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (p.phases && tid == 0) p.phases[blockIdx.x * 12 + 10] = tc::global_ns();  // diagnostics: CTA start
     const unsigned sbase = (unsigned)__cvta_generic_to_shared(smem);
+    const int rank = CTAS == 2 ? (int)tc::cluster_rank() : 0;
+    const int t_first = blockIdx.x / CTAS, t_step = gridDim.x / CTAS;
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -149,7 +192,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull_bar[b], 1);
-            tc::mbar_init(&tempty_bar[b], 8);  // one arrival per epilogue warp
+            tc::mbar_init(&tempty_bar[b], 8 * CTAS);  // one arrival per epilogue warp (of the pair)
         }
         tc::mbar_init(&drain_bar, 1);
         abort_flag = 0;
@@ -157,11 +200,13 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
         asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
     }
-    if (warp == 1) tc::tmem_alloc(&tmem_base, 2 * BN);
+    if (warp == 1) tc::tmem_alloc_g<CTAS>(&tmem_base, 2 * BN);
     tc::tc_fence_before();
     __syncthreads();
+    if (CTAS == 2) tc::cluster_sync();  // the peer's barriers exist before anything signals them
     tc::tc_fence_after();
     const uint32_t tmem0 = tmem_base;
+    TB_GRID_DEP_ENTRY();  // set-up above overlaps the previous kernel's tail; activations only after it
 
     if (warp == 0) {
         if (lane == 0) {
@@ -170,11 +215,11 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             bool ok = true;
             const long long c_start = clock64();
             long long c_wait = 0;
-            for (int w = blockIdx.x; ok && w < p.units; w += gridDim.x) {
-                const int t = w / p.splits, z = w - t * p.splits;
-                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
+            for (int w = t_first; ok && w < p.units; w += t_step) {
+                const NhUnit un = nh_unit(p, w);
+                const int t = un.t, kb = un.kb, ke = un.ke;
                 const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
-                const long long m0 = (long long)mt * NH_BM;
+                const long long m0 = (long long)mt * (NH_BM * CTAS) + rank * NH_BM;
                 const int n0 = (int)(m0 / p.OHW);
                 const int q = (int)(m0 - (long long)n0 * p.OHW);
                 const int oy = q / p.OW, ox = q - oy * p.OW;
@@ -189,12 +234,13 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                         break;
                     }
                     c_wait += clock64() - c0w;
-                    tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES);
+                    if (rank == 0) tc::mbar_arrive_expect_tx(&full_bar[st], STAGE_BYTES * CTAS);
                     const unsigned sa = sbase + st * STAGE_BYTES, sb = sa + NH_A_BYTES;
-                    tma_load_im2col_4d(sa, &maps.a, &full_bar[st], c0 * NH_BK, w0, h0, n0, (uint16_t)(s * p.DX),
-                                       (uint16_t)(r * p.DY));
-                    tc::tma_load_2d(sb, &maps.b, &full_bar[st], kt * NH_BK, nt * BN);
-                    if (PAIR) tc::tma_load_2d(sb + B_BYTES, &maps.b2, &full_bar[st], kt * NH_BK, nt * BN);
+                    tma_load_im2col_4d_g<CTAS>(sa, &maps.a, &full_bar[st], c0 * NH_BK, w0, h0, n0,
+                                               (uint16_t)(s * p.DX), (uint16_t)(r * p.DY));
+                    tc::tma_load_2d_g<CTAS>(sb, &maps.b, &full_bar[st], kt * NH_BK, nt * BN + rank * BNC);
+                    if (PAIR)
+                        tc::tma_load_2d_g<CTAS>(sb + B_BYTES, &maps.b2, &full_bar[st], kt * NH_BK, nt * BN + rank * BNC);
                     if (++c0 == p.csteps) {  // next 32-channel step, then the next tap
                         c0 = 0;
                         if (++s == p.KW) s = 0, ++r;
@@ -205,22 +251,24 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                 p.phases[blockIdx.x * 12 + 0] = clock64() - c_start;
                 p.phases[blockIdx.x * 12 + 1] = c_wait;
             }
-            if (!ok) {  // let the copies already issued land before the CTA exits
+            // an abort: let the copies already issued land before the CTA exits (a pair's odd CTA
+            // cannot see its copies complete: they are counted on the even CTA's barriers)
+            if (!ok && rank == 0) {
                 for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
                     tc::mbar_wait_limit(&full_bar[j % STAGES], (j / STAGES) & 1);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = PAIR ? idesc_bf16_k(NH_BM, BN) : idesc_tf32_k(NH_BM, BN);
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (the pair's even CTA) ----------------
+            constexpr uint32_t idesc = PAIR ? idesc_bf16_k(NH_BM * CTAS, BN) : idesc_tf32_k(NH_BM * CTAS, BN);
             int it = 0, tl = 0;
             bool ok = true, issued = false;
             const long long c_start = clock64();
             long long c_wf = 0, c_we = 0;
-            for (int w = blockIdx.x; ok && w < p.units; w += gridDim.x, ++tl) {
-                const int z = w % p.splits;
-                const int kb = z * p.kt_per_split, ke = min(p.ktiles, kb + p.kt_per_split);
+            for (int w = t_first; ok && w < p.units; w += t_step, ++tl) {
+                const NhUnit un = nh_unit(p, w);
+                const int kb = un.kb, ke = un.ke;
                 const int buf = tl & 1, u = tl >> 1;
                 long long c0w = clock64();
                 if (u > 0 && !tc::mbar_wait_bounded(&tempty_bar[buf], (u - 1) & 1, &abort_flag, p.status, 922)) break;
@@ -240,22 +288,22 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     if (PAIR) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            tc::mma_bf16(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
-                                         (kt != kb || kk) ? 1u : 0u);
+                            tc::mma_bf16_g<CTAS>(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32),
+                                                 idesc, (kt != kb || kk) ? 1u : 0u);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            tc::mma_bf16(d, smem_desc_k_sw128(sa + kk * 32),
-                                         smem_desc_k_sw128(sb + B_BYTES + kk * 32), idesc, 1u);
+                            tc::mma_bf16_g<CTAS>(d, smem_desc_k_sw128(sa + kk * 32),
+                                                 smem_desc_k_sw128(sb + B_BYTES + kk * 32), idesc, 1u);
                     } else {
 #pragma unroll
                         for (int kk = 0; kk < NH_BK / 8; ++kk)
-                            tc::mma_tf32(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32), idesc,
-                                         (kt != kb || kk) ? 1u : 0u);
+                            tc::mma_tf32_g<CTAS>(d, smem_desc_k_sw128(sa + kk * 32), smem_desc_k_sw128(sb + kk * 32),
+                                                 idesc, (kt != kb || kk) ? 1u : 0u);
                     }
                     issued = true;
-                    tc::mma_commit(&empty_bar[st]);
+                    tc::mma_commit_g<CTAS>(&empty_bar[st]);
                 }
-                if (ok) tc::mma_commit(&tfull_bar[buf]);
+                if (ok) tc::mma_commit_g<CTAS>(&tfull_bar[buf]);
             }
             if (p.phases) {
                 p.phases[blockIdx.x * 12 + 2] = clock64() - c_start;
@@ -263,7 +311,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                 p.phases[blockIdx.x * 12 + 4] = c_we;
             }
             if (issued) {  // every MMA has finished before TMEM is freed
-                tc::mma_commit(&drain_bar);
+                tc::mma_commit_g<CTAS>(&drain_bar);
                 tc::mbar_wait_limit(&drain_bar, 0);
             }
         }
@@ -285,18 +333,20 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
         int tl = 0;
         const long long c_start = clock64();
         long long c_wt = 0, c_st = 0, c_ldw = 0;
-        for (int w = blockIdx.x; w < p.units; w += gridDim.x, ++tl) {
-            const int t = w / p.splits;
+        for (int w = t_first; w < p.units; w += t_step, ++tl) {
+            const NhUnit un = nh_unit(p, w);
+            const int t = un.t;
             const int buf = tl & 1, u = tl >> 1;
             const long long c0w = clock64();
             const bool ok = !abort_flag && tc::mbar_wait_bounded(&tfull_bar[buf], u & 1, &abort_flag, p.status, 924);
             c_wt += clock64() - c0w;
             if (tc::epi_any(!ok)) break;  // tcgen05.ld is warp-collective: all epilogue warps leave together
             tc::tc_fence_after();
-            const bool from_tmem = p.splits == 1;
+            const bool from_tmem = un.slot < 0;
             if (!from_tmem) {
-                // split-K: this unit's raw accumulator rows -> its partial tile, then free TMEM
-                float* prow = p.part + ((size_t)w * NH_BM + quarter * 32 + lane) * BN;
+                // split unit: its raw accumulator -> its partial tile in groups of 4 filters (a warp's
+                // 32 lanes write 32 consecutive pixels' float4s: 512-byte stores), then free TMEM
+                float4* prow = reinterpret_cast<float4*>(p.part + (size_t)un.slot * NH_BM * BN) + quarter * 32 + lane;
                 const uint32_t ta = tmem0 + buf * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
                 for (int sl = half; sl < BN / 16; sl += 2) {
@@ -305,13 +355,13 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     tc::tmem_wait16(pr);
 #pragma unroll
                     for (int i = 0; i < 16; i += 4)
-                        __stcg(reinterpret_cast<float4*>(prow + sl * 16 + i),
+                        __stcg(prow + (size_t)((sl * 16 + i) >> 2) * NH_BM,
                                make_float4(__uint_as_float(pr[i]), __uint_as_float(pr[i + 1]),
                                            __uint_as_float(pr[i + 2]), __uint_as_float(pr[i + 3])));
                 }
                 tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);
+                if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);  // single CTAs only: pairs never split
                 // the last unit of the tile to arrive sums the partials in split order
                 __threadfence();
                 tc::epi_sync();
@@ -325,7 +375,8 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                 __threadfence();
             }
             const int mt = t / p.tiles_n, nt = t - mt * p.tiles_n;
-            const long long m = (long long)mt * NH_BM + quarter * 32 + lane;  // this lane's pixel
+            const long long mrow = (long long)mt * (NH_BM * CTAS) + rank * NH_BM + quarter * 32;  // this warp's pixels
+            const long long m = mrow + lane;  // this lane's pixel
             const bool valid = m < p.npix;
             const long long b = valid ? m / p.OHW : 0;
             const int q = valid ? (int)(m - b * p.OHW) : 0;
@@ -408,7 +459,7 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     }
                     tc::fence_proxy_async();
                     __syncwarp();
-                    if (lane == 0) tma_store_2d(&maps.y, slab, fb, (int)((long long)mt * NH_BM + quarter * 32));
+                    if (lane == 0) tma_store_2d(&maps.y, slab, fb, (int)mrow);
                     sbuf ^= 1;
                 } else if (valid) {
                     if (p.out_nchw) {
@@ -435,14 +486,21 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
                     return;
                 }
                 for (int i = 0; i < n; ++i) out[i] = 0.f;
-                const float* pb = p.part + ((size_t)t * p.splits * NH_BM + quarter * 32 + lane) * BN + c0;
+                const int slot0 = un.slot - un.slot % p.splits;  // the tile's first split
+                const float4* pb = reinterpret_cast<const float4*>(p.part + (size_t)slot0 * NH_BM * BN) +
+                                   (size_t)(c0 >> 2) * NH_BM + quarter * 32 + lane;
                 for (int zz = 0; zz < p.splits; ++zz) {
-                    for (int i = 0; i < n; i += 4) {
-                        const float4 q4 = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)zz * NH_BM * BN + i));
-                        out[i] = __fadd_rn(out[i], q4.x);
-                        out[i + 1] = __fadd_rn(out[i + 1], q4.y);
-                        out[i + 2] = __fadd_rn(out[i + 2], q4.z);
-                        out[i + 3] = __fadd_rn(out[i + 3], q4.w);
+                    float4 q4[8];  // every load of this split in flight before the adds
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (j < n / 4) q4[j] = __ldcg(pb + (size_t)zz * (NH_BM * BN / 4) + (size_t)j * NH_BM);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (j >= n / 4) break;
+                        out[4 * j] = __fadd_rn(out[4 * j], q4[j].x);
+                        out[4 * j + 1] = __fadd_rn(out[4 * j + 1], q4[j].y);
+                        out[4 * j + 2] = __fadd_rn(out[4 * j + 2], q4[j].z);
+                        out[4 * j + 3] = __fadd_rn(out[4 * j + 3], q4[j].w);
                     }
                 }
             };
@@ -467,7 +525,10 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
             if (!from_tmem) continue;  // the accumulator was released after the partial was written
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&tempty_bar[buf]);  // this warp's TMEM reads are done
+            if (lane == 0) {  // this warp's TMEM reads are done
+                if (CTAS == 1) tc::mbar_arrive(&tempty_bar[buf]);
+                else tc::mbar_arrive_cluster(&tempty_bar[buf], 0);
+            }
         }
         if (lane == 0) bulk_wait_read<0>();  // the shared-memory slabs are read before the CTA exits
         if (p.phases && warp == 2 && lane == 0) {
@@ -480,10 +541,12 @@ __global__ void __launch_bounds__(NH_THREADS, 1) k_conv_nhwc(const __grid_consta
     }
     tc::tc_fence_before();
     __syncthreads();
+    if (CTAS == 2) tc::cluster_sync();  // the pair's MMAs and its tempty arrivals are over
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem0, 2 * BN);
+        tc::tmem_dealloc_g<CTAS>(tmem0, 2 * BN);
     }
+    if (p.phases && tid == 0) p.phases[blockIdx.x * 12 + 11] = tc::global_ns();  // CTA end
 }
 
 // packed weights for the NHWC kernel: wp[f][(r * KW + s) * Cp + c] = tf32(w[f][c][r][s]), zero for c >= C;
@@ -520,20 +583,49 @@ PFN_cuTensorMapEncodeIm2col_v12000 im2col_encoder() {
     return fn;
 }
 
-template <int BN, int STAGES, bool PAIR>
-constexpr int nh_smem() { return STAGES * (NH_A_BYTES + (PAIR ? 2 : 1) * BN * NH_BK * 4) + NH_STG_BYTES + 1024; }
+template <int BN, int STAGES, bool PAIR, int CTAS>
+constexpr int nh_smem() {
+    return STAGES * (NH_A_BYTES + (PAIR ? 2 : 1) * (BN / CTAS) * NH_BK * 4) + NH_STG_BYTES + 1024;
+}
 
-template <int BN, int STAGES, bool PAIR>
+template <int BN, int STAGES, bool PAIR, int CTAS>
 int nh_launch(tb_ctx* ctx, const NhwcMaps& maps, const NhwcParams& p) {
-    constexpr int smem = nh_smem<BN, STAGES, PAIR>();
+    constexpr int smem = nh_smem<BN, STAGES, PAIR, CTAS>();
     static_assert(smem <= 232448, "shared memory per CTA");
-    static bool attr = false;
-    if (!attr) {
-        TB_CHECK_CUDA(cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr = true;
+    static std::mutex mu;
+    static bool done[64] = {false};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (ctx->device >= 64 || !done[ctx->device]) {  // the attribute is set per device
+            cudaError_t e = cudaFuncSetAttribute(k_conv_nhwc<BN, STAGES, PAIR, CTAS>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv_nhwc)");
+            if (ctx->device < 64) done[ctx->device] = true;
+        }
     }
-    const int grid = std::min(p.units, ctx->sm_count);
-    k_conv_nhwc<BN, STAGES, PAIR><<<grid, NH_THREADS, smem, ctx->stream>>>(maps, p);
+    const int slots = CTAS == 1 ? ctx->sm_count : (ctx->sm_count & ~1);
+    const int grid = (int)std::min<int64_t>((int64_t)p.units * CTAS, slots);
+    if constexpr (CTAS == 1) {
+        return launch(ctx, "k_conv_nhwc", k_conv_nhwc<BN, STAGES, PAIR, 1>, dim3((unsigned)grid), dim3(NH_THREADS),
+                      (size_t)smem, maps, p);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(NH_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = ctx->pdl ? 2 : 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, k_conv_nhwc<BN, STAGES, PAIR, CTAS>, maps, p);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(conv_nhwc pair)");
+    }
     return check_launch("k_conv_nhwc");
 }
 
@@ -559,9 +651,10 @@ int conv_nhwc_pack(tb_ctx* ctx, const ConvGeom& g, const float* w, float* wp, in
     return check_launch("k_pack_nhwc");
 }
 
-// Tile shape of one NHWC conv launch: filters per tile and K splits.
+// Tile shape of one NHWC conv launch: filters per tile, K splits, CTAs per tile (2: a cta_group::2
+// pair on 256 pixels, never split).
 struct NhShape {
-    int bn, splits;
+    int bn, splits, ctas;
 };
 
 std::mutex g_nh_mu;
@@ -575,23 +668,31 @@ std::vector<int64_t> nh_key(int device, const ConvGeom& g, int64_t x_ps, int pai
 int64_t nh_ktiles(const ConvGeom& g) { return g.KH * g.KW * (round_up(g.C, 32) / NH_BK); }
 
 // split-K partial tiles of a shape (floats)
-int64_t nh_part_floats(const ConvGeom& g, const NhShape& sh) {
+// tiles stored whole: every full wave over the SMs (the rest are split), all when not split
+int64_t nh_dp_tiles(int64_t tiles, const NhShape& sh, int sms) {
+    return sh.splits <= 1 ? tiles : (tiles / sms) * sms;
+}
+
+int64_t nh_part_floats(const ConvGeom& g, const NhShape& sh, int sms) {
     if (sh.splits <= 1) return 0;
     const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, sh.bn);
-    return tiles * sh.splits * NH_BM * sh.bn;
+    return (tiles - nh_dp_tiles(tiles, sh, sms)) * sh.splits * NH_BM * sh.bn;
 }
 
 constexpr int64_t NH_PART_CAP = (int64_t)1 << 26;  // 256 MiB of partial tiles at most
 
 // default shape: the widest tile that does not leave most of it empty, no split
-NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : g.F > 32 ? 64 : 32, 1}; }
+NhShape nh_default(const ConvGeom& g) { return NhShape{g.F > 128 ? 256 : g.F > 64 ? 128 : g.F > 32 ? 64 : 32, 1, 1}; }
 
 NhShape nh_choose(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps, int pair) {
     if (t_nh_pin) return *t_nh_pin;
-    if (const char* f = getenv("TB_NHWC_FORCE")) {  // test hook: "BN,SPLITS"
-        NhShape sh{256, 1};
-        if (sscanf(f, "%d,%d", &sh.bn, &sh.splits) >= 1 && (sh.bn == 32 || sh.bn == 64 || sh.bn == 128 || sh.bn == 256)) {
+    if (const char* f = getenv("TB_NHWC_FORCE")) {  // test hook: "BN,SPLITS[,CTAS]"
+        NhShape sh{256, 1, 1};
+        if (sscanf(f, "%d,%d,%d", &sh.bn, &sh.splits, &sh.ctas) >= 1 &&
+            (sh.bn == 32 || sh.bn == 64 || sh.bn == 128 || sh.bn == 256)) {
             if (sh.splits < 1) sh.splits = 1;
+            if (sh.ctas != 2 || sh.bn < 128) sh.ctas = 1;
+            if (sh.ctas == 2) sh.splits = 1;
             return sh;
         }
     }
@@ -627,19 +728,21 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
         if (r != CUDA_SUCCESS) return fail(TB_ERR_CUDA, "NHWC conv: cuTensorMapEncodeIm2col failed (%d)", (int)r);
     }
     NhShape sh = nh_choose(ctx, g, x_ps, pair);
-    const int bn = sh.bn;
+    const int bn = sh.bn, ctas = sh.ctas == 2 ? 2 : 1;
+    if (ctas == 2) sh.splits = 1;
     const int64_t ktiles = nh_ktiles(g);
     const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
     if (sh.splits > ktiles) sh.splits = (int)ktiles;
     const int kps = (int)ceil_div(ktiles, sh.splits);
     sh.splits = (int)ceil_div(ktiles, kps);  // no empty split
-    if (sh.splits > 1 && (tiles > ctx->tile_cnt_len || nh_part_floats(g, sh) > NH_PART_CAP ||
-                          (size_t)nh_part_floats(g, sh) * sizeof(float) > ctx->ws_bytes))
+    if (sh.splits > 1 && (tiles > ctx->tile_cnt_len || nh_part_floats(g, sh, ctx->sm_count) > NH_PART_CAP ||
+                          (size_t)nh_part_floats(g, sh, ctx->sm_count) * sizeof(float) > ctx->ws_bytes))
         sh.splits = 1;  // no room for the partial tiles or counters: one unit per tile
+    if (sh.splits > 1 && nh_dp_tiles(tiles, sh, ctx->sm_count) == tiles) sh.splits = 1;  // whole waves only
     {
         const uint64_t dims[2] = {(uint64_t)(g.KH * g.KW * Cp), (uint64_t)g.F};
         const uint64_t strides[1] = {(uint64_t)(g.KH * g.KW * Cp * 4)};
-        const uint32_t box[2] = {(uint32_t)NH_BK, (uint32_t)bn};
+        const uint32_t box[2] = {(uint32_t)NH_BK, (uint32_t)(bn / ctas)};  // a pair's CTA holds half the filters
         int r = encode_map(&maps.b, wp, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (r != TB_OK) return r;
         if (pair) {  // the (lo, lo) operand follows the (hi, hi) one
@@ -649,7 +752,8 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
         }
     }
     NhwcParams p{};
-    if (y_ps > 0 && y_ps % 4 == 0 && aligned16(y)) {
+    static const bool no_tma_store = getenv("TB_NHWC_NO_TMA_STORE") != nullptr;  // experiment hook
+    if (y_ps > 0 && y_ps % 4 == 0 && aligned16(y) && !no_tma_store) {
         const uint64_t dims[2] = {(uint64_t)g.F, (uint64_t)(g.B * g.OH * g.OW)};
         const uint64_t strides[1] = {(uint64_t)(y_ps * 4)};
         const uint32_t box[2] = {16, 32};
@@ -667,10 +771,11 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     p.csteps = (int)(Cp / NH_BK);
     p.ktiles = (int)(g.KH * g.KW * p.csteps);
     p.tiles_n = (int)ceil_div(g.F, bn);
-    p.tiles_total = (int)(ceil_div(p.npix, NH_BM) * p.tiles_n);
+    p.tiles_total = (int)(ceil_div(p.npix, (int64_t)NH_BM * ctas) * p.tiles_n);
     p.splits = sh.splits;
     p.kt_per_split = sh.splits > 1 ? (int)ceil_div(ktiles, sh.splits) : (int)ktiles;
-    p.units = p.tiles_total * p.splits;
+    p.dp_tiles = (int)nh_dp_tiles(p.tiles_total, sh, ctx->sm_count);
+    p.units = p.dp_tiles + (p.tiles_total - p.dp_tiles) * p.splits;
     p.part = sh.splits > 1 ? reinterpret_cast<float*>(ctx->ws) : nullptr;
     p.tile_cnt = ctx->tile_cnt;
     p.out_nchw = y_ps > 0 ? 0 : 1;
@@ -679,21 +784,25 @@ int conv_nhwc_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x_p
     p.vec = y_ps % 4 == 0 && aligned16(y) && (!res || (r_ps % 4 == 0 && aligned16(res))) ? 1 : 0;
     p.act = act;
     p.yolo_classes = yolo_classes;
-    if (pair) {
-        if (bn == 256) return nh_launch<256, 2, true>(ctx, maps, p);
-        if (bn == 128) return nh_launch<128, 4, true>(ctx, maps, p);
-        if (bn == 32) return nh_launch<32, 8, true>(ctx, maps, p);
-        return nh_launch<64, 6, true>(ctx, maps, p);
+    if (ctas == 2) {
+        if (pair) return bn == 256 ? nh_launch<256, 4, true, 2>(ctx, maps, p) : nh_launch<128, 6, true, 2>(ctx, maps, p);
+        return bn == 256 ? nh_launch<256, 6, false, 2>(ctx, maps, p) : nh_launch<128, 8, false, 2>(ctx, maps, p);
     }
-    if (bn == 256) return nh_launch<256, 4, false>(ctx, maps, p);
-    if (bn == 128) return nh_launch<128, 6, false>(ctx, maps, p);
-    if (bn == 32) return nh_launch<32, 8, false>(ctx, maps, p);
-    return nh_launch<64, 8, false>(ctx, maps, p);
+    if (pair) {
+        if (bn == 256) return nh_launch<256, 2, true, 1>(ctx, maps, p);
+        if (bn == 128) return nh_launch<128, 4, true, 1>(ctx, maps, p);
+        if (bn == 32) return nh_launch<32, 8, true, 1>(ctx, maps, p);
+        return nh_launch<64, 6, true, 1>(ctx, maps, p);
+    }
+    if (bn == 256) return nh_launch<256, 4, false, 1>(ctx, maps, p);
+    if (bn == 128) return nh_launch<128, 6, false, 1>(ctx, maps, p);
+    if (bn == 32) return nh_launch<32, 8, false, 1>(ctx, maps, p);
+    return nh_launch<64, 8, false, 1>(ctx, maps, p);
 }
 
 // Workspace the NHWC conv of this geometry needs (split-K partials of its tuned shape).
 int64_t conv_nhwc_ws_floats(tb_ctx* ctx, const ConvGeom& g, int64_t x_ps, int pair) {
-    return nh_part_floats(g, nh_choose(ctx, g, x_ps, pair));
+    return nh_part_floats(g, nh_choose(ctx, g, x_ps, pair), ctx->sm_count);
 }
 
 // Time the tile shapes (filters per tile x K splits) of this geometry on the given buffers
@@ -706,17 +815,20 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
     for (int bn : {32, 64, 128, 256}) {
         if (bn > 32 && bn / 2 >= g.F) continue;  // a tile at least half full
         const int64_t tiles = ceil_div(g.B * g.OH * g.OW, NH_BM) * ceil_div(g.F, bn);
+        // splits cut only the tiles of the last partial wave: worth it while they fit one wave or two
+        const int64_t rem = tiles - nh_dp_tiles(tiles, NhShape{bn, 2, 1}, ctx->sm_count);
         for (int sp : {1, 2, 3, 4, 6, 8}) {
-            if (sp > 1 && (ktiles < 4 * sp || tiles > ctx->tile_cnt_len || tiles * sp > 4 * (int64_t)ctx->sm_count))
+            if (sp > 1 && (rem == 0 || ktiles < 2 * sp || tiles > ctx->tile_cnt_len || rem * sp > 2 * (int64_t)ctx->sm_count))
                 continue;
-            NhShape sh{bn, sp};
-            if (nh_part_floats(g, sh) > NH_PART_CAP) continue;
+            NhShape sh{bn, sp, 1};
+            if (nh_part_floats(g, sh, ctx->sm_count) > NH_PART_CAP) continue;
             cands.push_back(sh);
         }
+        if (bn >= 128) cands.push_back(NhShape{bn, 1, 2});  // a cta_group::2 pair on 256 pixels
     }
     if (cands.empty()) return TB_OK;
     int64_t ws = 0;
-    for (const NhShape& c : cands) ws = std::max(ws, nh_part_floats(g, c));
+    for (const NhShape& c : cands) ws = std::max(ws, nh_part_floats(g, c, ctx->sm_count));
     int r = ensure_workspace(ctx, (size_t)std::max<int64_t>(ws, 1) * sizeof(float));
     if (r != TB_OK) return r;
     cudaEvent_t e0, e1;
@@ -727,6 +839,7 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
     for (const NhShape& c : cands) {
         t_nh_pin = &c;
         r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr, pair);
+        stream_delay_us(ctx, 200);  // the timed launches queue behind it: device time only
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && r == TB_OK; ++rep)
             r = conv_nhwc_launch(ctx, g, x, x_ps, wp, nullptr, nullptr, 0, y, y_ps, TB_ACT_LINEAR, 0, nullptr, pair);
@@ -738,9 +851,9 @@ int conv_nhwc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, int64_t x
         float ms = 0.f;
         cudaEventElapsedTime(&ms, e0, e1);
         if (getenv("TB_AUTOTUNE_VERBOSE"))
-            fprintf(stderr, "nhwc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d splits %d: %.4f ms\n",
+            fprintf(stderr, "nhwc autotune C%lld H%lld F%lld k%lld s%lld B%lld: bn %d splits %d ctas %d: %.4f ms\n",
                     (long long)g.C, (long long)g.H, (long long)g.F, (long long)g.KH, (long long)g.SY,
-                    (long long)g.B, c.bn, c.splits, ms / 3);
+                    (long long)g.B, c.bn, c.splits, c.ctas, ms / 3);
         if (ms < best_ms) best_ms = ms, best = c;
     }
     cudaEventDestroy(e0);
@@ -814,9 +927,19 @@ int tb_diag_conv_nhwc_phases(tb_ctx* ctx, const tb_conv_desc* d, const float* x,
     for (int c = 0; c < ctx->sm_count; ++c) {
         if (h[c * 12 + 0] == 0) continue;
         ++ctas;
-        for (int i = 0; i < 12; ++i) out12[i] += (double)h[c * 12 + i];
+        for (int i = 0; i < 10; ++i) out12[i] += (double)h[c * 12 + i];
     }
-    for (int i = 0; i < 12 && ctas; ++i) out12[i] /= ctas;
+    for (int i = 0; i < 10 && ctas; ++i) out12[i] /= ctas;
+    // 10: the launch's span (first CTA start to last CTA end), 11: the longest CTA, both in ns
+    unsigned long long t0 = ~0ull, t1 = 0, tmax = 0;
+    for (int c = 0; c < ctx->sm_count; ++c) {
+        if (h[c * 12 + 0] == 0) continue;
+        t0 = std::min(t0, h[c * 12 + 10]);
+        t1 = std::max(t1, h[c * 12 + 11]);
+        tmax = std::max(tmax, h[c * 12 + 11] - h[c * 12 + 10]);
+    }
+    out12[10] = ctas ? (double)(t1 - t0) : 0.0;
+    out12[11] = (double)tmax;
     return TB_OK;
 }
 

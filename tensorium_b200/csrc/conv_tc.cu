@@ -1038,6 +1038,7 @@ int conv_tc_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const float
         t_tc_pin = &c;
         float* ws = reinterpret_cast<float*>(ctx->ws);
         r = conv_tc_launch(ctx, g, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR, 0, ws, nullptr);
+        stream_delay_us(ctx, 200);  // the timed launches queue behind it: device time only
         cudaEventRecord(e0, ctx->stream);
         for (int rep = 0; rep < 3 && r == TB_OK; ++rep)
             r = conv_tc_launch(ctx, g, x, wp, nullptr, nullptr, nullptr, nullptr, nullptr, y, TB_ACT_LINEAR, 0, ws,

@@ -237,6 +237,13 @@ __device__ __forceinline__ bool epi_any(bool v) {
 }
 
 // --- CTA pairs (cta_group::2): a cluster of 2 CTAs on two SMs computes one M = 256 tile -----
+// the GPU's global nanosecond timer
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ unsigned cluster_rank() {
     unsigned r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
@@ -288,6 +295,19 @@ __device__ __forceinline__ void mma_tf32_g(uint32_t tmem_d, uint64_t desc_a, uin
         asm volatile(
             "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
             "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+            "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// kind::f16 (BF16 A and B) for one CTA or the pair, as mma_tf32_g
+template <int CTAS>
+__device__ __forceinline__ void mma_bf16_g(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                           uint32_t accumulate) {
+    if constexpr (CTAS == 1)
+        mma_bf16(tmem_d, desc_a, desc_b, idesc, accumulate);
+    else
+        asm volatile(
+            "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
             "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 

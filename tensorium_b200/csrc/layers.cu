@@ -13,6 +13,7 @@ using namespace tbi;
 __global__ void k_maxpool(int64_t total, int c, int h, int w, int out_h, int out_w, int size,
                           int stride_x, int stride_y, int off, const float* __restrict__ x,
                           float* __restrict__ y, int64_t* __restrict__ idx) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
          o += (int64_t)gridDim.x * blockDim.x) {
         int j = (int)(o % out_w);
@@ -44,6 +45,7 @@ __global__ void k_maxpool(int64_t total, int c, int h, int w, int out_h, int out
 __global__ void k_maxpool2x2(int64_t total2, int h, int w, int out_h, int out_w,
                              const float* __restrict__ x, float* __restrict__ y,
                              int64_t* __restrict__ idx) {
+    TB_GRID_DEP_ENTRY();
     const int half = out_w / 2;
     for (int64_t o2 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o2 < total2;
          o2 += (int64_t)gridDim.x * blockDim.x) {
@@ -76,6 +78,7 @@ __global__ void k_maxpool2x2(int64_t total2, int h, int w, int out_h, int out_w,
 // ---- upsample: upsample() forward (source/nupsamplelayer.pas:83-113) ----
 __global__ void k_upsample(int64_t total, int c, int h, int w, int s, float scale,
                            const float* __restrict__ x, float* __restrict__ y, int64_t y_bs) {
+    TB_GRID_DEP_ENTRY();
     const int ow = w * s, oh = h * s;
     for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
          o += (int64_t)gridDim.x * blockDim.x) {
@@ -92,6 +95,7 @@ __global__ void k_upsample(int64_t total, int c, int h, int w, int s, float scal
 // stride-2 fast path: one thread reads 2 inputs and writes a float4 into each of 2 rows.
 __global__ void k_upsample2(int64_t total2, int c, int h, int w, float scale,
                             const float* __restrict__ x, float* __restrict__ y, int64_t y_bs) {
+    TB_GRID_DEP_ENTRY();
     const int ow = 2 * w, oh = 2 * h, half = w / 2;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     for (int64_t o0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o0 < total2; o0 += 4 * step) {
@@ -126,6 +130,7 @@ __global__ void k_upsample2(int64_t total2, int c, int h, int w, float scale,
 // ---- route / concat: copy rows of `n` elements from `batch` images ----
 __global__ void k_copy_rows(int64_t batch, int64_t n, const float* __restrict__ src, int64_t src_bs,
                             float* __restrict__ dst, int64_t dst_bs) {
+    TB_GRID_DEP_ENTRY();
     const int64_t total = batch * n;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -136,6 +141,7 @@ __global__ void k_copy_rows(int64_t batch, int64_t n, const float* __restrict__ 
 
 __global__ void k_copy_rows4(int64_t batch, int64_t n4, const float4* __restrict__ src, int64_t src_bs4,
                              float4* __restrict__ dst, int64_t dst_bs4) {
+    TB_GRID_DEP_ENTRY();
     const int64_t total = batch * n4;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * step) {
@@ -161,6 +167,7 @@ __global__ void k_copy_rows4(int64_t batch, int64_t n4, const float4* __restrict
 // ---- shortcut: y = act(a + b) (source/naddlayer.pas:696-699) ----
 __global__ void k_shortcut4(int64_t n4, const float4* __restrict__ a, const float4* __restrict__ b,
                             float4* __restrict__ y, int act) {
+    TB_GRID_DEP_ENTRY();
     // four vectors per thread per round, all loads issued before any use (more bytes in flight)
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * step) {
@@ -186,6 +193,7 @@ __global__ void k_shortcut4(int64_t n4, const float4* __restrict__ a, const floa
 
 __global__ void k_shortcut(int64_t n, const float* __restrict__ a, const float* __restrict__ b,
                            float* __restrict__ y, int act) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         y[i] = tb_activate_dev(a[i] + b[i], act);
@@ -196,6 +204,7 @@ __global__ void k_shortcut(int64_t n, const float* __restrict__ a, const float* 
 // logistic applies) is uniform in a block; float4 accesses when every plane is 16-byte aligned.
 __global__ void k_yolo(int entries, int hw, int vec4, const float* __restrict__ x, float* __restrict__ y,
                        float scale_xy, float bias_xy) {
+    TB_GRID_DEP_ENTRY();
     const int e = blockIdx.y % entries;
     const bool logi = e != 2 && e != 3, sxy = e < 2 && scale_xy != 1.0f;
     const int64_t base = (int64_t)blockIdx.y * hw;
@@ -226,6 +235,7 @@ __global__ void k_yolo(int entries, int hw, int vec4, const float* __restrict__ 
 // ---- softmax: softmaxBatch / softmax (source/nsoftmaxlayer.pas:83-137), sequential per group ----
 __global__ void k_softmax(int64_t groups_total, int n, int groups, int64_t inputs, float temp,
                           const float* __restrict__ x, float* __restrict__ y) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups_total;
          gi += (int64_t)gridDim.x * blockDim.x) {
         int64_t b = gi / groups, g = gi - b * groups;
@@ -248,6 +258,7 @@ __global__ void k_softmax(int64_t groups_total, int n, int groups, int64_t input
 // of vssum_avx2 (source/ntensors.pas:3592-3620), which vsSumI uses on AVX2 CPUs: eight lane sums
 // over the whole blocks of 8, (l0+l4) .. (l3+l7), two horizontal adds, then the tail in order ----
 __global__ void k_avgpool(int64_t total, int im, const float* __restrict__ x, float* __restrict__ y) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float* p = x + i * im;
@@ -271,12 +282,15 @@ int copy_rows(tb_ctx* ctx, int64_t batch, int64_t n, const float* src, int64_t s
               int64_t dst_bs) {
     if (batch == 0 || n == 0) return TB_OK;
     if (n % 4 == 0 && src_bs % 4 == 0 && dst_bs % 4 == 0 && aligned16(src) && aligned16(dst)) {
-        k_copy_rows4<<<grid_for(batch * n / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            batch, n / 4, reinterpret_cast<const float4*>(src), src_bs / 4,
-            reinterpret_cast<float4*>(dst), dst_bs / 4);
+        {
+            const int _lr = launch(ctx, "k_copy_rows4", k_copy_rows4, dim3(grid_for(batch * n / 4, 256, ctx->sm_count)), dim3(256), 0, batch, n / 4, reinterpret_cast<const float4*>(src), src_bs / 4, reinterpret_cast<float4*>(dst), dst_bs / 4);
+            if (_lr != TB_OK) return _lr;
+        }
     } else {
-        k_copy_rows<<<grid_for(batch * n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            batch, n, src, src_bs, dst, dst_bs);
+        {
+            const int _lr = launch(ctx, "k_copy_rows", k_copy_rows, dim3(grid_for(batch * n, 256, ctx->sm_count)), dim3(256), 0, batch, n, src, src_bs, dst, dst_bs);
+            if (_lr != TB_OK) return _lr;
+        }
     }
     return check_launch("k_copy_rows");
 }
@@ -301,13 +315,16 @@ int tb_maxpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int6
     if (ksize == 2 && stride_x == 2 && stride_y == 2 && padding == 0 && w % 4 == 0 &&
         h == 2 * out_h && w == 2 * out_w && aligned16(x) && aligned16(y)) {
         const int64_t total2 = total / 2;
-        k_maxpool2x2<<<grid_for(total2, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            total2, (int)h, (int)w, (int)out_h, (int)out_w, x, y, indexes);
+        {
+            const int _lr = launch(ctx, "k_maxpool2x2", k_maxpool2x2, dim3(grid_for(total2, 256, ctx->sm_count)), dim3(256), 0, total2, (int)h, (int)w, (int)out_h, (int)out_w, x, y, indexes);
+            if (_lr != TB_OK) return _lr;
+        }
         return check_launch("k_maxpool2x2");
     }
-    k_maxpool<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        total, (int)channels, (int)h, (int)w, (int)out_h, (int)out_w, (int)ksize, (int)stride_x,
-        (int)stride_y, off, x, y, indexes);
+    {
+        const int _lr = launch(ctx, "k_maxpool", k_maxpool, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, total, (int)channels, (int)h, (int)w, (int)out_h, (int)out_w, (int)ksize, (int)stride_x, (int)stride_y, off, x, y, indexes);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_maxpool");
 }
 
@@ -323,13 +340,17 @@ int tb_upsample_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int
     if (!x || !y) return fail(TB_ERR_INVALID, "upsample: null pointer");
     if (stride == 2 && w % 2 == 0 && aligned16(y) && y_bs % 4 == 0 && ((uintptr_t)x & 7u) == 0) {
         const int64_t total2 = batch * channels * h * (w / 2);
-        k_upsample2<<<grid_for(total2, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            total2, (int)channels, (int)h, (int)w, scale, x, y, y_bs);
+        {
+            const int _lr = launch(ctx, "k_upsample2", k_upsample2, dim3(grid_for(total2, 256, ctx->sm_count)), dim3(256), 0, total2, (int)channels, (int)h, (int)w, scale, x, y, y_bs);
+            if (_lr != TB_OK) return _lr;
+        }
         return check_launch("k_upsample2");
     }
     const int64_t total = batch * per;
-    k_upsample<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        total, (int)channels, (int)h, (int)w, (int)stride, scale, x, y, y_bs);
+    {
+        const int _lr = launch(ctx, "k_upsample", k_upsample, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, total, (int)channels, (int)h, (int)w, (int)stride, scale, x, y, y_bs);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_upsample");
 }
 
@@ -363,11 +384,15 @@ int tb_shortcut_fwd(tb_ctx* ctx, int64_t n, const float* a, const float* b, floa
     if (!act_supported(act)) return fail(TB_ERR_UNSUPPORTED, "shortcut: activation %lld not supported", (long long)act);
     if (n == 0) return TB_OK;
     if (n % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(y)) {
-        k_shortcut4<<<grid_for(n / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            n / 4, reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),
-            reinterpret_cast<float4*>(y), (int)act);
+        {
+            const int _lr = launch(ctx, "k_shortcut4", k_shortcut4, dim3(grid_for(n / 4, 256, ctx->sm_count)), dim3(256), 0, n / 4, reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y), (int)act);
+            if (_lr != TB_OK) return _lr;
+        }
     } else {
-        k_shortcut<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(n, a, b, y, (int)act);
+        {
+            const int _lr = launch(ctx, "k_shortcut", k_shortcut, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, n, a, b, y, (int)act);
+            if (_lr != TB_OK) return _lr;
+        }
     }
     return check_launch("k_shortcut");
 }
@@ -387,7 +412,10 @@ int tb_yolo_fwd(tb_ctx* ctx, int64_t batch, int64_t n, int64_t classes, int64_t 
     if (grid.y > 65535) {  // fall back to fewer, longer planes per block is not needed at darknet sizes
         return fail(TB_ERR_UNSUPPORTED, "yolo: more than 65535 (image, anchor, entry) planes");
     }
-    k_yolo<<<grid, 256, 0, ctx->stream>>>((int)(classes + 5), (int)hw, vec4, x, y, scale_xy, bias_xy);
+    {
+        const int _lr = launch(ctx, "k_yolo", k_yolo, dim3(grid), dim3(256), 0, (int)(classes + 5), (int)hw, vec4, x, y, scale_xy, bias_xy);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_yolo");
 }
 
@@ -399,8 +427,10 @@ int tb_softmax_fwd(tb_ctx* ctx, int64_t batch, int64_t inputs, int64_t groups, f
     if (batch == 0) return TB_OK;
     if (!x || !y) return fail(TB_ERR_INVALID, "softmax: null pointer");
     const int64_t gt = batch * groups;
-    k_softmax<<<grid_for(gt, 128, ctx->sm_count), 128, 0, ctx->stream>>>(
-        gt, (int)(inputs / groups), (int)groups, inputs, temperature, x, y);
+    {
+        const int _lr = launch(ctx, "k_softmax", k_softmax, dim3(grid_for(gt, 128, ctx->sm_count)), dim3(128), 0, gt, (int)(inputs / groups), (int)groups, inputs, temperature, x, y);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_softmax");
 }
 
@@ -411,7 +441,10 @@ int tb_avgpool_fwd(tb_ctx* ctx, int64_t batch, int64_t channels, int64_t h, int6
     if (batch == 0) return TB_OK;
     if (!x || !y) return fail(TB_ERR_INVALID, "avgpool: null pointer");
     const int64_t total = batch * channels;
-    k_avgpool<<<grid_for(total, 128, ctx->sm_count), 128, 0, ctx->stream>>>(total, (int)(h * w), x, y);
+    {
+        const int _lr = launch(ctx, "k_avgpool", k_avgpool, dim3(grid_for(total, 128, ctx->sm_count)), dim3(128), 0, total, (int)(h * w), x, y);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_avgpool");
 }
 
@@ -425,6 +458,7 @@ namespace tbi {
 // adds.  One thread per output keeps those eight lanes in registers; the block stages 64-deep k
 // chunks of 8 images' inputs and 32 outputs' packed weights (Wp[k][m]) in shared memory.
 __global__ void __launch_bounds__(256) k_fc_sdot8(const ConvParams p, int batch, int inputs) {
+    TB_GRID_DEP_ENTRY();
     __shared__ float Xs[8][64];
     __shared__ float Ws[64][32];
     const int tid = threadIdx.x, ol = tid & 31, bl = tid >> 5;
@@ -463,7 +497,10 @@ int fc_sdot_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* 
     p.y = y; p.F = (int)g.F; p.Mpad = (int)g.Mpad; p.x_bs = g.x_bs; p.y_bs = g.y_bs; p.act = act;
     dim3 grid((unsigned)ceil_div(g.F, 32), (unsigned)ceil_div(g.B, 8));
     if (grid.y > 65535) return fail(TB_ERR_INVALID, "fc: batch too large");
-    k_fc_sdot8<<<grid, 256, 0, ctx->stream>>>(p, (int)g.B, (int)g.C);
+    {
+        const int _lr = launch(ctx, "k_fc_sdot8", k_fc_sdot8, dim3(grid), dim3(256), 0, p, (int)g.B, (int)g.C);
+        if (_lr != TB_OK) return _lr;
+    }
     if (launches) ++*launches;
     return check_launch("k_fc_sdot8");
 }

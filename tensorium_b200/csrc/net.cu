@@ -911,7 +911,14 @@ int tb_net_forward(tb_net* net, const float* x, int64_t use_graph) {
         ctx->stream = ctx->own_stream;
         cudaError_t e = cudaStreamBeginCapture(ctx->own_stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) { ctx->stream = saved; return cuda_fail(e, "cudaStreamBeginCapture"); }
+        // TB_PDL=1: each layer's kernel may start while the previous one drains (programmatic
+        // dependent launch; set-up overlaps that tail, reads wait for all of it). Off by default:
+        // measured on YOLOv3 at batch 8 it gains nothing on the tensor-core plans and costs the
+        // FP32 plan ~7% (dependent CTAs held resident beside the multi-wave FP32 grids).
+        static const bool pdl = getenv("TB_PDL") != nullptr && atoi(getenv("TB_PDL")) != 0;
+        ctx->pdl = pdl ? 1 : 0;
         int r = run_all(net, x);
+        ctx->pdl = 0;
         cudaGraph_t g = nullptr;
         e = cudaStreamEndCapture(ctx->own_stream, &g);
         ctx->stream = saved;

@@ -14,6 +14,7 @@ namespace {
 // zero; values rounded to TF32 (nearest), as every activation the tensor cores read
 __global__ void k_nchw_to_nhwc(int64_t npix, int c, int hw, int ps, const float* __restrict__ x, int64_t x_bs,
                                float* __restrict__ y, int pair) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npix * ps;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t pix = i / ps;
@@ -28,6 +29,7 @@ __global__ void k_nchw_to_nhwc(int64_t npix, int c, int hw, int ps, const float*
 // upsample: y[b][oy][ox][ch] = scale * x[b][oy/s][ox/s][ch], 4 channels per thread
 __global__ void k_upsample_nhwc4(int64_t total4, int c4, int w, int h, int s, float scale,
                                  const float4* __restrict__ x, int xps4, float4* __restrict__ y, int yps4) {
+    TB_GRID_DEP_ENTRY();
     const int ow = w * s, oh = h * s;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t opix = i / c4;
@@ -44,6 +46,7 @@ __global__ void k_upsample_nhwc4(int64_t total4, int c4, int w, int h, int s, fl
 // copy c channels per pixel between two pixel strides (route slices)
 __global__ void k_copy_nhwc4(int64_t total4, int c4, const float4* __restrict__ x, int xps4, float4* __restrict__ y,
                              int yps4) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t pix = i / c4;
         const int q = (int)(i - pix * c4);
@@ -55,6 +58,7 @@ __global__ void k_copy_nhwc4(int64_t total4, int c4, const float4* __restrict__ 
 __global__ void k_shortcut_nhwc(int64_t total, int c, const float* __restrict__ a, int aps,
                                 const float* __restrict__ b, int bps, float* __restrict__ y, int yps, int act,
                                 int pair) {
+    TB_GRID_DEP_ENTRY();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t pix = i / c;
         const int ch = (int)(i - pix * c);
@@ -70,6 +74,7 @@ __global__ void k_shortcut_nhwc(int64_t total, int c, const float* __restrict__ 
 __global__ void k_im2col_first(int64_t npix, int C, int H, int W, int KW, int K, int OW, int OHW, int SY, int SX,
                                int PY, int PX, int DY, int DX, const float* __restrict__ x, int64_t x_bs,
                                float* __restrict__ y, int pair) {
+    TB_GRID_DEP_ENTRY();
     // one thread per output pixel: the lanes of a warp read neighbouring pixels of the same tap
     // (coalesced) and each writes its 128-byte row of 32 values
     for (int64_t pix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pix < npix; pix += (int64_t)gridDim.x * blockDim.x) {
@@ -128,9 +133,10 @@ int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, i
                       const float* x, int64_t x_bs, float* y, int pair) {
     const int64_t npix = B * OH * OW;
     if (npix == 0) return TB_OK;
-    k_im2col_first<<<grid_for(npix, 128, ctx->sm_count), 128, 0, ctx->stream>>>(
-        npix, (int)C, (int)H, (int)W, (int)KW, (int)(C * KH * KW), (int)OW, (int)(OH * OW), (int)SY, (int)SX,
-        (int)PY, (int)PX, (int)DY, (int)DX, x, x_bs, y, pair);
+    {
+        const int _lr = launch(ctx, "k_im2col_first", k_im2col_first, dim3(grid_for(npix, 128, ctx->sm_count)), dim3(128), 0, npix, (int)C, (int)H, (int)W, (int)KW, (int)(C * KH * KW), (int)OW, (int)(OH * OW), (int)SY, (int)SX, (int)PY, (int)PX, (int)DY, (int)DX, x, x_bs, y, pair);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_im2col_first");
 }
 
@@ -144,8 +150,10 @@ int nhwc_from_nchw(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, 
                    float* y, int64_t ps, int pair) {
     const int64_t npix = batch * h * w;
     if (npix == 0) return TB_OK;
-    k_nchw_to_nhwc<<<grid_for(npix * ps, 256, ctx->sm_count), 256, 0, ctx->stream>>>(npix, (int)c, (int)(h * w),
-                                                                                     (int)ps, x, x_bs, y, pair);
+    {
+        const int _lr = launch(ctx, "k_nchw_to_nhwc", k_nchw_to_nhwc, dim3(grid_for(npix * ps, 256, ctx->sm_count)), dim3(256), 0, npix, (int)c, (int)(h * w), (int)ps, x, x_bs, y, pair);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_nchw_to_nhwc");
 }
 
@@ -156,9 +164,10 @@ int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, i
         return fail(TB_ERR_STATE, "NHWC upsample: channels, strides and pointers must be 16-byte multiples");
     const int64_t total4 = batch * h * s * w * s * (c / 4);
     if (total4 == 0) return TB_OK;
-    k_upsample_nhwc4<<<grid_for(total4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        total4, (int)(c / 4), (int)w, (int)h, (int)s, scale, reinterpret_cast<const float4*>(x), (int)(xps / 4),
-        reinterpret_cast<float4*>(y), (int)(yps / 4));
+    {
+        const int _lr = launch(ctx, "k_upsample_nhwc4", k_upsample_nhwc4, dim3(grid_for(total4, 256, ctx->sm_count)), dim3(256), 0, total4, (int)(c / 4), (int)w, (int)h, (int)s, scale, reinterpret_cast<const float4*>(x), (int)(xps / 4), reinterpret_cast<float4*>(y), (int)(yps / 4));
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_upsample_nhwc4");
 }
 
@@ -167,9 +176,10 @@ int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps,
         return fail(TB_ERR_STATE, "NHWC copy: channels, strides and pointers must be 16-byte multiples");
     const int64_t total4 = npix * (c / 4);
     if (total4 == 0) return TB_OK;
-    k_copy_nhwc4<<<grid_for(total4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        total4, (int)(c / 4), reinterpret_cast<const float4*>(x), (int)(xps / 4), reinterpret_cast<float4*>(y),
-        (int)(yps / 4));
+    {
+        const int _lr = launch(ctx, "k_copy_nhwc4", k_copy_nhwc4, dim3(grid_for(total4, 256, ctx->sm_count)), dim3(256), 0, total4, (int)(c / 4), reinterpret_cast<const float4*>(x), (int)(xps / 4), reinterpret_cast<float4*>(y), (int)(yps / 4));
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_copy_nhwc4");
 }
 
@@ -177,8 +187,10 @@ int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t 
                   float* y, int64_t yps, int act, int pair) {
     const int64_t total = npix * c;
     if (total == 0) return TB_OK;
-    k_shortcut_nhwc<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(total, (int)c, a, (int)aps, b,
-                                                                                  (int)bps, y, (int)yps, act, pair);
+    {
+        const int _lr = launch(ctx, "k_shortcut_nhwc", k_shortcut_nhwc, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, total, (int)c, a, (int)aps, b, (int)bps, y, (int)yps, act, pair);
+        if (_lr != TB_OK) return _lr;
+    }
     return check_launch("k_shortcut_nhwc");
 }
 

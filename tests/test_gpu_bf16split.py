@@ -77,3 +77,20 @@ def test_yolov3_bf16split_heads(ctx, calibrated, which):
                 assert abs(obj[k] - 0.25) < 1e-3, (b, k, obj[k])
             assert len(want) > 100
     net.close()
+
+
+@pytest.mark.parametrize("shape", ["256,1,2", "128,1,2"])
+def test_yolov3_bf16split_cta_pairs(ctx, shape, monkeypatch):
+    """Every conv of the BF16-split network on one CTA-pair tile shape (cta_group::2 kind::f16
+    MMAs, pinned through the TB_NHWC_FORCE test hook): the heads stay within the bar."""
+    monkeypatch.setenv("TB_NHWC_FORCE", shape)
+    specs = synth.yolov3_specs()
+    batch = 2
+    x = synth.input_images(7, "yolov3", batch, (3, 416, 416))
+    ref = O.run_network(specs, x, keep=HEADS)
+    net = TNNet(ctx, specs, batch, (3, 416, 416), math_mode=MATH_BF16_SPLIT)
+    net.forward(torch.from_numpy(x).to(ctx.torch_device), use_graph=False)
+    for h in HEADS:
+        e = rel_l2(net.output(h).cpu().numpy(), ref[h], batch)
+        assert e <= 1e-3, (shape, h, e)
+    net.close()

@@ -108,15 +108,19 @@ def test_nhwc_rejects_what_it_cannot_take(ctx):
     assert rc < 0
 
 
-@pytest.mark.parametrize("shape", ["32,1", "32,3", "64,1", "128,1", "256,1", "256,3", "128,2", "64,4", "256,8"])
+@pytest.mark.parametrize("shape", ["32,1", "32,3", "64,1", "128,1", "256,1", "256,3", "128,2", "64,4", "256,8",
+                                   "128,1,2", "256,1,2"])
 def test_nhwc_every_tile_shape(ctx, shape, monkeypatch):
-    """Each (filters per tile, K splits) shape, pinned through the TB_NHWC_FORCE test hook; split
-    units are summed by the last arriving unit in split order, so two runs are identical."""
+    """Each (filters per tile, K splits, CTAs per tile) shape, pinned through the TB_NHWC_FORCE test
+    hook; the tiles past the last whole wave are split, and a split tile is summed by its last
+    arriving unit in split order, so two runs are identical. The CTA-pair shapes (cta_group::2, 256 pixels per tile) meet geometries whose last
+    tile leaves the odd CTA's pixels wholly past the end and filters past F in the odd CTA's half."""
     monkeypatch.setenv("TB_NHWC_FORCE", shape)
     ctx.reserve(256 << 20)  # room for the split-K partial tiles
     rng = np.random.default_rng(31)
+    # (8, 64, 52, 72): more tiles than SMs, so split shapes store whole waves and split the rest
     for (B, Cc, H, F, k, s, p) in [(2, 128, 26, 256, 3, 1, 1), (8, 512, 13, 160, 3, 1, 1), (2, 64, 52, 96, 1, 1, 0),
-                                   (2, 64, 40, 72, 3, 2, 1)]:
+                                   (2, 64, 40, 72, 3, 2, 1), (8, 64, 52, 72, 3, 1, 1)]:
         x = rng.uniform(0, 1, (B, Cc, H, H)).astype(np.float32)
         w = (rng.standard_normal((F, Cc * k * k)) * np.sqrt(2.0 / (Cc * k * k))).astype(np.float32)
         b = rng.standard_normal(F).astype(np.float32) * 0.1
