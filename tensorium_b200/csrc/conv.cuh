@@ -112,6 +112,18 @@ int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, i
                       int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
                       const float* x, int64_t x_bs, float* y, int pair = 0);
 int nhwc_pack_first(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wp, int pair = 0);
+// the first layer computed directly from the NCHW input into its NHWC output (C*KH*KW <= 32,
+// F <= 128, leaky or linear, no residual); weights packed [k][F rounded up to 32] by
+// nhwc_pack_first_direct (nhwc_first_direct_wcount floats)
+bool nhwc_first_direct_supported(int64_t C, int64_t KH, int64_t KW, int64_t SY, int64_t SX, int64_t DY, int64_t DX,
+                                 int64_t F, int64_t yps);
+int64_t nhwc_first_direct_wcount(int64_t F, int64_t C, int64_t KH, int64_t KW);
+int nhwc_pack_first_direct(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wd,
+                           int pair = 0);
+int nhwc_first_direct(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
+                      int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
+                      const float* x, int64_t x_bs, const float* wd, const float* bias, int64_t F, int act, float* y,
+                      int64_t yps, int pair = 0);
 int nhwc_upsample(tb_ctx* ctx, int64_t batch, int64_t c, int64_t h, int64_t w, int64_t s, float scale,
                   const float* x, int64_t xps, float* y, int64_t yps, int pair = 0);
 int nhwc_copy(tb_ctx* ctx, int64_t npix, int64_t c, const float* x, int64_t xps, float* y, int64_t yps);
@@ -120,6 +132,18 @@ int nhwc_shortcut(tb_ctx* ctx, int64_t npix, int64_t c, const float* a, int64_t 
 // Direct convolution for short reductions (C*KH*KW <= 32, CRS-packed weights, no residual, no
 // fused yolo): the first layer of an image network (conv_direct.cu).
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes);
+// The first-layer direct kernel (conv_direct.cu, k_first_direct): C*KH*KW <= 32, F <= 128, bias
+// then leaky or linear; w[k * wstride + f] with k = (c * KH + r) * KW + s. Output NCHW planes
+// (yps == 0, y_bs floats per image) or NHWC (yps floats per pixel, F % 4 == 0). fmt 0: fp32
+// operands and outputs, one FMA chain per output in ascending k from 0 (bit-identical to the
+// reference CPU path); 1: operands and outputs rounded to TF32; 2: fp32 operands, bf16-pair outputs.
+struct FirstGeom {
+    int64_t B, C, H, W, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW;
+};
+bool first_direct_supported(int64_t C, int64_t KH, int64_t KW, int64_t SY, int64_t SX, int64_t DY, int64_t DX, int64_t F,
+                            bool nhwc);
+int first_direct_launch(tb_ctx* ctx, const FirstGeom& g, const float* x, int64_t x_bs, const float* w, int64_t wstride,
+                        const float* bias, int64_t F, int act, float* y, int64_t y_bs, int64_t yps, int fmt);
 int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
                        const float* bn_scale, const float* bn_mean, const float* bn_var, float* y, int act,
                        int64_t* launches);

@@ -10,6 +10,9 @@
 // result is bit-identical to the reference's CPU arithmetic.
 #include "conv.cuh"
 
+#include <cstdlib>
+#include <mutex>
+
 namespace tbi {
 
 namespace {
@@ -129,10 +132,229 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
     }
 }
 
+
+// ---- the first-layer kernel: bias + leaky / linear only, NCHW or NHWC output ----
+//
+// A block makes FK_ROWS output rows x FK_SEG consecutive output pixels of one image (FK_PPT
+// pixels per thread, FK_THREADS apart). The weights ([k][filter], filters rounded up to FK_FG),
+// the bias and every input row the block's output rows read (per channel, zero in the padding) are
+// staged in shared memory once, behind one barrier; then for each output row each thread gathers
+// the K inputs of its pixels into registers, then FK_FG filters at a time: per k, four 16-byte broadcast loads of weights and
+// FK_FG x FK_PPT FMAs, each accumulator one chain in ascending k from 0 (the reference's order).
+// NHWC outputs go through a per-warp staging tile so that each store instruction writes whole
+// 64-byte pixel row pieces; NCHW outputs are stored per filter plane, 32 consecutive pixels per warp.
+constexpr int FK_THREADS = 128, FK_PPT = 2, FK_SEG = FK_THREADS * FK_PPT, FK_ROWS = 4;
+constexpr int FK_KMAX = 32, FK_FMAX = 128, FK_FG = 16;  // filters per pass
+constexpr int FK_STG = FK_FG + 4;                        // staging row pitch (floats)
+
+struct FirstParams {
+    const float* x;
+    long long x_bs;
+    int C, H, W, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW;
+    int segs, row_blocks;  // blocks per output row segment / output-row groups per image
+    const float* w;
+    int wstride;
+    const float* bias;
+    int F, act;
+    float* y;
+    long long y_bs;
+    int yps;  // NHWC: floats per pixel
+    int fmt;  // 0: fp32, 1: TF32 operands and outputs, 2: fp32 operands, bf16-pair outputs
+};
+
+__host__ __device__ inline int fk_cols(int SX, int KW, int DX) { return (FK_SEG - 1) * SX + (KW - 1) * DX + 1; }
+// input rows per channel that FK_ROWS consecutive output rows read
+__host__ __device__ inline int fk_rows(int SY, int KH, int DY) { return (FK_ROWS - 1) * SY + (KH - 1) * DY + 1; }
+
+// KT: 27 = 3 channels, 3x3; 25 = 1 channel, 5x5 (the window as compile-time constants); 0: any
+// window with C * KH * KW <= 32. FMT: the operand / output format (FirstParams::fmt); NHWC output
+// for FMT 1 and 2, NCHW planes for FMT 0.
+template <int KT, int FMT>
+__global__ void __launch_bounds__(FK_THREADS, 3) k_first_direct(const FirstParams p) {
+    TB_GRID_DEP_ENTRY();
+    constexpr bool NHWC = FMT != 0;
+    constexpr int CT = KT == 27 ? 3 : KT == 25 ? 1 : 0, KWT = KT == 27 ? 3 : KT == 25 ? 5 : 0;
+    extern __shared__ __align__(16) float fsm[];
+    const int C = CT ? CT : p.C, KH = KWT ? KWT : p.KH, KW = KWT ? KWT : p.KW;
+    const int K = KT > 0 ? KT : C * KH * KW;
+    const int FG = (p.F + FK_FG - 1) & ~(FK_FG - 1);
+    const int cols = fk_cols(p.SX, KW, p.DX);
+    float* wsm = fsm;                                    // [K][FG]
+    float* bsm = wsm + K * FG;                           // [FG]
+    const int nrin = fk_rows(p.SY, KH, p.DY);
+    float* xs = bsm + FG;                                // [c][nrin input rows][cols]
+    float* stg = xs + ((C * nrin * cols + 3) & ~3);      // NHWC: per warp 32 x FK_STG
+    const int seg = blockIdx.x % p.segs;
+    const int rb = (blockIdx.x / p.segs) % p.row_blocks;
+    const long long b = blockIdx.x / ((long long)p.segs * p.row_blocks);
+    const int ox0 = seg * FK_SEG;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int k = 0; k < K; ++k)
+        for (int f = t; f < FG; f += FK_THREADS) {
+            const float v = f < p.F ? __ldg(p.w + (long long)k * p.wstride + f) : 0.0f;
+            wsm[k * FG + f] = FMT == 1 ? tb_tf32_rna(v) : v;
+        }
+    for (int f = t; f < FG; f += FK_THREADS) bsm[f] = p.bias && f < p.F ? __ldg(p.bias + f) : 0.0f;
+    const float* xb = p.x + b * p.x_bs;
+    const int ix0 = ox0 * p.SX - p.PX;
+    const int OHW = p.OH * p.OW;
+    {
+        const int iy0 = rb * FK_ROWS * p.SY - p.PY;  // first input row of the block
+        int c = 0, ri = 0;
+        for (int row = 0; row < C * nrin; ++row) {
+            const int iy = iy0 + ri;
+            const bool rok = iy >= 0 && iy < p.H;
+            const float* src = xb + ((long long)c * p.H + (rok ? iy : 0)) * p.W;
+            for (int col = t; col < cols; col += FK_THREADS) {
+                const int ix = ix0 + col;
+                const float v = rok && ix >= 0 && ix < p.W ? __ldg(src + ix) : 0.0f;
+                xs[row * cols + col] = FMT == 1 ? tb_tf32_rna(v) : v;
+            }
+            if (++ri == nrin) ri = 0, ++c;
+        }
+    }
+    __syncthreads();
+    for (int rr = 0; rr < FK_ROWS; ++rr) {
+        const int oy = rb * FK_ROWS + rr;
+        if (oy >= p.OH) break;  // the same for every thread of the block
+        float xv[FK_PPT][FK_KMAX];
+        {
+            int c = 0, r = 0, s = 0;  // k = (c * KH + r) * KW + s
+#pragma unroll
+            for (int k = 0; k < FK_KMAX; ++k) {
+                const int off = (c * nrin + rr * p.SY + r * p.DY) * cols + s * p.DX + t * p.SX;
+#pragma unroll
+                for (int q = 0; q < FK_PPT; ++q) xv[q][k] = k < K ? xs[off + q * FK_THREADS * p.SX] : 0.0f;
+                if (k < K && ++s == KW) {
+                    s = 0;
+                    if (++r == KH) r = 0, ++c;
+                }
+            }
+        }
+        for (int f0 = 0; f0 < p.F; f0 += FK_FG) {
+            float acc[FK_PPT][FK_FG];
+#pragma unroll
+            for (int q = 0; q < FK_PPT; ++q)
+#pragma unroll
+                for (int j = 0; j < FK_FG; ++j) acc[q][j] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < FK_KMAX; ++k) {
+                if (k == K) break;
+                const float4* wk = reinterpret_cast<const float4*>(wsm + k * FG + f0);
+#pragma unroll
+                for (int j4 = 0; j4 < FK_FG / 4; ++j4) {
+                    const float4 w4 = wk[j4];
+#pragma unroll
+                    for (int q = 0; q < FK_PPT; ++q) {
+                        acc[q][4 * j4] = fmaf(w4.x, xv[q][k], acc[q][4 * j4]);
+                        acc[q][4 * j4 + 1] = fmaf(w4.y, xv[q][k], acc[q][4 * j4 + 1]);
+                        acc[q][4 * j4 + 2] = fmaf(w4.z, xv[q][k], acc[q][4 * j4 + 2]);
+                        acc[q][4 * j4 + 3] = fmaf(w4.w, xv[q][k], acc[q][4 * j4 + 3]);
+                    }
+                }
+            }
+            const int nf = min(FK_FG, p.F - f0);
+            const bool leaky = p.act == TB_ACT_LEAKY;
+#pragma unroll
+            for (int q = 0; q < FK_PPT; ++q) {
+                float o[FK_FG];
+#pragma unroll
+                for (int j = 0; j < FK_FG; ++j) {
+                    float v = __fadd_rn(acc[q][j], bsm[f0 + j]);  // forwardBias, then the activation
+                    if (leaky && v < 0.f) v = __fmul_rn(v, 0.1f);
+                    o[j] = FMT == 0 ? v : FMT == 1 ? tb_tf32_rna(v) : tb_pair_encode(v);
+                }
+                const int wox = ox0 + q * FK_THREADS + 32 * warp;  // this warp's first pixel
+                if constexpr (NHWC) {
+                    float* ws = stg + warp * 32 * FK_STG;
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < FK_FG; j += 4)
+                        *reinterpret_cast<float4*>(ws + lane * FK_STG + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+                    __syncwarp();
+                    // 32 pixels x nf filters: FK_FG / 4 lanes per pixel row
+                    constexpr int LPR = FK_FG / 4, RPI = 32 / LPR;  // lanes per row, rows per instruction
+                    const int nvalid = min(32, p.OW - wox);
+                    float* yw = p.y + b * p.y_bs + ((long long)oy * p.OW + wox) * p.yps + f0;
+#pragma unroll
+                    for (int i = 0; i < 32 / RPI; ++i) {
+                        const int px = i * RPI + lane / LPR, q4 = lane % LPR;
+                        if (px < nvalid && 4 * q4 < nf)
+                            __stcs(reinterpret_cast<float4*>(yw + (long long)px * p.yps) + q4,
+                                   *reinterpret_cast<const float4*>(ws + px * FK_STG + 4 * q4));
+                    }
+                } else {
+                    if (wox + lane < p.OW) {
+                        float* yp = p.y + b * p.y_bs + (long long)oy * p.OW + wox + lane;
+#pragma unroll
+                        for (int j = 0; j < FK_FG; ++j)
+                            if (j < nf) __stcs(yp + (long long)(f0 + j) * OHW, o[j]);
+                    }
+                }
+            }
+        }
+    }
+}
 }  // namespace
 
 static int64_t direct_smem(const ConvGeom& g) {
     return (int64_t)(DIRECT_KMAX * DIRECT_FMAX + g.C * g.KH * direct_cols((int)g.SX, (int)g.KW, (int)g.DX, DIRECT_SEG)) * 4;
+}
+
+
+static int64_t first_smem(int64_t C, int64_t KH, int64_t KW, int64_t SY, int64_t SX, int64_t DY, int64_t DX, int64_t F,
+                          bool nhwc) {
+    const int64_t FG = round_up(F, FK_FG), cols = fk_cols((int)SX, (int)KW, (int)DX);
+    const int64_t nrin = fk_rows((int)SY, (int)KH, (int)DY);
+    return (C * KH * KW * FG + FG + round_up(C * nrin * cols, 4) + (nhwc ? 4 * 32 * FK_STG : 0)) * 4;
+}
+
+bool first_direct_supported(int64_t C, int64_t KH, int64_t KW, int64_t SY, int64_t SX, int64_t DY, int64_t DX, int64_t F,
+                            bool nhwc) {
+    return C * KH * KW <= FK_KMAX && F <= FK_FMAX && F > 0 && SX <= 4 && SY <= 4 && DX * (KW - 1) <= 64 &&
+           DY * (KH - 1) <= 64 && first_smem(C, KH, KW, SY, SX, DY, DX, F, nhwc) <= 96 * 1024;
+}
+
+int first_direct_launch(tb_ctx* ctx, const FirstGeom& g, const float* x, int64_t x_bs, const float* w, int64_t wstride,
+                        const float* bias, int64_t F, int act, float* y, int64_t y_bs, int64_t yps, int fmt) {
+    const bool nhwc = yps > 0;
+    if (!first_direct_supported(g.C, g.KH, g.KW, g.SY, g.SX, g.DY, g.DX, F, nhwc) || (act != TB_ACT_LEAKY && act != TB_ACT_LINEAR) ||
+        (nhwc && (F % 4 || yps % 4 || !aligned16(y))) || wstride < F)
+        return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: unsupported geometry");
+    FirstParams p{};
+    p.x = x; p.x_bs = x_bs;
+    p.C = (int)g.C; p.H = (int)g.H; p.W = (int)g.W; p.KH = (int)g.KH; p.KW = (int)g.KW;
+    p.SY = (int)g.SY; p.SX = (int)g.SX; p.PY = (int)g.PY; p.PX = (int)g.PX; p.DY = (int)g.DY; p.DX = (int)g.DX;
+    p.OH = (int)g.OH; p.OW = (int)g.OW;
+    p.segs = (int)ceil_div(g.OW, FK_SEG);
+    p.row_blocks = (int)ceil_div(g.OH, FK_ROWS);
+    p.w = w; p.wstride = (int)wstride; p.bias = bias; p.F = (int)F; p.act = act;
+    p.y = y; p.y_bs = y_bs; p.yps = (int)yps; p.fmt = fmt;
+    const int64_t blocks = g.B * p.row_blocks * p.segs;
+    if (blocks == 0) return TB_OK;
+    if (blocks >= ((int64_t)1 << 31) || g.B * g.C * g.H * g.W >= ((int64_t)1 << 40))
+        return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: too many blocks");
+    const int64_t smem = first_smem(g.C, g.KH, g.KW, g.SY, g.SX, g.DY, g.DX, F, nhwc);
+    if (nhwc != (fmt != 0)) return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: NHWC goes with TF32 / pair outputs");
+    const int win = g.C == 3 && g.KH == 3 && g.KW == 3 ? 27 : g.C == 1 && g.KH == 5 && g.KW == 5 ? 25 : 0;
+    using Kern = void (*)(const FirstParams);
+    static const Kern kerns[3][3] = {
+        {k_first_direct<27, 0>, k_first_direct<27, 1>, k_first_direct<27, 2>},
+        {k_first_direct<25, 0>, k_first_direct<25, 1>, k_first_direct<25, 2>},
+        {k_first_direct<0, 0>, k_first_direct<0, 1>, k_first_direct<0, 2>}};
+    const Kern kern = kerns[win == 27 ? 0 : win == 25 ? 1 : 2][fmt];
+    static std::mutex mu;
+    static bool done[64] = {false};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (ctx->device >= 64 || !done[ctx->device]) {
+            for (int i = 0; i < 3; ++i)
+                for (int j = 0; j < 3; ++j)
+                    TB_CHECK_CUDA(cudaFuncSetAttribute(kerns[i][j], cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+            if (ctx->device < 64) done[ctx->device] = true;
+        }
+    }
+    return launch(ctx, "k_first_direct", kern, dim3((unsigned)blocks), dim3(FK_THREADS), (size_t)smem, p);
 }
 
 bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes) {
@@ -145,6 +367,14 @@ bool conv_direct_supported(const ConvGeom& g, const float* res, int yolo_classes
 int conv_direct_launch(tb_ctx* ctx, const ConvGeom& g, const float* x, const float* wp, const float* bias,
                        const float* bn_scale, const float* bn_mean, const float* bn_var, float* y, int act,
                        int64_t* launches) {
+    // bias + leaky / linear (the common first layer): the first-layer kernel, same arithmetic
+    if (!bn_mean && (act == TB_ACT_LEAKY || act == TB_ACT_LINEAR) &&
+        first_direct_supported(g.C, g.KH, g.KW, g.SY, g.SX, g.DY, g.DX, g.F, false) && !getenv("TB_DIRECT_OLD")) {
+        const FirstGeom fg{g.B, g.C, g.H, g.W, g.KH, g.KW, g.SY, g.SX, g.PY, g.PX, g.DY, g.DX, g.OH, g.OW};
+        const int r = first_direct_launch(ctx, fg, x, g.x_bs, wp, g.Mpad, bias, g.F, act, y, g.y_bs, 0, 0);
+        if (r == TB_OK && launches) ++*launches;
+        return r;
+    }
     ConvParams p{};
     p.x = x; p.w = wp; p.bias = bias; p.bn_scale = bn_scale; p.bn_mean = bn_mean; p.bn_var = bn_var;
     p.y = y;

@@ -92,6 +92,9 @@ struct tb_net {
     // the first conv with C * KH * KW <= 32 runs as a 1x1 conv over its receptive fields
     // (x_nhwc holds [batch][oh][ow][32], made by the input conversion)
     bool first_im2col = false;
+    // or, when it fits nhwc_first_direct (F <= 128, leaky or linear), computed straight from the
+    // NCHW network input into its NHWC output (no x_nhwc, no receptive-field pass)
+    bool first_direct = false;
 };
 
 namespace {
@@ -249,6 +252,13 @@ int run_layer_nhwc(tb_net* net, int64_t i, const float* x) {
     Layer& L = *net->layers[i];
     const int64_t B = net->batch;
     int r;
+    if (i == 0 && net->first_direct) {
+        const Layer& T = *net->layers[L.target];
+        net->launches++;
+        return nhwc_first_direct(ctx, B, net->c, net->h, net->w, L.ksize, L.ksize, L.stride, L.stride, L.pad, L.pad,
+                                 1, 1, L.oh, L.ow, x, net->c * net->h * net->w, L.d_wp, L.d_bias, L.oc, (int)L.act,
+                                 T.out.ptr, T.out.ps, net->pair);
+    }
     if (i == 0) {  // the network input, NCHW, into the NHWC staging buffer (or its receptive fields)
         if (net->first_im2col)
             r = nhwc_im2col_first(ctx, B, net->c, net->h, net->w, L.ksize, L.ksize, L.stride, L.stride, L.pad, L.pad,
@@ -632,6 +642,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     //     upsamples and fused yolo heads runs every activation in NHWC (TB_NET_NHWC=0: off)
     net->nhwc = false;
     net->first_im2col = false;
+    net->first_direct = false;
     {
         const char* ev = getenv("TB_NET_NHWC");
         const bool tc_mode = math_mode == TB_MATH_TF32 || math_mode == TB_MATH_BF16_SPLIT;
@@ -644,7 +655,12 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
                 desc_of(net, L, &d);
                 ConvGeom g;
                 if (L.bn || conv_geom(&d, &g) != TB_OK) { ok = false; break; }
-                if (i == 0 && L.c * L.ksize * L.ksize <= 32) {
+                const char* fdv = getenv("TB_FIRST_DIRECT");
+                if (i == 0 && L.target == 0 && (L.act == TB_ACT_LEAKY || L.act == TB_ACT_LINEAR) &&
+                    !(fdv && fdv[0] == '0') &&
+                    nhwc_first_direct_supported(L.c, L.ksize, L.ksize, L.stride, L.stride, 1, 1, L.oc, round_up(L.oc, 4))) {
+                    net->first_direct = true;
+                } else if (i == 0 && L.c * L.ksize * L.ksize <= 32) {
                     net->first_im2col = true;
                     if (!conv_nhwc_supported(first_as_1x1(g), 32)) ok = false;
                 } else {
@@ -674,7 +690,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         }
         net->nhwc = ok;
         net->pair = ok && math_mode == TB_MATH_BF16_SPLIT ? 1 : 0;
-        if (!ok) net->first_im2col = false;
+        if (!ok) net->first_im2col = net->first_direct = false;
     }
     // floats per image and batch / pixel strides of a layer's own output buffer
     auto own_view = [&](Layer& L, float* ptr, int64_t channels_total) {
@@ -771,7 +787,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         L.out.ptr = L.own;
         placed[i] = true;
     }
-    if (net->nhwc) {
+    if (net->nhwc && !net->first_direct) {
         const Layer& L0 = *net->layers[0];
         net->x_ps = net->first_im2col ? 32 : round_up(net->c, 4);
         net->x_nhwc = alloc(B * (net->first_im2col ? L0.oh * L0.ow : net->h * net->w) * net->x_ps);
@@ -795,7 +811,11 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
         if (r != TB_OK) return r;
         float* raw = dev_upload(net, L.weights, &err);
         if (!raw) return err;
-        if (net->nhwc && i == 0 && net->first_im2col) {
+        if (net->nhwc && i == 0 && net->first_direct) {
+            L.d_wp = alloc(nhwc_first_direct_wcount(g.F, g.C, g.KH, g.KW));
+            if (!L.d_wp) return err;
+            r = nhwc_pack_first_direct(net->ctx, g.F, g.C, g.KH, g.KW, raw, L.d_wp, net->pair);
+        } else if (net->nhwc && i == 0 && net->first_im2col) {
             L.d_wp = alloc(g.F * 32 * (net->pair ? 2 : 1));
             if (!L.d_wp) return err;
             r = nhwc_pack_first(net->ctx, g.F, g.C, g.KH, g.KW, raw, L.d_wp, net->pair);
@@ -829,7 +849,7 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     if (net->nhwc) {  // NHWC plan: tile width and K splits of every conv, measured on its buffers
         for (int64_t i = 0; i < n; ++i) {
             Layer& L = *net->layers[i];
-            if (L.type != TB_LAYER_CONV) continue;
+            if (L.type != TB_LAYER_CONV || (i == 0 && net->first_direct)) continue;
             tb_conv_desc d;
             desc_of(net, L, &d);
             const Layer& T = *net->layers[L.target];

@@ -4,7 +4,7 @@
 // (concatenation) buffer. Same arithmetic as the NCHW kernels: upsample multiplies by the scale
 // (source/nupsamplelayer.pas:83-113), shortcut adds then activates (source/naddlayer.pas:667-725),
 // route copies (source/nconcatlayer.pas:93-119).
-#include "common.cuh"
+#include "conv.cuh"
 
 namespace tbi {
 
@@ -126,7 +126,44 @@ __global__ void k_pack_first(const float* __restrict__ w, float* __restrict__ wp
     }
 }
 
+// its weights: wd[k][f] for k = (c * KH + r) * KW + s, FG = F rounded up to 32 filters (zero
+// past F); TF32 mode rounds them to TF32, pair mode keeps them exact
+__global__ void k_pack_first_direct(const float* __restrict__ w, float* __restrict__ wd, int F, int K, int pair) {
+    const int FG = (F + 31) & ~31;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < K * FG; i += gridDim.x * blockDim.x) {
+        const int k = i / FG, f = i - k * FG;
+        const float v = f < F ? w[(int64_t)f * K + k] : 0.0f;
+        wd[i] = pair ? v : tb_tf32_rna(v);
+    }
+}
+
 }  // namespace
+
+bool nhwc_first_direct_supported(int64_t C, int64_t KH, int64_t KW, int64_t SY, int64_t SX, int64_t DY, int64_t DX,
+                                 int64_t F, int64_t yps) {
+    return F % 4 == 0 && yps % 4 == 0 && first_direct_supported(C, KH, KW, SY, SX, DY, DX, F, true);
+}
+
+int64_t nhwc_first_direct_wcount(int64_t F, int64_t C, int64_t KH, int64_t KW) { return C * KH * KW * round_up(F, 32); }
+
+int nhwc_pack_first_direct(tb_ctx* ctx, int64_t F, int64_t C, int64_t KH, int64_t KW, const float* w, float* wd,
+                           int pair) {
+    const int64_t n = nhwc_first_direct_wcount(F, C, KH, KW);
+    k_pack_first_direct<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(w, wd, (int)F, (int)(C * KH * KW),
+                                                                                   pair);
+    return check_launch("k_pack_first_direct");
+}
+
+int nhwc_first_direct(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
+                      int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
+                      const float* x, int64_t x_bs, const float* wd, const float* bias, int64_t F, int act, float* y,
+                      int64_t yps, int pair) {
+    if (!nhwc_first_direct_supported(C, KH, KW, SY, SX, DY, DX, F, yps) || !aligned16(y))
+        return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: unsupported geometry");
+    FirstGeom fg{B, C, H, W, KH, KW, SY, SX, PY, PX, DY, DX, OH, OW};
+    return first_direct_launch(ctx, fg, x, x_bs, wd, round_up(F, 32), bias, F, act, y, OH * OW * yps, yps,
+                               pair ? 2 : 1);
+}
 
 int nhwc_im2col_first(tb_ctx* ctx, int64_t B, int64_t C, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t SY,
                       int64_t SX, int64_t PY, int64_t PX, int64_t DY, int64_t DX, int64_t OH, int64_t OW,
