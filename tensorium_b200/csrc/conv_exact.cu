@@ -40,6 +40,9 @@ constexpr int kWsBase = 100;
 bool ws_mode(int mode, bool fma) { return fma && (mode == EX_3X3 || mode == EX_1X1V); }
 // configurations 110 / 111: 32 outputs per thread, 64 x 64 (8 x 4) and 64 x 128 (4 x 8)
 constexpr int kSmallBase = 110;
+// configurations 120 .. 120 + SLIDE_TILES - 1: the staged-once 3x3 stride-1 kernel (conv_slide.cu)
+constexpr int kSlideBase = 120;
+bool is_slide(int t) { return t >= kSlideBase && t < kSlideBase + SLIDE_TILES; }
 
 // tile index t of kTiles plus a stage-depth variant (ExactShape) in t / kNumTiles
 int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool fma) {
@@ -57,16 +60,19 @@ int run_tile(tb_ctx* ctx, int t, const ConvParams& p, dim3 grid, int mode, bool 
 }
 
 int tile_bm(int t) {
+    if (is_slide(t)) return slide_tile_bm(t - kSlideBase);
     if (t == kSmallBase) return 64;
     if (t == kSmallBase + 1) return 64;
     return t >= kWsBase ? 128 : kTiles[t % kNumTiles].BM;
 }
 int tile_bn(int t) {
+    if (is_slide(t)) return slide_tile_bn(t - kSlideBase);
     if (t == kSmallBase) return 64;
     if (t == kSmallBase + 1) return 128;
     return t >= kWsBase ? (t == kWsBase ? 64 : 128) : kTiles[t % kNumTiles].BN;
 }
 int tile_nt(int t) {
+    if (is_slide(t)) return slide_tile_bm(t - kSlideBase) * slide_tile_bn(t - kSlideBase) / 64;
     if (t == kSmallBase) return 128;
     if (t == kSmallBase + 1) return 256;
     return t >= kWsBase ? (t == kWsBase ? 128 : 256) : kTiles[t % kNumTiles].NT;
@@ -112,6 +118,7 @@ int choose_tile(tb_ctx* ctx, const ConvGeom& g, int mode, bool fma) {
         int t = atoi(f);
         if (t >= kWsBase && t <= kWsBase + 1 && ws_mode(mode, fma) && tile_admissible(t, g.F)) return t;
         if (t >= kSmallBase && t <= kSmallBase + 1 && tile_admissible(t, g.F)) return t;
+        if (is_slide(t) && fma && conv_slide_supported(g, t - kSlideBase) && tile_admissible(t, g.F)) return t;
         if (t >= 0 && t < num_configs(mode, fma) && tile_admissible(t, g.F)) return t;
         if (t >= 0 && tile_admissible(t % kNumTiles, g.F)) return t % kNumTiles;
     }
@@ -153,6 +160,7 @@ ConvParams params_of(const ConvGeom& g, const float* x, const float* wp, const f
 }
 
 int launch_tile(tb_ctx* ctx, int t, const ConvGeom& g, const ConvParams& p, int mode, bool fma) {
+    if (is_slide(t)) return conv_slide_launch(ctx, t - kSlideBase, g, p, false);
     const ExactTile T{tile_bm(t), tile_bn(t), tile_nt(t)};
     dim3 grid((unsigned)ceil_div(p.Ntot, T.BN), (unsigned)ceil_div(g.F, T.BM), 1);
     if (grid.y > 65535) return fail(TB_ERR_INVALID, "conv: grid too large");
@@ -202,6 +210,9 @@ int conv_exact_autotune(tb_ctx* ctx, const ConvGeom& g, const float* x, const fl
     if (ws_mode(mode, fma)) cfgs.push_back(kWsBase), cfgs.push_back(kWsBase + 1);
     cfgs.push_back(kSmallBase);
     cfgs.push_back(kSmallBase + 1);
+    if (fma)
+        for (int t = 0; t < SLIDE_TILES; ++t)
+            if (conv_slide_supported(g, t)) cfgs.push_back(kSlideBase + t);
     for (int t : cfgs) {
         if (rc != TB_OK) break;
         if (!tile_admissible(t, g.F)) continue;
