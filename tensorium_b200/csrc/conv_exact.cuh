@@ -340,8 +340,9 @@ int exact_launch_64x64n4(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, 
 int exact_launch_64x128m4(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, bool fma, int var);
 // 3x3 stride-1 pad-1 windows with each input value staged once (conv_slide.cu): tiles
 // 0..3 = 128x128, 128x64, 64x128, 64x64 (filters x positions) with a register window over one
-// staged copy, 4..7 = the same tiles reading four shifted copies
-constexpr int SLIDE_TILES = 8;
+// staged copy, 4..7 = the same tiles reading four shifted copies, 8..10 = register window with a
+// relaxed register cap (128x64 at 2 and 3 CTAs per SM, 128x128 at 1)
+constexpr int SLIDE_TILES = 11;
 bool conv_slide_supported(const ConvGeom& g, int tile);
 int conv_slide_launch(tb_ctx* ctx, int tile, const ConvGeom& g, const ConvParams& p, bool query);
 int slide_tile_bm(int tile);

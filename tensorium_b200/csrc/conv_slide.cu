@@ -45,8 +45,9 @@ inline int slide_smem_bytes(int BM, int Ls, int SH) {
     return SL_STAGES * (9 * SL_CC * BM + (SH ? 4 : 1) * SL_CC * Ls) * 4;
 }
 
-template <int BM, int BN, int WPM, int SH>
-__global__ void __launch_bounds__(slide_threads<BM, BN>(), 512 / slide_threads<BM, BN>())
+// MB: resident CTAs per SM the register allocation is capped for (0: 512 threads per SM)
+template <int BM, int BN, int WPM, int SH, int MB>
+__global__ void __launch_bounds__(slide_threads<BM, BN>(), MB ? MB : 512 / slide_threads<BM, BN>())
 k_conv_slide(const ConvParams p, const SlideParams s) {
     constexpr int NT = slide_threads<BM, BN>(), TX = BN / 8, KS = 9 * SL_CC, NCOPY = SH ? 4 : 1;
     extern __shared__ __align__(16) float smem[];
@@ -229,11 +230,11 @@ int slide_pitch(int64_t W) {
     return (int)wp;
 }
 
-template <int BM, int BN, int WPM, int SH>
+template <int BM, int BN, int WPM, int SH, int MB>
 int slide_launch_one(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, bool query) {
     constexpr int NT = slide_threads<BM, BN>();
     const int smem = slide_smem_bytes(BM, s.Ls, SH);
-    auto kern = k_conv_slide<BM, BN, WPM, SH>;
+    auto kern = k_conv_slide<BM, BN, WPM, SH, MB>;
     static std::mutex mu;
     static int done[64] = {0};  // largest dynamic shared memory enabled so far, per device
     {
@@ -255,18 +256,19 @@ int slide_launch_one(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, boo
     return launch(ctx, "k_conv_slide", kern, grid, dim3(NT), (size_t)smem, p, s);
 }
 
-template <int BM, int BN, int SH>
+template <int BM, int BN, int SH, int MB = 0>
 int slide_launch_tile(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, bool query) {
     switch (s.Wp & 3) {
-    case 0: return slide_launch_one<BM, BN, 0, SH>(ctx, p, s, query);
-    case 1: return slide_launch_one<BM, BN, 1, SH>(ctx, p, s, query);
-    default: return slide_launch_one<BM, BN, 2, SH>(ctx, p, s, query);
+    case 0: return slide_launch_one<BM, BN, 0, SH, MB>(ctx, p, s, query);
+    case 1: return slide_launch_one<BM, BN, 1, SH, MB>(ctx, p, s, query);
+    default: return slide_launch_one<BM, BN, 2, SH, MB>(ctx, p, s, query);
     }
 }
 
 // tiles 0-3: register window; 4-7: the same CTA tiles with four shifted copies
-constexpr int kSlideBM[SLIDE_TILES] = {128, 128, 64, 64, 128, 128, 64, 64};
-constexpr int kSlideBN[SLIDE_TILES] = {128, 64, 128, 64, 128, 64, 128, 64};
+// 8-10: register window, register cap relaxed: 128x64 for 2 and 3 CTAs per SM, 128x128 for 1
+constexpr int kSlideBM[SLIDE_TILES] = {128, 128, 64, 64, 128, 128, 64, 64, 128, 128, 128};
+constexpr int kSlideBN[SLIDE_TILES] = {128, 64, 128, 64, 128, 64, 128, 64, 64, 64, 128};
 constexpr int slide_sh(int tile) { return tile >= 4 ? 1 : 0; }
 
 SlideParams slide_params(const ConvGeom& g, int tile) {
@@ -309,7 +311,10 @@ int conv_slide_launch(tb_ctx* ctx, int tile, const ConvGeom& g, const ConvParams
     case 4: return slide_launch_tile<128, 128, 1>(ctx, p, s, query);
     case 5: return slide_launch_tile<128, 64, 1>(ctx, p, s, query);
     case 6: return slide_launch_tile<64, 128, 1>(ctx, p, s, query);
-    default: return slide_launch_tile<64, 64, 1>(ctx, p, s, query);
+    case 7: return slide_launch_tile<64, 64, 1>(ctx, p, s, query);
+    case 8: return slide_launch_tile<128, 64, 0, 2>(ctx, p, s, query);
+    case 9: return slide_launch_tile<128, 64, 0, 3>(ctx, p, s, query);
+    default: return slide_launch_tile<128, 128, 0, 1>(ctx, p, s, query);
     }
 }
 

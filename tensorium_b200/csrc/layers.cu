@@ -106,7 +106,7 @@ __global__ void k_upsample2(int64_t total2, int c, int h, int w, float scale,
             if (o < total2) {
                 const int xq = (int)(o % half);
                 const int64_t t = o / half;
-                v[r] = __ldcs(reinterpret_cast<const float2*>(x + t * w + 2 * xq));
+                v[r] = __ldcs(reinterpret_cast<const float2*>(x + t * w + 2 * xq));  // read once: evict-first
             }
         }
 #pragma unroll
@@ -121,8 +121,8 @@ __global__ void k_upsample2(int64_t total2, int c, int h, int w, float scale,
             const float a = scale * v[r].x, bb = scale * v[r].y;
             const float4 o4 = make_float4(a, a, bb, bb);
             float* dst = y + b * y_bs + (ch * oh + 2 * iy) * (int64_t)ow + 4 * xq;
-            __stcs(reinterpret_cast<float4*>(dst), o4);
-            __stcs(reinterpret_cast<float4*>(dst + ow), o4);
+            *reinterpret_cast<float4*>(dst) = o4;  // the next layer's input: default caching
+            *reinterpret_cast<float4*>(dst + ow) = o4;
         }
     }
 }
@@ -151,7 +151,7 @@ __global__ void k_copy_rows4(int64_t batch, int64_t n4, const float4* __restrict
             const int64_t i = i0 + r * step;
             if (i < total) {
                 const int64_t b = i / n4, e = i - b * n4;
-                v[r] = __ldcs(src + b * src_bs4 + e);
+                v[r] = src[b * src_bs4 + e];  // a route source may be read again later
             }
         }
 #pragma unroll
@@ -159,7 +159,7 @@ __global__ void k_copy_rows4(int64_t batch, int64_t n4, const float4* __restrict
             const int64_t i = i0 + r * step;
             if (i >= total) break;
             const int64_t b = i / n4, e = i - b * n4;
-            __stcs(dst + b * dst_bs4 + e, v[r]);
+            dst[b * dst_bs4 + e] = v[r];
         }
     }
 }
@@ -175,7 +175,7 @@ __global__ void k_shortcut4(int64_t n4, const float4* __restrict__ a, const floa
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int64_t i = i0 + r * step;
-            if (i < n4) u[r] = __ldcs(a + i), v[r] = __ldcs(b + i);
+            if (i < n4) u[r] = a[i], v[r] = b[i];  // b (the residual source) may still be read later
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
@@ -186,7 +186,7 @@ __global__ void k_shortcut4(int64_t n4, const float4* __restrict__ a, const floa
             o.y = tb_activate_dev(u[r].y + v[r].y, act);
             o.z = tb_activate_dev(u[r].z + v[r].z, act);
             o.w = tb_activate_dev(u[r].w + v[r].w, act);
-            __stcs(y + i, o);
+            y[i] = o;
         }
     }
 }

@@ -79,13 +79,27 @@ class DetectionGather:
     from rank 0 to the others.  With one rank the gather is a device copy."""
 
     def __init__(self, net, world: int, rank: int, capacity: int = 1024, thresh: float = 0.45,
-                 timeout_ms: int = 120000):
+                 timeout_ms: int = 120000, overlap: bool = False):
+        """overlap: each step copies the yolo outputs into staging buffers on the forward's stream
+        (a ~30 MB device copy) and runs the extraction, the gather and the download on a side
+        stream (a second library context bound to it), so the next forward starts at once;
+        join() makes the forward's stream wait for the side stream's last step."""
         import ctypes as C
         from ._lib import Detection, YoloHead, check, lib
+        from .context import Context
         self._C, self._lib, self._check = C, lib, check
         self.net, self.world, self.rank = net, world, rank
         self.capacity, self.thresh = capacity, thresh
+        self.overlap = overlap
         ctx = net.ctx
+        self.sctx = None
+        if overlap:
+            self.side = torch.cuda.Stream(ctx.torch_device)
+            self.sctx = Context(ctx.device, use_torch_stream=False)
+            self.sctx.set_stream(self.side)
+            self.ev_copied, self.ev_free, self.ev_done = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
+            self._free_recorded = False
+        gctx = self.sctx if overlap else ctx
         uid = (C.c_uint8 * 128)()
         if rank == 0:
             check(lib.tb_group_unique_id(uid))
@@ -94,10 +108,12 @@ class DetectionGather:
             dist.broadcast_object_list(box, src=0)
             uid = (C.c_uint8 * 128).from_buffer_copy(box[0])
         self.group = C.c_void_p()
-        check(lib.tb_group_init_rank(ctx.handle, world, rank, uid, timeout_ms, C.byref(self.group)))
+        check(lib.tb_group_init_rank(gctx.handle, world, rank, uid, timeout_ms, C.byref(self.group)))
         heads, outs = net.yolo_heads()
         self.heads = heads
-        self.hs = (YoloHead * len(heads))(*[h.head(o) for h, o in zip(heads, outs)])
+        self.outs = outs
+        self.stage = [torch.empty_like(o) for o in outs] if overlap else outs
+        self.hs = (YoloHead * len(heads))(*[h.head(o) for h, o in zip(heads, self.stage)])
         self.classes = max(h.classes for h in heads)
         B = net.batch
         self.rec_bytes = B * capacity * C.sizeof(Detection)
@@ -111,26 +127,52 @@ class DetectionGather:
             self.host = torch.empty(world * self.pack_bytes, dtype=torch.uint8).pin_memory()
         else:
             self.out = self.host = None
+        torch.cuda.synchronize(ctx.torch_device)  # buffers zeroed before any side-stream use
 
     def step(self, download: bool = True):
         """Detections of the last forward, gathered on rank 0 (and, with download, copied to its
-        pinned host buffer), all queued on the context's stream behind the forward: the counts
-        stay on the device (tb_yolo_detect_device) and the NCCL gather is only enqueued
-        (tb_group_gather_async), so the host never waits inside a step.  wait() bounds the wait
-        for the queued transfers."""
+        pinned host buffer), all queued behind the forward: the counts stay on the device
+        (tb_yolo_detect_device) and the NCCL gather is only enqueued (tb_group_gather_async), so
+        the host never waits inside a step.  wait() bounds the wait for the queued transfers."""
         C, lib, check = self._C, self._lib, self._check
         ctx = self.net.ctx
         B = self.net.batch
-        check(lib.tb_yolo_detect_device(ctx.handle, B, len(self.heads), self.hs, 416, 416, 416, 416, self.thresh,
+        dctx = ctx
+        if self.overlap:
+            cs = ctx.stream if hasattr(ctx.stream, "wait_event") else torch.cuda.current_stream(ctx.torch_device)
+            with torch.cuda.stream(cs):
+                if self._free_recorded:  # the previous extraction has read the staging buffers
+                    cs.wait_event(self.ev_free)
+                for st, o in zip(self.stage, self.outs):
+                    st.copy_(o)
+                self.ev_copied.record(cs)
+            self.side.wait_event(self.ev_copied)
+            dctx = self.sctx
+        check(lib.tb_yolo_detect_device(dctx.handle, B, len(self.heads), self.hs, 416, 416, 416, 416, self.thresh,
                                         1, 0, self.capacity, C.c_void_p(self.pack.data_ptr() + 8 * B),
                                         C.c_void_p(self.prob.data_ptr()), C.c_void_p(self.pack.data_ptr())))
+        if self.overlap:
+            self.ev_free.record(self.side)
+            self._free_recorded = True
         out = C.c_void_p(self.out.data_ptr()) if self.out is not None else None
         check(lib.tb_group_gather_async(self.group, self.send, self.sizes, out))
         if download and self.host is not None:
-            self.host.copy_(self.out, non_blocking=True)
+            with torch.cuda.stream(self.side if self.overlap else torch.cuda.current_stream(ctx.torch_device)):
+                self.host.copy_(self.out, non_blocking=True)
+        if self.overlap:
+            self.ev_done.record(self.side)
+
+    def join(self):
+        """Make the forward's stream wait for everything the last step queued on the side stream."""
+        if self.overlap:
+            ctx = self.net.ctx
+            cs = ctx.stream if hasattr(ctx.stream, "wait_event") else torch.cuda.current_stream(ctx.torch_device)
+            cs.wait_event(self.ev_done)
 
     def wait(self):
         self._check(self._lib.tb_group_wait(self.group))
+        if self.overlap:
+            self.side.synchronize()
 
     @property
     def d2h_bytes(self) -> int:
@@ -155,3 +197,6 @@ class DetectionGather:
         if self.group:
             self._lib.tb_group_destroy(self.group)
             self.group = self._C.c_void_p()
+        if self.sctx is not None:
+            self.sctx.close()
+            self.sctx = None
