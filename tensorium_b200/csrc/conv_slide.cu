@@ -211,12 +211,16 @@ k_conv_slide(const ConvParams p, const SlideParams s) {
         const int m = m0 + (i < 4 ? ty * 4 + i : BM / 2 + ty * 4 + (i - 4));
         if (m >= p.F) continue;
         const float bm = has_bias ? __ldg(p.bias + m) : 0.f;
+        float rv[8];  // the row's residual values, all loads in flight before the first store
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            rv[e] = (p.res && opix[e] >= 0) ? __ldg(p.res + ob[e] * p.r_bs + (long long)m * p.OHW + opix[e]) : 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             if (opix[e] < 0) continue;
             const long long off = (long long)m * p.OHW + opix[e];
             float o = conv_epi_value(acc[i][e], m, p, simple, has_bias, leaky, bm);
-            if (p.res) o = __fadd_rn(o, p.res[ob[e] * p.r_bs + off]);
+            if (p.res) o = __fadd_rn(o, rv[e]);
             p.y[ob[e] * p.y_bs + off] = o;
         }
     }
