@@ -313,9 +313,10 @@ def run_ours(args):
         fma = __import__("ctypes").c_double()
         from tensorium_b200._lib import check, lib
         check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
-        peak, bound, kernel = fma.value, "fp32", ("k_conv_exact (order-exact FP32 implicit GEMM, bit-identical "
-                                                  "to the reference CPU path) for 74 convs and k_conv_direct for "
-                                                  "the first")
+        peak, bound, kernel = fma.value, "fp32", ("order-exact FP32 convs, bit-identical to the reference CPU path: "
+                                                  "k_conv_slide (3x3 stride-1, input staged once) and k_conv_exact "
+                                                  "(implicit GEMM) as the set-up autotuner picks them per geometry, "
+                                                  "k_first_direct for the first layer")
         peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
                        "and bf16 tensor peaks only")
     else:

@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <functional>
 #include <vector>
 
 namespace tbi {
@@ -95,6 +96,16 @@ struct tb_net {
     // or, when it fits nhwc_first_direct (F <= 128, leaky or linear), computed straight from the
     // NCHW network input into its NHWC output (no x_nhwc, no receptive-field pass)
     bool first_direct = false;
+    // Branch schedule (FP32 NCHW plans, whose kernels share no scratch memory): the layers on the
+    // network's longest remaining path run on the launch stream, every other layer (e.g. the
+    // tails of YOLOv3's 13x13 and 26x26 heads) on a second stream, concurrently with the next
+    // scale's trunk; the edges that cross the two streams are ordered by events.
+    bool branches = false;
+    std::vector<int> lane;                    // per layer: 0 = launch stream, 1 = branch stream
+    std::vector<std::vector<int64_t>> waits;  // per layer: producers on the other stream
+    std::vector<cudaEvent_t> done;            // per layer: recorded after it when a consumer waits
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
 };
 
 namespace {
@@ -408,10 +419,111 @@ int run_layer(tb_net* net, int64_t i, const float* x) {
 
 int run_all(tb_net* net, const float* x) {
     net->launches = 0;
-    for (int64_t i = 0; i < (int64_t)net->layers.size(); ++i) {
-        int r = run_layer(net, i, x);
-        if (r != TB_OK) return r;
+    const int64_t n = (int64_t)net->layers.size();
+    if (!net->branches) {
+        for (int64_t i = 0; i < n; ++i) {
+            int r = run_layer(net, i, x);
+            if (r != TB_OK) return r;
+        }
+        return TB_OK;
     }
+    tb_ctx* ctx = net->ctx;
+    cudaStream_t main = ctx->stream;
+    TB_CHECK_CUDA(cudaEventRecord(net->fork_ev, main));
+    TB_CHECK_CUDA(cudaStreamWaitEvent(net->side, net->fork_ev, 0));
+    int r = TB_OK;
+    for (int64_t i = 0; i < n && r == TB_OK; ++i) {
+        cudaStream_t st = net->lane[i] ? net->side : main;
+        for (int64_t p : net->waits[i])
+            if (cudaStreamWaitEvent(st, net->done[p], 0) != cudaSuccess) r = fail(TB_ERR_CUDA, "branch wait");
+        if (r != TB_OK) break;
+        ctx->stream = st;
+        r = run_layer(net, i, x);
+        ctx->stream = main;
+        if (r == TB_OK && net->done[i] && cudaEventRecord(net->done[i], st) != cudaSuccess)
+            r = fail(TB_ERR_CUDA, "branch event");
+    }
+    // join the branch stream back in every case (a capture must end with it joined)
+    cudaEventRecord(net->join_ev, net->side);
+    cudaStreamWaitEvent(main, net->join_ev, 0);
+    return r;
+}
+
+// The branch schedule of a finalized FP32 NCHW plan (see tb_net::branches).
+int plan_branches(tb_net* net) {
+    const int64_t n = (int64_t)net->layers.size();
+    // launches[i]: layer i launches a kernel; src(j): the layers whose launches write j's output
+    std::vector<char> launches((size_t)n, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const Layer& L = *net->layers[i];
+        launches[i] = !L.absorbed && !(L.type == TB_LAYER_ROUTE && L.route_zero_copy);
+    }
+    std::function<void(int64_t, std::vector<int64_t>&)> src = [&](int64_t j, std::vector<int64_t>& out) {
+        const Layer& L = *net->layers[j];
+        if (L.absorbed) { out.push_back(j - 1); return; }  // written by the conv that absorbed it
+        if (L.type == TB_LAYER_ROUTE && L.route_zero_copy) {
+            for (int64_t k : L.inputs) src(k, out);
+            return;
+        }
+        out.push_back(j);
+    };
+    std::vector<std::vector<int64_t>> prod((size_t)n), cons((size_t)n);
+    std::vector<double> cost((size_t)n, 0.0);
+    for (int64_t i = 0; i < n; ++i) {
+        if (!launches[i]) continue;
+        const Layer& L = *net->layers[i];
+        std::vector<int64_t> p;
+        if (L.type == TB_LAYER_ROUTE) {
+            for (int64_t k : L.inputs) src(k, p);
+        } else {
+            if (i > 0) src(i - 1, p);
+            if (L.type == TB_LAYER_SHORTCUT) src(L.from, p);
+            if (L.fuse_res >= 0) src(L.fuse_res, p);
+        }
+        std::sort(p.begin(), p.end());
+        p.erase(std::unique(p.begin(), p.end()), p.end());
+        for (int64_t q : p) cons[q].push_back(i);
+        prod[i] = p;
+        cost[i] = (L.type == TB_LAYER_CONV || L.type == TB_LAYER_CONNECTED)
+                      ? 2.0 * L.filters * L.oh * L.ow * L.c * L.ksize * L.ksize
+                      : 1e5;
+    }
+    // longest remaining path (by FLOPs) from each launch; the trunk follows its maximum
+    std::vector<double> rem((size_t)n, 0.0);
+    for (int64_t i = n - 1; i >= 0; --i) {
+        if (!launches[i]) continue;
+        double m = 0.0;
+        for (int64_t c : cons[i]) m = std::max(m, rem[c]);
+        rem[i] = cost[i] + m;
+    }
+    net->lane.assign((size_t)n, 0);
+    std::vector<char> trunk((size_t)n, 0);
+    int64_t t = -1;
+    for (int64_t i = 0; i < n && t < 0; ++i)
+        if (launches[i]) t = i;
+    while (t >= 0) {
+        trunk[t] = 1;
+        int64_t nx = -1;
+        for (int64_t c : cons[t])
+            if (nx < 0 || rem[c] > rem[nx]) nx = c;
+        t = nx;
+    }
+    bool any = false;
+    for (int64_t i = 0; i < n; ++i)
+        if (launches[i] && !trunk[i]) { net->lane[i] = 1; any = true; }
+    if (!any) return TB_OK;
+    net->waits.assign((size_t)n, {});
+    net->done.assign((size_t)n, nullptr);
+    for (int64_t i = 0; i < n; ++i)
+        for (int64_t q : prod[i])
+            if (net->lane[q] != net->lane[i]) {
+                net->waits[i].push_back(q);
+                if (!net->done[q]) TB_CHECK_CUDA(cudaEventCreateWithFlags(&net->done[q], cudaEventDisableTiming));
+            }
+    TB_CHECK_CUDA(cudaStreamCreateWithFlags(&net->side, cudaStreamNonBlocking));
+    TB_CHECK_CUDA(cudaEventCreateWithFlags(&net->fork_ev, cudaEventDisableTiming));
+    TB_CHECK_CUDA(cudaEventCreateWithFlags(&net->join_ev, cudaEventDisableTiming));
+    net->branches = true;
     return TB_OK;
 }
 
@@ -446,6 +558,12 @@ int tb_net_destroy(tb_net* net) {
     enter(net->ctx);
     cudaStreamSynchronize(net->ctx->stream);
     free_graph(net);
+    if (net->side) cudaStreamSynchronize(net->side);
+    for (cudaEvent_t e : net->done)
+        if (e) cudaEventDestroy(e);
+    if (net->fork_ev) cudaEventDestroy(net->fork_ev);
+    if (net->join_ev) cudaEventDestroy(net->join_ev);
+    if (net->side) cudaStreamDestroy(net->side);
     for (float* p : net->allocs) cudaFree(p);
     delete net;
     return TB_OK;
@@ -910,6 +1028,24 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     }
     r = ensure_workspace(net->ctx, (size_t)std::max<int64_t>(ws_floats, 1) * sizeof(float));
     if (r != TB_OK) return r;
+    // 5. branch schedule: FP32 NCHW plans whose convs all run on kernels without scratch memory
+    //    (order-exact, direct, connected); TB_NET_BRANCHES=0 keeps one stream
+    {
+        const char* bv = getenv("TB_NET_BRANCHES");
+        bool ok = !net->nhwc && math_mode == TB_MATH_FP32 && !(bv && bv[0] == '0');
+        for (int64_t i = 0; ok && i < n; ++i) {
+            const Layer& L = *net->layers[i];
+            if (L.type != TB_LAYER_CONV) continue;
+            tb_conv_desc d;
+            desc_of(net, L, &d);
+            ConvGeom g;
+            if (conv_geom(&d, &g) != TB_OK || !conv_exact_supported(g)) ok = false;
+        }
+        if (ok) {
+            r = plan_branches(net);
+            if (r != TB_OK) return r;
+        }
+    }
     TB_CHECK_CUDA(cudaStreamSynchronize(net->ctx->stream));
     net->finalized = true;
     return TB_OK;
