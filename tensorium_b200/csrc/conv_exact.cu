@@ -73,7 +73,7 @@ int tile_bn(int t) {
     return t >= kWsBase ? (t == kWsBase ? 64 : 128) : kTiles[t % kNumTiles].BN;
 }
 int tile_nt(int t) {
-    if (is_slide(t)) return slide_tile_bm(t - kSlideBase) * slide_tile_bn(t - kSlideBase) / 64;
+    if (is_slide(t)) return slide_tile_nt(t - kSlideBase);
     if (t == kSmallBase) return 128;
     if (t == kSmallBase + 1) return 256;
     return t >= kWsBase ? (t == kWsBase ? 128 : 256) : kTiles[t % kNumTiles].NT;
@@ -81,6 +81,7 @@ int tile_nt(int t) {
 
 bool tile_admissible(int t, int64_t M) {
     const int BM = tile_bm(t);
+    if (is_slide(t) && BM == 32) return true;  // the staged-once 32x64 tiles: more CTAs for small layers
     if (M <= 32) return BM == 32;
     if (M <= 64) return BM <= 64;
     return BM >= 64;

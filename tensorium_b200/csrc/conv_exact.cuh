@@ -342,11 +342,12 @@ int exact_launch_64x128m4(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode,
 // 0..3 = 128x128, 128x64, 64x128, 64x64 (filters x positions) with a register window over one
 // staged copy, 4..7 = the same tiles reading four shifted copies, 8..10 = register window with a
 // relaxed register cap (128x64 at 2 and 3 CTAs per SM, 128x128 at 1)
-constexpr int SLIDE_TILES = 11;
+constexpr int SLIDE_TILES = 17;  // 11..16: smaller thread tiles (8x4, 4x4, 4x8 outputs per thread)
 bool conv_slide_supported(const ConvGeom& g, int tile);
 int conv_slide_launch(tb_ctx* ctx, int tile, const ConvGeom& g, const ConvParams& p, bool query);
 int slide_tile_bm(int tile);
 int slide_tile_bn(int tile);
+int slide_tile_nt(int tile);
 // warp-specialised variant (conv_exact_ws.cu): 128 filters x bn (64 or 128) pixels per CTA
 int exact_ws_launch(tb_ctx* ctx, const ConvParams& p, dim3 grid, int mode, int bn);
 

@@ -16,7 +16,8 @@
 // P0 - Wp - 1 .. P0 + BN + Wp (Ls floats, ~BN + 2*Wp) with 4-byte cp.async copies whose source
 // offsets every thread computes once; the conv_exact 3x3 mode copies 9*BN gathered values instead.
 //
-// Mainloop.  A thread owns 8 filters (two quads BM/2 apart) x 8 positions (two quads BN/2 apart).
+// Mainloop.  A thread owns 8 filters (two quads BM/2 apart) x 8 positions (two quads BN/2 apart)
+// (4-filter / 4-position tiles for small layers).
 // For one (channel, kernel row r) it reads each position quad's 6-value input window with two
 // 16-byte shared loads and runs the three taps s = 0, 1, 2 from registers: 4 shared loads of input
 // and 6 of weights per 192 FMAs.  The window's misalignment (r*Wp) mod 4 is a compile-time constant
@@ -36,8 +37,8 @@ constexpr int SL_CC = 4;      // channels per stage: 36 k rows
 constexpr int SL_STAGES = 3;  // cp.async ring depth
 constexpr int SL_JMAX = 4;    // staged floats per channel <= SL_JMAX * threads
 
-template <int BM, int BN>
-__host__ __device__ constexpr int slide_threads() { return (BM / 8) * (BN / 8); }
+template <int BM, int BN, int TM, int TN>
+__host__ __device__ constexpr int slide_threads() { return (BM / TM) * (BN / TN); }
 
 // SH = 1 stages four copies of each channel's run, copy d shifted left by d floats, so that every
 // tap's position quads are aligned float4s of one copy (the plain outer-product k step).
@@ -45,11 +46,15 @@ inline int slide_smem_bytes(int BM, int Ls, int SH) {
     return SL_STAGES * (9 * SL_CC * BM + (SH ? 4 : 1) * SL_CC * Ls) * 4;
 }
 
-// MB: resident CTAs per SM the register allocation is capped for (0: 512 threads per SM)
-template <int BM, int BN, int WPM, int SH, int MB>
-__global__ void __launch_bounds__(slide_threads<BM, BN>(), MB ? MB : 512 / slide_threads<BM, BN>())
+// A thread owns TM filters (TM/4 quads, BM/2 apart when two) x TN positions (TN/4 quads, BN/2
+// apart when two).  MB: resident CTAs per SM the register allocation is capped for (0: 512
+// threads per SM).
+template <int BM, int BN, int TM, int TN, int WPM, int SH, int MB>
+__global__ void __launch_bounds__(slide_threads<BM, BN, TM, TN>(), MB ? MB : 512 / slide_threads<BM, BN, TM, TN>())
 k_conv_slide(const ConvParams p, const SlideParams s) {
-    constexpr int NT = slide_threads<BM, BN>(), TX = BN / 8, KS = 9 * SL_CC, NCOPY = SH ? 4 : 1;
+    constexpr int NT = slide_threads<BM, BN, TM, TN>(), TX = BN / TN, KS = 9 * SL_CC, NCOPY = SH ? 4 : 1;
+    constexpr int QM = TM / 4, QN = TN / 4, MSTEP = BM / QM, NSTEP = BN / QN;
+    static_assert((TM == 4 || TM == 8) && (TN == 4 || TN == 8), "thread tiles of 4 or 8");
     extern __shared__ __align__(16) float smem[];
     float* As = smem;                            // [STAGES][KS][BM]
     float* Bs = smem + SL_STAGES * KS * BM;      // [STAGES][NCOPY][CC][Ls]
@@ -119,11 +124,11 @@ k_conv_slide(const ConvParams p, const SlideParams s) {
         }
     };
 
-    float acc[8][8];
+    float acc[TM][TN];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
 #pragma unroll
     for (int st = 0; st < SL_STAGES - 1; ++st) {
@@ -141,7 +146,7 @@ k_conv_slide(const ConvParams p, const SlideParams s) {
         }
         const float* as = As + (t % SL_STAGES) * KS * BM + ty * 4;
         const float* bs = Bs + (t % SL_STAGES) * NCOPY * SL_CC * Ls + 4 * tx;
-        if (SH) {
+        if constexpr (SH != 0) {
 #pragma unroll 1
             for (int cc = 0; cc < SL_CC; ++cc)
 #pragma unroll
@@ -150,54 +155,58 @@ k_conv_slide(const ConvParams p, const SlideParams s) {
                     for (int sx = 0; sx < 3; ++sx) {
                         const int d = (r * WPM + sx) & 3;  // compile-time: the copy whose quads align
                         const float* bq = bs + (d * SL_CC + cc) * Ls + r * Wp + sx - d;
-                        float a[8], bv[8];
+                        float a[TM], bv[TN];
                         const float* ar = as + (cc * 9 + r * 3 + sx) * BM;
-                        *reinterpret_cast<float4*>(&a[0]) = *reinterpret_cast<const float4*>(ar);
-                        *reinterpret_cast<float4*>(&a[4]) = *reinterpret_cast<const float4*>(ar + BM / 2);
-                        *reinterpret_cast<float4*>(&bv[0]) = *reinterpret_cast<const float4*>(bq);
-                        *reinterpret_cast<float4*>(&bv[4]) = *reinterpret_cast<const float4*>(bq + BN / 2);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
+                        for (int q = 0; q < QM; ++q)
+                            *reinterpret_cast<float4*>(&a[4 * q]) = *reinterpret_cast<const float4*>(ar + q * MSTEP);
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
+                        for (int q = 0; q < QN; ++q)
+                            *reinterpret_cast<float4*>(&bv[4 * q]) = *reinterpret_cast<const float4*>(bq + q * NSTEP);
+#pragma unroll
+                        for (int i = 0; i < TM; ++i)
+#pragma unroll
+                            for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
                     }
-            continue;
-        }
+        } else {
 #pragma unroll 1
         for (int cc = 0; cc < SL_CC; ++cc) {
 #pragma unroll
             for (int r = 0; r < 3; ++r) {
                 const int o = (r * WPM) & 3;  // compile-time after unrolling: at most 2
                 const float* w0 = bs + cc * Ls + r * Wp - o;  // 16-byte aligned
-                float v0[8], v1[8];
-                *reinterpret_cast<float4*>(&v0[0]) = *reinterpret_cast<const float4*>(w0);
-                *reinterpret_cast<float4*>(&v0[4]) = *reinterpret_cast<const float4*>(w0 + 4);
-                *reinterpret_cast<float4*>(&v1[0]) = *reinterpret_cast<const float4*>(w0 + BN / 2);
-                *reinterpret_cast<float4*>(&v1[4]) = *reinterpret_cast<const float4*>(w0 + BN / 2 + 4);
+                float v[QN][8];  // each position quad's input window (6 of 8 values used)
+#pragma unroll
+                for (int q = 0; q < QN; ++q) {
+                    *reinterpret_cast<float4*>(&v[q][0]) = *reinterpret_cast<const float4*>(w0 + q * NSTEP);
+                    *reinterpret_cast<float4*>(&v[q][4]) = *reinterpret_cast<const float4*>(w0 + q * NSTEP + 4);
+                }
 #pragma unroll
                 for (int sx = 0; sx < 3; ++sx) {
                     const float* ar = as + (cc * 9 + r * 3 + sx) * BM;
-                    float a[8];
-                    *reinterpret_cast<float4*>(&a[0]) = *reinterpret_cast<const float4*>(ar);
-                    *reinterpret_cast<float4*>(&a[4]) = *reinterpret_cast<const float4*>(ar + BM / 2);
+                    float a[TM];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                    for (int q = 0; q < QM; ++q)
+                        *reinterpret_cast<float4*>(&a[4 * q]) = *reinterpret_cast<const float4*>(ar + q * MSTEP);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            acc[i][j] = fmaf(a[i], v0[o + sx + j], acc[i][j]);
-                            acc[i][4 + j] = fmaf(a[i], v1[o + sx + j], acc[i][4 + j]);
-                        }
+                    for (int i = 0; i < TM; ++i)
+#pragma unroll
+                        for (int q = 0; q < QN; ++q)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                acc[i][4 * q + j] = fmaf(a[i], v[q][o + sx + j], acc[i][4 * q + j]);
                 }
             }
+        }
         }
     }
     cp_async_wait<0>();
 
     // ---- epilogue: the conv_exact epilogue arithmetic, junk positions dropped ----
-    int ob[8], opix[8];  // image and pixel of the thread's 8 positions (opix -1: junk)
+    int ob[TN], opix[TN];  // image and pixel of the thread's positions (opix -1: junk)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const long long q = P0 + (e < 4 ? 4 * tx + e : BN / 2 + 4 * tx + (e - 4));
+    for (int e = 0; e < TN; ++e) {
+        const long long q = P0 + (e / 4) * NSTEP + 4 * tx + (e % 4);
         const long long row = q / Wp;
         const int xx = (int)(q - row * Wp);
         const int b = (int)(row / s.Hp), yy = (int)(row - (long long)b * s.Hp);
@@ -207,16 +216,16 @@ k_conv_slide(const ConvParams p, const SlideParams s) {
     const bool simple = !p.bn_mean && p.yolo_classes == 0 && (p.act == TB_ACT_LEAKY || p.act == TB_ACT_LINEAR);
     const bool has_bias = p.bias != nullptr, leaky = p.act == TB_ACT_LEAKY;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int m = m0 + (i < 4 ? ty * 4 + i : BM / 2 + ty * 4 + (i - 4));
+    for (int i = 0; i < TM; ++i) {
+        const int m = m0 + (i / 4) * MSTEP + ty * 4 + (i % 4);
         if (m >= p.F) continue;
         const float bm = has_bias ? __ldg(p.bias + m) : 0.f;
-        float rv[8];  // the row's residual values, all loads in flight before the first store
+        float rv[TN];  // the row's residual values, all loads in flight before the first store
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
+        for (int e = 0; e < TN; ++e)
             rv[e] = (p.res && opix[e] >= 0) ? __ldg(p.res + ob[e] * p.r_bs + (long long)m * p.OHW + opix[e]) : 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < TN; ++e) {
             if (opix[e] < 0) continue;
             const long long off = (long long)m * p.OHW + opix[e];
             float o = conv_epi_value(acc[i][e], m, p, simple, has_bias, leaky, bm);
@@ -234,11 +243,11 @@ int slide_pitch(int64_t W) {
     return (int)wp;
 }
 
-template <int BM, int BN, int WPM, int SH, int MB>
+template <int BM, int BN, int TM, int TN, int WPM, int SH, int MB>
 int slide_launch_one(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, bool query) {
-    constexpr int NT = slide_threads<BM, BN>();
+    constexpr int NT = slide_threads<BM, BN, TM, TN>();
     const int smem = slide_smem_bytes(BM, s.Ls, SH);
-    auto kern = k_conv_slide<BM, BN, WPM, SH, MB>;
+    auto kern = k_conv_slide<BM, BN, TM, TN, WPM, SH, MB>;
     static std::mutex mu;
     static int done[64] = {0};  // largest dynamic shared memory enabled so far, per device
     {
@@ -260,20 +269,24 @@ int slide_launch_one(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, boo
     return launch(ctx, "k_conv_slide", kern, grid, dim3(NT), (size_t)smem, p, s);
 }
 
-template <int BM, int BN, int SH, int MB = 0>
+template <int BM, int BN, int SH, int MB = 0, int TM = 8, int TN = 8>
 int slide_launch_tile(tb_ctx* ctx, const ConvParams& p, const SlideParams& s, bool query) {
     switch (s.Wp & 3) {
-    case 0: return slide_launch_one<BM, BN, 0, SH, MB>(ctx, p, s, query);
-    case 1: return slide_launch_one<BM, BN, 1, SH, MB>(ctx, p, s, query);
-    default: return slide_launch_one<BM, BN, 2, SH, MB>(ctx, p, s, query);
+    case 0: return slide_launch_one<BM, BN, TM, TN, 0, SH, MB>(ctx, p, s, query);
+    case 1: return slide_launch_one<BM, BN, TM, TN, 1, SH, MB>(ctx, p, s, query);
+    default: return slide_launch_one<BM, BN, TM, TN, 2, SH, MB>(ctx, p, s, query);
     }
 }
 
 // tiles 0-3: register window; 4-7: the same CTA tiles with four shifted copies
-// 8-10: register window, register cap relaxed: 128x64 for 2 and 3 CTAs per SM, 128x128 for 1
-constexpr int kSlideBM[SLIDE_TILES] = {128, 128, 64, 64, 128, 128, 64, 64, 128, 128, 128};
-constexpr int kSlideBN[SLIDE_TILES] = {128, 64, 128, 64, 128, 64, 128, 64, 64, 64, 128};
-constexpr int slide_sh(int tile) { return tile >= 4 ? 1 : 0; }
+// 8-10: register window, register cap relaxed: 128x64 for 2 and 3 CTAs per SM, 128x128 for 1;
+// 11-16: smaller thread tiles (more warps for small layers): 64x64 at 8x4, 64x64 at 4x4, 32x64 at
+// 4x4, 64x64 at 4x8, 128x64 at 8x4, 32x64 at 8x4
+constexpr int kSlideBM[SLIDE_TILES] = {128, 128, 64, 64, 128, 128, 64, 64, 128, 128, 128, 64, 64, 32, 64, 128, 32};
+constexpr int kSlideBN[SLIDE_TILES] = {128, 64, 128, 64, 128, 64, 128, 64, 64, 64, 128, 64, 64, 64, 64, 64, 64};
+constexpr int kSlideTM[SLIDE_TILES] = {8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 4, 4, 4, 8, 8};
+constexpr int kSlideTN[SLIDE_TILES] = {8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 4, 4, 4, 8, 4, 4};
+constexpr int slide_sh(int tile) { return tile >= 4 && tile < 8 ? 1 : 0; }
 
 SlideParams slide_params(const ConvGeom& g, int tile) {
     SlideParams s;
@@ -293,7 +306,7 @@ bool conv_slide_supported(const ConvGeom& g, int tile) {
         return false;
     if (g.OH != g.H || g.OW != g.W || g.C % SL_CC != 0 || g.C < SL_CC) return false;
     const SlideParams s = slide_params(g, tile);
-    const int nt = (kSlideBM[tile] / 8) * (kSlideBN[tile] / 8);
+    const int nt = (kSlideBM[tile] / kSlideTM[tile]) * (kSlideBN[tile] / kSlideTN[tile]);
     if (s.Ls > SL_JMAX * nt) return false;
     if (slide_smem_bytes(kSlideBM[tile], s.Ls, slide_sh(tile)) > 113 * 1024) return false;  // two CTAs per SM
     // 32-bit staged offsets and positions
@@ -302,6 +315,7 @@ bool conv_slide_supported(const ConvGeom& g, int tile) {
 }
 
 int slide_tile_bm(int tile) { return kSlideBM[tile]; }
+int slide_tile_nt(int tile) { return (kSlideBM[tile] / kSlideTM[tile]) * (kSlideBN[tile] / kSlideTN[tile]); }
 int slide_tile_bn(int tile) { return kSlideBN[tile]; }
 
 // query = true: resident CTAs per SM instead of a launch
@@ -318,7 +332,13 @@ int conv_slide_launch(tb_ctx* ctx, int tile, const ConvGeom& g, const ConvParams
     case 7: return slide_launch_tile<64, 64, 1>(ctx, p, s, query);
     case 8: return slide_launch_tile<128, 64, 0, 2>(ctx, p, s, query);
     case 9: return slide_launch_tile<128, 64, 0, 3>(ctx, p, s, query);
-    default: return slide_launch_tile<128, 128, 0, 1>(ctx, p, s, query);
+    case 10: return slide_launch_tile<128, 128, 0, 1>(ctx, p, s, query);
+    case 11: return slide_launch_tile<64, 64, 0, 0, 8, 4>(ctx, p, s, query);
+    case 12: return slide_launch_tile<64, 64, 0, 0, 4, 4>(ctx, p, s, query);
+    case 13: return slide_launch_tile<32, 64, 0, 0, 4, 4>(ctx, p, s, query);
+    case 14: return slide_launch_tile<64, 64, 0, 0, 4, 8>(ctx, p, s, query);
+    case 15: return slide_launch_tile<128, 64, 0, 0, 8, 4>(ctx, p, s, query);
+    default: return slide_launch_tile<32, 64, 0, 0, 8, 4>(ctx, p, s, query);
     }
 }
 

@@ -1,6 +1,7 @@
-"""The staged-once 3x3 stride-1 conv kernel (k_conv_slide, configurations 120-127 of the order-exact
+"""The staged-once 3x3 stride-1 conv kernel (k_conv_slide, configurations 120-136 of the order-exact
 FP32 conv: 128x128, 128x64, 64x128, 64x64 filters x positions, with a register window over
-one staged copy (120-123) or four shifted copies (124-127)) against the CPU oracle, bit for bit.
+one staged copy (120-123), four shifted copies (124-127), relaxed register caps (128-130) and
+smaller thread tiles (131-136)) against the CPU oracle, bit for bit.
 
 Its position space pads every image row to a pitch Wp (Wp mod 4 = 0, 1 or 2 give different
 compile-time window offsets) and every image by one junk row, so the cases cover each pitch class
@@ -20,7 +21,7 @@ from tensorium_b200.context import ptr
 
 pytestmark = pytest.mark.gpu
 
-TILES = list(range(120, 128))
+TILES = list(range(120, 137))
 
 
 def _conv(ctx, x, w, b, F, act=9, x_bs=0, residual=None, bn=None):
@@ -75,7 +76,7 @@ def test_slide_bit_exact(ctx, tile, monkeypatch):
         assert np.array_equal(y1, y2)
 
 
-@pytest.mark.parametrize("tile", [120, 123, 124, 127])
+@pytest.mark.parametrize("tile", [120, 123, 124, 127, 131, 133])
 def test_slide_channel_slice_input(ctx, tile, monkeypatch):
     """The input is channels [0, C) of a tensor with 3C channels per image (in_batch_stride)."""
     monkeypatch.setenv("TB_EXACT_FORCE", str(tile))
@@ -89,7 +90,7 @@ def test_slide_channel_slice_input(ctx, tile, monkeypatch):
     assert_bit_exact(y, ref, B * F, "slice")
 
 
-@pytest.mark.parametrize("tile", [121, 122, 125, 126])
+@pytest.mark.parametrize("tile", [121, 122, 125, 126, 132, 136])
 def test_slide_residual_and_batchnorm(ctx, tile, monkeypatch):
     monkeypatch.setenv("TB_EXACT_FORCE", str(tile))
     B, Cin, H, F = 2, 32, 13, 64
