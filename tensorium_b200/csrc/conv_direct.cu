@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(DIRECT_THREADS) k_conv_direct(const ConvParams
 // FK_FG x FK_PPT FMAs, each accumulator one chain in ascending k from 0 (the reference's order).
 // NHWC outputs go through a per-warp staging tile so that each store instruction writes whole
 // 64-byte pixel row pieces; NCHW outputs are stored per filter plane, 32 consecutive pixels per warp.
-constexpr int FK_THREADS = 128, FK_PPT = 2, FK_SEG = FK_THREADS * FK_PPT, FK_ROWS = 4;
+constexpr int FK_THREADS = 128, FK_PPT = 2, FK_SEG = FK_THREADS * FK_PPT, FK_ROWS = 8;
 constexpr int FK_KMAX = 32, FK_FMAX = 128, FK_FG = 16;  // filters per pass
 constexpr int FK_STG = FK_FG + 4;                        // staging row pitch (floats)
 
@@ -166,7 +166,14 @@ __host__ __device__ inline int fk_cols(int SX, int KW, int DX) { return (FK_SEG 
 // input rows per channel that FK_ROWS consecutive output rows read
 __host__ __device__ inline int fk_rows(int SY, int KH, int DY) { return (FK_ROWS - 1) * SY + (KH - 1) * DY + 1; }
 
-// KT: 27 = 3 channels, 3x3; 25 = 1 channel, 5x5 (the window as compile-time constants); 0: any
+// 4-byte asynchronous global -> shared copy; pred = false writes a zero.
+__device__ __forceinline__ void fk_cp4(float* smem, const float* gmem, bool pred) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(gmem), "r"(pred ? 4 : 0) : "memory");
+}
+
+// KT: 27 = 3 channels, 3x3; 25 = 1 channel, 5x5 (the window, stride 1 and no dilation as
+// compile-time constants); 0: any
 // window with C * KH * KW <= 32. FMT: the operand / output format (FirstParams::fmt); NHWC output
 // for FMT 1 and 2, NCHW planes for FMT 0.
 template <int KT, int FMT>
@@ -177,11 +184,14 @@ __global__ void __launch_bounds__(FK_THREADS, 3) k_first_direct(const FirstParam
     extern __shared__ __align__(16) float fsm[];
     const int C = CT ? CT : p.C, KH = KWT ? KWT : p.KH, KW = KWT ? KWT : p.KW;
     const int K = KT > 0 ? KT : C * KH * KW;
+    // the compile-time windows come with stride 1 and no dilation (the host checks), so every
+    // shared-memory offset below folds into an immediate
+    const int SX = KT ? 1 : p.SX, SY = KT ? 1 : p.SY, DX = KT ? 1 : p.DX, DY = KT ? 1 : p.DY;
     const int FG = (p.F + FK_FG - 1) & ~(FK_FG - 1);
-    const int cols = fk_cols(p.SX, KW, p.DX);
+    const int cols = fk_cols(SX, KW, DX);
     float* wsm = fsm;                                    // [K][FG]
     float* bsm = wsm + K * FG;                           // [FG]
-    const int nrin = fk_rows(p.SY, KH, p.DY);
+    const int nrin = fk_rows(SY, KH, DY);
     float* xs = bsm + FG;                                // [c][nrin input rows][cols]
     float* stg = xs + ((C * nrin * cols + 3) & ~3);      // NHWC: per warp 32 x FK_STG
     const int seg = blockIdx.x % p.segs;
@@ -189,29 +199,36 @@ __global__ void __launch_bounds__(FK_THREADS, 3) k_first_direct(const FirstParam
     const long long b = blockIdx.x / ((long long)p.segs * p.row_blocks);
     const int ox0 = seg * FK_SEG;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    for (int k = 0; k < K; ++k)
-        for (int f = t; f < FG; f += FK_THREADS) {
-            const float v = f < p.F ? __ldg(p.w + (long long)k * p.wstride + f) : 0.0f;
-            wsm[k * FG + f] = FMT == 1 ? tb_tf32_rna(v) : v;
-        }
-    for (int f = t; f < FG; f += FK_THREADS) bsm[f] = p.bias && f < p.F ? __ldg(p.bias + f) : 0.0f;
+    // Staging: every copy is an asynchronous 4-byte cp.async (zero-filled where the weight column
+    // or the input pixel does not exist), all in flight at once; a thread then waits for its own
+    // copies, rounds them in place for the TF32 output format, and the block synchronises.
     const float* xb = p.x + b * p.x_bs;
-    const int ix0 = ox0 * p.SX - p.PX;
+    const int ix0 = ox0 * SX - p.PX;
     const int OHW = p.OH * p.OW;
+    for (int i = t; i < K * FG; i += FK_THREADS) {
+        const int k = i / FG, f = i - k * FG;
+        const bool ok = f < p.F;
+        fk_cp4(wsm + i, ok ? p.w + (long long)k * p.wstride + f : p.w, ok);
+    }
+    for (int f = t; f < FG; f += FK_THREADS) {
+        const bool ok = p.bias && f < p.F;
+        fk_cp4(bsm + f, ok ? p.bias + f : p.w, ok);
+    }
     {
-        const int iy0 = rb * FK_ROWS * p.SY - p.PY;  // first input row of the block
-        int c = 0, ri = 0;
-        for (int row = 0; row < C * nrin; ++row) {
-            const int iy = iy0 + ri;
-            const bool rok = iy >= 0 && iy < p.H;
-            const float* src = xb + ((long long)c * p.H + (rok ? iy : 0)) * p.W;
-            for (int col = t; col < cols; col += FK_THREADS) {
-                const int ix = ix0 + col;
-                const float v = rok && ix >= 0 && ix < p.W ? __ldg(src + ix) : 0.0f;
-                xs[row * cols + col] = FMT == 1 ? tb_tf32_rna(v) : v;
-            }
-            if (++ri == nrin) ri = 0, ++c;
+        const int iy0 = rb * FK_ROWS * SY - p.PY;  // first input row of the block
+        const int n = C * nrin * cols;
+        for (int i = t; i < n; i += FK_THREADS) {
+            const int row = i / cols, col = i - row * cols;
+            const int c = row / nrin, ri = row - c * nrin;
+            const int iy = iy0 + ri, ix = ix0 + col;
+            const bool ok = iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
+            fk_cp4(xs + i, ok ? xb + ((long long)c * p.H + iy) * p.W + ix : p.x, ok);
         }
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    if constexpr (FMT == 1) {  // the TF32 operands: this thread's own copies, rounded in place
+        for (int i = t; i < K * FG; i += FK_THREADS) wsm[i] = tb_tf32_rna(wsm[i]);
+        for (int i = t; i < C * nrin * cols; i += FK_THREADS) xs[i] = tb_tf32_rna(xs[i]);
     }
     __syncthreads();
     for (int rr = 0; rr < FK_ROWS; ++rr) {
@@ -222,9 +239,9 @@ __global__ void __launch_bounds__(FK_THREADS, 3) k_first_direct(const FirstParam
             int c = 0, r = 0, s = 0;  // k = (c * KH + r) * KW + s
 #pragma unroll
             for (int k = 0; k < FK_KMAX; ++k) {
-                const int off = (c * nrin + rr * p.SY + r * p.DY) * cols + s * p.DX + t * p.SX;
+                const int off = (c * nrin + rr * SY + r * DY) * cols + s * DX + t * SX;
 #pragma unroll
-                for (int q = 0; q < FK_PPT; ++q) xv[q][k] = k < K ? xs[off + q * FK_THREADS * p.SX] : 0.0f;
+                for (int q = 0; q < FK_PPT; ++q) xv[q][k] = k < K ? xs[off + q * FK_THREADS * SX] : 0.0f;
                 if (k < K && ++s == KW) {
                     s = 0;
                     if (++r == KH) r = 0, ++c;
@@ -280,15 +297,15 @@ __global__ void __launch_bounds__(FK_THREADS, 3) k_first_direct(const FirstParam
                     for (int i = 0; i < 32 / RPI; ++i) {
                         const int px = i * RPI + lane / LPR, q4 = lane % LPR;
                         if (px < nvalid && 4 * q4 < nf)
-                            __stcs(reinterpret_cast<float4*>(yw + (long long)px * p.yps) + q4,
-                                   *reinterpret_cast<const float4*>(ws + px * FK_STG + 4 * q4));
+                            *(reinterpret_cast<float4*>(yw + (long long)px * p.yps) + q4) =
+                                *reinterpret_cast<const float4*>(ws + px * FK_STG + 4 * q4);  // the next layer reads it
                     }
                 } else {
                     if (wox + lane < p.OW) {
                         float* yp = p.y + b * p.y_bs + (long long)oy * p.OW + wox + lane;
 #pragma unroll
                         for (int j = 0; j < FK_FG; ++j)
-                            if (j < nf) __stcs(yp + (long long)(f0 + j) * OHW, o[j]);
+                            if (j < nf) yp[(long long)(f0 + j) * OHW] = o[j];  // the next layer reads it
                     }
                 }
             }
@@ -336,7 +353,8 @@ int first_direct_launch(tb_ctx* ctx, const FirstGeom& g, const float* x, int64_t
         return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: too many blocks");
     const int64_t smem = first_smem(g.C, g.KH, g.KW, g.SY, g.SX, g.DY, g.DX, F, nhwc);
     if (nhwc != (fmt != 0)) return fail(TB_ERR_UNSUPPORTED, "first-layer direct conv: NHWC goes with TF32 / pair outputs");
-    const int win = g.C == 3 && g.KH == 3 && g.KW == 3 ? 27 : g.C == 1 && g.KH == 5 && g.KW == 5 ? 25 : 0;
+    const bool unit = g.SY == 1 && g.SX == 1 && g.DY == 1 && g.DX == 1;  // the compile-time windows' stride
+    const int win = !unit ? 0 : g.C == 3 && g.KH == 3 && g.KW == 3 ? 27 : g.C == 1 && g.KH == 5 && g.KW == 5 ? 25 : 0;
     using Kern = void (*)(const FirstParams);
     static const Kern kerns[3][3] = {
         {k_first_direct<27, 0>, k_first_direct<27, 1>, k_first_direct<27, 2>},
