@@ -106,6 +106,12 @@ struct tb_net {
     std::vector<cudaEvent_t> done;            // per layer: recorded after it when a consumer waits
     cudaStream_t side = nullptr;
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+    // the branch stream's own split-K workspace and arrival counters (NHWC tensor-core plans, whose
+    // split-K layers would otherwise share the context's with the launch stream's layers)
+    void* side_ws = nullptr;
+    size_t side_ws_bytes = 0;
+    int* side_cnt = nullptr;
+    int64_t side_cnt_len = 0;
 };
 
 namespace {
@@ -438,8 +444,22 @@ int run_all(tb_net* net, const float* x) {
             if (cudaStreamWaitEvent(st, net->done[p], 0) != cudaSuccess) r = fail(TB_ERR_CUDA, "branch wait");
         if (r != TB_OK) break;
         ctx->stream = st;
+        void* ws = ctx->ws;
+        const size_t wsb = ctx->ws_bytes;
+        int* cnt = ctx->tile_cnt;
+        const int64_t cnt_len = ctx->tile_cnt_len;
+        if (net->lane[i] && net->side_ws) {
+            ctx->ws = net->side_ws;
+            ctx->ws_bytes = net->side_ws_bytes;
+            ctx->tile_cnt = net->side_cnt;
+            ctx->tile_cnt_len = net->side_cnt_len;
+        }
         r = run_layer(net, i, x);
         ctx->stream = main;
+        ctx->ws = ws;
+        ctx->ws_bytes = wsb;
+        ctx->tile_cnt = cnt;
+        ctx->tile_cnt_len = cnt_len;
         if (r == TB_OK && net->done[i] && cudaEventRecord(net->done[i], st) != cudaSuccess)
             r = fail(TB_ERR_CUDA, "branch event");
     }
@@ -1029,10 +1049,26 @@ int tb_net_finalize(tb_net* net, int64_t math_mode) {
     r = ensure_workspace(net->ctx, (size_t)std::max<int64_t>(ws_floats, 1) * sizeof(float));
     if (r != TB_OK) return r;
     // 5. branch schedule: FP32 NCHW plans whose convs all run on kernels without scratch memory
-    //    (order-exact, direct, connected); TB_NET_BRANCHES=0 keeps one stream
+    //    (order-exact, direct, connected), and NHWC tensor-core plans, whose branch stream gets its
+    //    own split-K workspace and counters; TB_NET_BRANCHES=0 keeps one stream
     {
         const char* bv = getenv("TB_NET_BRANCHES");
-        bool ok = !net->nhwc && math_mode == TB_MATH_FP32 && !(bv && bv[0] == '0');
+        const bool off = bv && bv[0] == '0';
+        if (net->nhwc && !off) {
+            r = plan_branches(net);
+            if (r != TB_OK) return r;
+            if (net->branches) {
+                net->side_ws_bytes = net->ctx->ws_bytes;
+                TB_CHECK_CUDA(cudaMalloc(&net->side_ws, std::max<size_t>(net->side_ws_bytes, 16)));
+                net->allocs.push_back(reinterpret_cast<float*>(net->side_ws));
+                net->side_cnt_len = net->ctx->tile_cnt_len;
+                float* c = alloc(std::max<int64_t>(net->side_cnt_len, 1));
+                if (!c) return err;
+                net->side_cnt = reinterpret_cast<int*>(c);
+                TB_CHECK_CUDA(cudaMemset(net->side_cnt, 0, (size_t)std::max<int64_t>(net->side_cnt_len, 1) * sizeof(int)));
+            }
+        }
+        bool ok = !net->nhwc && math_mode == TB_MATH_FP32 && !off;
         for (int64_t i = 0; ok && i < n; ++i) {
             const Layer& L = *net->layers[i];
             if (L.type != TB_LAYER_CONV) continue;
