@@ -332,7 +332,9 @@ def run_ours(args):
                 "peak_source": peak_source,
                 "traffic": traffic, "traffic_unit": "bytes per forward (ncu, summed over conv launches)",
                 "algorithmic_flops_per_forward": conv_flops, "conv_ms_per_forward": conv_ms,
-                "all_layers_ms_per_forward": total_ms}
+                "all_layers_ms_per_forward": total_ms,
+                # the same FLOPs over the graph-replayed step (every layer, branch stream included)
+                "frac_over_step": conv_flops / (ms / args.steps / 1e3) / 1e12 / peak}
 
     line = {"metric": {"fp32": METRIC, "tf32": METRIC_TF32, "bf16split": METRIC_BF16}.get(args.math, METRIC + " [" + args.math + "]"), "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -527,6 +529,7 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
                                         "TF32 tcgen05 MMA rate measured in this run with operands resident "
                                         "(tb_diag_tc_mma_rate, M=128 N=256 K=8, at the current SM clock)"),
                         "conv_ms_per_forward": conv_ms,
+                        "frac_over_step": flops / (ms / args.steps / 1e3) / 1e12 / tc_rate.value,
                         "traffic": (json.loads(PROFILE_SUMMARY_TF32.read_text()).get("dram_bytes_per_forward")
                                     if PROFILE_SUMMARY_TF32.exists() else None),
                         "traffic_unit": "bytes per forward (ncu, summed over every launch of one forward)"},
