@@ -324,7 +324,7 @@ def run_ours(args):
         bf16 = peaks.get("bf16_tflops", 1590.0)
         peak, bound = bf16 / 2, "tensor"
         kernel = ("k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) for all 75 convs "
-                  "+ the first layer's receptive-field conversion")
+                  "+ k_first_direct for the first layer (NHWC output)")
         peak_source = (f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)"
                        if "bf16_tflops" in peaks else "TF32 dense = half the fallback bf16 1590 TFLOP/s")
     roofline = {"bound": bound, "kernel": kernel,
@@ -518,8 +518,8 @@ def tf32_block(args, ctx, specs, x, net32, world, barrier, max_over_ranks, strea
            "gpu_launches": int(launches * args.steps),
            "roofline": {"bound": "tensor", "kernel": ("k_conv_nhwc<PAIR> (tcgen05 kind::f16, 8 MMAs per 32 channels) "
                                                       if is_bf else "k_conv_nhwc (tcgen05 TF32, ") +
-                                                     "A by TMA im2col, NHWC activations) + input / receptive-field "
-                                                     "conversion and NHWC upsample",
+                                                     "A by TMA im2col, NHWC activations) + k_first_direct (first layer, "
+                                                     "NHWC output) and NHWC upsample",
                         "achieved": achieved, "peak": tc_rate.value, "unit": "TFLOP/s",
                         "frac": achieved / tc_rate.value,
                         "peak_source": ("TF32 tcgen05 MMA rate measured in this run with operands resident "
