@@ -309,7 +309,7 @@ def run_ours(args):
     traffic = None
     if PROFILE_SUMMARY.exists() and args.math == "fp32":
         traffic = json.loads(PROFILE_SUMMARY.read_text()).get("dram_bytes_per_forward")
-    if args.math == "fp32":
+    if args.math in ("fp32", "fp32_tiled"):
         fma = __import__("ctypes").c_double()
         from tensorium_b200._lib import check, lib
         check(lib.tb_diag_fp32_fma_tflops(ctx.handle, __import__("ctypes").byref(fma)))
@@ -320,13 +320,18 @@ def run_ours(args):
         peak_source = ("FFMA rate measured in this run (tb_diag_fp32_fma_tflops); MEASURED_PEAKS.json holds HBM "
                        "and bf16 tensor peaks only")
     else:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        bf16 = peaks.get("bf16_tflops", 1590.0)
-        peak, bound = bf16 / 2, "tensor"
-        kernel = ("k_conv_nhwc (tcgen05 TF32, A by TMA im2col, NHWC activations) for all 75 convs "
+        import ctypes as _C
+        from tensorium_b200._lib import check, lib
+        tc_rate, cyc = _C.c_double(), _C.c_double()
+        check(lib.tb_diag_tc_mma_rate(ctx.handle, 1, _C.byref(tc_rate), _C.byref(cyc)))
+        peak, bound = tc_rate.value, "tensor"
+        kernel = ("k_conv_nhwc (tcgen05, A by TMA im2col, NHWC activations) for 74 convs "
                   "+ k_first_direct for the first layer (NHWC output)")
-        peak_source = (f"TF32 dense = half the measured cuBLAS bf16 burst rate ({bf16} TFLOP/s, MEASURED_PEAKS.json)"
-                       if "bf16_tflops" in peaks else "TF32 dense = half the fallback bf16 1590 TFLOP/s")
+        peak_source = ("TF32 tcgen05 MMA rate measured in this run with operands resident (tb_diag_tc_mma_rate, "
+                       "M=128 N=256 K=8, at the current SM clock); the BF16-split path issues twice the MMAs per "
+                       "FLOP" if args.math == "bf16split" else
+                       "TF32 tcgen05 MMA rate measured in this run with operands resident (tb_diag_tc_mma_rate, "
+                       "M=128 N=256 K=8, at the current SM clock)")
     roofline = {"bound": bound, "kernel": kernel,
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": peak_source,
